@@ -1,0 +1,334 @@
+"""Benchmark of the substitution hot path on B200 (one JSON line on rank 0).
+
+Workload: quantize_q8_1 of fp32 activations + Q4_K mul_mat_vec_q over an
+8192 x 2048 Q4_K weight matrix at batch 1, 2, 4 and 8 columns.  One step = the four
+(quantize, GEMV) pairs.  Metric: GB/s of algorithmic bytes (weights + q8_1 activations + fp32
+outputs + quantizer traffic) against the measured HBM peak.  Weights rotate over enough copies
+that every GEMV reads from HBM (inputs larger than L2).  Kernels are launched through the
+substitution C ABI (cfi_subst_launch with ggml kernelParams) and each step is replayed as a
+CUDA graph.  With --gpus N (torchrun) every rank owns an 8192-row shard of an (8192 N) x 2048
+matrix (weak scaling) and the outputs are all-gathered over NCCL each step.
+
+--impl reference times the CPU evaluation of the same step (the oracle port of the reference's
+host math, row-parallel over every host core) on rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cuda-for-intel_b200"))
+
+ROWS, K, BATCHES = 8192, 2048, (1, 2, 4, 8)
+W_BYTES = ROWS * K // 256 * 144                       # 9,437,184
+Q81 = lambda b: b * K // 32 * 36                       # q8_1 bytes of b columns
+MMVQ_BYTES = lambda b: W_BYTES + b * (Q81(1) + ROWS * 4)
+QUANT_BYTES = lambda b: b * (K * 4 + Q81(1))
+STEP_BYTES = sum(MMVQ_BYTES(b) + QUANT_BYTES(b) for b in BATCHES)
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "Q4_K decode GEMV + quantize_q8_1 throughput (8192x2048, batch 1/2/4/8)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def traffic_per_launch():
+    """dram bytes per mmvq launch from the committed ncu summary, if one exists."""
+    p = os.path.join(ROOT, "profiles", "mmvq_q4k_8192x2048_traffic.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["dram_bytes_per_launch_b1"])
+    except Exception:
+        return None
+
+
+def cpu_baseline(seconds, threads=0):
+    """The oracle's CPU decode step (reference host math, row-parallel) on a bounded sample."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import cfi_b200 as cfi
+    import oracle_py as O
+
+    w = cfi.synthetic_weights(cfi.Q4_K, ROWS, K, seed=7)
+    xs = {b: np.random.default_rng(b).normal(size=(b, K)).astype(np.float32) for b in BATCHES}
+    O.cpu_decode_step(cfi.Q4_K, w, ROWS, K, xs[1], 1, threads)
+    n, t0, used = 0, time.perf_counter(), 1
+    while True:
+        for b in BATCHES:
+            _, _, used = O.cpu_decode_step(cfi.Q4_K, w, ROWS, K, xs[b], b, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return STEP_BYTES * n / el / 1e9, used, n, el
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    gbs, used, n, el = cpu_baseline(max(1.0, min(20.0, 0.5 * (args.steps + args.warmup))))
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / n, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": {"workload": "config2: Q4_K 8192x2048 GEMV + quantize_q8_1, batch 1/2/4/8"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
+                             "sample": "%d full steps in %.1f s" % (n, el)},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu(args, rank, world):
+    import torch
+
+    import cfi_b200 as cfi
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    ctx = cfi.Ctx(local)
+    g = cfi.GgmlCaller(ctx, "all")
+    stream = torch.cuda.Stream(device=dev)
+
+    ncopy = max(8, int(np.ceil(3 * L2_BYTES / W_BYTES / 4.0)) * 4)   # > 3x L2 of weight copies
+    w = cfi.synthetic_weights(cfi.Q4_K, ROWS, K, seed=7 + rank)
+    wd = torch.empty((ncopy, w.size), dtype=torch.uint8, device=dev)
+    wd[0].copy_(torch.from_numpy(w.ravel()))
+    for i in range(1, ncopy):
+        wd[i].copy_(wd[0])
+    xs_host = {b: torch.from_numpy(np.random.default_rng(b).normal(size=(b, K)).astype(np.float32)).pin_memory()
+               for b in BATCHES}
+    xs = {b: xs_host[b].to(dev) for b in BATCHES}
+    qs = {b: torch.zeros(Q81(b), dtype=torch.uint8, device=dev) for b in BATCHES}
+    ys = {b: torch.zeros(b * ROWS, dtype=torch.float32, device=dev) for b in BATCHES}
+    y_all = torch.zeros(sum(b for b in BATCHES) * ROWS, dtype=torch.float32, device=dev)
+    offs, o = {}, 0
+    for b in BATCHES:
+        offs[b] = o
+        o += b * ROWS
+    y_views = {b: y_all[offs[b]:offs[b] + b * ROWS] for b in BATCHES}
+    gathered = torch.zeros(world * y_all.numel(), dtype=torch.float32, device=dev) if world > 1 else None
+    ys_host = torch.zeros(y_all.numel(), dtype=torch.float32).pin_memory()
+
+    def step(phase, s):
+        for j, b in enumerate(BATCHES):
+            g.quantize_q8_1(xs[b].data_ptr(), qs[b].data_ptr(), K, K, b, stream=s)
+            wcopy = wd[(phase * len(BATCHES) + j) % ncopy]
+            g.mmvq(cfi.Q4_K, b, wcopy.data_ptr(), qs[b].data_ptr(), y_views[b].data_ptr(), K, ROWS, stream=s)
+
+    nphase = ncopy // len(BATCHES)
+    # warm-up (first-use probes run here, outside any capture)
+    with torch.cuda.stream(stream):
+        for i in range(max(1, args.warmup)):
+            step(i % nphase, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graphs = []
+    for ph in range(nphase):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step(ph, torch.cuda.current_stream().cuda_stream)
+        graphs.append(gr)
+    launches_per_step = 2 * len(BATCHES)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % nphase].replay()
+            if dist:
+                dist.all_gather_into_tensor(gathered, y_all)
+    torch.cuda.synchronize()
+
+    # ---- timed region: device time, max over ranks ----
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(args.steps):
+                graphs[i % nphase].replay()
+                if dist:
+                    dist.all_gather_into_tensor(gathered, y_all)
+            e1.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * STEP_BYTES / (ms_step * 1e-3) / 1e9
+
+    # ---- dominant kernel: mmvq Q4_K batch 1, CUDA events around each launch ----
+    nrep = max(20, 4 * args.steps)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nrep)]
+    with torch.cuda.stream(stream):
+        for i in range(nrep):
+            evs[i][0].record(stream)
+            g.mmvq(cfi.Q4_K, 1, wd[i % ncopy].data_ptr(), qs[1].data_ptr(), y_views[1].data_ptr(), K, ROWS,
+                   stream=stream.cuda_stream)
+            evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    kms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    peak, peak_kind = peaks()
+    achieved = MMVQ_BYTES(1) / (kms * 1e-3) / 1e9
+
+    # ---- end to end: host activations in, outputs back to the host, every step ----
+    h2d = sum(xs_host[b].numel() * 4 for b in BATCHES)
+    d2h = y_all.numel() * 4
+    ge = []
+    for ph in range(nphase):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for b in BATCHES:
+                xs[b].copy_(xs_host[b], non_blocking=True)
+            step(ph, torch.cuda.current_stream().cuda_stream)
+            ys_host.copy_(y_all, non_blocking=True)
+        ge.append(gr)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            ge[i % nphase].replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            ge[i % nphase].replay()
+            if dist:
+                dist.all_gather_into_tensor(gathered, y_all)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * STEP_BYTES * args.steps / e2e_s / 1e9
+
+    stats = ctx.stats()
+    ok = stats["stock_launches"] == 0 and stats["native_failures"] == 0
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,0.02) weights quantized to Q4_K, "
+                "N(0,1) activations)",
+                "config": {"workload": "config2: Q4_K 8192x2048 GEMV + quantize_q8_1, batch 1/2/4/8",
+                           "rows_per_gpu": ROWS, "k": K, "batches": list(BATCHES), "weight_copies": ncopy,
+                           "l2": "inputs larger than L2: %d weight copies (%.0f MB) rotated" % (ncopy, ncopy * W_BYTES / 1e6),
+                           "parallelism": "row-sharded x%d + NCCL all-gather" % world if world > 1 else "single GPU",
+                           "bytes_per_step_per_gpu": STEP_BYTES, "cuda_graph": True},
+                "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "note": "host fp32 activations in and fp32 outputs out every step (weights resident), "
+                                "stream synchronized per step"},
+                "gpu_launches": launches_per_step * args.steps,
+                "roofline": {"bound": "hbm", "kernel": "mul_mat_vec_q<Q4_K,1> 8192x2048", "achieved": round(achieved, 1),
+                             "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                             "traffic": traffic_per_launch(), "launch_us": round(kms * 1e3, 3),
+                             "bytes_per_launch": MMVQ_BYTES(1)},
+                "clocks": clk.summary(), "native_only": ok}
+        if not args.no_cpu and world == 1:
+            gbs, used, n, el = cpu_baseline(args.cpu_seconds)
+            line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
+                                    "sample": "%d full steps (4 batches each) in %.1f s" % (n, el)}
+        print(json.dumps(line), flush=True)
+    del graphs, ge
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_gpu(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

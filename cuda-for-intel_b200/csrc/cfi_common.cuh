@@ -1,0 +1,41 @@
+// cfi_common.cuh -- device helpers shared by the sm_100a kernels of the substitution path.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define CFI_DEV __device__ __forceinline__
+
+// ggml block sizes (ggml-common.h layouts; see the block structs below).
+constexpr int QK8_0 = 32, QK8_1 = 32, QK4_0 = 32, QK_K = 256;
+constexpr int Q8_0_BYTES = 34, Q8_1_BYTES = 36, Q4_0_BYTES = 18, Q4_K_BYTES = 144, Q6_K_BYTES = 210;
+constexpr int MMQ_BLOCK_BYTES = 144;  // block_q8_1_mmq: 4 scales (16 B) + 128 int8
+
+// ggml type ids.
+constexpr uint32_t T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14;
+
+// ggml's fastdiv triple {mp, L, d}: n / d == (umulhi(n, mp) + n) >> L.
+CFI_DEV uint32_t fastdiv(uint32_t n, uint3 v) { return (__umulhi(n, v.x) + n) >> v.y; }
+CFI_DEV uint32_t fastmodulo(uint32_t n, uint3 v) { return n - fastdiv(n, v) * v.z; }
+
+CFI_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+CFI_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+CFI_DEV float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+CFI_DEV uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+CFI_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Bounded waits that give up record a code in a device error word instead of hanging; the
+// host reads it back after a synchronize (first code wins).
+CFI_DEV void cfi_set_error(unsigned int *err, unsigned int code) {
+    if (err) atomicCAS(err, 0u, code);
+}

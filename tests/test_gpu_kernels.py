@@ -1,0 +1,295 @@
+"""GPU parity tests of the native kernels, driven through the substitution C ABI
+(cfi_subst_launch with ggml-layout kernelParams), against the CPU oracle.
+
+Bars: quantizers byte-exact; GEMV integer block dots exact (checked bitwise with unit scales) and
+every output column bitwise equal to the oracle's one-warp whole-group decode model
+(refs.rs:435-497), within nmse 1e-10 of the stock thread order and 1e-3 relative L2 (stated bar);
+fp32 row ops within 1e-3 relative L2 (measured far tighter)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import cfi_b200 as cfi
+import oracle_py as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    yield ctx, g
+    ctx.close()
+
+
+def to_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def sync():
+    torch.cuda.synchronize()
+    err = cfi.lib().cfi_device_error()
+    assert err == 0, "device error word %x" % err
+
+
+# ------------------------------------------------------------------------------------------
+# quantize_q8_1 (refs.rs:117-147; probe.rs:392-401)
+# ------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("shape", [(96, 128, 3, 2, 1), (96, 128, 3, 2, 2), (896, 1024, 1, 1, 1), (2048, 2048, 8, 1, 1),
+                                   (97, 128, 2, 1, 1), (1536, 1536, 631, 1, 1)])
+def test_quantize_q8_1_is_byte_exact(dev, shape):
+    ctx, g = dev
+    ne00, ne0, ne1, ne2, ne3 = shape
+    x, ref = O.quantize_case(ne00, ne0, ne1, ne2, ne3, 0x71 + ne00)
+    dx = to_dev(x)
+    dy = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+    g.quantize_q8_1(dx.data_ptr(), dy.data_ptr(), ne00, ne0, ne1, ne2, ne3, stream=stream())
+    sync()
+    got = dy.cpu().numpy()
+    assert np.array_equal(got, ref), "%d of %d bytes differ" % ((got != ref).sum(), ref.size)
+
+
+def test_quantize_q8_1_large_magnitudes_and_ties(dev):
+    ctx, g = dev
+    rng = np.random.default_rng(9)
+    x = rng.normal(0, 1, 4096).astype(np.float32)
+    x[:32] = np.arange(32, dtype=np.float32) - 15.5      # ties at q = x/d
+    x[32:64] = 1e30
+    x[64:96] = -1e-30
+    x[96:128] = np.float32(127.0) * np.arange(32)
+    ref = O.quantize_q8_1(x)
+    dx = to_dev(x)
+    dy = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+    g.quantize_q8_1(dx.data_ptr(), dy.data_ptr(), 4096, 4096, 1, stream=stream())
+    sync()
+    assert np.array_equal(dy.cpu().numpy(), ref)
+
+
+# ------------------------------------------------------------------------------------------
+# mul_mat_vec_q
+# ------------------------------------------------------------------------------------------
+def run_mmvq(g, p, x, y, ids, n, use_ids=False):
+    dx, dy = to_dev(x), to_dev(y)
+    dids = to_dev(ids) if use_ids else None
+    dd = torch.zeros(n, dtype=torch.float32, device="cuda")
+    st = {"channel_x": p.stride_channel_x, "channel_y": p.stride_channel_y, "channel_dst": p.stride_channel_dst,
+          "sample_x": p.stride_sample_x, "sample_y": p.stride_sample_y, "sample_dst": p.stride_sample_dst}
+    g.mmvq(p.ty, p.ncols_dst, dx.data_ptr(), dy.data_ptr(), dd.data_ptr(), p.ncols_x, p.nrows_x,
+           stride_row_x=p.stride_row_x, stride_col_y=p.stride_col_y, stride_col_dst=p.stride_col_dst,
+           nchannels=p.nchannels_dst, channel_ratio=p.channel_ratio, nsamples=p.nsamples_dst,
+           ids=dids.data_ptr() if use_ids else 0, nchannels_y=p.nchannels_y, strides=st, stream=stream())
+    sync()
+    return dd.cpu().numpy()
+
+
+def per_column_decode_model(p, x, y, ids, n):
+    """Each output column through the oracle's one-warp whole-group model (refs.rs:435-497)."""
+    out = np.zeros(n, dtype=np.float32)
+    for c in range(p.ncols_dst):
+        q = O.Mmvq.from_buffer_copy(p)
+        q.ncols_dst = 1
+        ysub = np.ascontiguousarray(y[c * p.stride_col_y * 36:])
+        col = np.zeros(n, dtype=np.float32)
+        O.lib().cfo_mmvq_fast(C.byref(q), O.u8(x), O.u8(ysub), O.i32(ids), O.f32(col), 1, 1, 1)
+        for s in range(p.nsamples_dst):
+            for ch in range(p.nchannels_dst):
+                base = s * p.stride_sample_dst + ch * p.stride_channel_dst
+                out[base + c * p.stride_col_dst:base + c * p.stride_col_dst + p.nrows_x] = col[base:base + p.nrows_x]
+    return out
+
+
+@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K])
+@pytest.mark.parametrize("ncols", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_mmvq_matches_the_oracle(dev, ty, ncols):
+    ctx, g = dev
+    for nrows, ncols_x in [(5, 512), (11, 2304 if ty == cfi.Q8_0 else 2304 // 256 * 256), (300, 4096)]:
+        p, x, y, ids, n = O.mmvq_case(ty, ncols, nrows, ncols_x, 1, 1, 1, False, 7 + ty + ncols + nrows)
+        got = run_mmvq(g, p, x, y, ids, n)
+        model = per_column_decode_model(p, x, y, ids, n)
+        assert np.array_equal(got.view(np.uint32), model.view(np.uint32)), "bitwise vs the decode model"
+        stock = O.mmvq_ref(p, x, y, ids, n)
+        assert O.nmse(got, stock) < 1e-10
+        assert O.rel_l2(got, stock) < REL_L2
+        assert np.any(stock != 0)
+
+
+@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K])
+def test_mmvq_channels_samples_and_ids(dev, ty):
+    ctx, g = dev
+    for (nch, ratio, ns, use_ids, seed) in [(4, 2, 2, False, 99), (5, 1, 1, True, 100)]:
+        p, x, y, ids, n = O.mmvq_case(ty, 1, 3, 512, nch, ratio, ns, use_ids, seed)
+        got = run_mmvq(g, p, x, y, ids, n, use_ids)
+        want = O.mmvq_fast_ref(p, x, y, ids, n, 1, 1, True)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert O.nmse(got, O.mmvq_ref(p, x, y, ids, n)) < 1e-10
+
+
+@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K])
+def test_mmvq_integer_block_dots_are_exact(dev, ty):
+    """With every scale 1.0 (and Q4_K mins 0) each output is the exact integer sum of the int32
+    block dot products, so a bitwise match proves the integer path exact."""
+    ctx, g = dev
+    rng = np.random.default_rng(11)
+    rows, k, nc = 97, 2048, 3
+    if ty == cfi.Q8_0:
+        q = rng.integers(-128, 128, size=(rows, k // 32, 32)).astype(np.int8)
+        w = np.zeros((rows, k // 32, 34), dtype=np.uint8)
+        w[..., 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+        w[..., 2:] = q.view(np.uint8)
+        wq = q.reshape(rows, k).astype(np.int64)
+    else:
+        nib = rng.integers(0, 16, size=(rows, k // 256, 8, 32)).astype(np.uint8)
+        w = np.zeros((rows, k // 256, 144), dtype=np.uint8)
+        w[..., 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+        w[..., 4:8] = 1   # sc = 1 for sub-blocks 0..3, m = 0
+        w[..., 12:16] = 1  # low nibbles: sc = 1 for sub-blocks 4..7
+        for c in range(4):
+            w[..., 16 + 32 * c:48 + 32 * c] = nib[..., 2 * c, :] | (nib[..., 2 * c + 1, :] << 4)
+        wq = nib.reshape(rows, k).astype(np.int64)
+    qa = rng.integers(-127, 128, size=(nc, k)).astype(np.int8)
+    yb = np.zeros((nc, k // 32, 36), dtype=np.uint8)
+    yb[..., 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    yb[..., 4:] = qa.reshape(nc, k // 32, 32).view(np.uint8)
+    want = (wq @ qa.astype(np.int64).T).T.astype(np.float32)  # exact: |sum| < 2^24
+    dx, dy = to_dev(w.reshape(rows, -1)), to_dev(yb.reshape(-1))
+    dd = torch.zeros(nc * rows, dtype=torch.float32, device="cuda")
+    g.mmvq(ty, nc, dx.data_ptr(), dy.data_ptr(), dd.data_ptr(), k, rows, stream=stream())
+    sync()
+    assert np.array_equal(dd.cpu().numpy().reshape(nc, rows), want)
+
+
+@pytest.mark.parametrize("ty,rows,k,ncols", [(cfi.Q8_0, 4864, 896, 1), (cfi.Q8_0, 896, 4864, 1),
+                                             (cfi.Q4_K, 8192, 2048, 1), (cfi.Q4_K, 8192, 2048, 2),
+                                             (cfi.Q4_K, 8192, 2048, 4), (cfi.Q4_K, 8192, 2048, 8)])
+def test_decode_configs_full_size(dev, ty, rows, k, ncols):
+    """BASELINE configs 1 and 2 at full size: quantize + GEMV through the C ABI vs the oracle."""
+    ctx, g = dev
+    w = cfi.synthetic_weights(ty, rows, k, seed=rows + k)
+    acts = np.random.default_rng(k).normal(0, 1, size=(ncols, k)).astype(np.float32)
+    dw, dxf = to_dev(w), to_dev(acts)
+    dq = torch.zeros(ncols * k // 32 * 36, dtype=torch.uint8, device="cuda")
+    dd = torch.zeros(ncols * rows, dtype=torch.float32, device="cuda")
+    g.quantize_q8_1(dxf.data_ptr(), dq.data_ptr(), k, k, ncols, stream=stream())
+    g.mmvq(ty, ncols, dw.data_ptr(), dq.data_ptr(), dd.data_ptr(), k, rows, stream=stream())
+    sync()
+    yq = O.quantize_q8_1(acts)
+    assert np.array_equal(dq.cpu().numpy(), yq)
+    got = dd.cpu().numpy()
+    want, _, _ = O.cpu_decode_step(ty, w, rows, k, acts, ncols)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # and against a float64 dequantised product (the stated 1e-3 relative L2 bar holds by far)
+    assert O.rel_l2(got, want) < REL_L2
+
+
+# ------------------------------------------------------------------------------------------
+# row ops
+# ------------------------------------------------------------------------------------------
+def test_rms_norm_matches_the_oracle(dev):
+    ctx, g = dev
+    rng = np.random.default_rng(12)
+    for rows, ncols, mul in [(4, 896, True), (631, 1536, True), (3, 896, False)]:
+        x = rng.normal(size=(rows, ncols)).astype(np.float32)
+        w = rng.normal(size=ncols).astype(np.float32)
+        dx, dw = to_dev(x), to_dev(w)
+        dd = torch.zeros_like(dx)
+        g.rms_norm(dx.data_ptr(), dd.data_ptr(), ncols, rows, mul=dw.data_ptr() if mul else 0, eps=1e-6, stream=stream())
+        sync()
+        want = O.rms_norm(x, w if mul else None, rows, ncols, 1e-6)
+        assert O.rel_l2(dd.cpu().numpy().ravel(), want) < 1e-5
+
+
+def test_rms_norm_reference_test_case(dev):
+    """tests/gpu/ggml_rms_norm.rs:34-55: 4 x 32, eps 1e-5, LCG data, tolerance 2e-3*(1+|y|)."""
+    ctx, g = dev
+    rng, vals = 0xA11CE, []
+    for _ in range(128):
+        rng = (rng * 1664525 + 1013904223) & 0xFFFFFFFF
+        vals.append((rng >> 9) * (1.0 / 8388608.0) - 0.5)
+    x = np.array(vals, dtype=np.float32)
+    dx = to_dev(x)
+    dd = torch.zeros_like(dx)
+    g.rms_norm_plain(dx.data_ptr(), dd.data_ptr(), 32, 4, eps=1e-5, stream=stream())
+    sync()
+    want = O.rms_norm(x, None, 4, 32, 1e-5)
+    got = dd.cpu().numpy()
+    assert np.all(np.abs(got - want) <= 2e-3 * (1 + np.abs(want)))
+    assert O.rel_l2(got, want) < 1e-5
+
+
+@pytest.mark.parametrize("head_dim,heads,ff", [(64, 16, False), (128, 14, False), (128, 14, True)])
+def test_rope_neox_matches_the_oracle(dev, head_dim, heads, ff):
+    ctx, g = dev
+    rng = np.random.default_rng(head_dim + heads)
+    ntok = 7
+    pos = np.array([0, 1, 5, 100, 630, 631, 2047], dtype=np.int32)
+    x = rng.normal(size=(ntok, heads, head_dim)).astype(np.float32)
+    ffv = (1.0 + rng.random(head_dim // 2)).astype(np.float32) if ff else None
+    dx, dp = to_dev(x), to_dev(pos)
+    dff = to_dev(ffv) if ff else None
+    dd = torch.zeros_like(dx)
+    g.rope_neox(dx.data_ptr(), dd.data_ptr(), head_dim, heads, ntok, head_dim, dp.data_ptr(), freq_base=1e6,
+                freq_factors=dff.data_ptr() if ff else 0, stream=stream())
+    sync()
+    want = O.rope_neox(x, head_dim, heads, ntok, head_dim, pos, 1e6, ff=ffv)
+    assert O.rel_l2(dd.cpu().numpy().ravel(), want.ravel()) < 1e-4
+
+
+@pytest.mark.parametrize("ncols,ne01,nheads,f16,max_bias", [(12, 1, 2, False, 0.0), (631, 1, 14, False, 0.0),
+                                                          (631, 5, 12, True, 0.0), (700, 3, 12, False, 8.0)])
+def test_soft_max_matches_the_oracle(dev, ncols, ne01, nheads, f16, max_bias):
+    ctx, g = dev
+    rng = np.random.default_rng(ncols + nheads)
+    rows = ne01 * nheads
+    x = rng.normal(size=(rows, ncols)).astype(np.float32)
+    mask = np.where(rng.random((ne01, ncols)) < 0.1, -np.inf, rng.normal(size=(ne01, ncols))).astype(np.float32)
+    mask[:, 0] = 0.0
+    if f16:
+        mask = mask.astype(np.float16).astype(np.float32)
+    dx = to_dev(x)
+    dm = to_dev(mask.astype(np.float16) if f16 else mask)
+    dd = torch.zeros_like(dx)
+    g.soft_max(dx.data_ptr(), dm.data_ptr(), dd.data_ptr(), ncols, ne01, nheads, 0.125, max_bias=max_bias, mask_f16=f16,
+               stream=stream())
+    sync()
+    want = O.soft_max(x.ravel(), mask.ravel(), None, ncols, ne01, nheads, rows, 0.125, max_bias)
+    assert O.rel_l2(dd.cpu().numpy().ravel(), want) < 1e-5
+
+
+# ------------------------------------------------------------------------------------------
+# first-use probes and the router on the device
+# ------------------------------------------------------------------------------------------
+def test_every_native_kernel_passes_its_first_use_probe(dev):
+    ctx, g = dev
+    plans = []
+    for ty in (8, 12):
+        for n in (1, 2, 5, 8):
+            plans.append(cfi.decide(cfi.NAMES["mmvq"].format(ty=ty, ncols=n), "mmvq", "all")[1])
+    plans.append(cfi.decide(cfi.NAMES["quantize_q8_1"], "quantize_q8_1", "all")[1])
+    for lay in (0, 1):
+        plans.append(cfi.decide(cfi.NAMES["quantize_mmq"].format(layout=lay), "quantize_mmq", "all")[1])
+    for m, a in ((0, 0), (1, 0), (1, 1)):
+        plans.append(cfi.decide(cfi.NAMES["rms_norm"].format(mul=m, add=a), "rms_norm", "all")[1])
+    plans.append(cfi.decide(cfi.NAMES["rms_norm_plain"], "rms_norm_plain", "all")[1])
+    for fwd, ff in ((1, 0), (1, 1), (0, 0)):
+        plans.append(cfi.decide(cfi.NAMES["rope_neox"].format(fwd=fwd, ff=ff), "rope_neox", "all")[1])
+    for t in ("f", "6__half"):
+        plans.append(cfi.decide(cfi.NAMES["soft_max"].format(t=t), "soft_max", "all")[1])
+    for p in plans:
+        rc, why = ctx.probe(p, stream())
+        assert rc == 0, (p.key, why)
+
+
+def test_router_runs_native_kernels_only(dev):
+    ctx, g = dev
+    s = ctx.stats()
+    assert s["native_launches"] > 0 and s["native_failures"] == 0 and s["stock_launches"] == 0
