@@ -232,17 +232,23 @@ def run_gpu(args, rank, world):
     ms_step = ms / args.steps
     value = world * STEP_BYTES / (ms_step * 1e-3) / 1e9
 
-    # ---- dominant kernel: mmvq Q4_K batch 1, CUDA events around each launch ----
-    nrep = max(20, 4 * args.steps)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nrep)]
+    # ---- dominant kernel: mmvq Q4_K batch 1, back to back (one graph of ncopy launches over the
+    # rotated weight copies), CUDA events on the launching stream around the replays ----
+    gk = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gk, stream=stream):
+        for i in range(ncopy):
+            g.mmvq(cfi.Q4_K, 1, wd[i].data_ptr(), qs[1].data_ptr(), y_views[1].data_ptr(), K, ROWS,
+                   stream=torch.cuda.current_stream().cuda_stream)
+    reps = max(3, args.steps // 10)
     with torch.cuda.stream(stream):
-        for i in range(nrep):
-            evs[i][0].record(stream)
-            g.mmvq(cfi.Q4_K, 1, wd[i % ncopy].data_ptr(), qs[1].data_ptr(), y_views[1].data_ptr(), K, ROWS,
-                   stream=stream.cuda_stream)
-            evs[i][1].record(stream)
+        gk.replay()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(reps):
+            gk.replay()
+        k1.record(stream)
     torch.cuda.synchronize()
-    kms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    kms = k0.elapsed_time(k1) / (reps * ncopy)
     peak, peak_kind = peaks()
     achieved = MMVQ_BYTES(1) / (kms * 1e-3) / 1e9
 

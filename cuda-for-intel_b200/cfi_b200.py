@@ -374,6 +374,14 @@ class GgmlCaller:
         vals = [("ptr", vx), ("ptr", vy), ("ptr", 0), ("ptr", 0), ("ptr", dst), ("ptr", tmp_fixup)] + [("u32", v) for v in w]
         return self._go(p, (148, 1, 1), (32, 8, 1), vals, stream, "mul_mat_q")
 
+    def mmq_words(self, ty, vx, vy, dst, words, mmq_x=128, stream=0, tmp_fixup=0):
+        """mul_mat_q<ty> with the 17 integer words given explicitly (ncols_x, nrows_x, ncols_dst,
+        stride_row_x, ncols_y, stride_col_dst, channel_ratio, nchannels_y, stride_channel_x/y/dst,
+        sample_ratio, nsamples_y, stride_sample_x/y/dst, ncols_max; probe.rs:293-321)."""
+        p = self.plan(("mmq", ty, mmq_x), NAMES["mmq"].format(ty=ty, mmq_x=mmq_x, check=0), "mmq")
+        vals = [("ptr", vx), ("ptr", vy), ("ptr", 0), ("ptr", 0), ("ptr", dst), ("ptr", tmp_fixup)] + [("u32", v) for v in words]
+        return self._go(p, (148, 1, 1), (32, 8, 1), vals, stream, "mul_mat_q")
+
     def rms_norm(self, x, dst, ncols, nrows, mul=0, add=0, eps=1e-6, nchannels=1, nsamples=1, stream=0):
         m, a = int(bool(mul)), int(bool(add))
         p = self.plan(("rms", m, a), NAMES["rms_norm"].format(mul=m, add=a), "rms_norm")

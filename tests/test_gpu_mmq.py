@@ -1,0 +1,134 @@
+"""GPU tests of the tcgen05 prefill GEMM (native mul_mat_q) through the substitution C ABI.
+
+The tensor-core path dequantises both operands to fp16, so it is held to the stated 1e-3 relative
+L2 bound against the oracle's mmq reference (refs.rs:771-834), on the reference's own test shapes
+(src/subst/tests.rs:312, 480) and on BASELINE config 3 at full size."""
+import numpy as np
+import pytest
+
+import cfi_b200 as cfi
+import oracle_py as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available()
+    ctx = cfi.Ctx(0)
+    yield ctx, cfi.GgmlCaller(ctx, "all")
+    ctx.close()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def words(p):
+    return [p.ncols_x, p.nrows_x, p.ncols_dst, p.stride_row_x, p.ncols_y, p.stride_col_dst, p.channel_ratio,
+            p.nchannels_y, p.stride_channel_x, p.stride_channel_y, p.stride_channel_dst, p.sample_ratio, p.nsamples_y,
+            p.stride_sample_x, p.stride_sample_y, p.stride_sample_dst, p.ncols_dst]
+
+
+def run(g, ty, p, x, y, n):
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.from_numpy(y).cuda()
+    dd = torch.zeros(n, dtype=torch.float32, device="cuda")
+    g.mmq_words(ty, dx.data_ptr(), dy.data_ptr(), dd.data_ptr(), words(p), stream=stream())
+    torch.cuda.synchronize()
+    assert cfi.lib().cfi_device_error() == 0
+    return dd.cpu().numpy()
+
+
+@pytest.mark.parametrize("ty,shapes", [
+    (cfi.Q8_0, [(256, 70, 40, 2, 1, 1), (384, 65, 9, 4, 2, 2), (128, 3, 1, 1, 1, 1), (512, 300, 300, 1, 1, 1)]),
+    (cfi.Q4_K, [(512, 70, 40, 2, 1, 1), (256, 65, 9, 4, 2, 2), (768, 3, 1, 1, 1, 1), (2048, 129, 17, 1, 1, 1)]),
+])
+def test_mmq_matches_the_oracle(dev, ty, shapes):
+    ctx, g = dev
+    for (ncols_x, nrows, ncols, nch, ratio, nsamples) in shapes:
+        p, x, y, n = O.mmq_case(ty, ncols_x, nrows, ncols, nch, ratio, nsamples, 5 + ncols + ty)
+        got = run(g, ty, p, x, y, n)
+        want = O.mmq_ref(ty, p, x, y, n)
+        assert np.any(want != 0)
+        err = O.rel_l2(got, want)
+        assert err < REL_L2, (ty, ncols_x, nrows, ncols, err)
+
+
+def dequant_q8_0(w, rows, k):
+    b = w.reshape(rows, k // 32, 34)
+    d = b[..., :2].copy().view(np.float16).astype(np.float64)
+    q = b[..., 2:].view(np.int8).astype(np.float64)
+    return (q * d).reshape(rows, k)
+
+
+@pytest.mark.parametrize("m,k", [(4864, 896), (896, 4864)])
+def test_prefill_config3_full_size(dev, m, k):
+    """Q8_0 weights x 631 quantised tokens -> fp32 631 x m."""
+    ctx, g = dev
+    n = 631
+    w = cfi.synthetic_weights(cfi.Q8_0, m, k, seed=m)
+    acts = np.random.default_rng(k).normal(0, 1, size=(n, k)).astype(np.float32)
+    dw = torch.from_numpy(w).cuda()
+    dxf = torch.from_numpy(acts).cuda()
+    dq = torch.zeros(k // 128 * n * 144, dtype=torch.uint8, device="cuda")
+    dd = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+    g.quantize_mmq(0, dxf.data_ptr(), dq.data_ptr(), k, k, n, stream=stream())
+    g.mmq(cfi.Q8_0, dw.data_ptr(), dq.data_ptr(), dd.data_ptr(), k, m, n, stream=stream())
+    torch.cuda.synchronize()
+    yq = O.quantize_mmq(cfi.Q8_0, acts, k, n)
+    assert np.array_equal(dq.cpu().numpy(), yq), "quantize_mmq_q8_1 differs from the oracle"
+    got = dd.cpu().numpy().reshape(n, m)
+    # exact-arithmetic product of the dequantised operands (float64)
+    yb = yq.reshape(k // 128, n, 144)
+    d = yb[..., :16].copy().view(np.float32).astype(np.float64)            # [k/128, n, 4]
+    q = yb[..., 16:].view(np.int8).astype(np.float64).reshape(k // 128, n, 4, 32)
+    xa = (q * d[..., None]).transpose(1, 0, 2, 3).reshape(n, k)
+    want = xa @ dequant_q8_0(w, m, k).T
+    assert O.rel_l2(got, want) < REL_L2
+    # the oracle's sequential-k reference on a slice of columns, including the ragged last tile
+    cols = list(range(0, 8)) + list(range(n - 8, n))
+    p = O.Mmq()
+    p.ncols_x, p.nrows_x, p.ncols_dst, p.nchannels_y, p.nsamples_y = k, m, n, 1, 1
+    p.channel_ratio = p.sample_ratio = 1
+    p.stride_row_x, p.ncols_y, p.stride_col_dst = k // 32, n, m
+    ref = O.mmq_ref(cfi.Q8_0, p, w.ravel(), yq, n * m).reshape(n, m)
+    assert O.rel_l2(got[cols], ref[cols]) < REL_L2
+
+
+def test_mmq_quantize_mmq_layouts_are_byte_exact(dev):
+    ctx, g = dev
+    for ty, ds4 in ((cfi.Q8_0, 0), (cfi.Q4_K, 1)):
+        k, n = 1536, 37
+        acts = np.random.default_rng(3).normal(0, 1, size=(n, k)).astype(np.float32)
+        acts[0, :32] = 0
+        dxf = torch.from_numpy(acts).cuda()
+        dq = torch.zeros(k // 128 * n * 144, dtype=torch.uint8, device="cuda")
+        g.quantize_mmq(ds4, dxf.data_ptr(), dq.data_ptr(), k, k, n, stream=stream())
+        torch.cuda.synchronize()
+        assert np.array_equal(dq.cpu().numpy(), O.quantize_mmq(ty, acts, k, n))
+
+
+def test_mmq_probe_and_fixup_skip(dev):
+    ctx, g = dev
+    for ty in (cfi.Q8_0, cfi.Q4_K):
+        _, p, _ = cfi.decide(cfi.NAMES["mmq"].format(ty=ty, mmq_x=64, check=0), "mmq", "all")
+        rc, why = ctx.probe(p, stream())
+        assert rc == 0, why
+    _, fp, _ = cfi.decide(cfi.NAMES["mmq_fixup"].format(ty=8, mmq_x=128, check=0), "mmq_fixup", "all")
+    p, x, y, n = O.mmq_case(cfi.Q8_0, 256, 70, 40, 1, 1, 1, 9)
+    dx, dy = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    dd = torch.zeros(n, dtype=torch.float32, device="cuda")
+    tmp = torch.zeros(16, dtype=torch.float32, device="cuda")
+    before = ctx.stats()
+    g.mmq_words(cfi.Q8_0, dx.data_ptr(), dy.data_ptr(), dd.data_ptr(), words(p), stream=stream(), tmp_fixup=tmp.data_ptr())
+    fix = cfi.KernelArgs([("ptr", 0), ("ptr", 0), ("ptr", dd.data_ptr()), ("ptr", tmp.data_ptr())] + [("u32", 1)] * 9)
+    assert ctx.launch(fp, (148, 1, 1), (32, 8, 1), fix, stream()) == 0
+    torch.cuda.synchronize()
+    after = ctx.stats()
+    assert after["fixups_skipped"] == before["fixups_skipped"] + 1
+    assert after["native_launches"] == before["native_launches"] + 1 and after["stock_launches"] == before["stock_launches"]
+    assert O.rel_l2(dd.cpu().numpy(), O.mmq_ref(cfi.Q8_0, p, x, y, n)) < REL_L2
