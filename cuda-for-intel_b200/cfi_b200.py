@@ -93,6 +93,7 @@ def lib():
     L.cfi_ctx_stats.restype = None
     L.cfi_ctx_inject.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
     L.cfi_ctx_inject.restype = None
+    L.cfi_mmq_static_scratch.argtypes = [C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p, C.c_char_p, C.c_size_t]
     L.cfi_device_error.restype = C.c_uint
     L.cfi_version.restype = C.c_char_p
     _lib = L

@@ -20,8 +20,12 @@
 // relative L2 of the reference (measured ~1e-4), the bound this path is held to.
 #include <cuda.h>
 
+#include <stdio.h>
+#include <string.h>
+
 #include <map>
 #include <mutex>
+#include <string>
 
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
@@ -456,7 +460,7 @@ uint32_t tile_n(uint32_t ncols_dst) {
 }
 
 template <uint32_t TY>
-int launch_tc(const uint64_t* v, cudaStream_t stream) {
+int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, size_t fixed_cap = 0) {
     // v: the 23 mul_mat_q words (6 pointers, 17 u32), subst_hook.rs arg order (probe.rs:293-321)
     const uint8_t* x = reinterpret_cast<const uint8_t*>(v[0]);
     const uint8_t* y = reinterpret_cast<const uint8_t*>(v[1]);
@@ -476,7 +480,13 @@ int launch_tc(const uint64_t* v, cudaStream_t stream) {
     const uint32_t planes = nch * ns;
     void* xh = nullptr;
     const size_t xh_bytes = (size_t)planes * ncols_dst * Kt * 2;
-    int rc = scratch_for(xh_bytes, stream, &xh);
+    int rc = 0;
+    if (fixed_xh) {
+        if (xh_bytes > fixed_cap) return (int)cudaErrorInvalidValue;
+        xh = fixed_xh;
+    } else {
+        rc = scratch_for(xh_bytes, stream, &xh);
+    }
     if (rc) return rc;
     // 1. activations -> fp16 K-major
     {
@@ -544,6 +554,96 @@ int mmq_launch(const cfi_plan& plan, void** args, void* stream) {
     return (int)cudaErrorNotSupported;
 }
 }  // namespace cfi
+
+// ---------------------------------------------------------------------------------------------
+// cfi_mmq_static_scratch: the same GEMM for callers that may not allocate device memory.  Its fp16
+// activation copy lives in this fixed array (CFI_MMQ_STATIC_SCRATCH_BYTES on every GPU where the
+// library is loaded, held until the process exits) instead of a buffer from cudaMalloc.  Host
+// code must not hand the array's name to a kernel (on the host it is only a stand-in for the
+// device symbol): its device address is looked up once per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_mmq_static_scratch[CFI_MMQ_STATIC_SCRATCH_BYTES];
+
+namespace {
+constexpr int MAX_DEVICES = 64;
+std::mutex g_static_mu;
+void* g_static_addr[MAX_DEVICES];
+
+// Device address of the static scratch on the current device (set up on first use).
+int static_scratch_addr(void** out, std::string* why) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *why = std::string("no current CUDA device: ") + cudaGetErrorString(e);
+        return (int)e;
+    }
+    if (dev < 0 || dev >= MAX_DEVICES) {
+        *why = "device index out of range";
+        return (int)cudaErrorInvalidDevice;
+    }
+    std::lock_guard<std::mutex> g(g_static_mu);
+    if (!g_static_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_mmq_static_scratch);
+        if (e != cudaSuccess || !p) {
+            *why = std::string("cudaGetSymbolAddress of the static scratch failed: ") + cudaGetErrorString(e);
+            return (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+        }
+        g_static_addr[dev] = p;
+    }
+    *out = g_static_addr[dev];
+    return 0;
+}
+}  // namespace
+
+extern "C" int cfi_mmq_static_scratch(uint32_t ggml_type, void** kernel_params, void* stream, char* why, size_t why_len) {
+    std::string w;
+    auto fail = [&](int code) {
+        if (why && why_len) snprintf(why, why_len, "%s", w.c_str());
+        return code;
+    };
+    if (!kernel_params) {
+        w = "kernel_params is NULL";
+        return fail((int)cudaErrorInvalidValue);
+    }
+    if (ggml_type != T_Q8_0 && ggml_type != T_Q4_K) {
+        w = "only Q8_0 (8) and Q4_K (12) weights are supported";
+        return fail((int)cudaErrorNotSupported);
+    }
+    uint64_t v[23];
+    for (int i = 0; i < 23; i++) {
+        if (!kernel_params[i]) {
+            w = "kernel_params entry " + std::to_string(i) + " is NULL";
+            return fail((int)cudaErrorInvalidValue);
+        }
+        v[i] = 0;
+        memcpy(&v[i], kernel_params[i], i < 6 ? 8 : 4);
+    }
+    if (v[2] != 0 || v[3] != 0) {
+        w = "expert routing (ids_dst / expert_bounds) is not supported";
+        return fail((int)cudaErrorNotSupported);
+    }
+    const uint64_t K = (uint32_t)v[6], ncols_dst = (uint32_t)v[8], planes = (uint64_t)(uint32_t)v[13] * (uint32_t)v[18];
+    if (K == 0 || K % 128 || ncols_dst == 0 || planes == 0) {
+        w = "ncols_x must be a non-zero multiple of 128 and ncols_dst, nchannels_y, nsamples_y non-zero";
+        return fail((int)cudaErrorInvalidValue);
+    }
+    const uint64_t Kt = K + (ggml_type == T_Q4_K ? (K / 32 + BK - 1) / BK * BK : 0);
+    const uint64_t need = planes * ncols_dst * Kt * 2;
+    if (need > CFI_MMQ_STATIC_SCRATCH_BYTES) {
+        w = "this GEMM needs " + std::to_string(need) + " bytes of scratch (ncols_dst x ncols_x x 2 per channel); the "
+            "static scratch holds " + std::to_string((unsigned long long)CFI_MMQ_STATIC_SCRATCH_BYTES);
+        return fail((int)cudaErrorInvalidValue);
+    }
+    void* scratch = nullptr;
+    int rc = static_scratch_addr(&scratch, &w);
+    if (rc) return fail(rc);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rc = ggml_type == T_Q8_0 ? launch_tc<T_Q8_0>(v, s, scratch, CFI_MMQ_STATIC_SCRATCH_BYTES)
+                             : launch_tc<T_Q4_K>(v, s, scratch, CFI_MMQ_STATIC_SCRATCH_BYTES);
+    if (rc) w = std::string("launch failed: ") + cudaGetErrorString((cudaError_t)rc);
+    return rc ? fail(rc) : 0;
+}
 
 extern "C" unsigned int cfi_device_error(void) {
     unsigned int v = 0, z = 0;

@@ -141,6 +141,32 @@ CFI_API void cfi_ctx_stats(cfi_ctx *ctx, cfi_stats *out);
 enum { CFI_SITE_NATIVE_LAUNCH = 1, CFI_SITE_PROBE = 2, CFI_SITE_STOCK_LAUNCH = 3, CFI_SITE_BUILD = 4 };
 CFI_API void cfi_ctx_inject(cfi_ctx *ctx, int site, int nth, int code);
 
+/* ---- prefill GEMM without device allocation ----
+ * No counterpart in the reference: cuda-for-intel has no equivalent entry point.
+ *
+ * cfi_mmq_static_scratch runs the native tensor-core mul_mat_q (Q8_0 or Q4_K weights, non-MoE)
+ * exactly as cfi_subst_launch does, for callers that are not allowed to allocate device memory:
+ * a launch hook sitting inside the host application's cuLaunchKernel (allocating there would
+ * re-enter the driver's allocator and change the application's own memory accounting), a
+ * serving process whose memory pool reserved all free HBM up front (cudaMalloc would fail at run
+ * time), or a code path that cannot afford cudaMalloc's implicit device synchronisation.  The
+ * GEMM's one piece of scratch -- an fp16 copy of the activations, ncols_dst x ncols_x x 2 bytes per
+ * channel and sample -- then lives in a fixed array of CFI_MMQ_STATIC_SCRATCH_BYTES compiled into
+ * the library; every GPU on which the library's kernels are loaded holds that array until the
+ * process exits.  Larger problems are rejected with cudaErrorInvalidValue and a message in `why`
+ * before anything is launched.
+ *
+ * kernel_params are the 23 parameters of ggml-cuda's mul_mat_q<type, mmq_x, need_check> (x, y,
+ * ids_dst, expert_bounds, dst, tmp_fixup, then 17 ints); inputs and outputs stay the caller's.
+ * The array's device address is looked up (cudaGetSymbolAddress) on the first call on each
+ * device, which must be the current device; make that first call before any stream capture.
+ * Every call uses the same array and leaves its contents behind (nothing in it has to start at
+ * zero), so two calls whose work overlaps on the GPU -- on different streams without ordering
+ * between them -- race on it.  The entry point itself calls no cudaMalloc, cudaFree or other
+ * allocating routine.  Returns 0 or a CUDA error code. */
+#define CFI_MMQ_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
+CFI_API int cfi_mmq_static_scratch(uint32_t ggml_type, void **kernel_params, void *stream, char *why, size_t why_len);
+
 /* Reads and clears the device error word of the bounded waits in the tcgen05 kernels. */
 CFI_API unsigned int cfi_device_error(void);
 
