@@ -15,6 +15,10 @@ const void* cfi_native_quantize_mmq(int ds4);
 // unsupported (ty, ncols).  Dynamic shared memory for a launch: cfi_mmvq_smem_bytes.
 const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols);
 size_t cfi_mmvq_smem_bytes(uint32_t ty, uint32_t ncols, uint32_t ncols_x);
+// Rows a warp computes at once (all loads of an iteration for those rows are issued together).
+inline uint32_t cfi_mmvq_rows_per_warp(uint32_t ty, uint32_t ncols) {
+    return ty == 12 ? (ncols == 1 ? 2 : 1) : (ncols <= 2 ? 2 : 1);
+}
 int cfi_mmvq_max_smem_bytes();
 constexpr int CFI_MMVQ_THREADS = 256;
 constexpr int CFI_MMVQ_WARPS = CFI_MMVQ_THREADS / 32;

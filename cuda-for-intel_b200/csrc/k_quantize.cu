@@ -13,6 +13,7 @@
 // left fold of the 32 floats, as the reference does.
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
+#include "sm100_ptx.cuh"
 
 // The 32-lane butterfly (offsets 16,8,4,2,1) of the reference, evaluated when thread t of an
 // 8-thread group holds values 4t..4t+3: offsets 16/8/4 pair threads (xor 4/2/1), offsets 2/1 pair
@@ -41,6 +42,9 @@ CFI_DEV float amax8_from4(float4 v, unsigned mask) {
 extern "C" __global__ void __launch_bounds__(256)
     cfi_quantize_q8_1(const float* __restrict__ x, void* __restrict__ vy, int64_t ne00, int64_t s01, int64_t s02,
                       int64_t s03, int64_t ne0, uint32_t ne1, uint3 ne2) {
+    // programmatic dependent launch: wait for the producer of x, then let the next kernel start
+    sm100::pdl_wait();
+    sm100::pdl_launch_dependents();
     const int64_t i0 = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
     // whole 8-thread groups (32 values) leave together (ne0 is a multiple of 32); the shuffles
     // below stay inside a group, over the lanes that remain

@@ -42,14 +42,27 @@ CFI_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is incomplete (the
+// hardware wakes it when the phase completes), so a waiting warp issues few instructions.
+CFI_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 // Waits for the phase of `parity` to complete; false when `abort` is raised or the wait runs past
 // WAIT_LIMIT_NS (the caller then records an error and skips its remaining work).
 CFI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; i++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0) {
+        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+        if ((i & 15) == 0) {
             if (*abort) return false;
             if (globaltimer() - t0 > WAIT_LIMIT_NS) return false;
         }
@@ -134,4 +147,18 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t m, uint32_t n, uint32_
     return (1u << 4) | (fmt_ab << 7) | (fmt_ab << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+}  // namespace sm100
+
+namespace sm100 {
+// ---- 1-D bulk copy global -> shared (TMA, no multicast): 16-byte aligned, size % 16 == 0 ----
+CFI_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---- programmatic dependent launch ----
+CFI_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+CFI_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 }  // namespace sm100

@@ -553,6 +553,19 @@ std::vector<uint64_t> arg_values(const cfi_plan& plan, void** args) {
 
 static bool block_is(const uint32_t b[3], uint32_t x, uint32_t y, uint32_t z) { return b[0] == x && b[1] == y && b[2] == z; }
 
+// Numeric tuning knob from the environment, clamped to [lo, hi].
+static uint32_t env_u32(const char* name, uint32_t dflt, uint32_t lo, uint32_t hi) {
+    const char* v = getenv(name);
+    if (!v || !*v) return dflt;
+    char* end = nullptr;
+    unsigned long x = strtoul(v, &end, 10);
+    if (!end || *end) return dflt;
+    return (uint32_t)std::min<unsigned long>(hi, std::max<unsigned long>(lo, x));
+}
+
+// Programmatic dependent launch for the decode kernels (CFI_PDL=0 turns it off).
+static bool pdl_enabled() { return env_u32("CFI_PDL", 1, 0, 1) != 0; }
+
 int mmq_tile_n(uint32_t ncols_dst);  // k_mmq_sm100.cu
 int mmq_threads();
 bool mmq_type_ok(uint32_t ty);
@@ -571,23 +584,27 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         if (plan.ty == 8 && (vals[0] & 1)) return false;
         if ((vals[1] & 3)) return false;                       // q8_1 blocks are read as words
         const uint32_t nrows = plan.ncols == 1 ? grid[0] : std::min(2 * grid[0], stride_col_dst);
+        const uint32_t planes = std::max(1u, grid[1] * grid[2]);
         nl.smem = cfi_mmvq_smem_bytes(plan.ty, plan.ncols, ncols_x);
         if (nl.smem > (size_t)cfi_mmvq_max_smem_bytes()) return false;
         nl.fn = cfi_native_mmvq(plan.ty, plan.ncols);
-        const uint32_t planes = std::max(1u, grid[1] * grid[2]);
-        const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * 4) / planes);
-        const uint32_t tiles = (nrows + CFI_MMVQ_WARPS - 1) / CFI_MMVQ_WARPS;
+        const uint32_t per_sm = env_u32("CFI_MMVQ_CTAS", 4, 1, 8);
+        const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
+        const uint32_t rows_per_pass = CFI_MMVQ_WARPS * cfi_mmvq_rows_per_warp(plan.ty, plan.ncols);
+        const uint32_t tiles = (nrows + rows_per_pass - 1) / rows_per_pass;
         nl.grid[0] = std::max(1u, std::min(tiles, cap));
-        nl.grid[1] = grid[1];
-        nl.grid[2] = grid[2];
         nl.block[0] = CFI_MMVQ_THREADS;
         nl.extra.push_back(nrows);
+        nl.pdl = pdl_enabled();
+        nl.grid[1] = grid[1];
+        nl.grid[2] = grid[2];
         break;
     }
     case CFI_K_QUANTIZE_Q8_1:
         if (!block_is(block, 256, 1, 1)) return false;
         if (nvals >= 7 && (vals[6] % 32)) return false;
         nl.fn = cfi_native_quantize_q8_1();
+        nl.pdl = pdl_enabled();
         nl.grid[0] = (grid[0] + 3) / 4;
         nl.grid[1] = grid[1];
         nl.grid[2] = grid[2];
@@ -784,8 +801,23 @@ int issue_native(const NativeLaunch& nl, const cfi_plan& plan, void** args, void
     for (auto& w : extra) argv.push_back(&w);
     int e = ensure_smem(nl.fn, nl.smem);
     if (e) return e;
-    cudaError_t rc = cudaLaunchKernel(nl.fn, dim3(nl.grid[0], nl.grid[1], nl.grid[2]), dim3(nl.block[0], nl.block[1], nl.block[2]),
-                                      argv.data(), nl.smem, static_cast<cudaStream_t>(stream));
+    cudaError_t rc;
+    if (nl.pdl) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(nl.grid[0], nl.grid[1], nl.grid[2]);
+        cfg.blockDim = dim3(nl.block[0], nl.block[1], nl.block[2]);
+        cfg.dynamicSmemBytes = nl.smem;
+        cfg.stream = static_cast<cudaStream_t>(stream);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        rc = cudaLaunchKernelExC(&cfg, nl.fn, argv.data());
+    } else {
+        rc = cudaLaunchKernel(nl.fn, dim3(nl.grid[0], nl.grid[1], nl.grid[2]), dim3(nl.block[0], nl.block[1], nl.block[2]),
+                              argv.data(), nl.smem, static_cast<cudaStream_t>(stream));
+    }
     return (int)rc;
 }
 

@@ -70,6 +70,7 @@ struct NativeLaunch {
     std::vector<uint32_t> extra;  // trailing u32 words after the stock parameters
     int nparams = 0;              // stock parameters forwarded
     bool own_launch = false;      // tcgen05 GEMM: launched by its own code (see gemm_launch)
+    bool pdl = false;             // launch with programmatic stream serialization
 };
 bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t block[3], const uint64_t* vals, int nvals,
                 void** args, NativeLaunch* out);
