@@ -94,6 +94,19 @@ def lib():
     L.cfi_ctx_inject.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
     L.cfi_ctx_inject.restype = None
     L.cfi_mmq_static_scratch.argtypes = [C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p, C.c_char_p, C.c_size_t]
+    vp, i, ll = C.c_void_p, C.c_int, C.c_longlong
+    L.cfi_blas_create.argtypes = [C.POINTER(vp)]
+    L.cfi_blas_destroy.argtypes = [vp]
+    L.cfi_blas_set_stream.argtypes = [vp, vp]
+    L.cfi_blas_get_stream.argtypes = [vp, C.POINTER(vp)]
+    L.cfi_blas_set_pointer_mode.argtypes = [vp, i]
+    L.cfi_blas_last_path.argtypes = [vp]
+    L.cfi_blas_validate.argtypes = [i] * 12
+    L.cfi_blas_gemm_ex.argtypes = [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i]
+    L.cfi_blas_gemm_strided_batched_ex.argtypes = [vp, i, i, i, i, i, vp, vp, i, i, ll, vp, i, i, ll, vp, vp, i, i, ll, i,
+                                                   i, i]
+    L.cfi_blas_gemm_batched_ex.argtypes = [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i, i]
+    L.cfi_blas_sgemm.argtypes = [vp, i, i, i, i, i, vp, vp, i, vp, i, vp, vp, i]
     L.cfi_device_error.restype = C.c_uint
     L.cfi_version.restype = C.c_char_p
     _lib = L
@@ -290,6 +303,64 @@ class Ctx:
 
     def inject(self, site, nth, code):
         lib().cfi_ctx_inject(self.h, site, nth, code)
+
+
+class Blas:
+    """A cfi_blas handle (the cuBLAS-compatible GEMM entry points of include/cfi_cublas.h)."""
+
+    OP_N, OP_T = 0, 1
+    R_32F, R_16F, R_16BF = 0, 2, 14
+    COMPUTE_16F, COMPUTE_32F = 64, 68
+
+    def __init__(self, stream=0):
+        h = C.c_void_p()
+        st = lib().cfi_blas_create(C.byref(h))
+        if st:
+            raise RuntimeError("cfi_blas_create: %d" % st)
+        self.h = h
+        lib().cfi_blas_set_stream(self.h, C.c_void_p(stream))
+
+    def close(self):
+        if self.h:
+            lib().cfi_blas_destroy(self.h)
+            self.h = None
+
+    def set_stream(self, stream):
+        return lib().cfi_blas_set_stream(self.h, C.c_void_p(stream))
+
+    def set_pointer_mode(self, mode):
+        return lib().cfi_blas_set_pointer_mode(self.h, mode)
+
+    def last_path(self):
+        return lib().cfi_blas_last_path(self.h)
+
+    @staticmethod
+    def _scalar(v, f16):
+        return C.byref(C.c_uint16(int(np.float16(v).view(np.uint16))) if f16 else C.c_float(v))
+
+    def gemm_ex(self, ta, tb, m, n, k, alpha, A, at, lda, B, bt, ldb, beta, Cp, ct, ldc, compute=68, dev_scalars=None):
+        f16 = compute == self.COMPUTE_16F
+        al, be = (dev_scalars if dev_scalars else (self._scalar(alpha, f16), self._scalar(beta, f16)))
+        return lib().cfi_blas_gemm_ex(self.h, ta, tb, m, n, k, al, C.c_void_p(A), at, lda, C.c_void_p(B), bt, ldb, be,
+                                      C.c_void_p(Cp), ct, ldc, compute, -1)
+
+    def gemm_strided_batched_ex(self, ta, tb, m, n, k, alpha, A, at, lda, sa, B, bt, ldb, sb, beta, Cp, ct, ldc, sc,
+                                batch, compute=68):
+        f16 = compute == self.COMPUTE_16F
+        return lib().cfi_blas_gemm_strided_batched_ex(self.h, ta, tb, m, n, k, self._scalar(alpha, f16), C.c_void_p(A),
+                                                      at, lda, sa, C.c_void_p(B), bt, ldb, sb, self._scalar(beta, f16),
+                                                      C.c_void_p(Cp), ct, ldc, sc, batch, compute, -1)
+
+    def gemm_batched_ex(self, ta, tb, m, n, k, alpha, Aarr, at, lda, Barr, bt, ldb, beta, Carr, ct, ldc, batch,
+                        compute=68):
+        f16 = compute == self.COMPUTE_16F
+        return lib().cfi_blas_gemm_batched_ex(self.h, ta, tb, m, n, k, self._scalar(alpha, f16), C.c_void_p(Aarr), at,
+                                              lda, C.c_void_p(Barr), bt, ldb, self._scalar(beta, f16), C.c_void_p(Carr),
+                                              ct, ldc, batch, compute, -1)
+
+    def sgemm(self, ta, tb, m, n, k, alpha, A, lda, B, ldb, beta, Cp, ldc):
+        return lib().cfi_blas_sgemm(self.h, ta, tb, m, n, k, C.byref(C.c_float(alpha)), C.c_void_p(A), lda,
+                                    C.c_void_p(B), ldb, C.byref(C.c_float(beta)), C.c_void_p(Cp), ldc)
 
 
 def check(rc, what):

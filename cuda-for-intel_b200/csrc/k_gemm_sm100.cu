@@ -1,0 +1,522 @@
+// k_gemm_sm100.cu -- cuBLAS-compatible GEMM of libcfi_b200.so (the dense path ggml reaches through
+// cublasGemmEx, served by cuda-for-intel's cuBLAS shim, crates/cublas_shim/src/lib.rs:627-1076).
+//
+// C = alpha * op(A) * op(B) + beta * C, column-major.  The layout ggml uses -- op(A) = A^T (A stored
+// k x m, lda >= k) and op(B) = B (B stored k x n, ldb >= k), f16 or bf16 -- has both operands
+// K-major and runs on the tensor cores:
+//   * one thread of warp 5 streams 128 x 64 tiles of A and BN x 64 tiles of B with TMA
+//     (128-byte swizzle: the UMMA canonical K-major layout; rows/columns/K past the matrix read as
+//     zero), strided batches as the third tensor dimension;
+//   * one thread of warp 4 issues tcgen05.mma kind::f16 (M 128, N BN <= 256, K 16) into an fp32
+//     accumulator in tensor memory;
+//   * warps 0-3 apply alpha/beta and store C in its dtype (f32, f16 or bf16), coalesced by column.
+// Every other legal call (other transposes, f32 inputs, device pointer arrays) runs a tiled SIMT
+// kernel with fp32 accumulation.  Validation follows cuBLAS (plan.rs:160-215).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/cfi_cublas.h"
+#include "cfi_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BK = 64, NSTAGE = 4, THREADS = 192;
+constexpr int A_STAGE = BM * BK * 2, B_STAGE = 256 * BK * 2;
+constexpr size_t SMEM_BYTES = 1024 + (size_t)NSTAGE * (A_STAGE + B_STAGE) + 256;
+
+static __device__ unsigned int g_gemm_error;
+
+struct GemmArgs {
+    void* c;
+    long long stride_c;
+    int c_type, ldc;
+    uint32_t m, n, k, bn;
+    float alpha, beta;
+    const void* alpha_ptr;  // device pointer mode
+    const void* beta_ptr;
+    int scalar_f16;
+    unsigned int* err;
+};
+
+CFI_DEV float load_scalar(const void* p, int f16) {
+    return f16 ? __half2float(*static_cast<const __half*>(p)) : *static_cast<const float*>(p);
+}
+
+CFI_DEV float ld_elem(const void* p, size_t i, int t) {
+    if (t == CFI_R_32F) return static_cast<const float*>(p)[i];
+    if (t == CFI_R_16F) return __half2float(static_cast<const __half*>(p)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+CFI_DEV void st_elem(void* p, size_t i, int t, float v) {
+    if (t == CFI_R_32F)
+        static_cast<float*>(p)[i] = v;
+    else if (t == CFI_R_16F)
+        static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else
+        static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(THREADS, 1)
+    cfi_gemm_tc(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + NSTAGE * A_STAGE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + NSTAGE * B_STAGE);
+    uint64_t* empty = full + NSTAGE;
+    uint64_t* done = empty + NSTAGE;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* epi_ok = abort_flag + 1;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t bn = a.bn;
+    const uint32_t tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+    const int ksteps = (int)((a.k + BK - 1) / BK);
+    const uint32_t m0 = blockIdx.x * BM, n0 = blockIdx.y * bn, z = blockIdx.z;
+
+    if (tid == 0) {
+        for (int i = 0; i < NSTAGE; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 4) {
+        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 5) {
+        if (lane == 0) {
+            prefetch_tmap(&tma);
+            prefetch_tmap(&tmb);
+            const uint32_t bytes = (BM + bn) * BK * 2;
+            for (int s = 0; s < ksteps; s++) {
+                const int slot = s % NSTAGE;
+                if (!mbar_wait(&empty[slot], ((uint32_t)(s / NSTAGE) & 1) ^ 1, abort_flag)) {
+                    cfi_set_error(a.err, 0x500 + slot);
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                tma_load_3d(sA + slot * A_STAGE, &tma, s * BK, (int)m0, (int)z, &full[slot]);
+                tma_load_3d(sB + slot * B_STAGE, &tmb, s * BK, (int)n0, (int)z, &full[slot]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 4) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BM, bn, FMT);
+            for (int s = 0; s < ksteps; s++) {
+                const int slot = s % NSTAGE;
+                if (!mbar_wait(&full[slot], (uint32_t)(s / NSTAGE) & 1, abort_flag)) {
+                    cfi_set_error(a.err, 0x600 + slot);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ab = smem_u32(sA + slot * A_STAGE), bb = smem_u32(sB + slot * B_STAGE);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++)
+                    mma_f16(tmem, sw128_kmajor_desc(ab + 32 * kk), sw128_kmajor_desc(bb + 32 * kk), idesc,
+                            (s > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&empty[slot]);
+            }
+            mma_commit(done);
+        }
+        __syncwarp();
+    } else {
+        // ================= epilogue (warps 0-3: TMEM lanes = rows of the tile) =================
+        if (tid == 0) {
+            bool got = false;
+            if (!*abort_flag) {
+                got = mbar_wait(done, 0, abort_flag);
+                if (!got) {
+                    cfi_set_error(a.err, 0x700);
+                    *abort_flag = 1;
+                }
+            }
+            *epi_ok = got ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        tc_fence_after();
+        if (*epi_ok) {
+            const float alpha = a.alpha_ptr ? load_scalar(a.alpha_ptr, a.scalar_f16) : a.alpha;
+            const float beta = a.beta_ptr ? load_scalar(a.beta_ptr, a.scalar_f16) : a.beta;
+            const uint32_t row = m0 + 32 * warp + lane;
+            uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)z * (size_t)a.stride_c * (a.c_type == CFI_R_32F ? 4 : 2);
+            for (uint32_t cb = 0; cb < bn; cb += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + cb, v);
+                tmem_ld_wait();
+                if (row < a.m) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const uint32_t col = n0 + cb + i;
+                        if (col < a.n && cb + i < bn) {
+                            const size_t ci = (size_t)col * a.ldc + row;
+                            float r = alpha * __uint_as_float(v[i]);
+                            if (beta != 0.0f) r += beta * ld_elem(cz, ci, a.c_type);
+                            st_elem(cz, ci, a.c_type, r);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
+// Tiled SIMT GEMM: 16 x 16 output tile per block, any op/dtype combination, fp32 accumulation.
+// `ptrs` non-zero: A, B, C are device arrays of per-batch pointers (cublasGemmBatchedEx).
+struct SimtArgs {
+    const void* a;
+    const void* b;
+    void* c;
+    long long sa, sb, sc;
+    int lda, ldb, ldc, ta, tb, at, bt, ct;
+    uint32_t m, n, k;
+    float alpha, beta;
+    const void* alpha_ptr;
+    const void* beta_ptr;
+    int scalar_f16, ptrs;
+};
+
+__global__ void __launch_bounds__(256) cfi_gemm_simt(const SimtArgs p) {
+    __shared__ float As[16][17], Bs[16][17];
+    const uint32_t tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const uint32_t i = blockIdx.x * 16 + tx, j = blockIdx.y * 16 + ty, z = blockIdx.z;
+    const void* A;
+    const void* B;
+    void* Cp;
+    if (p.ptrs) {
+        A = static_cast<const void* const*>(p.a)[z];
+        B = static_cast<const void* const*>(p.b)[z];
+        Cp = static_cast<void* const*>(p.c)[z];
+    } else {
+        const size_t ea = p.at == CFI_R_32F ? 4 : 2, ec = p.ct == CFI_R_32F ? 4 : 2;
+        A = static_cast<const uint8_t*>(p.a) + (size_t)z * p.sa * ea;
+        B = static_cast<const uint8_t*>(p.b) + (size_t)z * p.sb * ea;
+        Cp = static_cast<uint8_t*>(p.c) + (size_t)z * p.sc * ec;
+    }
+    float acc = 0.0f;
+    for (uint32_t l0 = 0; l0 < p.k; l0 += 16) {
+        // As[tx][ty] = op(A)(blockrow + tx, l0 + ty); Bs[ty][tx] = op(B)(l0 + ty, blockcol + tx)
+        {
+            const uint32_t r = blockIdx.x * 16 + tx, l = l0 + ty;
+            float v = 0.0f;
+            if (r < p.m && l < p.k) v = ld_elem(A, p.ta ? (size_t)l + (size_t)r * p.lda : (size_t)r + (size_t)l * p.lda, p.at);
+            As[tx][ty] = v;
+        }
+        {
+            const uint32_t l = l0 + ty, cidx = blockIdx.y * 16 + tx;
+            float v = 0.0f;
+            if (cidx < p.n && l < p.k) v = ld_elem(B, p.tb ? (size_t)cidx + (size_t)l * p.ldb : (size_t)l + (size_t)cidx * p.ldb, p.bt);
+            Bs[ty][tx] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int l = 0; l < 16; l++) acc = fmaf(As[tx][l], Bs[l][ty], acc);
+        __syncthreads();
+    }
+    if (i < p.m && j < p.n) {
+        const float alpha = p.alpha_ptr ? load_scalar(p.alpha_ptr, p.scalar_f16) : p.alpha;
+        const float beta = p.beta_ptr ? load_scalar(p.beta_ptr, p.scalar_f16) : p.beta;
+        const size_t ci = (size_t)j * p.ldc + i;
+        float r = alpha * acc;
+        if (beta != 0.0f) r += beta * ld_elem(Cp, ci, p.ct);
+        st_elem(Cp, ci, p.ct, r);
+    }
+}
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled encode_fn() {
+    static PFN_encodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+unsigned int* err_ptr() {
+    static unsigned int* p = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_gemm_error) != cudaSuccess) {
+            cudaGetLastError();
+            p = nullptr;
+        }
+    });
+    return p;
+}
+
+int scalar_kind(int compute_type) {  // 0 f16, 1 f32, -1 unsupported (plan.rs:84-95)
+    switch (compute_type) {
+    case 64: case 65: case CFI_R_16F: return 0;
+    case 68: case 69: case 74: case 75: case 77: case CFI_R_32F: return 1;
+    default: return -1;
+    }
+}
+
+bool dtype_ok(int t) { return t == CFI_R_32F || t == CFI_R_16F || t == CFI_R_16BF; }
+
+}  // namespace
+
+// Reads and clears the error word of the GEMM kernel's bounded waits (folded into cfi_device_error).
+unsigned int cfi_gemm_error_take() {
+    unsigned int v = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof v) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaMemcpyToSymbol(g_gemm_error, &z, sizeof z);
+    return v;
+}
+
+struct cfi_blas {
+    cudaStream_t stream = nullptr;
+    int pointer_mode = CFI_POINTER_MODE_HOST;
+    int last_path = 0;
+};
+
+extern "C" {
+
+int cfi_blas_validate(int transa, int transb, int m, int n, int k, int lda, int ldb, int ldc, int a_type, int b_type,
+                      int c_type, int compute_type) {
+    if (transa < 0 || transa > 2 || transb < 0 || transb > 2) return CFI_BLAS_INVALID_VALUE;
+    if (m < 0 || n < 0 || k < 0) return CFI_BLAS_INVALID_VALUE;
+    const int rows_a = transa ? k : m, rows_b = transb ? n : k;
+    if (lda < (rows_a > 1 ? rows_a : 1) || ldb < (rows_b > 1 ? rows_b : 1) || ldc < (m > 1 ? m : 1))
+        return CFI_BLAS_INVALID_VALUE;
+    if (!dtype_ok(a_type) || !dtype_ok(b_type) || !dtype_ok(c_type)) return CFI_BLAS_NOT_SUPPORTED;
+    const int sk = scalar_kind(compute_type);
+    if (sk < 0) return CFI_BLAS_NOT_SUPPORTED;
+    if (a_type != b_type) return CFI_BLAS_NOT_SUPPORTED;
+    const bool ok = (a_type == CFI_R_32F && c_type == CFI_R_32F) ||
+                    (a_type == CFI_R_16F && (c_type == CFI_R_16F || c_type == CFI_R_32F)) ||
+                    (a_type == CFI_R_16BF && (c_type == CFI_R_16BF || c_type == CFI_R_32F));
+    if (!ok) return CFI_BLAS_NOT_SUPPORTED;
+    if (sk == 0 && (a_type != CFI_R_16F || c_type != CFI_R_16F)) return CFI_BLAS_NOT_SUPPORTED;
+    return CFI_BLAS_SUCCESS;
+}
+
+int cfi_blas_create(cfi_blas** handle) {
+    if (!handle) return CFI_BLAS_INVALID_VALUE;
+    *handle = new (std::nothrow) cfi_blas();
+    return *handle ? CFI_BLAS_SUCCESS : CFI_BLAS_ALLOC_FAILED;
+}
+int cfi_blas_destroy(cfi_blas* h) {
+    if (!h) return CFI_BLAS_NOT_INITIALIZED;
+    delete h;
+    return CFI_BLAS_SUCCESS;
+}
+int cfi_blas_set_stream(cfi_blas* h, void* stream) {
+    if (!h) return CFI_BLAS_NOT_INITIALIZED;
+    h->stream = static_cast<cudaStream_t>(stream);
+    return CFI_BLAS_SUCCESS;
+}
+int cfi_blas_get_stream(cfi_blas* h, void** stream) {
+    if (!h) return CFI_BLAS_NOT_INITIALIZED;
+    if (!stream) return CFI_BLAS_INVALID_VALUE;
+    *stream = h->stream;
+    return CFI_BLAS_SUCCESS;
+}
+int cfi_blas_set_pointer_mode(cfi_blas* h, int mode) {
+    if (!h) return CFI_BLAS_NOT_INITIALIZED;
+    if (mode != CFI_POINTER_MODE_HOST && mode != CFI_POINTER_MODE_DEVICE) return CFI_BLAS_INVALID_VALUE;
+    h->pointer_mode = mode;
+    return CFI_BLAS_SUCCESS;
+}
+int cfi_blas_last_path(cfi_blas* h) { return h ? h->last_path : 0; }
+
+}  // extern "C"
+
+namespace {
+
+int gemm_common(cfi_blas* h, int transa, int transb, int m, int n, int k, const void* alpha, const void* A, int a_type,
+                int lda, long long sa, const void* B, int b_type, int ldb, long long sb, const void* beta, void* C,
+                int c_type, int ldc, long long sc, int batch, int compute_type, bool ptr_arrays) {
+    if (!h) return CFI_BLAS_NOT_INITIALIZED;
+    int st = cfi_blas_validate(transa, transb, m, n, k, lda, ldb, ldc, a_type, b_type, c_type, compute_type);
+    if (st) return st;
+    if (batch < 0) return CFI_BLAS_INVALID_VALUE;
+    if (!alpha || !beta) return CFI_BLAS_INVALID_VALUE;
+    h->last_path = 0;
+    if (m == 0 || n == 0 || batch == 0) return CFI_BLAS_SUCCESS;
+    const int sf16 = scalar_kind(compute_type) == 0;
+    const bool dev_ptrs = h->pointer_mode == CFI_POINTER_MODE_DEVICE;
+    float al = 0.0f, be = 0.0f;
+    if (!dev_ptrs) {
+        al = sf16 ? __half2float(*static_cast<const __half*>(alpha)) : *static_cast<const float*>(alpha);
+        be = sf16 ? __half2float(*static_cast<const __half*>(beta)) : *static_cast<const float*>(beta);
+    }
+    const char* tc_env = getenv("CFI_GEMM_TC");
+    const bool tc_allowed = !(tc_env && strcmp(tc_env, "0") == 0);
+    const bool fmt16 = a_type == CFI_R_16F || a_type == CFI_R_16BF;
+    const bool tc = tc_allowed && !ptr_arrays && fmt16 && transa == CFI_OP_T && transb == CFI_OP_N && k > 0 &&
+                    compute_type != CFI_COMPUTE_32F_FAST_TF32 && lda % 8 == 0 && ldb % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(A) & 15) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
+                    (batch == 1 || ((sa % 8) == 0 && (sb % 8) == 0 && sa > 0 && sb > 0));
+    if (tc) {
+        PFN_encodeTiled enc = encode_fn();
+        if (enc) {
+            const uint32_t bn = n >= 256 ? 256 : ((uint32_t)n + 15) / 16 * 16;
+            const CUtensorMapDataType dt = a_type == CFI_R_16F ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+            CUtensorMap ta, tb;
+            cuuint64_t da[3] = {(cuuint64_t)k, (cuuint64_t)m, (cuuint64_t)batch};
+            cuuint64_t sA[2] = {(cuuint64_t)lda * 2, (cuuint64_t)(batch > 1 ? sa : (long long)lda * m) * 2};
+            cuuint64_t db[3] = {(cuuint64_t)k, (cuuint64_t)n, (cuuint64_t)batch};
+            cuuint64_t sB[2] = {(cuuint64_t)ldb * 2, (cuuint64_t)(batch > 1 ? sb : (long long)ldb * n) * 2};
+            sA[1] = (sA[1] + 15) & ~(cuuint64_t)15;
+            sB[1] = (sB[1] + 15) & ~(cuuint64_t)15;
+            cuuint32_t boxa[3] = {BK, BM, 1}, boxb[3] = {BK, bn, 1}, es[3] = {1, 1, 1};
+            CUresult r1 = enc(&ta, dt, 3, const_cast<void*>(A), da, sA, boxa, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            CUresult r2 = enc(&tb, dt, 3, const_cast<void*>(B), db, sB, boxb, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS) {
+                GemmArgs g;
+                g.c = C;
+                g.stride_c = batch > 1 ? sc : 0;
+                g.c_type = c_type;
+                g.ldc = ldc;
+                g.m = (uint32_t)m;
+                g.n = (uint32_t)n;
+                g.k = (uint32_t)k;
+                g.bn = bn;
+                g.alpha = al;
+                g.beta = be;
+                g.alpha_ptr = dev_ptrs ? alpha : nullptr;
+                g.beta_ptr = dev_ptrs ? beta : nullptr;
+                g.scalar_f16 = sf16;
+                g.err = err_ptr();
+                static std::once_flag attr;
+                std::call_once(attr, [] {
+                    cudaFuncSetAttribute(cfi_gemm_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+                    cudaFuncSetAttribute(cfi_gemm_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+                });
+                dim3 grid((m + BM - 1) / BM, (n + bn - 1) / bn, batch);
+                if (a_type == CFI_R_16F)
+                    cfi_gemm_tc<0><<<grid, THREADS, SMEM_BYTES, h->stream>>>(ta, tb, g);
+                else
+                    cfi_gemm_tc<1><<<grid, THREADS, SMEM_BYTES, h->stream>>>(ta, tb, g);
+                if (cudaGetLastError() != cudaSuccess) return CFI_BLAS_EXECUTION_FAILED;
+                h->last_path = 1;
+                return CFI_BLAS_SUCCESS;
+            }
+        }
+    }
+    SimtArgs p;
+    p.a = A;
+    p.b = B;
+    p.c = C;
+    p.sa = sa;
+    p.sb = sb;
+    p.sc = sc;
+    p.lda = lda;
+    p.ldb = ldb;
+    p.ldc = ldc;
+    p.ta = transa != 0;
+    p.tb = transb != 0;
+    p.at = a_type;
+    p.bt = b_type;
+    p.ct = c_type;
+    p.m = (uint32_t)m;
+    p.n = (uint32_t)n;
+    p.k = (uint32_t)k;
+    p.alpha = al;
+    p.beta = be;
+    p.alpha_ptr = dev_ptrs ? alpha : nullptr;
+    p.beta_ptr = dev_ptrs ? beta : nullptr;
+    p.scalar_f16 = sf16;
+    p.ptrs = ptr_arrays ? 1 : 0;
+    for (int z0 = 0; z0 < batch; z0 += 65535) {
+        const int bz = batch - z0 < 65535 ? batch - z0 : 65535;
+        SimtArgs q = p;
+        if (ptr_arrays) {
+            q.a = static_cast<const void* const*>(p.a) + z0;
+            q.b = static_cast<const void* const*>(p.b) + z0;
+            q.c = const_cast<void**>(static_cast<void* const*>(p.c) + z0);
+        } else {
+            const size_t ea = a_type == CFI_R_32F ? 4 : 2, ec = c_type == CFI_R_32F ? 4 : 2;
+            q.a = static_cast<const uint8_t*>(p.a) + (size_t)z0 * sa * ea;
+            q.b = static_cast<const uint8_t*>(p.b) + (size_t)z0 * sb * ea;
+            q.c = static_cast<uint8_t*>(p.c) + (size_t)z0 * sc * ec;
+        }
+        dim3 grid((m + 15) / 16, (n + 15) / 16, bz);
+        if (grid.y > 65535) return CFI_BLAS_NOT_SUPPORTED;
+        cfi_gemm_simt<<<grid, 256, 0, h->stream>>>(q);
+        if (cudaGetLastError() != cudaSuccess) return CFI_BLAS_EXECUTION_FAILED;
+    }
+    h->last_path = 2;
+    return CFI_BLAS_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cfi_blas_gemm_ex(cfi_blas* h, int transa, int transb, int m, int n, int k, const void* alpha, const void* A,
+                     int a_type, int lda, const void* B, int b_type, int ldb, const void* beta, void* C, int c_type,
+                     int ldc, int compute_type, int algo) {
+    (void)algo;
+    return gemm_common(h, transa, transb, m, n, k, alpha, A, a_type, lda, 0, B, b_type, ldb, 0, beta, C, c_type, ldc, 0, 1,
+                       compute_type, false);
+}
+
+int cfi_blas_gemm_strided_batched_ex(cfi_blas* h, int transa, int transb, int m, int n, int k, const void* alpha,
+                                     const void* A, int a_type, int lda, long long stride_a, const void* B, int b_type,
+                                     int ldb, long long stride_b, const void* beta, void* C, int c_type, int ldc,
+                                     long long stride_c, int batch_count, int compute_type, int algo) {
+    (void)algo;
+    return gemm_common(h, transa, transb, m, n, k, alpha, A, a_type, lda, stride_a, B, b_type, ldb, stride_b, beta, C,
+                       c_type, ldc, stride_c, batch_count, compute_type, false);
+}
+
+int cfi_blas_gemm_batched_ex(cfi_blas* h, int transa, int transb, int m, int n, int k, const void* alpha,
+                             const void* const A[], int a_type, int lda, const void* const B[], int b_type, int ldb,
+                             const void* beta, void* const C[], int c_type, int ldc, int batch_count, int compute_type,
+                             int algo) {
+    (void)algo;
+    if (batch_count > 0 && (!A || !B || !C)) return CFI_BLAS_INVALID_VALUE;
+    return gemm_common(h, transa, transb, m, n, k, alpha, A, a_type, lda, 0, B, b_type, ldb, 0, beta,
+                       const_cast<void*>(static_cast<const void*>(C)), c_type, ldc, 0, batch_count, compute_type, true);
+}
+
+int cfi_blas_sgemm(cfi_blas* h, int transa, int transb, int m, int n, int k, const float* alpha, const float* A, int lda,
+                   const float* B, int ldb, const float* beta, float* C, int ldc) {
+    return gemm_common(h, transa, transb, m, n, k, alpha, A, CFI_R_32F, lda, 0, B, CFI_R_32F, ldb, 0, beta, C, CFI_R_32F,
+                       ldc, 0, 1, CFI_COMPUTE_32F, false);
+}
+
+}  // extern "C"

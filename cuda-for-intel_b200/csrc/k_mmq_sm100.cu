@@ -645,12 +645,16 @@ extern "C" int cfi_mmq_static_scratch(uint32_t ggml_type, void** kernel_params, 
     return rc ? fail(rc) : 0;
 }
 
+unsigned int cfi_gemm_error_take();  // k_gemm_sm100.cu
+
 extern "C" unsigned int cfi_device_error(void) {
     unsigned int v = 0, z = 0;
     if (cudaMemcpyFromSymbol(&v, g_cfi_device_error, sizeof v) != cudaSuccess) {
         cudaGetLastError();
-        return 0;
+        v = 0;
+    } else {
+        cudaMemcpyToSymbol(g_cfi_device_error, &z, sizeof z);
     }
-    cudaMemcpyToSymbol(g_cfi_device_error, &z, sizeof z);
-    return v;
+    const unsigned int g = cfi_gemm_error_take();
+    return v ? v : g;
 }
