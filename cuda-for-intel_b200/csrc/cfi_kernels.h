@@ -11,15 +11,24 @@
 const void* cfi_native_quantize_q8_1();
 const void* cfi_native_quantize_mmq(int ds4);
 
-// k_mmvq.cu: mul_mat_vec_q<ty, ncols> with one trailing u32 `nrows`.  Returns nullptr for an
-// unsupported (ty, ncols).  Dynamic shared memory for a launch: cfi_mmvq_smem_bytes.
-const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols);
+// k_mmvq.cu: mul_mat_vec_q<ty, ncols> with three trailing u32 words appended by the router:
+// `nrows`, `chunk_rows` and `nstages` (rows per shared-memory stage and stage count of the
+// streaming kernel, ncols <= 2; ignored by the row kernel of ncols >= 3).  Returns nullptr for an unsupported (ty, ncols);
+// `stream` false selects the row kernel for ncols <= 2 as well.
+const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols, bool stream);
+bool cfi_mmvq_streams(uint32_t ncols);
+// streaming kernel: rows per shared-memory stage and dynamic shared memory of a launch
+void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
+                            uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,
+                            uint32_t* chunk_rows, uint32_t* nstages, size_t* smem);
+// row kernel (ncols >= 3): dynamic shared memory of a launch
 size_t cfi_mmvq_smem_bytes(uint32_t ty, uint32_t ncols, uint32_t ncols_x);
-// Rows a warp computes at once (all loads of an iteration for those rows are issued together).
+// Rows a warp of the row kernel computes at once (all loads of an iteration issued together).
 inline uint32_t cfi_mmvq_rows_per_warp(uint32_t ty, uint32_t ncols) {
     return ty == 12 ? (ncols == 1 ? 2 : 1) : (ncols <= 2 ? 2 : 1);
 }
 int cfi_mmvq_max_smem_bytes();
+unsigned int cfi_mmvq_error_take();
 constexpr int CFI_MMVQ_THREADS = 256;
 constexpr int CFI_MMVQ_WARPS = CFI_MMVQ_THREADS / 32;
 

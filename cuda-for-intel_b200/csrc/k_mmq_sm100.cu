@@ -656,5 +656,6 @@ extern "C" unsigned int cfi_device_error(void) {
         cudaMemcpyToSymbol(g_cfi_device_error, &z, sizeof z);
     }
     const unsigned int g = cfi_gemm_error_take();
-    return v ? v : g;
+    const unsigned int m = cfi_mmvq_error_take();
+    return v ? v : (g ? g : m);
 }

@@ -31,6 +31,8 @@
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
 
+#include <algorithm>
+
 namespace {
 
 using namespace sm100;
@@ -150,11 +152,12 @@ CFI_DEV void store_row(const float (&acc)[NCOLS], uint32_t lane, float* dst_row,
 
 template <uint32_t TY, int NCOLS>
 __global__ void __launch_bounds__(NW * 32)
-    cfi_mmvq(const void* __restrict__ vx, const void* __restrict__ vy, const int32_t* __restrict__ ids,
+    cfi_mmvq_rows(const void* __restrict__ vx, const void* __restrict__ vy, const int32_t* __restrict__ ids,
              float* __restrict__ dst, uint32_t ncols_x, uint3 nchannels_y, uint32_t stride_row_x,
              uint32_t stride_col_y, uint32_t stride_col_dst, uint3 channel_ratio, uint32_t stride_channel_x,
              uint32_t stride_channel_y, uint32_t stride_channel_dst, uint3 sample_ratio, uint32_t stride_sample_x,
-             uint32_t stride_sample_y, uint32_t stride_sample_dst, uint32_t nrows) {
+             uint32_t stride_sample_y, uint32_t stride_sample_dst, uint32_t nrows, uint32_t /*chunk_rows*/,
+             uint32_t /*nstages*/) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int R = rows_per_warp<TY, NCOLS>();
     constexpr uint32_t BB = block_bytes<TY>();
@@ -325,27 +328,352 @@ __global__ void __launch_bounds__(NW * 32)
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Streaming kernel (ncols_dst 1 and 2): weights staged through shared memory by bulk copies.
+//
+// Launch order with programmatic dependent launch: before waiting on its predecessor a CTA only
+// asks L2 for its weight rows (a hint, never a read) and lets its own dependents launch, so a
+// chain of GEMVs (with the quantizer between them, which also triggers first) keeps several
+// grids resident and the HBM stream of later launches overlaps the work of earlier ones.  After
+// the wait the CTA copies its rows L2 -> shared memory in chunks (cp.async.bulk, two stages,
+// 16-byte-aligned interior of every row; Q8_0's ragged 2-byte ends by plain loads) while it
+// stages the q8_1 activations, and computes chunk k while chunk k+1 lands.
+//
+// Arithmetic (per output column, bit-exact to the one-warp decode-fast model of the reference,
+// src/subst/refs.rs:435-497): model lane l accumulates the 32-value groups l, l+32, l+64, ... of
+// its row in that order and the 32 lane sums are combined by the xor butterfly 16, 8, 4, 2, 1.
+//   * Q4_K: 16 threads per row; thread j computes model lanes 2j and 2j+1, which read the low and
+//     high nibbles of the same 32 bytes, so each 32-byte chunk is loaded once; the butterfly
+//     becomes xor 8, 4, 2, 1 across the 16 threads for both lanes, then lane 2j + lane 2j+1.  The
+//     high-nibble dot is taken on the bytes masked with 0xF0 (unsigned x signed dp4a, 16x the
+//     nibble dot, exact) and shifted back.
+//   * Q8_0: one warp per row, lane l = model lane l.
+// R rows per team are computed together so their loads and butterflies interleave.
+constexpr uint32_t ST_MAX_STAGES = 4;
+
+// Shared-memory layout of one stage.  Dense rows (stride_row_x == blocks per row) are copied as
+// one contiguous range, row k of the chunk at (address of its first row & 15) + k * row_bytes;
+// strided rows are copied one by one at k * pitch + (row address & 15).
+__host__ __device__ inline uint32_t st_pitch(uint32_t row_bytes) { return ((row_bytes + 15u) & ~15u) + 16u; }
+__host__ __device__ inline uint32_t st_row_stride(uint32_t row_bytes, bool dense) { return dense ? row_bytes : st_pitch(row_bytes); }
+__host__ __device__ inline uint32_t st_stage_bytes(uint32_t chunk_rows, uint32_t row_bytes, bool dense) {
+    return (chunk_rows * st_row_stride(row_bytes, dense) + 16u + 127u) & ~127u;
+}
+
+static __device__ unsigned int g_mmvq_error;
+static __device__ int g_mmvq_abort;  // never set: the bounded waits end on their time limit
+
+CFI_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsigned bytes of a x signed bytes of b
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+CFI_DEV int dot8m(const uint32_t (&q)[8], uint32_t mask, uint4 a, uint4 b) {
+    int s0 = dp4a_us(q[0] & mask, a.x, 0), s1 = dp4a_us(q[1] & mask, a.y, 0);
+    s0 = dp4a_us(q[2] & mask, a.z, s0);
+    s1 = dp4a_us(q[3] & mask, a.w, s1);
+    s0 = dp4a_us(q[4] & mask, b.x, s0);
+    s1 = dp4a_us(q[5] & mask, b.y, s1);
+    s0 = dp4a_us(q[6] & mask, b.z, s0);
+    s1 = dp4a_us(q[7] & mask, b.w, s1);
+    return s0 + s1;
+}
+// get_scale_min_k4 for sub-block g of a superblock header (scales in words h.y, h.z, h.w)
+CFI_DEV void q4k_scale_min(uint4 h, uint32_t g, int& sc, int& m) {
+    const uint32_t sh = 8u * (g & 3u);
+    const uint32_t a = h.y >> sh, b = h.z >> sh, c = h.w >> sh;
+    if (g < 4) {
+        sc = (int)(a & 63u);
+        m = (int)(b & 63u);
+    } else {
+        sc = (int)((c & 15u) | ((a >> 2) & 0x30u));
+        m = (int)(((c >> 4) & 15u) | ((b >> 2) & 0x30u));
+    }
+}
+CFI_DEV float q4k_term(float dx, float dmin, float d8, int sumi, int sc, int sumy, int m, float acc) {
+    const float a = __fmul_rn(d8, (float)(sumi * sc));
+    const float b = __fmul_rn(d8, (float)(sumy * m));
+    return __fadd_rn(acc, __fsub_rn(__fmul_rn(dx, a), __fmul_rn(dmin, b)));
+}
+
+// Rows of one chunk.  Each pass holds the weights of R rows per team in registers and streams
+// the activations column by column, so a column's q8_1 block is read once per R rows.
+template <int NCOLS>
+CFI_DEV void q4k_chunk(uint32_t sbase, uint32_t rstride, uint32_t r0, uint32_t r1, const YStage& y, uint32_t tid,
+                       float* dplane, uint32_t stride_col_dst) {
+    constexpr int R = 2;
+    constexpr uint32_t NTEAM = NW * 32 / 16;
+    const uint32_t j = tid & 15, team = tid >> 4, c4 = j & 3;
+    const uint32_t G = y.nb32;
+    for (uint32_t p0 = r0; p0 < r1; p0 += NTEAM * R) {
+        float acc[R][NCOLS][2];
+#pragma unroll
+        for (int k = 0; k < R; k++)
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) acc[k][c][0] = acc[k][c][1] = 0.0f;
+        for (uint32_t g0 = 2 * j; g0 < G; g0 += 32) {
+            const uint32_t sbo = (g0 >> 3) * Q4_K_BYTES;
+            uint32_t q[R][8];
+            int sc0[R], mn0[R], sc1[R], mn1[R];
+            float dx[R], dmin[R];
+#pragma unroll
+            for (int k = 0; k < R; k++) {
+                const uint32_t r = min(p0 + team + NTEAM * k, r1 - 1);
+                const uint32_t a = sbase + (r - r0) * rstride + sbo;
+                const uint4 h = lds128(a), q0 = lds128(a + 16 + 32 * c4), q1 = lds128(a + 32 + 32 * c4);
+                dx[k] = h2f_bits((uint16_t)(h.x & 0xffffu));
+                dmin[k] = h2f_bits((uint16_t)(h.x >> 16));
+                q[k][0] = q0.x; q[k][1] = q0.y; q[k][2] = q0.z; q[k][3] = q0.w;
+                q[k][4] = q1.x; q[k][5] = q1.y; q[k][6] = q1.z; q[k][7] = q1.w;
+                q4k_scale_min(h, 2 * c4, sc0[k], mn0[k]);
+                q4k_scale_min(h, 2 * c4 + 1, sc1[k], mn1[k]);
+            }
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                const uint32_t o = c * G + g0;
+                const uint4 ya0 = lds128(y.ya + o * 16), yb0 = lds128(y.yb + o * 16);
+                const uint4 ya1 = lds128(y.ya + o * 16 + 16), yb1 = lds128(y.yb + o * 16 + 16);
+                const uint2 m0 = lds64(y.ym + o * 8), m1 = lds64(y.ym + o * 8 + 8);
+#pragma unroll
+                for (int k = 0; k < R; k++) {
+                    const int lo = dot8m(q[k], 0x0F0F0F0Fu, ya0, yb0);
+                    const int hi = dot8m(q[k], 0xF0F0F0F0u, ya1, yb1) >> 4;
+                    acc[k][c][0] = q4k_term(dx[k], dmin[k], __uint_as_float(m0.x), lo, sc0[k], (int)m0.y, mn0[k], acc[k][c][0]);
+                    acc[k][c][1] = q4k_term(dx[k], dmin[k], __uint_as_float(m1.x), hi, sc1[k], (int)m1.y, mn1[k], acc[k][c][1]);
+                }
+            }
+        }
+        // model butterfly: lanes 2j and 2j+1 pair with 2(j^8), 2(j^4), 2(j^2), 2(j^1) (+0/+1), then with each other
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = p0 + team + NTEAM * k;
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                float a0 = acc[k][c][0], a1 = acc[k][c][1];
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) {
+                    a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, o));
+                    a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, o));
+                }
+                if (j == 0 && r < r1) dplane[(size_t)c * stride_col_dst + r] = __fadd_rn(a0, a1);
+            }
+        }
+    }
+}
+
+template <int NCOLS>
+CFI_DEV void q80_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0, uint32_t r1, const YStage& y,
+                       uint32_t lane, uint32_t warp, uintptr_t plane, uint32_t stride_row_x, float* dplane,
+                       uint32_t stride_col_dst) {
+    constexpr int R = NCOLS == 1 ? 4 : 2;
+    const uint32_t nb = y.nb32;
+    for (uint32_t p0 = r0; p0 < r1; p0 += NW * R) {
+        float acc[R][NCOLS];
+        uint32_t rb[R];
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = min(p0 + warp + NW * k, r1 - 1);
+            const uintptr_t rs = plane + (uintptr_t)(dense ? r0 : r) * stride_row_x * Q8_0_BYTES;
+            rb[k] = sbase + (r - r0) * rstride + (uint32_t)(rs & 15);
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) acc[k][c] = 0.0f;
+        }
+        for (uint32_t b = lane; b < nb; b += 32) {
+            int wq[R][8];
+            float dx[R];
+#pragma unroll
+            for (int k = 0; k < R; k++) {
+                const uint32_t blk = rb[k] + b * Q8_0_BYTES;
+                dx[k] = h2f_bits((uint16_t)lds16(blk));
+                const uint32_t qo = blk + 2, shq = (qo & 3u) * 8, wa = qo & ~3u;
+                uint32_t prev = lds32(wa);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const uint32_t nxt = lds32(wa + 4 * (i + 1));
+                    wq[k][i] = (int)__funnelshift_r(prev, nxt, shq);
+                    prev = nxt;
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                const uint4 ya = lds128(y.ya + (c * nb + b) * 16), yb = lds128(y.yb + (c * nb + b) * 16);
+                const float d8 = __uint_as_float(lds32(y.ym + (c * nb + b) * 8));
+#pragma unroll
+                for (int k = 0; k < R; k++)
+                    acc[k][c] = __fmaf_rn(__fmul_rn(dx[k], d8), (float)dot8(wq[k], ya, yb), acc[k][c]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = p0 + warp + NW * k;
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                float v = acc[k][c];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane == 0 && r < r1) dplane[(size_t)c * stride_col_dst + r] = v;
+            }
+        }
+    }
+}
+
+template <uint32_t TY, int NCOLS>
+__global__ void __launch_bounds__(NW * 32)
+    cfi_mmvq_stream(const void* __restrict__ vx, const void* __restrict__ vy, const int32_t* __restrict__ ids,
+                    float* __restrict__ dst, uint32_t ncols_x, uint3 nchannels_y, uint32_t stride_row_x,
+                    uint32_t stride_col_y, uint32_t stride_col_dst, uint3 channel_ratio, uint32_t stride_channel_x,
+                    uint32_t stride_channel_y, uint32_t stride_channel_dst, uint3 sample_ratio, uint32_t stride_sample_x,
+                    uint32_t stride_sample_y, uint32_t stride_sample_dst, uint32_t nrows, uint32_t chunk_rows,
+                    uint32_t nst) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[ST_MAX_STAGES];
+    constexpr uint32_t BB = block_bytes<TY>();
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t nb = TY == T_Q4_K ? ncols_x / QK_K : ncols_x / QK8_0;
+    const uint32_t nb32 = ncols_x / 32;
+    const uint32_t row_bytes = nb * BB;
+    const bool dense = stride_row_x == nb;
+    const uint32_t rstride = st_row_stride(row_bytes, dense);
+    const uint32_t stage_bytes = st_stage_bytes(chunk_rows, row_bytes, dense);
+    const uint32_t channel_dst = blockIdx.y, sample_dst = blockIdx.z;
+    const bool use_ids = NCOLS == 1 && ids != nullptr;
+    const uint32_t sample_x = fastdiv(sample_dst, sample_ratio);
+    const uint32_t rbeg = (uint32_t)((uint64_t)blockIdx.x * nrows / gridDim.x);
+    const uint32_t rend = (uint32_t)((uint64_t)(blockIdx.x + 1) * nrows / gridDim.x);
+    const uint32_t nchunks = (rend - rbeg + chunk_rows - 1) / chunk_rows;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < nst; s++) mbar_init(&full[s], 1);
+        fence_mbar_init();
+        // L2 hint for this CTA's rows (the ids table may come from the previous kernel: skip)
+        if (!use_ids && rend > rbeg) {
+            const uint32_t channel_x = fastdiv(channel_dst, channel_ratio);
+            const uint8_t* pl = static_cast<const uint8_t*>(vx) +
+                                ((size_t)sample_x * stride_sample_x + (size_t)channel_x * stride_channel_x) * BB;
+            uintptr_t a0 = (reinterpret_cast<uintptr_t>(pl + (size_t)rbeg * stride_row_x * BB) + 15) & ~(uintptr_t)15;
+            const uintptr_t a1 = reinterpret_cast<uintptr_t>(pl + (size_t)(rend - 1) * stride_row_x * BB + row_bytes) & ~(uintptr_t)15;
+            while (a0 < a1) {
+                const uint32_t n = (uint32_t)min((uintptr_t)(1u << 20), a1 - a0);
+                l2_prefetch(reinterpret_cast<const void*>(a0), n);
+                a0 += n;
+            }
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    __syncthreads();
+
+    const uint32_t channel_x = use_ids ? (uint32_t)ids[channel_dst] : fastdiv(channel_dst, channel_ratio);
+    const uint32_t channel_y = use_ids ? fastmodulo(channel_dst, nchannels_y) : channel_dst;
+    const size_t y_base = (size_t)sample_dst * stride_sample_y + (size_t)channel_y * stride_channel_y;
+    const uintptr_t plane = reinterpret_cast<uintptr_t>(vx) +
+                            ((size_t)sample_x * stride_sample_x + (size_t)channel_x * stride_channel_x) * BB;
+    float* dplane = dst + (size_t)sample_dst * stride_sample_dst + (size_t)channel_dst * stride_channel_dst;
+
+    // copies one byte range [b0, b1) (2-byte aligned) to shared memory at st + (x - (b0 & ~15)):
+    // the 16-byte-aligned interior by one bulk copy (issued by `issuer`), the ragged ends as
+    // halfwords by threads base .. base + 15.  Returns the bulk byte count.
+    auto range_bytes = [](uintptr_t b0, uintptr_t b1) -> uint32_t {
+        const uintptr_t a0 = (b0 + 15) & ~(uintptr_t)15, a1 = b1 & ~(uintptr_t)15;
+        return a1 > a0 ? (uint32_t)(a1 - a0) : 0u;
+    };
+    auto range_copy = [&](uint8_t* st, uintptr_t b0, uintptr_t b1, uint64_t* bar, bool issuer, uint32_t hw) {
+        const uintptr_t base = b0 & ~(uintptr_t)15;
+        uintptr_t a0 = (b0 + 15) & ~(uintptr_t)15, a1 = b1 & ~(uintptr_t)15;
+        if (a1 <= a0) a0 = a1 = b1;
+        if (issuer && a1 > a0) bulk_g2s(st + (a0 - base), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), bar);
+        if (TY != T_Q4_K && hw < 16) {  // Q8_0 rows are 2-byte aligned: at most 7 halfwords per end
+            const uintptr_t src = hw < 8 ? b0 + 2 * hw : a1 + 2 * (hw - 8);
+            if (hw < 8 ? src < a0 : src < b1)
+                *reinterpret_cast<uint16_t*>(st + (src - base)) = __ldg(reinterpret_cast<const unsigned short*>(src));
+        }
+    };
+    auto fill = [&](uint32_t ch, uint32_t s) {
+        const uint32_t r0 = rbeg + ch * chunk_rows, r1 = min(r0 + chunk_rows, rend);
+        uint8_t* st = smem + s * stage_bytes;
+        if (dense) {
+            const uintptr_t b0 = plane + (uintptr_t)r0 * nb * BB, b1 = plane + (uintptr_t)r1 * nb * BB;
+            if (tid == 0) mbar_arrive_expect_tx(&full[s], range_bytes(b0, b1));
+            range_copy(st, b0, b1, &full[s], tid == 0, tid);
+        } else {
+            if (tid == 0) {
+                uint32_t tx = 0;
+                for (uint32_t r = r0; r < r1; r++) {
+                    const uintptr_t rs = plane + (uintptr_t)r * stride_row_x * BB;
+                    tx += range_bytes(rs, rs + row_bytes);
+                }
+                mbar_arrive_expect_tx(&full[s], tx);
+            }
+            __syncthreads();
+            for (uint32_t idx = tid; idx < (r1 - r0) * 16; idx += NW * 32) {
+                const uint32_t k = idx / 16;
+                const uintptr_t rs = plane + (uintptr_t)(r0 + k) * stride_row_x * BB;
+                range_copy(st + k * rstride, rs, rs + row_bytes, &full[s], (idx & 15) == 0, idx & 15);
+            }
+        }
+    };
+    for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
+    const YStage y = stage_y(smem + nst * stage_bytes, NCOLS, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
+    __syncthreads();
+
+    for (uint32_t ch = 0; ch < nchunks; ch++) {
+        const uint32_t s = ch % nst;
+        const bool ok = __syncthreads_and(mbar_wait(&full[s], (ch / nst) & 1, &g_mmvq_abort));
+        if (!ok) {
+            if (tid == 0) cfi_set_error(&g_mmvq_error, 0x4d560000u | ch);
+            return;
+        }
+        const uint32_t r0 = rbeg + ch * chunk_rows, r1 = min(r0 + chunk_rows, rend);
+        const uint32_t sb = smem_u32(smem + s * stage_bytes);
+        if constexpr (TY == T_Q4_K)
+            q4k_chunk<NCOLS>(sb, rstride, r0, r1, y, tid, dplane, stride_col_dst);
+        else
+            q80_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
+        __syncthreads();
+        if (ch + nst < nchunks) fill(ch + nst, s);
+    }
+}
+
 template <uint32_t TY>
-const void* pick(uint32_t ncols) {
+const void* pick(uint32_t ncols, bool stream) {
     switch (ncols) {
-    case 1: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 1>);
-    case 2: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 2>);
-    case 3: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 3>);
-    case 4: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 4>);
-    case 5: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 5>);
-    case 6: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 6>);
-    case 7: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 7>);
-    case 8: return reinterpret_cast<const void*>(&cfi_mmvq<TY, 8>);
+    case 1: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 1>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 1>);
+    case 2: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 2>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 2>);
+    case 3: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 3>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 3>);
+    case 4: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 4>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 4>);
+    case 5: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 5>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 5>);
+    case 6: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 6>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 6>);
+    case 7: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 7>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 7>);
+    case 8: return stream ? reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 8>) : reinterpret_cast<const void*>(&cfi_mmvq_rows<TY, 8>);
     default: return nullptr;
     }
 }
 
 }  // namespace
 
-const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols) {
-    if (ty == T_Q8_0) return pick<T_Q8_0>(ncols);
-    if (ty == T_Q4_K) return pick<T_Q4_K>(ncols);
+const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols, bool stream) {
+    if (ty == T_Q8_0) return pick<T_Q8_0>(ncols, stream);
+    if (ty == T_Q4_K) return pick<T_Q4_K>(ncols, stream);
     return nullptr;
+}
+
+bool cfi_mmvq_streams(uint32_t ncols) { return ncols >= 1 && ncols <= 8; }
+
+void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
+                            uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,
+                            uint32_t* chunk_rows, uint32_t* nstages, size_t* smem) {
+    const uint32_t nb = ty == T_Q4_K ? ncols_x / QK_K : ncols_x / QK8_0;
+    const uint32_t row_bytes = nb * (ty == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES);
+    const bool dense = stride_row_x == nb;
+    const uint32_t per_cta = (nrows + grid_x - 1) / grid_x;
+    uint32_t c = std::min(std::max(1u, chunk_target), std::max(1u, per_cta));
+    while (c > 1 && st_stage_bytes(c, row_bytes, dense) > stage_budget) c--;
+    const uint32_t chunks = (per_cta + c - 1) / c;
+    const uint32_t nst = std::max(1u, std::min(std::min(max_stages, ST_MAX_STAGES), chunks));
+    *chunk_rows = c;
+    *nstages = nst;
+    const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127;
+    *smem = (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys;
 }
 
 size_t cfi_mmvq_smem_bytes(uint32_t ty, uint32_t ncols, uint32_t ncols_x) {
@@ -356,3 +684,14 @@ size_t cfi_mmvq_smem_bytes(uint32_t ty, uint32_t ncols, uint32_t ncols_x) {
 }
 
 int cfi_mmvq_max_smem_bytes() { return 200 * 1024; }
+
+// Reads and clears the error word of the GEMV's bounded waits (folded into cfi_device_error).
+unsigned int cfi_mmvq_error_take() {
+    unsigned int v = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&v, g_mmvq_error, sizeof v) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaMemcpyToSymbol(g_mmvq_error, &z, sizeof z);
+    return v;
+}

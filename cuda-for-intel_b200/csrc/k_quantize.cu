@@ -42,9 +42,10 @@ CFI_DEV float amax8_from4(float4 v, unsigned mask) {
 extern "C" __global__ void __launch_bounds__(256)
     cfi_quantize_q8_1(const float* __restrict__ x, void* __restrict__ vy, int64_t ne00, int64_t s01, int64_t s02,
                       int64_t s03, int64_t ne0, uint32_t ne1, uint3 ne2) {
-    // programmatic dependent launch: wait for the producer of x, then let the next kernel start
-    sm100::pdl_wait();
+    // programmatic dependent launch: let the next kernel (a GEMV, which before its own wait only
+    // prefetches its weights into L2) start at once, then wait for the producer of x
     sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
     const int64_t i0 = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
     // whole 8-thread groups (32 values) leave together (ne0 is a multiple of 32); the shuffles
     // below stay inside a group, over the lanes that remain

@@ -585,16 +585,32 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         if ((vals[1] & 3)) return false;                       // q8_1 blocks are read as words
         const uint32_t nrows = plan.ncols == 1 ? grid[0] : std::min(2 * grid[0], stride_col_dst);
         const uint32_t planes = std::max(1u, grid[1] * grid[2]);
-        nl.smem = cfi_mmvq_smem_bytes(plan.ty, plan.ncols, ncols_x);
+        // CFI_MMVQ_STREAM=0 selects the row kernel for ncols <= 2 too
+        const bool stream = cfi_mmvq_streams(plan.ncols) && env_u32("CFI_MMVQ_STREAM", 1, 0, 1) != 0;
+        nl.fn = cfi_native_mmvq(plan.ty, plan.ncols, stream);
+        uint32_t chunk = 0, nstages = 0;
+        if (stream) {
+            // CFI_MMVQ_STREAM_CTAS CTAs per SM shared by the channel/sample planes; chunks of
+            // CFI_MMVQ_CHUNK rows within CFI_MMVQ_STAGE_KB per stage, CFI_MMVQ_STAGES stages
+            const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", 2, 1, 8);
+            const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
+            nl.grid[0] = std::max(1u, std::min(nrows, cap));
+            cfi_mmvq_stream_layout(plan.ty, plan.ncols, ncols_x, nrows, nl.grid[0], (uint32_t)vals[6],
+                                   env_u32("CFI_MMVQ_CHUNK", 32, 1, 256), 1024 * env_u32("CFI_MMVQ_STAGE_KB", 48, 4, 112),
+                                   env_u32("CFI_MMVQ_STAGES", 3, 1, 4), &chunk, &nstages, &nl.smem);
+        } else {
+            const uint32_t per_sm = env_u32("CFI_MMVQ_CTAS", 4, 1, 8);
+            const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
+            const uint32_t rows_per_pass = CFI_MMVQ_WARPS * cfi_mmvq_rows_per_warp(plan.ty, plan.ncols);
+            const uint32_t tiles = (nrows + rows_per_pass - 1) / rows_per_pass;
+            nl.grid[0] = std::max(1u, std::min(tiles, cap));
+            nl.smem = cfi_mmvq_smem_bytes(plan.ty, plan.ncols, ncols_x);
+        }
         if (nl.smem > (size_t)cfi_mmvq_max_smem_bytes()) return false;
-        nl.fn = cfi_native_mmvq(plan.ty, plan.ncols);
-        const uint32_t per_sm = env_u32("CFI_MMVQ_CTAS", 4, 1, 8);
-        const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
-        const uint32_t rows_per_pass = CFI_MMVQ_WARPS * cfi_mmvq_rows_per_warp(plan.ty, plan.ncols);
-        const uint32_t tiles = (nrows + rows_per_pass - 1) / rows_per_pass;
-        nl.grid[0] = std::max(1u, std::min(tiles, cap));
         nl.block[0] = CFI_MMVQ_THREADS;
         nl.extra.push_back(nrows);
+        nl.extra.push_back(chunk);
+        nl.extra.push_back(nstages);
         nl.pdl = pdl_enabled();
         nl.grid[1] = grid[1];
         nl.grid[2] = grid[2];
@@ -674,7 +690,7 @@ const void* native_kernel(const cfi_plan& plan, std::string* why) {
     NativeLaunch nl;
     const void* fn = nullptr;
     switch (plan.kernel) {
-    case CFI_K_MMVQ: fn = cfi_native_mmvq(plan.ty, plan.ncols); break;
+    case CFI_K_MMVQ: fn = cfi_native_mmvq(plan.ty, plan.ncols, true); break;
     case CFI_K_QUANTIZE_Q8_1: fn = cfi_native_quantize_q8_1(); break;
     case CFI_K_QUANTIZE_MMQ: fn = cfi_native_quantize_mmq(plan.ty == 1); break;
     case CFI_K_MMQ: fn = mmq_type_ok(plan.ty) ? reinterpret_cast<const void*>(&mmq_launch) : nullptr; break;
