@@ -45,6 +45,14 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -107,6 +115,46 @@ def traffic_per_launch():
             return float(json.load(f)["dram_bytes_per_launch_b1"])
     except Exception:
         return None
+
+
+def prefill_gemm(cfi, g, stream, dev, peak_tf):
+    """Q8_0 weights (4864x896 and 896x4864) x 631 tokens quantised to
+    q8_1_mmq, through the native mul_mat_q (tcgen05).  CUDA graph of back-to-back calls."""
+    import torch
+
+    out = {}
+    for m, k in ((4864, 896), (896, 4864)):
+        n = 631
+        w = torch.from_numpy(cfi.synthetic_weights(cfi.Q8_0, m, k, seed=m)).to(dev)
+        xf = torch.from_numpy(np.random.default_rng(k).normal(size=(n, k)).astype(np.float32)).to(dev)
+        q = torch.zeros(k // 128 * n * 144, dtype=torch.uint8, device=dev)
+        d = torch.zeros(n * m, dtype=torch.float32, device=dev)
+        with torch.cuda.stream(stream):
+            g.quantize_mmq(0, xf.data_ptr(), q.data_ptr(), k, k, n, stream=stream.cuda_stream)
+            g.mmq(cfi.Q8_0, w.data_ptr(), q.data_ptr(), d.data_ptr(), k, m, n, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        reps, calls = 5, 20
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(calls):
+                g.mmq(cfi.Q8_0, w.data_ptr(), q.data_ptr(), d.data_ptr(), k, m, n,
+                      stream=torch.cuda.current_stream().cuda_stream)
+        with torch.cuda.stream(stream):
+            gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+        out["%dx%dx%d" % (m, k, n)] = {"us": round(us, 2), "tflops": round(2.0 * m * n * k / us / 1e6, 1)}
+        del gr
+    best = max(v["tflops"] for v in out.values())
+    return {"workload": "config3: Q8_0 W x 631 q8_1_mmq tokens -> f32 (mul_mat_q on tcgen05, incl. activation pre-pass)",
+            "shapes": out,
+            "roofline": {"bound": "tensor", "achieved": best, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": round(best / peak_tf, 4), "peak_kind": "measured bf16 dense (burst)"}}
 
 
 def cpu_baseline(seconds, threads=0):
@@ -305,6 +353,8 @@ def run_gpu(args, rank, world):
                              "traffic": traffic_per_launch(), "launch_us": round(kms * 1e3, 3),
                              "bytes_per_launch": MMVQ_BYTES(1)},
                 "clocks": clk.summary(), "native_only": ok}
+        if not args.no_prefill and world == 1:
+            line["prefill"] = prefill_gemm(cfi, g, stream, dev, tensor_peak())
         if not args.no_cpu and world == 1:
             gbs, used, n, el = cpu_baseline(args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
@@ -324,6 +374,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     args = ap.parse_args()
     if args.warmup < 3:
