@@ -7,7 +7,8 @@ outputs + quantizer traffic) against the measured HBM peak.  Weights rotate over
 that every GEMV reads from HBM (inputs larger than L2).  Kernels are launched through the
 substitution C ABI (cfi_subst_launch with ggml kernelParams) and each step is replayed as a
 CUDA graph.  With --gpus N (torchrun) every rank owns an 8192-row shard of an (8192 N) x 2048
-matrix (weak scaling) and the outputs are all-gathered over NCCL each step.
+matrix (weak scaling) and the outputs are all-gathered over NCCL each step (step i gathers
+step i-1's outputs on a second stream while its own kernels run, all inside the step's graph).
 
 --impl reference times the CPU evaluation of the same step (the oracle port of the reference's
 host math, row-parallel over every host core) on rank 0.
@@ -150,9 +151,41 @@ def prefill_gemm(cfi, g, stream, dev, peak_tf):
         us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
         out["%dx%dx%d" % (m, k, n)] = {"us": round(us, 2), "tflops": round(2.0 * m * n * k / us / 1e6, 1)}
         del gr
+    # the cuBLAS-compatible GemmEx path on the same shapes (ggml's T,N f16 -> f32 call)
+    blas = cfi.Blas(stream.cuda_stream)
+    gemm = {}
+    for m, k in ((4864, 896), (896, 4864)):
+        n = 631
+        A = torch.randn(m, k, device=dev).half()
+        B = torch.randn(n, k, device=dev).half()
+        C = torch.zeros(n, m, device=dev)
+        def call(st):
+            blas.set_stream(st)
+            blas.gemm_ex(1, 0, m, n, k, 1.0, A.data_ptr(), 2, k, B.data_ptr(), 2, k, 0.0, C.data_ptr(), 0, m)
+        with torch.cuda.stream(stream):
+            call(stream.cuda_stream)
+        torch.cuda.synchronize()
+        reps, calls = 5, 20
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(calls):
+                call(torch.cuda.current_stream().cuda_stream)
+        with torch.cuda.stream(stream):
+            gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+        gemm["%dx%dx%d" % (m, n, k)] = {"us": round(us, 2), "tflops": round(2.0 * m * n * k / us / 1e6, 1),
+                                         "path": "tcgen05" if blas.last_path() == 1 else "simt"}
+        del gr
+    blas.close()
     best = max(v["tflops"] for v in out.values())
     return {"workload": "config3: Q8_0 W x 631 q8_1_mmq tokens -> f32 (mul_mat_q on tcgen05, incl. activation pre-pass)",
-            "shapes": out,
+            "shapes": out, "gemm_ex_f16": gemm,
             "roofline": {"bound": "tensor", "achieved": best, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(best / peak_tf, 4), "peak_kind": "measured bf16 dense (burst)"}}
 
@@ -203,6 +236,7 @@ def run_gpu(args, rank, world):
         import torch.distributed as dist
         from datetime import timedelta
 
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # rank 0's stdout carries only the JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     ctx = cfi.Ctx(local)
@@ -220,39 +254,60 @@ def run_gpu(args, rank, world):
     xs = {b: xs_host[b].to(dev) for b in BATCHES}
     qs = {b: torch.zeros(Q81(b), dtype=torch.uint8, device=dev) for b in BATCHES}
     ys = {b: torch.zeros(b * ROWS, dtype=torch.float32, device=dev) for b in BATCHES}
-    y_all = torch.zeros(sum(b for b in BATCHES) * ROWS, dtype=torch.float32, device=dev)
+    # two output sets: with N > 1 step i all-gathers step i-1's outputs while it computes its own
+    y_sets = [torch.zeros(sum(b for b in BATCHES) * ROWS, dtype=torch.float32, device=dev) for _ in range(2)]
+    y_all = y_sets[0]
     offs, o = {}, 0
     for b in BATCHES:
         offs[b] = o
         o += b * ROWS
-    y_views = {b: y_all[offs[b]:offs[b] + b * ROWS] for b in BATCHES}
+    y_views_p = [{b: ya[offs[b]:offs[b] + b * ROWS] for b in BATCHES} for ya in y_sets]
+    y_views = y_views_p[0]
     gathered = torch.zeros(world * y_all.numel(), dtype=torch.float32, device=dev) if world > 1 else None
     ys_host = torch.zeros(y_all.numel(), dtype=torch.float32).pin_memory()
+    comm = torch.cuda.Stream(device=dev) if world > 1 else None
 
-    def step(phase, s):
+    def step(phase, s, parity=0):
         for j, b in enumerate(BATCHES):
             g.quantize_q8_1(xs[b].data_ptr(), qs[b].data_ptr(), K, K, b, stream=s)
             wcopy = wd[(phase * len(BATCHES) + j) % ncopy]
-            g.mmvq(cfi.Q4_K, b, wcopy.data_ptr(), qs[b].data_ptr(), y_views[b].data_ptr(), K, ROWS, stream=s)
+            g.mmvq(cfi.Q4_K, b, wcopy.data_ptr(), qs[b].data_ptr(), y_views_p[parity][b].data_ptr(), K, ROWS, stream=s)
+
+    def step_pipelined(phase, parity):
+        """Inside a capture: the all-gather of the other output set on the comm stream (one exchange
+        per step for the step's four sharded GEMVs) overlapping this step's kernels."""
+        cur = torch.cuda.current_stream()
+        if dist:
+            fork = torch.cuda.Event()
+            fork.record(cur)
+            comm.wait_event(fork)
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(gathered, y_sets[1 - parity])
+        step(phase, cur.cuda_stream, parity)
+        if dist:
+            join = torch.cuda.Event()
+            join.record(comm)
+            cur.wait_event(join)
 
     nphase = ncopy // len(BATCHES)
     # warm-up (first-use probes run here, outside any capture)
     with torch.cuda.stream(stream):
         for i in range(max(1, args.warmup)):
             step(i % nphase, stream.cuda_stream)
+            if dist:
+                dist.all_gather_into_tensor(gathered, y_all)
     torch.cuda.synchronize()
-    graphs = []
+    graphs = {}
     for ph in range(nphase):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            step(ph, torch.cuda.current_stream().cuda_stream)
-        graphs.append(gr)
+        for par in (0, 1):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step_pipelined(ph, par)
+            graphs[(ph, par)] = gr
     launches_per_step = 2 * len(BATCHES)
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
-            graphs[i % nphase].replay()
-            if dist:
-                dist.all_gather_into_tensor(gathered, y_all)
+            graphs[(i % nphase, i % 2)].replay()
     torch.cuda.synchronize()
 
     # ---- timed region: device time, max over ranks ----
@@ -264,9 +319,7 @@ def run_gpu(args, rank, world):
         with torch.cuda.stream(stream):
             e0.record(stream)
             for i in range(args.steps):
-                graphs[i % nphase].replay()
-                if dist:
-                    dist.all_gather_into_tensor(gathered, y_all)
+                graphs[(i % nphase, i % 2)].replay()
             e1.record(stream)
         torch.cuda.synchronize()
     if dist:
@@ -348,6 +401,7 @@ def run_gpu(args, rank, world):
                         "note": "host fp32 activations in and fp32 outputs out every step (weights resident), "
                                 "stream synchronized per step"},
                 "gpu_launches": launches_per_step * args.steps,
+                "collectives_per_step": 1 if world > 1 else 0,
                 "roofline": {"bound": "hbm", "kernel": "mul_mat_vec_q<Q4_K,1> 8192x2048", "achieved": round(achieved, 1),
                              "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                              "traffic": traffic_per_launch(), "launch_us": round(kms * 1e3, 3),

@@ -9,7 +9,8 @@
 //     zero), strided batches as the third tensor dimension;
 //   * one thread of warp 4 issues tcgen05.mma kind::f16 (M 128, N BN <= 256, K 16) into an fp32
 //     accumulator in tensor memory;
-//   * warps 0-3 apply alpha/beta and store C in its dtype (f32, f16 or bf16), coalesced by column.
+//   * warps 0-3 apply alpha/beta and store C in its dtype (f32, f16 or bf16) in runs of 4 rows
+//     (accumulator chunks transposed through shared memory).
 // Every other legal call (other transposes, f32 inputs, device pointer arrays) runs a tiled SIMT
 // kernel with fp32 accumulation.  Validation follows cuBLAS (plan.rs:160-215).
 #include <cuda.h>
@@ -22,6 +23,7 @@
 #include "../../include/cfi_cublas.h"
 #include "cfi_common.cuh"
 #include "sm100_ptx.cuh"
+#include "tc_epilogue.cuh"
 
 namespace {
 
@@ -158,25 +160,56 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (*epi_ok) {
             const float alpha = a.alpha_ptr ? load_scalar(a.alpha_ptr, a.scalar_f16) : a.alpha;
             const float beta = a.beta_ptr ? load_scalar(a.beta_ptr, a.scalar_f16) : a.beta;
-            const uint32_t row = m0 + 32 * warp + lane;
-            uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)z * (size_t)a.stride_c * (a.c_type == CFI_R_32F ? 4 : 2);
-            for (uint32_t cb = 0; cb < bn; cb += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + cb, v);
-                tmem_ld_wait();
-                if (row < a.m) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const uint32_t col = n0 + cb + i;
-                        if (col < a.n && cb + i < bn) {
-                            const size_t ci = (size_t)col * a.ldc + row;
-                            float r = alpha * __uint_as_float(v[i]);
-                            if (beta != 0.0f) r += beta * ld_elem(cz, ci, a.c_type);
-                            st_elem(cz, ci, a.c_type, r);
+            const int ct = a.c_type, es = ct == CFI_R_32F ? 4 : 2;
+            uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)z * (size_t)a.stride_c * es;
+            // 4 consecutive rows as one 16-byte (f32) or 8-byte (f16/bf16) access
+            const bool vec = (a.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(cz) & (uintptr_t)(4 * es - 1)) == 0;
+            // every MMA has completed: the A ring is free for the 4 KB per-warp staging buffers
+            float* buf = reinterpret_cast<float*>(sA) + warp * 1024;
+            tmem_tile_store(tmem, warp, lane, 4, bn, buf, [&](uint32_t c, uint32_t rr, float4 f) {
+                const uint32_t col = n0 + c, row = m0 + rr;
+                if (col >= a.n || row >= a.m) return;
+                const size_t ci = (size_t)col * a.ldc + row;
+                float r[4] = {alpha * f.x, alpha * f.y, alpha * f.z, alpha * f.w};
+                if (vec && row + 3 < a.m) {
+                    if (ct == CFI_R_32F) {
+                        float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(cz) + ci);
+                        if (beta != 0.0f) {
+                            const float4 o = *p;
+                            r[0] += beta * o.x;
+                            r[1] += beta * o.y;
+                            r[2] += beta * o.z;
+                            r[3] += beta * o.w;
                         }
+                        *p = make_float4(r[0], r[1], r[2], r[3]);
+                    } else {
+                        uint2* p = reinterpret_cast<uint2*>(cz + ci * 2);
+                        if (beta != 0.0f) {
+                            const uint2 o = *p;
+                            const uint16_t h[4] = {(uint16_t)(o.x & 0xffffu), (uint16_t)(o.x >> 16), (uint16_t)(o.y & 0xffffu),
+                                                   (uint16_t)(o.y >> 16)};
+#pragma unroll
+                            for (int e = 0; e < 4; e++)
+                                r[e] += beta * (ct == CFI_R_16F ? __half2float(__ushort_as_half(h[e]))
+                                                                : __bfloat162float(__ushort_as_bfloat16(h[e])));
+                        }
+                        uint16_t h[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            h[e] = ct == CFI_R_16F ? __half_as_ushort(__float2half_rn(r[e]))
+                                                   : __bfloat16_as_ushort(__float2bfloat16_rn(r[e]));
+                        *p = make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        if (row + e >= a.m) break;
+                        float v = r[e];
+                        if (beta != 0.0f) v += beta * ld_elem(cz, ci + e, ct);
+                        st_elem(cz, ci + e, ct, v);
                     }
                 }
-            }
+            });
         }
     }
     tc_fence_before();
@@ -390,7 +423,8 @@ int gemm_common(cfi_blas* h, int transa, int transb, int m, int n, int k, const 
     if (tc) {
         PFN_encodeTiled enc = encode_fn();
         if (enc) {
-            const uint32_t bn = n >= 256 ? 256 : ((uint32_t)n + 15) / 16 * 16;
+            const uint32_t tiles_n = ((uint32_t)n + 255) / 256;
+            const uint32_t bn = (((uint32_t)n + tiles_n - 1) / tiles_n + 15) / 16 * 16;  // balanced tiles
             const CUtensorMapDataType dt = a_type == CFI_R_16F ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
             CUtensorMap ta, tb;
             cuuint64_t da[3] = {(cuuint64_t)k, (cuuint64_t)m, (cuuint64_t)batch};

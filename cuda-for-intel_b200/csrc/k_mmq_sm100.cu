@@ -5,17 +5,19 @@
 // block_q8_1_mmq (144 B per 128 values of a column), the inputs of ggml-cuda's
 // mul_mat_q<type, mmq_x, need_check> (cuda-for-intel src/subst/mmq.rs:1-14, refs.rs:771-834).
 //
-// Design (one CTA per 128-row x BN-column output tile, BN <= 256):
+// Design (one CTA per 128-row x BN-column output tile, BN <= 256, 320 threads):
 //   1. pre-pass: the quantized activations become an fp16 K-major matrix  Xh[plane][col][Kt]
 //      (fp16(q * d) per value; for Q4_K the per-32 float sums s are appended as extra K columns);
-//   2. warp 5 streams Xh tiles with TMA (128-byte swizzle, the UMMA canonical K-major layout);
-//   3. warps 0-3 stream the raw weight bytes with coalesced cp.async into shared memory and
-//      dequantize them to fp16 in the same swizzled layout (Q8_0: fp16(q * d); Q4_K: fp16(q *
-//      half(d*sc)) and, in the appended K columns, half(-dmin*m) against s -- the reference's
-//      `fma(dmA.y, dsB.y, sum)` term);
-//   4. one thread of warp 4 issues tcgen05.mma kind::f16 (M=128, N=BN, K=16) with the fp32
+//   2. warp 9 streams Xh tiles with TMA (128-byte swizzle, the UMMA canonical K-major layout);
+//   3. warps 0-7 stream the raw weight bytes with coalesced cp.async into shared memory (a copy
+//      plan computed once per thread) and dequantize them, two threads per tile row, to fp16 in
+//      the same swizzled layout (Q8_0: fp16(q * d); Q4_K: fp16(q * half(d*sc)) and, in the
+//      appended K columns, half(-dmin*m) against s -- the reference's `fma(dmA.y, dsB.y, sum)`
+//      term); one reducing named barrier per stage;
+//   4. one thread of warp 8 issues tcgen05.mma kind::f16 (M=128, N=BN, K=16) with the fp32
 //      accumulator in tensor memory; commits free each pipeline slot;
-//   5. warps 0-3 drain TMEM (tcgen05.ld 32x32b) and store coalesced fp32 columns.
+//   5. warps 0-7 drain TMEM (tcgen05.ld 32x32b), transpose 32x32 chunks through shared memory
+//      and store 16-byte runs of rows.
 // Integer exactness does not apply here: fp16 rounding of q*d keeps the result within 1e-3
 // relative L2 of the reference (measured ~1e-4), the bound this path is held to.
 #include <cuda.h>
@@ -31,6 +33,7 @@
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
 #include "subst_host.hpp"
+#include "tc_epilogue.cuh"
 
 static __device__ unsigned int g_cfi_device_error;
 
@@ -41,12 +44,14 @@ using namespace sm100;
 constexpr int BM = 128;          // rows per tile (TMEM lanes)
 constexpr int BK = 64;           // K per pipeline stage (one 128-byte swizzle atom of fp16)
 constexpr int NSTAGE = 4;        // A/B smem ring
-constexpr int NRAW = 3;          // raw weight staging ring (cp.async prefetch depth)
+constexpr int NRAW = 3;          // raw weight staging ring (cp.async prefetch depth NRAW - 1)
 constexpr int A_STAGE = BM * BK * 2;      // 16 KB
 constexpr int B_STAGE = 256 * BK * 2;     // 32 KB (sized for BN = 256)
 constexpr int RAW_WORDS_Q8 = 17;          // 68 bytes = 2 Q8_0 blocks per row per stage
 constexpr int RAW_STAGE = BM * 20 * 4;    // 10 KB (room for 20 words per row)
-constexpr int THREADS = 192;
+constexpr int NPROD = 256;                // warps 0-7: weight producers, then the epilogue
+constexpr int MMA_WARP = 8, TMA_WARP = 9;
+constexpr int THREADS = 320;
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)NSTAGE * (A_STAGE + B_STAGE) + (size_t)NRAW * RAW_STAGE + 256;
 
 struct MmqArgs {
@@ -95,6 +100,19 @@ CFI_DEV void st_chunk(uint8_t* atom, int r, int c, uint32_t a, uint32_t b, uint3
 
 CFI_DEV int scale_byte(const uint32_t* s, int k) { return (int)((s[k >> 2] >> (8 * (k & 3))) & 0xffu); }
 
+// bar.red.and over `n` threads of named barrier `id`: true on every thread iff `v` on all.
+CFI_DEV bool named_bar_and(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+
+// Warp roles: 0-7 weight producers (two threads per tile row, one 32-value group each per stage)
+// and afterwards the epilogue; 8 tensor memory + MMA issue; 9 activation TMA.
 template <uint32_t TY>
 __global__ void __launch_bounds__(THREADS, 1)
     cfi_mmq_tc(const __grid_constant__ CUtensorMap tmap_b, const MmqArgs a) {
@@ -108,8 +126,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* done = empty + NSTAGE;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    volatile int* prod_ok = abort_flag + 1;
-    volatile int* epi_ok = abort_flag + 2;
+    volatile int* epi_ok = abort_flag + 1;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t bn = a.bn;
@@ -119,14 +136,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(&full[i], 128 + 1);  // 128 weight producers + the TMA thread's expect_tx
-            mbar_init(&empty[i], 1);       // tcgen05.commit
+            mbar_init(&full[i], NPROD + 1);  // the producers + the TMA thread's expect_tx
+            mbar_init(&empty[i], 1);         // tcgen05.commit
         }
         mbar_init(done, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 4) {
+    if (warp == MMA_WARP) {
         tmem_alloc(tmem_slot, tmem_cols);
         tmem_relinquish();
     }
@@ -141,81 +158,92 @@ __global__ void __launch_bounds__(THREADS, 1)
     const size_t x_off = (size_t)(wt / a.sample_ratio) * a.stride_sample_x + (size_t)(zt / a.channel_ratio) * a.stride_channel_x;
     float* dst = a.dst + (size_t)wt * a.stride_sample_dst + (size_t)zt * a.stride_channel_dst;
 
-    if (warp < 4) {
-        // ================= weight producers (128 threads) =================
+    if (warp < NPROD / 32) {
+        // ================= weight producers (256 threads) =================
         constexpr uint32_t BB = TY == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES;
         // raw words per row per stage: Q8_0 two blocks (17 words); Q4_K header (4) + 32 qs bytes (8);
         // RS is the padded row stride in shared memory (odd: conflict-free row-per-thread reads)
         constexpr int RW = TY == T_Q4_K ? 12 : RAW_WORDS_Q8;
         constexpr int RS = TY == T_Q4_K ? 13 : RAW_WORDS_Q8;
-        auto row_ptr = [&](uint32_t row) {
-            return a.x + (x_off + (size_t)min(row, a.nrows - 1) * a.stride_row_x) * BB;
-        };
+        constexpr int NCP = (BM * RW + NPROD - 1) / NPROD;  // raw words this thread copies per stage
+        const int r = tid & (BM - 1), hh = tid >> 7;        // tile row, group of the stage (0/1)
+        // copy plan, fixed for the whole K loop: word w = tid + NPROD * m of the stage
+        const uint8_t* xbase = a.x + (x_off + (size_t)row0 * a.stride_row_x) * BB;
+        uint32_t goff[NCP], soff[NCP], live = 0, inrow = 0, qsword = 0;
+#pragma unroll
+        for (int m = 0; m < NCP; m++) {
+            const int w = tid + NPROD * m;
+            const int rr = w / RW, j = w - rr * RW;
+            const uint32_t row = row0 + (uint32_t)rr;
+            goff[m] = (min(row, a.nrows - 1) - row0) * a.stride_row_x * BB +
+                      (uint32_t)(TY == T_Q4_K ? (j < 4 ? 4 * j : 16 + 4 * (j - 4)) : 4 * j);
+            soff[m] = (uint32_t)(rr * RS + j) * 4u;
+            if (w < BM * RW) live |= 1u << m;
+            if (row < a.nrows) inrow |= 1u << m;
+            if (TY == T_Q4_K && j >= 4) qsword |= 1u << m;
+        }
         auto issue = [&](int s) {
-            if (s >= kstages) return;  // correction stages read their headers directly
-            uint32_t* raw = reinterpret_cast<uint32_t*>(sRaw + (s % NRAW) * RAW_STAGE);
-            for (int w = tid; w < BM * RW; w += 128) {
-                const int r = w / RW, j = w - r * RW;
-                const uint32_t row = row0 + r;
-                const uint8_t* rowp = row_ptr(row);
-                const uint8_t* src;
-                if (TY == T_Q4_K) {
-                    const uint8_t* blk = rowp + (size_t)(s >> 2) * Q4_K_BYTES;  // 4 stages per superblock
-                    src = j < 4 ? blk + 4 * j : blk + 16 + 32 * (s & 3) + 4 * (j - 4);
-                } else {
-                    src = rowp + (size_t)s * 68 + 4 * j;
-                }
-                cp_async4(raw + r * RS + j, src, row < a.nrows ? 4u : 0u);
-            }
+            if (s >= kstages) return;  // Q4_K correction stages read their headers directly
+            uint8_t* raw = sRaw + (s % NRAW) * RAW_STAGE;
+            const uint32_t st = TY == T_Q4_K ? (uint32_t)(s >> 2) * Q4_K_BYTES : (uint32_t)s * 68u;
+            const uint32_t sq = TY == T_Q4_K ? 32u * (uint32_t)(s & 3) : 0u;
+#pragma unroll
+            for (int m = 0; m < NCP; m++)
+                if (live >> m & 1u)
+                    cp_async4(raw + soff[m], xbase + goff[m] + st + ((qsword >> m & 1u) ? sq : 0u), (inrow >> m & 1u) ? 4u : 0u);
         };
         for (int s = 0; s < NRAW - 1; s++) {
             if (s < nstages) issue(s);
             cp_async_commit();
         }
         for (int s = 0; s < nstages; s++) {
-            if (s + NRAW - 1 < nstages) issue(s + NRAW - 1);
-            cp_async_commit();
-            cp_async_wait<NRAW - 1>();
+            cp_async_wait<NRAW - 2>();  // this thread's copies of stage s have landed
             const int slot = s % NSTAGE;
             const uint32_t round = (uint32_t)(s / NSTAGE);
-            if (tid == 0) {
-                const bool got = mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag);
-                if (!got) {
+            bool ok = mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag);
+            // every producer's stage-s copies are visible, every producer finished stage s-1
+            // (its raw slot may be refilled), and the MMA released this A slot -- on all or none
+            ok = named_bar_and(1, NPROD, ok);
+            if (!ok) {
+                if (tid == 0) {
                     cfi_set_error(a.err, 0x100 + slot);
                     *abort_flag = 1;
                 }
-                *prod_ok = got ? 1 : 0;
+                break;
             }
-            named_bar_sync(1, 128);  // stage s copies landed everywhere; prod_ok published
-            if (!*prod_ok) break;    // uniform across the 128 producers
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(sRaw + (s % NRAW) * RAW_STAGE);
+            if (s + NRAW - 1 < nstages) issue(s + NRAW - 1);
+            cp_async_commit();
+            const uint32_t* W = reinterpret_cast<const uint32_t*>(sRaw + (s % NRAW) * RAW_STAGE) + r * RS;
             uint8_t* atom = sA + slot * A_STAGE;
-            const int r = tid;
             if (TY == T_Q8_0) {
-                const uint32_t* W = raw + r * RS;
-                uint32_t w[17];
+                if (hh == 0) {  // block 0: d at bytes 0..1, quants at bytes 2..33
+                    uint32_t w[9];
 #pragma unroll
-                for (int j = 0; j < 17; j++) w[j] = W[j];
-                const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(w[0] & 0xffffu)));
-                const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(w[8] >> 16)));
+                    for (int j = 0; j < 9; j++) w[j] = W[j];
+                    const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(w[0] & 0xffffu)));
 #pragma unroll
-                for (int c = 0; c < 4; c++) {  // block 0: quants at bytes 2..33
-                    const uint32_t q0 = __funnelshift_r(w[2 * c], w[2 * c + 1], 16);
-                    const uint32_t q1 = __funnelshift_r(w[2 * c + 1], w[2 * c + 2], 16);
-                    uint32_t v0, v1, v2, v3;
-                    dequant4(q0, d0, v0, v1);
-                    dequant4(q1, d0, v2, v3);
-                    st_chunk(atom, r, c, v0, v1, v2, v3);
+                    for (int c = 0; c < 4; c++) {
+                        const uint32_t q0 = __funnelshift_r(w[2 * c], w[2 * c + 1], 16);
+                        const uint32_t q1 = __funnelshift_r(w[2 * c + 1], w[2 * c + 2], 16);
+                        uint32_t v0, v1, v2, v3;
+                        dequant4(q0, d0, v0, v1);
+                        dequant4(q1, d0, v2, v3);
+                        st_chunk(atom, r, c, v0, v1, v2, v3);
+                    }
+                } else {  // block 1: d at bytes 34..35, quants at bytes 36..67 (words 9..16)
+                    uint32_t w[9];
+#pragma unroll
+                    for (int j = 0; j < 9; j++) w[j] = W[8 + j];
+                    const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(w[0] >> 16)));
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t v0, v1, v2, v3;
+                        dequant4(w[1 + 2 * c], d1, v0, v1);
+                        dequant4(w[2 + 2 * c], d1, v2, v3);
+                        st_chunk(atom, r, 4 + c, v0, v1, v2, v3);
+                    }
                 }
-#pragma unroll
-                for (int c = 0; c < 4; c++) {  // block 1: quants at bytes 36..67 (words 9..16)
-                    uint32_t v0, v1, v2, v3;
-                    dequant4(w[9 + 2 * c], d1, v0, v1);
-                    dequant4(w[10 + 2 * c], d1, v2, v3);
-                    st_chunk(atom, r, 4 + c, v0, v1, v2, v3);
-                }
-            } else if (s < kstages) {  // Q4_K: sub-blocks 2(s%4), 2(s%4)+1 of superblock s/4
-                const uint32_t* W = raw + r * RS;
+            } else if (s < kstages) {  // Q4_K: sub-block 2(s%4) + hh of superblock s/4
                 uint32_t hdr[4], q[8];
 #pragma unroll
                 for (int j = 0; j < 4; j++) hdr[j] = W[j];
@@ -223,31 +251,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int j = 0; j < 8; j++) q[j] = W[4 + j];
                 const float dd = __half2float(__ushort_as_half((uint16_t)(hdr[0] & 0xffffu)));
                 const uint32_t* sc = hdr + 1;
+                const int g = 2 * (s & 3) + hh;
+                int scv;
+                if (g < 4)
+                    scv = scale_byte(sc, g) & 63;
+                else
+                    scv = (scale_byte(sc, g + 4) & 0xF) | ((scale_byte(sc, g - 4) >> 6) << 4);
+                // the reference's tile loader stores half(d * sc) (refs.rs:709-712)
+                const __half2 d2 = __half2half2(__float2half_rn(dd * (float)scv));
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int g = 2 * (s & 3) + h;
-                    int scv;
-                    if (g < 4)
-                        scv = scale_byte(sc, g) & 63;
-                    else
-                        scv = (scale_byte(sc, g + 4) & 0xF) | ((scale_byte(sc, g - 4) >> 6) << 4);
-                    // the reference's tile loader stores half(d * sc) (refs.rs:709-712)
-                    const __half2 d2 = __half2half2(__float2half_rn(dd * (float)scv));
-#pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        uint32_t v0, v1, v2, v3;
-                        dequant4_u4(q[2 * c], 4 * h, d2, v0, v1);
-                        dequant4_u4(q[2 * c + 1], 4 * h, d2, v2, v3);
-                        st_chunk(atom, r, 4 * h + c, v0, v1, v2, v3);
-                    }
+                for (int c = 0; c < 4; c++) {
+                    uint32_t v0, v1, v2, v3;
+                    dequant4_u4(q[2 * c], 4 * hh, d2, v0, v1);
+                    dequant4_u4(q[2 * c + 1], 4 * hh, d2, v2, v3);
+                    st_chunk(atom, r, 4 * hh + c, v0, v1, v2, v3);
                 }
             } else {  // Q4_K correction stage: A[r][K + g] = half(-dmin * m_g) (refs.rs:712)
                 const int g0 = (s - kstages) * BK;
                 const int ngroups = (int)(a.K / 32);
                 const uint32_t row = row0 + r;
-                const uint8_t* rowp = row_ptr(row);
+                const uint8_t* rowp = xbase + (size_t)(min(row, a.nrows - 1) - row0) * a.stride_row_x * BB;
 #pragma unroll 1
-                for (int sbl = 0; sbl < BK / 8; sbl++) {  // 8 superblocks (8 groups each) per stage
+                for (int sbl = 4 * hh; sbl < 4 * hh + 4; sbl++) {  // 8 superblocks (8 groups each) per stage
                     const int gbase = g0 + 8 * sbl;
                     uint32_t hw0 = 0, hs[3] = {0, 0, 0};
                     if (row < a.nrows && gbase < ngroups) {
@@ -264,9 +289,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                         uint32_t hv[2];
 #pragma unroll
                         for (int e = 0; e < 2; e++) {
-                            const int g = 2 * p + e;
-                            const int mv = g < 4 ? (scale_byte(hs, g + 4) & 63)
-                                                 : ((scale_byte(hs, g + 4) >> 4) | ((scale_byte(hs, g) >> 6) << 4));
+                            const int gg = 2 * p + e;
+                            const int mv = gg < 4 ? (scale_byte(hs, gg + 4) & 63)
+                                                  : ((scale_byte(hs, gg + 4) >> 4) | ((scale_byte(hs, gg) >> 6) << 4));
                             hv[e] = gbase < ngroups ? (uint32_t)__half_as_ushort(__float2half_rn(-dmin * (float)mv)) : 0u;
                         }
                         v[p] = hv[0] | (hv[1] << 16);
@@ -276,10 +301,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             fence_proxy_async_smem();
             mbar_arrive(&full[slot]);
-            named_bar_sync(1, 128);  // raw slot s % NRAW may be refilled now
         }
         cp_async_wait<0>();
-        // ================= epilogue: TMEM -> registers -> dst =================
+        // ================= epilogue: TMEM -> shared -> dst (16-byte stores) =================
         if (tid == 0) {
             bool got = false;
             if (!*abort_flag) {
@@ -291,24 +315,27 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             *epi_ok = got ? 1 : 0;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, NPROD);
         tc_fence_after();
         if (*epi_ok) {
-            const uint32_t row = row0 + 32 * warp + lane;
-            for (uint32_t cb = 0; cb < bn; cb += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + cb, v);
-                tmem_ld_wait();
-                if (row < a.nrows) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const uint32_t col = col0 + cb + i;
-                        if (col < a.ncols_dst && cb + i < bn) dst[(size_t)col * a.stride_col_dst + row] = __uint_as_float(v[i]);
-                    }
+            // every MMA has completed: the A ring is free for the 4 KB per-warp staging buffers
+            float* buf = reinterpret_cast<float*>(sA) + warp * 1024;
+            const bool vec = (a.stride_col_dst & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+            tmem_tile_store(tmem, warp, lane, NPROD / 32, bn, buf, [&](uint32_t c, uint32_t rr, float4 f) {
+                const uint32_t col = col0 + c, row = row0 + rr;
+                if (col >= a.ncols_dst || row >= a.nrows) return;
+                float* p = dst + (size_t)col * a.stride_col_dst + row;
+                if (vec && row + 3 < a.nrows) {
+                    *reinterpret_cast<float4*>(p) = f;
+                } else {
+                    p[0] = f.x;
+                    if (row + 1 < a.nrows) p[1] = f.y;
+                    if (row + 2 < a.nrows) p[2] = f.z;
+                    if (row + 3 < a.nrows) p[3] = f.w;
                 }
-            }
+            });
         }
-    } else if (warp == 4) {
+    } else if (warp == MMA_WARP) {
         // ================= MMA issuer =================
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(BM, bn, 0);
@@ -350,7 +377,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, tmem_cols);
     }
@@ -454,9 +481,10 @@ unsigned int* device_error_ptr() {
     return p;
 }
 
+// Tile width: the fewest tiles of at most 256 columns, balanced (631 columns -> 3 x 224).
 uint32_t tile_n(uint32_t ncols_dst) {
-    if (ncols_dst >= 256) return 256;
-    return (ncols_dst + 15) / 16 * 16;
+    const uint32_t tiles = (ncols_dst + 255) / 256;
+    return ((ncols_dst + tiles - 1) / tiles + 15) / 16 * 16;
 }
 
 template <uint32_t TY>
@@ -475,6 +503,8 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     if (TY == T_Q8_0 && ((reinterpret_cast<uintptr_t>(x) & 3) || (srx & 1) || (scx & 1) || (ssx & 1)))
         return (int)cudaErrorInvalidValue;
     if (TY == T_Q4_K && (reinterpret_cast<uintptr_t>(x) & 3)) return (int)cudaErrorInvalidValue;
+    // the producers address a tile's 128 rows with 32-bit offsets
+    if ((uint64_t)BM * srx * (TY == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES) >= (1ull << 31)) return (int)cudaErrorInvalidValue;
     const uint32_t Kc = TY == T_Q4_K ? (K / 32 + BK - 1) / BK * BK : 0;
     const uint32_t Kt = K + Kc;
     const uint32_t planes = nch * ns;
