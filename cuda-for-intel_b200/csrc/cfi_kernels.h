@@ -39,4 +39,25 @@ const void* cfi_native_rope_neox(int forward, int has_ff);     // rope_neox<fwd,
 const void* cfi_native_soft_max(int mask_f16);                  // soft_max_f32<*, *, *, T>
 constexpr int CFI_ROWOP_THREADS = 256;
 
-// k_gemm_sm100.cu: tcgen05 GEMMs (own launch code; see cfi_gemm.h)
+// k_gemm_sm100.cu: tcgen05 GEMM on K-major fp16/bf16 operands, fp32 accumulation:
+//   C[plane][col][row] = alpha * sum_k A[aplane][row][k] * B[plane][col][k] (+ beta * C)
+// Output plane p: channel p % nch, sample p / nch; its A plane (sample / smr) * (nch / chr) +
+// channel / chr.  Strides in elements.  Returns 0 when launched, -1 when the operands cannot be
+// described by tensor maps (alignment), or a CUDA error code.
+struct TcGemm {
+    const void* a;
+    const void* b;
+    void* c;
+    int fmt;  // 0 f16, 1 bf16
+    uint32_t m, n, k;
+    uint64_t lda, ldb, a_plane, b_plane;
+    uint32_t a_planes, nch, nsamples, chr, smr;
+    int c_type;  // CFI_R_32F / 16F / 16BF
+    uint64_t ldc;
+    long long c_zstride, c_wstride;
+    float alpha, beta;
+    const void* alpha_ptr;
+    const void* beta_ptr;
+    int scalar_f16;
+};
+int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream);

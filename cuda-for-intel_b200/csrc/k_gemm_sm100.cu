@@ -9,8 +9,9 @@
 //     zero), strided batches as the third tensor dimension;
 //   * one thread of warp 4 issues tcgen05.mma kind::f16 (M 128, N BN <= 256, K 16) into an fp32
 //     accumulator in tensor memory;
-//   * warps 0-3 apply alpha/beta and store C in its dtype (f32, f16 or bf16) in runs of 4 rows
-//     (accumulator chunks transposed through shared memory).
+//   * warps 0-3 apply alpha/beta and store C: f32 with beta 0 through TMA tensor stores of
+//     32 x 32 chunks, otherwise in its dtype (f32, f16 or bf16) in runs of 4 rows (accumulator
+//     chunks transposed through shared memory).
 // Every other legal call (other transposes, f32 inputs, device pointer arrays) runs a tiled SIMT
 // kernel with fp32 accumulation.  Validation follows cuBLAS (plan.rs:160-215).
 #include <cuda.h>
@@ -24,6 +25,7 @@
 #include "cfi_common.cuh"
 #include "sm100_ptx.cuh"
 #include "tc_epilogue.cuh"
+#include "cfi_kernels.h"
 
 namespace {
 
@@ -37,13 +39,15 @@ static __device__ unsigned int g_gemm_error;
 
 struct GemmArgs {
     void* c;
-    long long stride_c;
+    long long c_zstride, c_wstride;  // elements between output channel / sample planes
     int c_type, ldc;
     uint32_t m, n, k, bn;
+    uint32_t nch, chr, smr, nch_x;   // output plane p: channel p % nch, sample p / nch; A plane below
     float alpha, beta;
     const void* alpha_ptr;  // device pointer mode
     const void* beta_ptr;
     int scalar_f16;
+    int tma_c;  // C is f32, beta 0 and host scalars: the epilogue stores through tmc
     unsigned int* err;
 };
 
@@ -67,7 +71,8 @@ CFI_DEV void st_elem(void* p, size_t i, int t, float v) {
 
 template <int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
-    cfi_gemm_tc(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs a) {
+    cfi_gemm_tc(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                const __grid_constant__ CUtensorMap tmc, const GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
@@ -84,6 +89,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
     const int ksteps = (int)((a.k + BK - 1) / BK);
     const uint32_t m0 = blockIdx.x * BM, n0 = blockIdx.y * bn, z = blockIdx.z;
+    // output plane z = (sample wt, channel zt); its A plane follows the channel / sample ratios
+    const uint32_t wt = z / a.nch, zt = z - wt * a.nch;
+    const uint32_t za = (wt / a.smr) * a.nch_x + zt / a.chr;
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; i++) {
@@ -116,7 +124,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                tma_load_3d(sA + slot * A_STAGE, &tma, s * BK, (int)m0, (int)z, &full[slot]);
+                tma_load_3d(sA + slot * A_STAGE, &tma, s * BK, (int)m0, (int)za, &full[slot]);
                 tma_load_3d(sB + slot * B_STAGE, &tmb, s * BK, (int)n0, (int)z, &full[slot]);
             }
         }
@@ -160,8 +168,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (*epi_ok) {
             const float alpha = a.alpha_ptr ? load_scalar(a.alpha_ptr, a.scalar_f16) : a.alpha;
             const float beta = a.beta_ptr ? load_scalar(a.beta_ptr, a.scalar_f16) : a.beta;
+            if (a.tma_c) {
+                // every MMA has completed: the A ring holds the 8 KB per-warp staging buffers
+                float* tbuf = reinterpret_cast<float*>(sA) + warp * 2048;
+                tmem_tile_tma_store(tmem, warp, lane, 4, bn, tbuf, &tmc, (int)m0, (int)n0, (int)zt, (int)wt,
+                                    [&](float v) { return alpha * v; });
+            } else {
             const int ct = a.c_type, es = ct == CFI_R_32F ? 4 : 2;
-            uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)z * (size_t)a.stride_c * es;
+            uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)((long long)zt * a.c_zstride + (long long)wt * a.c_wstride) * es;
             // 4 consecutive rows as one 16-byte (f32) or 8-byte (f16/bf16) access
             const bool vec = (a.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(cz) & (uintptr_t)(4 * es - 1)) == 0;
             // every MMA has completed: the A ring is free for the 4 KB per-warp staging buffers
@@ -210,6 +224,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             });
+            }
         }
     }
     tc_fence_before();
@@ -325,6 +340,83 @@ bool dtype_ok(int t) { return t == CFI_R_32F || t == CFI_R_16F || t == CFI_R_16B
 
 }  // namespace
 
+// Shared tensor-core launcher (the cuBLAS-compatible GEMM and the prefill mul_mat_q use it).
+// Returns 0 on launch, -1 when the descriptor cannot be expressed with tensor maps (the caller
+// then takes another path), or a CUDA error code.
+int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
+    PFN_encodeTiled enc = encode_fn();
+    if (!enc) return -1;
+    if ((d.lda % 8) || (d.ldb % 8) || (d.a_plane % 8) || (d.b_plane % 8) || d.k == 0 ||
+        (reinterpret_cast<uintptr_t>(d.a) & 15) || (reinterpret_cast<uintptr_t>(d.b) & 15) || d.nch == 0 || d.nsamples == 0 ||
+        d.chr == 0 || d.smr == 0 || d.nch % d.chr)
+        return -1;
+    const uint32_t planes = d.nch * d.nsamples;
+    // balanced tiles; a multiple of 32 columns when there are several (the epilogue writes
+    // whole 32-column chunks)
+    const uint32_t tiles_n = (d.n + 255) / 256;
+    const uint32_t per = (d.n + tiles_n - 1) / tiles_n;
+    const uint32_t bn = tiles_n > 1 ? (per + 31) / 32 * 32 : (per + 15) / 16 * 16;
+    const CUtensorMapDataType dt = d.fmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap ta, tb, tcm;
+    cuuint64_t da[3] = {d.k, d.m, d.a_planes};
+    cuuint64_t sA[2] = {d.lda * 2, d.a_plane * 2};
+    cuuint64_t db[3] = {d.k, d.n, planes};
+    cuuint64_t sB[2] = {d.ldb * 2, d.b_plane * 2};
+    cuuint32_t boxa[3] = {BK, BM, 1}, boxb[3] = {BK, bn, 1}, es[3] = {1, 1, 1};
+    if (enc(&ta, dt, 3, const_cast<void*>(d.a), da, sA, boxa, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&tb, dt, 3, const_cast<void*>(d.b), db, sB, boxb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return -1;
+    // C through TMA stores: f32, beta 0 known on the host, 16-byte multiple strides, aligned base
+    memset(&tcm, 0, sizeof tcm);
+    bool tma_c = d.c_type == CFI_R_32F && !d.alpha_ptr && !d.beta_ptr && d.beta == 0.0f && (d.ldc % 4) == 0 &&
+                 (reinterpret_cast<uintptr_t>(d.c) & 15) == 0 && (d.nch == 1 || d.c_zstride % 4 == 0) &&
+                 (d.nsamples == 1 || d.c_wstride % 4 == 0);
+    if (tma_c) {
+        const cuuint64_t s1 = d.ldc * 4;
+        const cuuint64_t s2 = d.nch > 1 ? (cuuint64_t)d.c_zstride * 4 : s1 * d.n;
+        const cuuint64_t s3 = d.nsamples > 1 ? (cuuint64_t)d.c_wstride * 4 : s2 * d.nch;
+        cuuint64_t dc[4] = {d.m, d.n, d.nch, d.nsamples};
+        cuuint64_t scs[3] = {s1, (s2 + 15) & ~(cuuint64_t)15, (s3 + 15) & ~(cuuint64_t)15};
+        cuuint32_t boxc[4] = {32, 32, 1, 1}, esc[4] = {1, 1, 1, 1};
+        tma_c = enc(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d.c, dc, scs, boxc, esc, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    GemmArgs g;
+    g.c = d.c;
+    g.c_zstride = d.c_zstride;
+    g.c_wstride = d.c_wstride;
+    g.c_type = d.c_type;
+    g.ldc = (int)d.ldc;
+    g.m = d.m;
+    g.n = d.n;
+    g.k = d.k;
+    g.bn = bn;
+    g.nch = d.nch;
+    g.chr = d.chr;
+    g.smr = d.smr;
+    g.nch_x = d.nch / d.chr;
+    g.alpha = d.alpha;
+    g.beta = d.beta;
+    g.alpha_ptr = d.alpha_ptr;
+    g.beta_ptr = d.beta_ptr;
+    g.scalar_f16 = d.scalar_f16;
+    g.tma_c = tma_c ? 1 : 0;
+    g.err = err_ptr();
+    static std::once_flag attr;
+    std::call_once(attr, [] {
+        cudaFuncSetAttribute(cfi_gemm_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+        cudaFuncSetAttribute(cfi_gemm_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    });
+    dim3 grid((d.m + BM - 1) / BM, (d.n + bn - 1) / bn, planes);
+    if (d.fmt == 0)
+        cfi_gemm_tc<0><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tcm, g);
+    else
+        cfi_gemm_tc<1><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tcm, g);
+    return (int)cudaGetLastError();
+}
+
 // Reads and clears the error word of the GEMM kernel's bounded waits (folded into cfi_device_error).
 unsigned int cfi_gemm_error_take() {
     unsigned int v = 0, z = 0;
@@ -421,54 +513,38 @@ int gemm_common(cfi_blas* h, int transa, int transb, int m, int n, int k, const 
                     (reinterpret_cast<uintptr_t>(A) & 15) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
                     (batch == 1 || ((sa % 8) == 0 && (sb % 8) == 0 && sa > 0 && sb > 0));
     if (tc) {
-        PFN_encodeTiled enc = encode_fn();
-        if (enc) {
-            const uint32_t tiles_n = ((uint32_t)n + 255) / 256;
-            const uint32_t bn = (((uint32_t)n + tiles_n - 1) / tiles_n + 15) / 16 * 16;  // balanced tiles
-            const CUtensorMapDataType dt = a_type == CFI_R_16F ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-            CUtensorMap ta, tb;
-            cuuint64_t da[3] = {(cuuint64_t)k, (cuuint64_t)m, (cuuint64_t)batch};
-            cuuint64_t sA[2] = {(cuuint64_t)lda * 2, (cuuint64_t)(batch > 1 ? sa : (long long)lda * m) * 2};
-            cuuint64_t db[3] = {(cuuint64_t)k, (cuuint64_t)n, (cuuint64_t)batch};
-            cuuint64_t sB[2] = {(cuuint64_t)ldb * 2, (cuuint64_t)(batch > 1 ? sb : (long long)ldb * n) * 2};
-            sA[1] = (sA[1] + 15) & ~(cuuint64_t)15;
-            sB[1] = (sB[1] + 15) & ~(cuuint64_t)15;
-            cuuint32_t boxa[3] = {BK, BM, 1}, boxb[3] = {BK, bn, 1}, es[3] = {1, 1, 1};
-            CUresult r1 = enc(&ta, dt, 3, const_cast<void*>(A), da, sA, boxa, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            CUresult r2 = enc(&tb, dt, 3, const_cast<void*>(B), db, sB, boxb, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS) {
-                GemmArgs g;
-                g.c = C;
-                g.stride_c = batch > 1 ? sc : 0;
-                g.c_type = c_type;
-                g.ldc = ldc;
-                g.m = (uint32_t)m;
-                g.n = (uint32_t)n;
-                g.k = (uint32_t)k;
-                g.bn = bn;
-                g.alpha = al;
-                g.beta = be;
-                g.alpha_ptr = dev_ptrs ? alpha : nullptr;
-                g.beta_ptr = dev_ptrs ? beta : nullptr;
-                g.scalar_f16 = sf16;
-                g.err = err_ptr();
-                static std::once_flag attr;
-                std::call_once(attr, [] {
-                    cudaFuncSetAttribute(cfi_gemm_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-                    cudaFuncSetAttribute(cfi_gemm_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-                });
-                dim3 grid((m + BM - 1) / BM, (n + bn - 1) / bn, batch);
-                if (a_type == CFI_R_16F)
-                    cfi_gemm_tc<0><<<grid, THREADS, SMEM_BYTES, h->stream>>>(ta, tb, g);
-                else
-                    cfi_gemm_tc<1><<<grid, THREADS, SMEM_BYTES, h->stream>>>(ta, tb, g);
-                if (cudaGetLastError() != cudaSuccess) return CFI_BLAS_EXECUTION_FAILED;
-                h->last_path = 1;
-                return CFI_BLAS_SUCCESS;
-            }
+        TcGemm d;
+        d.a = A;
+        d.b = B;
+        d.c = C;
+        d.fmt = a_type == CFI_R_16F ? 0 : 1;
+        d.m = (uint32_t)m;
+        d.n = (uint32_t)n;
+        d.k = (uint32_t)k;
+        d.lda = (uint64_t)lda;
+        d.ldb = (uint64_t)ldb;
+        d.a_plane = batch > 1 ? (uint64_t)sa : (uint64_t)lda * m;
+        d.b_plane = batch > 1 ? (uint64_t)sb : (uint64_t)ldb * n;
+        d.a_planes = (uint32_t)batch;
+        d.nch = (uint32_t)batch;
+        d.nsamples = 1;
+        d.chr = 1;
+        d.smr = 1;
+        d.c_type = c_type;
+        d.ldc = (uint64_t)ldc;
+        d.c_zstride = batch > 1 ? sc : (long long)ldc * n;
+        d.c_wstride = 0;
+        d.alpha = al;
+        d.beta = be;
+        d.alpha_ptr = dev_ptrs ? alpha : nullptr;
+        d.beta_ptr = dev_ptrs ? beta : nullptr;
+        d.scalar_f16 = sf16;
+        const int rc = cfi_tc_gemm(d, h->stream);
+        if (rc == 0) {
+            h->last_path = 1;
+            return CFI_BLAS_SUCCESS;
         }
+        if (rc > 0) return CFI_BLAS_EXECUTION_FAILED;
     }
     SimtArgs p;
     p.a = A;

@@ -16,8 +16,8 @@
 //      term); one reducing named barrier per stage;
 //   4. one thread of warp 8 issues tcgen05.mma kind::f16 (M=128, N=BN, K=16) with the fp32
 //      accumulator in tensor memory; commits free each pipeline slot;
-//   5. warps 0-7 drain TMEM (tcgen05.ld 32x32b), transpose 32x32 chunks through shared memory
-//      and store 16-byte runs of rows.
+//   5. warps 0-7 drain TMEM (tcgen05.ld 32x32b) into 32x32 chunks in shared memory, stored by
+//      TMA (or, for strides TMA cannot describe, as 16-byte runs of rows).
 // Integer exactness does not apply here: fp16 rounding of q*d keeps the result within 1e-3
 // relative L2 of the reference (measured ~1e-4), the bound this path is held to.
 #include <cuda.h>
@@ -64,6 +64,7 @@ struct MmqArgs {
     uint32_t nchannels_y, channel_ratio, sample_ratio;
     uint32_t stride_channel_x, stride_sample_x;    // blocks
     uint32_t stride_channel_dst, stride_sample_dst;
+    int tma_c;  // dst stored through tmap_c (16-byte aligned column, channel and sample strides)
     unsigned int* err;
 };
 
@@ -115,7 +116,7 @@ CFI_DEV bool named_bar_and(int id, int n, bool v) {
 // and afterwards the epilogue; 8 tensor memory + MMA issue; 9 activation TMA.
 template <uint32_t TY>
 __global__ void __launch_bounds__(THREADS, 1)
-    cfi_mmq_tc(const __grid_constant__ CUtensorMap tmap_b, const MmqArgs a) {
+    cfi_mmq_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_c, const MmqArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(&full[i], NPROD + 1);  // the producers + the TMA thread's expect_tx
+            mbar_init(&full[i], NPROD / 32 + 1);  // one arrival per producer warp + the TMA thread's expect_tx
             mbar_init(&empty[i], 1);         // tcgen05.commit
         }
         mbar_init(done, 1);
@@ -200,9 +201,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             cp_async_wait<NRAW - 2>();  // this thread's copies of stage s have landed
             const int slot = s % NSTAGE;
             const uint32_t round = (uint32_t)(s / NSTAGE);
-            bool ok = mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag);
-            // every producer's stage-s copies are visible, every producer finished stage s-1
-            // (its raw slot may be refilled), and the MMA released this A slot -- on all or none
+            bool ok = lane != 0 || mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag);
+            // (lane 0 of each warp waits for the MMA to release this A slot)  every producer's
+            // stage-s copies are visible, every producer finished stage s-1 (its raw slot may be
+            // refilled), and the slot is free -- on all threads or none
             ok = named_bar_and(1, NPROD, ok);
             if (!ok) {
                 if (tid == 0) {
@@ -299,8 +301,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     st_chunk(atom, r, sbl, v[0], v[1], v[2], v[3]);
                 }
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&full[slot]);
+            fence_proxy_async_smem();  // this thread's A-tile writes, visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[slot]);
         }
         cp_async_wait<0>();
         // ================= epilogue: TMEM -> shared -> dst (16-byte stores) =================
@@ -317,7 +320,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         named_bar_sync(1, NPROD);
         tc_fence_after();
-        if (*epi_ok) {
+        if (*epi_ok && a.tma_c) {
+            // every MMA has completed: the A ring holds the 8 KB per-warp staging buffers
+            float* tbuf = reinterpret_cast<float*>(sA) + warp * 2048;
+            tmem_tile_tma_store(tmem, warp, lane, NPROD / 32, bn, tbuf, &tmap_c, (int)row0, (int)col0, (int)zt, (int)wt,
+                                [](float v) { return v; });
+        } else if (*epi_ok) {
             // every MMA has completed: the A ring is free for the 4 KB per-warp staging buffers
             float* buf = reinterpret_cast<float*>(sA) + warp * 1024;
             const bool vec = (a.stride_col_dst & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
@@ -421,6 +429,86 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Weights -> fp16 K-major rows: Wh[xplane][row][k].  Q8_0: fp16(q * d).  Q4_K: fp16(q *
+// half(d * sc)) and, in the appended columns K + g, half(-dmin * m_g) (the terms the fused kernel
+// builds in shared memory; refs.rs:709-712), zero up to Kt.  One thread per weight block
+// (Q8_0: 32 values, Q4_K: 256 values), consecutive threads on consecutive blocks of a row.
+template <uint32_t TY>
+__global__ void __launch_bounds__(256)
+    cfi_mmq_w_to_f16(const uint8_t* __restrict__ x, __half* __restrict__ wh, uint32_t K, uint32_t Kt, uint32_t nrows,
+                     uint32_t srx, uint32_t nch_x, uint32_t scx, uint32_t ssx) {
+    constexpr uint32_t QKB = TY == T_Q4_K ? QK_K : QK8_0;
+    const uint32_t nb = K / QKB;
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (uint64_t)nrows * nb) return;
+    const uint32_t row = (uint32_t)(t / nb), b = (uint32_t)(t - (uint64_t)row * nb);
+    const uint32_t xp = blockIdx.y, sx = xp / nch_x, cx = xp - sx * nch_x;
+    __half* out = wh + ((size_t)xp * nrows + row) * Kt;
+    if (TY == T_Q8_0) {
+        const uint8_t* blk = x + ((size_t)sx * ssx + (size_t)cx * scx + (size_t)row * srx + b) * Q8_0_BYTES;
+        const uint32_t* wa = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(blk) & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(blk) & 3) * 8;  // 0 or 16
+        // the 9 aligned words that hold the 34-byte block (the bytes outside it share a word
+        // with block bytes, so no page is touched that the block does not touch)
+        uint32_t w[9];
+#pragma unroll
+        for (int i = 0; i < 9; i++) w[i] = __ldg(wa + i);
+        const uint16_t dbits = (uint16_t)(__funnelshift_r(w[0], w[1], sh) & 0xffffu);
+        const __half2 d2 = __half2half2(__ushort_as_half(dbits));
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t q = __funnelshift_r(w[i], w[i + 1], sh + 16);  // quants start 2 bytes in
+            uint32_t lo, hi;
+            dequant4(sh + 16 >= 32 ? w[i + 1] : q, d2, lo, hi);
+            v[2 * i] = lo;
+            v[2 * i + 1] = hi;
+        }
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)b * 32);
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+        const uint4* blk = reinterpret_cast<const uint4*>(x + ((size_t)sx * ssx + (size_t)cx * scx + (size_t)row * srx + b) * Q4_K_BYTES);
+        const uint4 h = __ldg(blk);
+        const uint32_t hs[3] = {h.y, h.z, h.w};
+        const float dd = __half2float(__ushort_as_half((uint16_t)(h.x & 0xffffu)));
+        const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)b * 256);
+        uint32_t corr[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {  // 32 bytes of nibbles: sub-blocks 2c (low) and 2c+1 (high)
+            const uint4 q0 = __ldg(blk + 1 + 2 * c), q1 = __ldg(blk + 2 + 2 * c);
+            const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            uint32_t hv[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int g = 2 * c + e;
+                int scv, mv;
+                if (g < 4) {
+                    scv = scale_byte(hs, g) & 63;
+                    mv = scale_byte(hs, g + 4) & 63;
+                } else {
+                    scv = (scale_byte(hs, g + 4) & 0xF) | ((scale_byte(hs, g - 4) >> 6) << 4);
+                    mv = (scale_byte(hs, g + 4) >> 4) | ((scale_byte(hs, g) >> 6) << 4);
+                }
+                const __half2 d2 = __half2half2(__float2half_rn(dd * (float)scv));
+                hv[e] = (uint32_t)__half_as_ushort(__float2half_rn(-dmin * (float)mv));
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    uint32_t a0, a1, b0, b1;
+                    dequant4_u4(q[i], 4 * e, d2, a0, a1);
+                    dequant4_u4(q[i + 1], 4 * e, d2, b0, b1);
+                    o[g * 4 + i / 2] = make_uint4(a0, a1, b0, b1);
+                }
+            }
+            corr[c] = hv[0] | (hv[1] << 16);
+        }
+        *reinterpret_cast<uint4*>(out + K + (size_t)b * 8) = make_uint4(corr[0], corr[1], corr[2], corr[3]);
+        if (b == 0)  // the padding of the appended columns, once per row
+            for (uint32_t k = K + K / 32; k < Kt; k++) out[k] = __float2half(0.0f);
+    }
+}
+
 // ---- host side ----
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -482,9 +570,11 @@ unsigned int* device_error_ptr() {
 }
 
 // Tile width: the fewest tiles of at most 256 columns, balanced (631 columns -> 3 x 224).
+// (a multiple of 32 when there are several: the epilogue writes whole 32-column chunks).
 uint32_t tile_n(uint32_t ncols_dst) {
     const uint32_t tiles = (ncols_dst + 255) / 256;
-    return ((ncols_dst + tiles - 1) / tiles + 15) / 16 * 16;
+    const uint32_t per = (ncols_dst + tiles - 1) / tiles;
+    return tiles > 1 ? (per + 31) / 32 * 32 : (per + 15) / 16 * 16;
 }
 
 template <uint32_t TY>
@@ -510,12 +600,17 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     const uint32_t planes = nch * ns;
     void* xh = nullptr;
     const size_t xh_bytes = (size_t)planes * ncols_dst * Kt * 2;
+    // weight planes: (samples / sample_ratio) x (channels / channel_ratio)
+    const uint32_t nch_x = nch / chr, planes_x = (ns / smr) * nch_x;
+    if (nch % chr || ns % smr) return (int)cudaErrorInvalidValue;
+    const size_t xh_pad = (xh_bytes + 255) & ~(size_t)255;
+    const size_t wh_bytes = (size_t)planes_x * nrows * Kt * 2;
     int rc = 0;
     if (fixed_xh) {
         if (xh_bytes > fixed_cap) return (int)cudaErrorInvalidValue;
         xh = fixed_xh;
     } else {
-        rc = scratch_for(xh_bytes, stream, &xh);
+        rc = scratch_for(xh_pad + wh_bytes, stream, &xh);
     }
     if (rc) return rc;
     // 1. activations -> fp16 K-major
@@ -529,6 +624,45 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
         rc = (int)cudaGetLastError();
         if (rc) return rc;
     }
+    if (!fixed_xh) {
+        // 2. weights -> fp16 K-major, then the shared TMA-fed tcgen05 GEMM (C = Wh Xh^T per plane)
+        __half* wh = reinterpret_cast<__half*>(static_cast<uint8_t*>(xh) + xh_pad);
+        const uint64_t nblk = (uint64_t)nrows * (K / (TY == T_Q4_K ? QK_K : QK8_0));
+        dim3 wgrid((uint32_t)((nblk + 255) / 256), planes_x);
+        cfi_mmq_w_to_f16<TY><<<wgrid, 256, 0, stream>>>(x, wh, K, Kt, nrows, srx, nch_x, scx, ssx);
+        rc = (int)cudaGetLastError();
+        if (rc) return rc;
+        TcGemm d;
+        d.a = wh;
+        d.b = xh;
+        d.c = dst;
+        d.fmt = 0;
+        d.m = nrows;
+        d.n = ncols_dst;
+        d.k = Kt;
+        d.lda = Kt;
+        d.ldb = Kt;
+        d.a_plane = (uint64_t)nrows * Kt;
+        d.b_plane = (uint64_t)ncols_dst * Kt;
+        d.a_planes = planes_x;
+        d.nch = nch;
+        d.nsamples = ns;
+        d.chr = chr;
+        d.smr = smr;
+        d.c_type = 0;  // f32
+        d.ldc = scd;
+        d.c_zstride = scdst;
+        d.c_wstride = ssd;
+        d.alpha = 1.0f;
+        d.beta = 0.0f;
+        d.alpha_ptr = nullptr;
+        d.beta_ptr = nullptr;
+        d.scalar_f16 = 0;
+        rc = cfi_tc_gemm(d, stream);
+        return rc < 0 ? (int)cudaErrorInvalidValue : rc;
+    }
+    // fixed scratch (no room for the fp16 weights): the fused kernel dequantizes weight tiles in
+    // shared memory
     // 2. tensor map over Xh: dims (Kt, ncols, planes), box (64, BN, 1), 128-byte swizzle
     const uint32_t bn = tile_n(ncols_dst);
     PFN_encodeTiled enc = encode_fn();
@@ -541,7 +675,23 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, xh, gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return (int)cudaErrorInvalidValue;
+    // dst through TMA stores when its strides allow (16-byte multiples, aligned base)
+    CUtensorMap tmap_c;
+    memset(&tmap_c, 0, sizeof tmap_c);
+    bool tma_c = (scd % 4) == 0 && (nch == 1 || scdst % 4 == 0) && (ns == 1 || ssd % 4 == 0) &&
+                 (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+    if (tma_c) {
+        const cuuint64_t s1 = (cuuint64_t)scd * 4;
+        const cuuint64_t s2 = nch > 1 ? (cuuint64_t)scdst * 4 : s1 * ncols_dst;
+        const cuuint64_t s3 = ns > 1 ? (cuuint64_t)ssd * 4 : s2 * nch;
+        cuuint64_t dc[4] = {nrows, ncols_dst, nch, ns};
+        cuuint64_t scs[3] = {s1, (s2 + 15) & ~(cuuint64_t)15, (s3 + 15) & ~(cuuint64_t)15};
+        cuuint32_t boxc[4] = {32, 32, 1, 1}, esc[4] = {1, 1, 1, 1};
+        tma_c = enc(&tmap_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dst, dc, scs, boxc, esc, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
     MmqArgs a;
+    a.tma_c = tma_c ? 1 : 0;
     a.x = x;
     a.dst = dst;
     a.K = K;
@@ -564,7 +714,7 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
         cudaFuncSetAttribute(cfi_mmq_tc<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     });
     dim3 grid((nrows + BM - 1) / BM, (ncols_dst + bn - 1) / bn, planes);
-    cfi_mmq_tc<TY><<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, a);
+    cfi_mmq_tc<TY><<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, tmap_c, a);
     return (int)cudaGetLastError();
 }
 
