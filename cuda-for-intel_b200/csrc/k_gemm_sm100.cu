@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // launched early (programmatic dependent launch): the operands may come from the previous kernel
 
     if (warp == 5) {
         if (lane == 0) {
@@ -235,6 +236,149 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---- 2-SM variant: a cluster of 2 CTAs computes a 256-row tile with tcgen05.mma.cta_group::2 ----
+// CTA r of the pair holds rows 128 r .. 128 r + 127 of the tile (A) and columns r BN/2 .. of B; the
+// leader (r = 0) issues the MMA (M 256, N BN) over both CTAs' shared memory, each CTA's TMEM gets
+// its own 128 rows.  Both CTAs' TMA loads complete on the leader's `full` barrier; the leader's
+// commits arrive on both CTAs' `empty` and `done` barriers.  Half-width B stages let 6 stages fit.
+constexpr int NSTAGE2 = 6;
+constexpr int A2_STAGE = BM * BK * 2;   // 16 KB
+constexpr int B2_STAGE = 128 * BK * 2;  // 16 KB: half of BN <= 256
+constexpr size_t SMEM2_BYTES = 1024 + (size_t)NSTAGE2 * (A2_STAGE + B2_STAGE) + 256;
+
+template <int FMT>
+__global__ void __launch_bounds__(THREADS, 1)
+    cfi_gemm_tc2(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                 const __grid_constant__ CUtensorMap tmc, const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + NSTAGE2 * A2_STAGE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + NSTAGE2 * B2_STAGE);
+    uint64_t* empty = full + NSTAGE2;
+    uint64_t* done = empty + NSTAGE2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* epi_ok = abort_flag + 1;
+
+    const uint32_t rank = cluster_ctarank();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t bn = a.bn, half = bn / 2;
+    const uint32_t tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+    const int ksteps = (int)((a.k + BK - 1) / BK);
+    const uint32_t m0 = (blockIdx.x >> 1) * (2 * BM) + rank * BM, n0 = blockIdx.y * bn, z = blockIdx.z;
+    const uint32_t wt = z / a.nch, zt = z - wt * a.nch;
+    const uint32_t za = (wt / a.smr) * a.nch_x + zt / a.chr;
+
+    if (tid == 0) {
+        for (int i = 0; i < NSTAGE2; i++) {
+            mbar_init(&full[i], 1);   // the leader's expect_tx (bytes of both CTAs)
+            mbar_init(&empty[i], 1);  // the leader's tcgen05.commit
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 4) {
+        tmem_alloc2(tmem_slot, tmem_cols);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA arrive
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // launched early (programmatic dependent launch): the operands may come from the previous kernel
+
+    if (warp == 5) {
+        if (lane == 0) {
+            prefetch_tmap(&tma);
+            prefetch_tmap(&tmb);
+            const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);
+            const uint32_t bytes = 2u * (uint32_t)(A2_STAGE + half * BK * 2);
+            for (int s = 0; s < ksteps; s++) {
+                const int slot = s % NSTAGE2;
+                if (!mbar_wait(&empty[slot], ((uint32_t)(s / NSTAGE2) & 1) ^ 1, abort_flag)) {
+                    cfi_set_error(a.err, 0x800 + slot);
+                    *abort_flag = 1;
+                    break;
+                }
+                if (rank == 0) mbar_arrive_expect_tx(&full[slot], bytes);
+                const uint32_t fb = full0 + (uint32_t)slot * 8u;
+                tma_load_3d_2sm(sA + slot * A2_STAGE, &tma, s * BK, (int)m0, (int)za, fb);
+                tma_load_3d_2sm(sB + slot * B2_STAGE, &tmb, s * BK, (int)(n0 + rank * half), (int)z, fb);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 4) {
+        if (rank == 0 && lane == 0) {
+            const uint32_t idesc = idesc_f16(2 * BM, bn, FMT);
+            for (int s = 0; s < ksteps; s++) {
+                const int slot = s % NSTAGE2;
+                if (!mbar_wait(&full[slot], (uint32_t)(s / NSTAGE2) & 1, abort_flag)) {
+                    cfi_set_error(a.err, 0x900 + slot);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ab = smem_u32(sA + slot * A2_STAGE), bb = smem_u32(sB + slot * B2_STAGE);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++)
+                    mma2_f16(tmem, sw128_kmajor_desc(ab + 32 * kk), sw128_kmajor_desc(bb + 32 * kk), idesc,
+                             (s > 0 || kk > 0) ? 1u : 0u);
+                mma2_commit_mc(&empty[slot], 0x3);
+            }
+            mma2_commit_mc(done, 0x3);  // also after a failure: the MMAs already issued
+        }
+        __syncwarp();
+    } else {
+        // ================= epilogue (warps 0-3: this CTA's 128 TMEM lanes) =================
+        if (tid == 0) {
+            const bool got = mbar_wait(done, 0, abort_flag);
+            if (!got) {
+                cfi_set_error(a.err, 0xA00);
+                *abort_flag = 1;
+            }
+            *epi_ok = got ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        tc_fence_after();
+        if (*epi_ok) {
+            const float alpha = a.alpha_ptr ? load_scalar(a.alpha_ptr, a.scalar_f16) : a.alpha;
+            const float beta = a.beta_ptr ? load_scalar(a.beta_ptr, a.scalar_f16) : a.beta;
+            if (a.tma_c) {
+                float* tbuf = reinterpret_cast<float*>(sA) + warp * 2048;
+                tmem_tile_tma_store(tmem, warp, lane, 4, bn, tbuf, &tmc, (int)m0, (int)n0, (int)zt, (int)wt,
+                                    [&](float v) { return alpha * v; });
+            } else {
+                const int ct = a.c_type, es = ct == CFI_R_32F ? 4 : 2;
+                uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)((long long)zt * a.c_zstride + (long long)wt * a.c_wstride) * es;
+                float* buf = reinterpret_cast<float*>(sA) + warp * 1024;
+                tmem_tile_store(tmem, warp, lane, 4, bn, buf, [&](uint32_t c, uint32_t rr, float4 f) {
+                    const uint32_t col = n0 + c, row = m0 + rr;
+                    if (col >= a.n || row >= a.m) return;
+                    const size_t ci = (size_t)col * a.ldc + row;
+                    const float r[4] = {alpha * f.x, alpha * f.y, alpha * f.z, alpha * f.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        if (row + e >= a.m) break;
+                        float v = r[e];
+                        if (beta != 0.0f) v += beta * ld_elem(cz, ci + e, ct);
+                        st_elem(cz, ci + e, ct, v);
+                    }
+                });
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // neither CTA leaves while the pair still reads its TMEM or shared memory
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc2(tmem, tmem_cols);
+    }
+}
+
 // Tiled SIMT GEMM: 16 x 16 output tile per block, any op/dtype combination, fp32 accumulation.
 // `ptrs` non-zero: A, B, C are device arrays of per-batch pointers (cublasGemmBatchedEx).
 struct SimtArgs {
@@ -355,14 +499,26 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
     // whole 32-column chunks)
     const uint32_t tiles_n = (d.n + 255) / 256;
     const uint32_t per = (d.n + tiles_n - 1) / tiles_n;
-    const uint32_t bn = tiles_n > 1 ? (per + 31) / 32 * 32 : (per + 15) / 16 * 16;
+    // CTA pairs (2-SM MMA, half-width B tiles) for more than one 128-row tile; CFI_GEMM_2SM=0 off
+    // pairs pay off once the single-SM grid needs two or more waves (measured: single-wave, short-K
+    // shapes are faster on single SMs)
+    const char* e2 = getenv("CFI_GEMM_2SM");
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    const uint64_t ctas1 = (uint64_t)((d.m + BM - 1) / BM) * tiles_n * planes;
+    const bool pair = d.m > (uint32_t)BM && (e2 ? strcmp(e2, "0") != 0 : ctas1 >= 2ull * (uint64_t)sms);
+    const uint32_t bn = (tiles_n > 1 || pair) ? (per + 31) / 32 * 32 : (per + 15) / 16 * 16;
     const CUtensorMapDataType dt = d.fmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap ta, tb, tcm;
     cuuint64_t da[3] = {d.k, d.m, d.a_planes};
     cuuint64_t sA[2] = {d.lda * 2, d.a_plane * 2};
     cuuint64_t db[3] = {d.k, d.n, planes};
     cuuint64_t sB[2] = {d.ldb * 2, d.b_plane * 2};
-    cuuint32_t boxa[3] = {BK, BM, 1}, boxb[3] = {BK, bn, 1}, es[3] = {1, 1, 1};
+    cuuint32_t boxa[3] = {BK, BM, 1}, boxb[3] = {BK, pair ? bn / 2 : bn, 1}, es[3] = {1, 1, 1};
     if (enc(&ta, dt, 3, const_cast<void*>(d.a), da, sA, boxa, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
         enc(&tb, dt, 3, const_cast<void*>(d.b), db, sB, boxb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -404,17 +560,51 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
     g.scalar_f16 = d.scalar_f16;
     g.tma_c = tma_c ? 1 : 0;
     g.err = err_ptr();
+    // programmatic dependent launch (CFI_PDL=0 turns it off): the prologue overlaps the tail of
+    // the previous kernel; the kernel waits for it before its first tensor load
+    const char* ep = getenv("CFI_PDL");
+    const bool pdl = !(ep && strcmp(ep, "0") == 0);
     static std::once_flag attr;
     std::call_once(attr, [] {
         cudaFuncSetAttribute(cfi_gemm_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
         cudaFuncSetAttribute(cfi_gemm_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+        cudaFuncSetAttribute(cfi_gemm_tc2<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
+        cudaFuncSetAttribute(cfi_gemm_tc2<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
     });
-    dim3 grid((d.m + BM - 1) / BM, (d.n + bn - 1) / bn, planes);
-    if (d.fmt == 0)
-        cfi_gemm_tc<0><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tcm, g);
-    else
-        cfi_gemm_tc<1><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tcm, g);
-    return (int)cudaGetLastError();
+    if (pair) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * ((d.m + 2 * BM - 1) / (2 * BM)), (d.n + bn - 1) / bn, planes);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = SMEM2_BYTES;
+        cfg.stream = stream;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (pdl) {
+            at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[1].val.programmaticStreamSerializationAllowed = 1;
+            cfg.numAttrs = 2;
+        }
+        cudaError_t e = d.fmt == 0 ? cudaLaunchKernelEx(&cfg, cfi_gemm_tc2<0>, ta, tb, tcm, g)
+                                   : cudaLaunchKernelEx(&cfg, cfi_gemm_tc2<1>, ta, tb, tcm, g);
+        return (int)e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((d.m + BM - 1) / BM, (d.n + bn - 1) / bn, planes);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return (int)(d.fmt == 0 ? cudaLaunchKernelEx(&cfg, cfi_gemm_tc<0>, ta, tb, tcm, g)
+                            : cudaLaunchKernelEx(&cfg, cfi_gemm_tc<1>, ta, tb, tcm, g));
 }
 
 // Reads and clears the error word of the GEMM kernel's bounded waits (folded into cfi_device_error).

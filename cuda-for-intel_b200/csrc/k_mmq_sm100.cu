@@ -25,6 +25,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -395,11 +396,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // (Q4_K) Xh[plane][col][K + g] = s_g (the half float sum of group g), zero up to Kt.
 // One warp per (column, 128-value block); lane l handles values 4l..4l+3.
 template <int DS4>
-__global__ void __launch_bounds__(256)
-    cfi_mmq_x_to_f16(const uint8_t* __restrict__ y, __half* __restrict__ xh, uint32_t K, uint32_t Kt, uint32_t ncols,
-                     uint32_t ncols_y, uint32_t nchannels_y, uint32_t stride_channel_y, uint32_t stride_sample_y) {
-    const uint32_t warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const uint32_t nkb = K / 128, plane = blockIdx.y;
+CFI_DEV void x_to_f16(uint32_t bx, uint32_t plane, const uint8_t* __restrict__ y, __half* __restrict__ xh, uint32_t K,
+                      uint32_t Kt, uint32_t ncols, uint32_t ncols_y, uint32_t nchannels_y, uint32_t stride_channel_y,
+                      uint32_t stride_sample_y) {
+    const uint32_t warp_g = (bx * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const uint32_t nkb = K / 128;
     if (warp_g >= ncols * nkb) return;
     const uint32_t col = warp_g / nkb, kb = warp_g - col * nkb;
     const uint32_t wt = plane / nchannels_y, zt = plane - wt * nchannels_y;
@@ -429,20 +430,26 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+template <int DS4>
+__global__ void __launch_bounds__(256)
+    cfi_mmq_x_to_f16(const uint8_t* __restrict__ y, __half* __restrict__ xh, uint32_t K, uint32_t Kt, uint32_t ncols,
+                     uint32_t ncols_y, uint32_t nchannels_y, uint32_t stride_channel_y, uint32_t stride_sample_y) {
+    x_to_f16<DS4>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y, stride_sample_y);
+}
+
 // Weights -> fp16 K-major rows: Wh[xplane][row][k].  Q8_0: fp16(q * d).  Q4_K: fp16(q *
 // half(d * sc)) and, in the appended columns K + g, half(-dmin * m_g) (the terms the fused kernel
 // builds in shared memory; refs.rs:709-712), zero up to Kt.  One thread per weight block
 // (Q8_0: 32 values, Q4_K: 256 values), consecutive threads on consecutive blocks of a row.
 template <uint32_t TY>
-__global__ void __launch_bounds__(256)
-    cfi_mmq_w_to_f16(const uint8_t* __restrict__ x, __half* __restrict__ wh, uint32_t K, uint32_t Kt, uint32_t nrows,
-                     uint32_t srx, uint32_t nch_x, uint32_t scx, uint32_t ssx) {
+CFI_DEV void w_to_f16(uint32_t bx, uint32_t xp, const uint8_t* __restrict__ x, __half* __restrict__ wh, uint32_t K,
+                      uint32_t Kt, uint32_t nrows, uint32_t srx, uint32_t nch_x, uint32_t scx, uint32_t ssx) {
     constexpr uint32_t QKB = TY == T_Q4_K ? QK_K : QK8_0;
     const uint32_t nb = K / QKB;
-    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t t = (uint64_t)bx * blockDim.x + threadIdx.x;
     if (t >= (uint64_t)nrows * nb) return;
     const uint32_t row = (uint32_t)(t / nb), b = (uint32_t)(t - (uint64_t)row * nb);
-    const uint32_t xp = blockIdx.y, sx = xp / nch_x, cx = xp - sx * nch_x;
+    const uint32_t sx = xp / nch_x, cx = xp - sx * nch_x;
     __half* out = wh + ((size_t)xp * nrows + row) * Kt;
     if (TY == T_Q8_0) {
         const uint8_t* blk = x + ((size_t)sx * ssx + (size_t)cx * scx + (size_t)row * srx + b) * Q8_0_BYTES;
@@ -507,6 +514,24 @@ __global__ void __launch_bounds__(256)
         if (b == 0)  // the padding of the appended columns, once per row
             for (uint32_t k = K + K / 32; k < Kt; k++) out[k] = __float2half(0.0f);
     }
+}
+
+// Both pre-passes in one launch: grid.y < planes converts activation plane y, the rest weight
+// plane y - planes.  Lets the GEMM launch at once (programmatic dependent launch); it waits for
+// this grid before its first tensor load.
+template <uint32_t TY>
+__global__ void __launch_bounds__(256)
+    cfi_mmq_prepass(const uint8_t* __restrict__ y, __half* __restrict__ xh, const uint8_t* __restrict__ x,
+                    __half* __restrict__ wh, uint32_t K, uint32_t Kt, uint32_t ncols, uint32_t ncols_y,
+                    uint32_t nchannels_y, uint32_t stride_channel_y, uint32_t stride_sample_y, uint32_t planes,
+                    uint32_t nrows, uint32_t srx, uint32_t nch_x, uint32_t scx, uint32_t ssx) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (blockIdx.y < planes)
+        x_to_f16<TY == T_Q4_K ? 1 : 0>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y,
+                                       stride_sample_y);
+    else
+        w_to_f16<TY>(blockIdx.x, blockIdx.y - planes, x, wh, K, Kt, nrows, srx, nch_x, scx, ssx);
 }
 
 // ---- host side ----
@@ -613,23 +638,16 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
         rc = scratch_for(xh_pad + wh_bytes, stream, &xh);
     }
     if (rc) return rc;
-    // 1. activations -> fp16 K-major
-    {
-        const uint32_t warps = ncols_dst * (K / 128);
-        dim3 grid((warps * 32 + 255) / 256, planes);
-        if (TY == T_Q4_K)
-            cfi_mmq_x_to_f16<1><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
-        else
-            cfi_mmq_x_to_f16<0><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
-        rc = (int)cudaGetLastError();
-        if (rc) return rc;
-    }
     if (!fixed_xh) {
-        // 2. weights -> fp16 K-major, then the shared TMA-fed tcgen05 GEMM (C = Wh Xh^T per plane)
+        // 1. activations and weights -> fp16 K-major (one launch), then the shared TMA-fed
+        // tcgen05 GEMM (C = Wh Xh^T per plane)
         __half* wh = reinterpret_cast<__half*>(static_cast<uint8_t*>(xh) + xh_pad);
         const uint64_t nblk = (uint64_t)nrows * (K / (TY == T_Q4_K ? QK_K : QK8_0));
-        dim3 wgrid((uint32_t)((nblk + 255) / 256), planes_x);
-        cfi_mmq_w_to_f16<TY><<<wgrid, 256, 0, stream>>>(x, wh, K, Kt, nrows, srx, nch_x, scx, ssx);
+        const uint32_t gx_w = (uint32_t)((nblk + 255) / 256);
+        const uint32_t gx_x = (ncols_dst * (K / 128) * 32 + 255) / 256;
+        dim3 pgrid(std::max(gx_w, gx_x), planes + planes_x);
+        cfi_mmq_prepass<TY><<<pgrid, 256, 0, stream>>>(y, static_cast<__half*>(xh), x, wh, K, Kt, ncols_dst, ncols_y, nch,
+                                                       scy, ssy, planes, nrows, srx, nch_x, scx, ssx);
         rc = (int)cudaGetLastError();
         if (rc) return rc;
         TcGemm d;
@@ -661,8 +679,18 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
         rc = cfi_tc_gemm(d, stream);
         return rc < 0 ? (int)cudaErrorInvalidValue : rc;
     }
-    // fixed scratch (no room for the fp16 weights): the fused kernel dequantizes weight tiles in
-    // shared memory
+    // fixed scratch (no room for the fp16 weights): activations -> fp16, then the fused kernel
+    // dequantizes weight tiles in shared memory
+    {
+        const uint32_t warps = ncols_dst * (K / 128);
+        dim3 grid((warps * 32 + 255) / 256, planes);
+        if (TY == T_Q4_K)
+            cfi_mmq_x_to_f16<1><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
+        else
+            cfi_mmq_x_to_f16<0><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
+        rc = (int)cudaGetLastError();
+        if (rc) return rc;
+    }
     // 2. tensor map over Xh: dims (Kt, ncols, planes), box (64, BN, 1), 128-byte swizzle
     const uint32_t bn = tile_n(ncols_dst);
     PFN_encodeTiled enc = encode_fn();
