@@ -19,6 +19,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "../../include/cfi_cublas.h"
@@ -48,6 +50,7 @@ struct GemmArgs {
     const void* beta_ptr;
     int scalar_f16;
     int tma_c;  // C is f32, beta 0 and host scalars: the epilogue stores through tmc
+    uint32_t splits, kchunk;  // split K: blockIdx.z = plane * splits + split, k steps [split kchunk, ..)
     unsigned int* err;
 };
 
@@ -87,8 +90,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t bn = a.bn;
     const uint32_t tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
-    const int ksteps = (int)((a.k + BK - 1) / BK);
-    const uint32_t m0 = blockIdx.x * BM, n0 = blockIdx.y * bn, z = blockIdx.z;
+    const int ktotal = (int)((a.k + BK - 1) / BK);
+    const uint32_t split = blockIdx.z % a.splits;
+    const uint32_t m0 = blockIdx.x * BM, n0 = blockIdx.y * bn, z = blockIdx.z / a.splits;
+    // this CTA's k steps [k0, k0 + ksteps) (all of K unless split)
+    const int k0 = (int)(split * a.kchunk);
+    const int ksteps = max(0, min(ktotal, k0 + (int)a.kchunk) - k0);
     // output plane z = (sample wt, channel zt); its A plane follows the channel / sample ratios
     const uint32_t wt = z / a.nch, zt = z - wt * a.nch;
     const uint32_t za = (wt / a.smr) * a.nch_x + zt / a.chr;
@@ -125,8 +132,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                tma_load_3d(sA + slot * A_STAGE, &tma, s * BK, (int)m0, (int)za, &full[slot]);
-                tma_load_3d(sB + slot * B_STAGE, &tmb, s * BK, (int)n0, (int)z, &full[slot]);
+                tma_load_3d(sA + slot * A_STAGE, &tma, (k0 + s) * BK, (int)m0, (int)za, &full[slot]);
+                tma_load_3d(sB + slot * B_STAGE, &tmb, (k0 + s) * BK, (int)n0, (int)z, &full[slot]);
             }
         }
         __syncwarp();
@@ -172,8 +179,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (a.tma_c) {
                 // every MMA has completed: the A ring holds the 8 KB per-warp staging buffers
                 float* tbuf = reinterpret_cast<float*>(sA) + warp * 2048;
-                tmem_tile_tma_store(tmem, warp, lane, 4, bn, tbuf, &tmc, (int)m0, (int)n0, (int)zt, (int)wt,
-                                    [&](float v) { return alpha * v; });
+                if (a.splits > 1)  // raw partial sums into the split-K workspace (plane, split)
+                    tmem_tile_tma_store(tmem, warp, lane, 4, bn, tbuf, &tmc, (int)m0, (int)n0, (int)z, (int)split,
+                                        [](float v) { return v; });
+                else
+                    tmem_tile_tma_store(tmem, warp, lane, 4, bn, tbuf, &tmc, (int)m0, (int)n0, (int)zt, (int)wt,
+                                        [&](float v) { return alpha * v; });
             } else {
             const int ct = a.c_type, es = ct == CFI_R_32F ? 4 : 2;
             uint8_t* cz = static_cast<uint8_t*>(a.c) + (size_t)((long long)zt * a.c_zstride + (long long)wt * a.c_wstride) * es;
@@ -379,6 +390,56 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// Split-K reduction: C[plane][col][row] = alpha * sum_s ws[s][plane][col][row] (+ beta C), the
+// partials added in split order (deterministic).  Thread: 4 consecutive rows of one column.
+struct ReduceArgs {
+    const float* ws;
+    uint32_t ld_ws, m, n, planes, splits;
+    void* c;
+    int c_type;
+    long long ldc, c_zstride, c_wstride;
+    uint32_t nch;
+    float alpha, beta;
+    const void* alpha_ptr;
+    const void* beta_ptr;
+    int scalar_f16;
+};
+
+__global__ void __launch_bounds__(256) cfi_gemm_splitk_reduce(const ReduceArgs r) {
+    pdl_wait();
+    const uint32_t mq = (r.m + 3) / 4;
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (uint64_t)mq * r.n * r.planes) return;
+    const uint32_t rq = (uint32_t)(t % mq);
+    const uint64_t cp = t / mq;
+    const uint32_t col = (uint32_t)(cp % r.n), plane = (uint32_t)(cp / r.n);
+    const uint32_t row = 4 * rq;
+    const size_t split_stride = (size_t)r.planes * r.n * r.ld_ws;
+    const float* p = r.ws + ((size_t)plane * r.n + col) * r.ld_ws + row;
+    float4 acc = *reinterpret_cast<const float4*>(p);
+    for (uint32_t sp = 1; sp < r.splits; sp++) {
+        const float4 v = *reinterpret_cast<const float4*>(p + sp * split_stride);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    const float alpha = r.alpha_ptr ? load_scalar(r.alpha_ptr, r.scalar_f16) : r.alpha;
+    const float beta = r.beta_ptr ? load_scalar(r.beta_ptr, r.scalar_f16) : r.beta;
+    const uint32_t wt = plane / r.nch, zt = plane - wt * r.nch;
+    const int es = r.c_type == CFI_R_32F ? 4 : 2;
+    uint8_t* cz = static_cast<uint8_t*>(r.c) + (size_t)((long long)zt * r.c_zstride + (long long)wt * r.c_wstride) * es;
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        if (row + e >= r.m) break;
+        const size_t ci = (size_t)col * r.ldc + row + e;
+        float o = alpha * v[e];
+        if (beta != 0.0f) o += beta * ld_elem(cz, ci, r.c_type);
+        st_elem(cz, ci, r.c_type, o);
+    }
+}
+
 // Tiled SIMT GEMM: 16 x 16 output tile per block, any op/dtype combination, fp32 accumulation.
 // `ptrs` non-zero: A, B, C are device arrays of per-batch pointers (cublasGemmBatchedEx).
 struct SimtArgs {
@@ -484,6 +545,30 @@ bool dtype_ok(int t) { return t == CFI_R_32F || t == CFI_R_16F || t == CFI_R_16B
 
 }  // namespace
 
+// Per-device split-K workspace (fp32 partial tiles), grown outside stream capture only.
+static std::mutex g_ws_mu;
+static std::map<int, std::pair<void*, size_t>> g_ws;
+static float* splitk_workspace(size_t bytes, cudaStream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> g(g_ws_mu);
+    auto& w = g_ws[dev];
+    if (w.second < bytes) {
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone) return nullptr;
+        if (w.first) cudaFree(w.first);
+        w.first = nullptr;
+        w.second = 0;
+        const size_t want = bytes + bytes / 4;
+        if (cudaMalloc(&w.first, want) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        w.second = want;
+    }
+    return static_cast<float*>(w.first);
+}
+
 // Shared tensor-core launcher (the cuBLAS-compatible GEMM and the prefill mul_mat_q use it).
 // Returns 0 on launch, -1 when the descriptor cannot be expressed with tensor maps (the caller
 // then takes another path), or a CUDA error code.
@@ -539,7 +624,40 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
         tma_c = enc(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d.c, dc, scs, boxc, esc, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
+    // split K when the output tiles fill under half the SMs and K is deep (CFI_GEMM_SPLITK=0 off)
+    uint32_t splits = 1, kchunk = (d.k + BK - 1) / BK;
+    float* ws = nullptr;
+    uint32_t ld_ws = 0;
+    CUtensorMap wsm;
+    {
+        const char* es = getenv("CFI_GEMM_SPLITK");
+        const uint64_t tiles = (uint64_t)((d.m + BM - 1) / BM) * tiles_n * planes;
+        const uint32_t ksteps = kchunk;
+        if (!pair && !(es && strcmp(es, "0") == 0) && tiles * 2 <= (uint64_t)sms && ksteps >= 16) {
+            uint32_t sp = std::min<uint32_t>((uint32_t)(sms / tiles), ksteps / 8);
+            if (sp >= 2) {
+                const uint32_t kc = (ksteps + sp - 1) / sp;
+                sp = (ksteps + kc - 1) / kc;
+                ld_ws = (d.m + 3) / 4 * 4;
+                const size_t bytes = (size_t)sp * planes * d.n * ld_ws * 4;
+                ws = splitk_workspace(bytes, stream);
+                if (ws) {
+                    cuuint64_t dw[4] = {d.m, d.n, planes, sp};
+                    cuuint64_t sw[3] = {(cuuint64_t)ld_ws * 4, (cuuint64_t)ld_ws * 4 * d.n, (cuuint64_t)ld_ws * 4 * d.n * planes};
+                    cuuint32_t bw[4] = {32, 32, 1, 1}, ew[4] = {1, 1, 1, 1};
+                    if (enc(&wsm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws, dw, sw, bw, ew, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+                        splits = sp;
+                        kchunk = kc;
+                    }
+                }
+            }
+        }
+    }
     GemmArgs g;
+    g.splits = splits;
+    g.kchunk = kchunk;
     g.c = d.c;
     g.c_zstride = d.c_zstride;
     g.c_wstride = d.c_wstride;
@@ -594,7 +712,7 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
         return (int)e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((d.m + BM - 1) / BM, (d.n + bn - 1) / bn, planes);
+    cfg.gridDim = dim3((d.m + BM - 1) / BM, (d.n + bn - 1) / bn, planes * splits);
     cfg.blockDim = dim3(THREADS, 1, 1);
     cfg.dynamicSmemBytes = SMEM_BYTES;
     cfg.stream = stream;
@@ -603,6 +721,38 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
+    if (splits > 1) {
+        g.tma_c = 1;  // partials go to the workspace through its tensor map
+        cudaError_t e = d.fmt == 0 ? cudaLaunchKernelEx(&cfg, cfi_gemm_tc<0>, ta, tb, wsm, g)
+                                   : cudaLaunchKernelEx(&cfg, cfi_gemm_tc<1>, ta, tb, wsm, g);
+        if (e != cudaSuccess) return (int)e;
+        ReduceArgs r;
+        r.ws = ws;
+        r.ld_ws = ld_ws;
+        r.m = d.m;
+        r.n = d.n;
+        r.planes = planes;
+        r.splits = splits;
+        r.c = d.c;
+        r.c_type = d.c_type;
+        r.ldc = (long long)d.ldc;
+        r.c_zstride = d.c_zstride;
+        r.c_wstride = d.c_wstride;
+        r.nch = d.nch;
+        r.alpha = d.alpha;
+        r.beta = d.beta;
+        r.alpha_ptr = d.alpha_ptr;
+        r.beta_ptr = d.beta_ptr;
+        r.scalar_f16 = d.scalar_f16;
+        cudaLaunchConfig_t rc = {};
+        const uint64_t nthr = (uint64_t)((d.m + 3) / 4) * d.n * planes;
+        rc.gridDim = dim3((uint32_t)((nthr + 255) / 256), 1, 1);
+        rc.blockDim = dim3(256, 1, 1);
+        rc.stream = stream;
+        rc.attrs = at;
+        rc.numAttrs = pdl ? 1 : 0;
+        return (int)cudaLaunchKernelEx(&rc, cfi_gemm_splitk_reduce, r);
+    }
     return (int)(d.fmt == 0 ? cudaLaunchKernelEx(&cfg, cfi_gemm_tc<0>, ta, tb, tcm, g)
                             : cudaLaunchKernelEx(&cfg, cfi_gemm_tc<1>, ta, tb, tcm, g));
 }
