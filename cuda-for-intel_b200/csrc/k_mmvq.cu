@@ -398,10 +398,26 @@ CFI_DEV float q4k_term(float dx, float dmin, float d8, int sumi, int sc, int sum
 
 // Rows of one chunk.  Each pass holds the weights of R rows per team in registers and streams
 // the activations column by column, so a column's q8_1 block is read once per R rows.
+CFI_DEV int dot8u(const uint32_t (&q)[8], uint4 a, uint4 b) {
+    int s0 = dp4a_us(q[0], a.x, 0), s1 = dp4a_us(q[1], a.y, 0);
+    s0 = dp4a_us(q[2], a.z, s0);
+    s1 = dp4a_us(q[3], a.w, s1);
+    s0 = dp4a_us(q[4], b.x, s0);
+    s1 = dp4a_us(q[5], b.y, s1);
+    s0 = dp4a_us(q[6], b.z, s0);
+    s1 = dp4a_us(q[7], b.w, s1);
+    return s0 + s1;
+}
+
+// Q4_K: 2 rows per team and pass (each activation block read once per 2 rows); the nibble words
+// are masked once per row for up to 4 columns, per column beyond (register budget)
+template <int NCOLS> constexpr int q4k_rows() { return 2; }
+template <int NCOLS> constexpr bool q4k_hoist() { return NCOLS <= 4; }
+
 template <int NCOLS>
 CFI_DEV void q4k_chunk(uint32_t sbase, uint32_t rstride, uint32_t r0, uint32_t r1, const YStage& y, uint32_t tid,
                        float* dplane, uint32_t stride_col_dst) {
-    constexpr int R = 2;
+    constexpr int R = q4k_rows<NCOLS>();
     constexpr uint32_t NTEAM = NW * 32 / 16;
     const uint32_t j = tid & 15, team = tid >> 4, c4 = j & 3;
     const uint32_t G = y.nb32;
@@ -413,7 +429,8 @@ CFI_DEV void q4k_chunk(uint32_t sbase, uint32_t rstride, uint32_t r0, uint32_t r
             for (int c = 0; c < NCOLS; c++) acc[k][c][0] = acc[k][c][1] = 0.0f;
         for (uint32_t g0 = 2 * j; g0 < G; g0 += 32) {
             const uint32_t sbo = (g0 >> 3) * Q4_K_BYTES;
-            uint32_t q[R][8];
+            constexpr bool H = q4k_hoist<NCOLS>();
+            uint32_t ql[R][8], qh[R][H ? 8 : 1];  // low nibbles (or raw words), high nibbles in place (16 x value)
             int sc0[R], mn0[R], sc1[R], mn1[R];
             float dx[R], dmin[R];
 #pragma unroll
@@ -423,8 +440,16 @@ CFI_DEV void q4k_chunk(uint32_t sbase, uint32_t rstride, uint32_t r0, uint32_t r
                 const uint4 h = lds128(a), q0 = lds128(a + 16 + 32 * c4), q1 = lds128(a + 32 + 32 * c4);
                 dx[k] = h2f_bits((uint16_t)(h.x & 0xffffu));
                 dmin[k] = h2f_bits((uint16_t)(h.x >> 16));
-                q[k][0] = q0.x; q[k][1] = q0.y; q[k][2] = q0.z; q[k][3] = q0.w;
-                q[k][4] = q1.x; q[k][5] = q1.y; q[k][6] = q1.z; q[k][7] = q1.w;
+                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    if constexpr (H) {
+                        ql[k][i] = qw[i] & 0x0F0F0F0Fu;
+                        qh[k][i] = qw[i] & 0xF0F0F0F0u;
+                    } else {
+                        ql[k][i] = qw[i];
+                    }
+                }
                 q4k_scale_min(h, 2 * c4, sc0[k], mn0[k]);
                 q4k_scale_min(h, 2 * c4 + 1, sc1[k], mn1[k]);
             }
@@ -436,8 +461,14 @@ CFI_DEV void q4k_chunk(uint32_t sbase, uint32_t rstride, uint32_t r0, uint32_t r
                 const uint2 m0 = lds64(y.ym + o * 8), m1 = lds64(y.ym + o * 8 + 8);
 #pragma unroll
                 for (int k = 0; k < R; k++) {
-                    const int lo = dot8m(q[k], 0x0F0F0F0Fu, ya0, yb0);
-                    const int hi = dot8m(q[k], 0xF0F0F0F0u, ya1, yb1) >> 4;
+                    int lo, hi;
+                    if constexpr (H) {
+                        lo = dot8u(ql[k], ya0, yb0);
+                        hi = dot8u(qh[k], ya1, yb1) >> 4;
+                    } else {
+                        lo = dot8m(ql[k], 0x0F0F0F0Fu, ya0, yb0);
+                        hi = dot8m(ql[k], 0xF0F0F0F0u, ya1, yb1) >> 4;
+                    }
                     acc[k][c][0] = q4k_term(dx[k], dmin[k], __uint_as_float(m0.x), lo, sc0[k], (int)m0.y, mn0[k], acc[k][c][0]);
                     acc[k][c][1] = q4k_term(dx[k], dmin[k], __uint_as_float(m1.x), hi, sc1[k], (int)m1.y, mn1[k], acc[k][c][1]);
                 }
