@@ -190,6 +190,50 @@ def prefill_gemm(cfi, g, stream, dev, peak_tf):
                          "frac": round(best / peak_tf, 4), "peak_kind": "measured bf16 dense (burst)"}}
 
 
+def decode_bench(stream, dev, ntok=48, warm=3):
+    """Qwen2.5-0.5B-architecture decode (24 layers, Q8_0 random weights, 631-token
+    seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens."""
+    import torch
+
+    import cfi_b200 as cfi
+    from decode import DecodeModel
+
+    ctx = cfi.Ctx(dev.index or 0)
+    m = DecodeModel(torch, ctx, dev)
+    m.reset(token=1234)
+    with torch.cuda.stream(stream):
+        m.step(stream.cuda_stream)  # first-use probes outside the capture
+    torch.cuda.synchronize()
+    m.reset(token=1234)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        m.step(torch.cuda.current_stream().cuda_stream)
+    m.reset(token=1234)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            gr.replay()
+    torch.cuda.synchronize()
+    m.reset(token=1234)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(ntok):
+            gr.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    assert int(m.pos.item()) == m.cfg.prompt + ntok and cfi.lib().cfi_device_error() == 0
+    bpt = m.cfg.weight_bytes_per_token()
+    out = {"workload": "config4: Qwen2.5-0.5B-architecture decode, 24 layers, Q8_0 random weights, 631-token seeded "
+                       "KV cache, %d greedy tokens, one CUDA graph per token" % ntok,
+           "tok_per_s": round(ntok / (ms * 1e-3), 1), "ms_per_token": round(ms / ntok, 4),
+           "launches_per_token": m.launches_per_step, "weight_bytes_per_token": bpt,
+           "weights_gbs": round(bpt * ntok / (ms * 1e-3) / 1e9, 1)}
+    del gr
+    ctx.close()
+    return out
+
+
 def cpu_baseline(seconds, threads=0):
     """The oracle's CPU decode step (reference host math, row-parallel) on a bounded sample."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -409,6 +453,8 @@ def run_gpu(args, rank, world):
                 "clocks": clk.summary(), "native_only": ok}
         if not args.no_prefill and world == 1:
             line["prefill"] = prefill_gemm(cfi, g, stream, dev, tensor_peak())
+        if not args.no_decode and world == 1:
+            line["decode"] = decode_bench(stream, dev)
         if not args.no_cpu and world == 1:
             gbs, used, n, el = cpu_baseline(args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
@@ -429,6 +475,7 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     args = ap.parse_args()
     if args.warmup < 3:

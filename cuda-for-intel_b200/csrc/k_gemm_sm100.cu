@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/cfi_cublas.h"
 #include "cfi_common.cuh"
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
     pdl_wait();  // launched early (programmatic dependent launch): the operands may come from the previous kernel
 
     if (warp == 5) {
@@ -299,6 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
     pdl_wait();  // launched early (programmatic dependent launch): the operands may come from the previous kernel
 
     if (warp == 5) {
@@ -406,6 +409,7 @@ struct ReduceArgs {
 };
 
 __global__ void __launch_bounds__(256) cfi_gemm_splitk_reduce(const ReduceArgs r) {
+    pdl_launch_dependents();
     pdl_wait();
     const uint32_t mq = (r.m + 3) / 4;
     const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -437,6 +441,93 @@ __global__ void __launch_bounds__(256) cfi_gemm_splitk_reduce(const ReduceArgs r
         float o = alpha * v[e];
         if (beta != 0.0f) o += beta * ld_elem(cz, ci, r.c_type);
         st_elem(cz, ci, r.c_type, o);
+    }
+}
+
+// Skinny GEMM (op(A) = A^T, op(B) = B, f16/bf16, n <= 8 columns): the decode-time attention
+// products (KQ, KQV per KV head).  One warp per output row: 16-byte loads of A's row and of
+// each B column over k, fp32 FMAs, a butterfly per column.  Launched with PDL like the other
+// kernels.  Strided batches in blockIdx.y.
+struct SkinnyArgs {
+    const void* a;
+    const void* b;
+    void* c;
+    long long sa, sb, sc;
+    int lda, ldb, ldc, ct;
+    uint32_t m, n, k;
+    float alpha, beta;
+    const void* alpha_ptr;
+    const void* beta_ptr;
+    int scalar_f16;
+};
+
+template <int FMT>
+__global__ void __launch_bounds__(256) cfi_gemm_skinny(const SkinnyArgs p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t row = blockIdx.x * 8 + (threadIdx.x >> 5), z = blockIdx.y;
+    if (row >= p.m) return;
+    typedef typename std::conditional<FMT == 0, __half2, __nv_bfloat162>::type T2;
+    const uint16_t* A = static_cast<const uint16_t*>(p.a) + (size_t)z * p.sa + (size_t)row * p.lda;
+    const uint16_t* B = static_cast<const uint16_t*>(p.b) + (size_t)z * p.sb;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    auto f2 = [](uint32_t w) -> float2 {
+        T2 h = *reinterpret_cast<const T2*>(&w);
+        if constexpr (FMT == 0)
+            return __half22float2(h);
+        else
+            return __bfloat1622float2(h);
+    };
+    for (uint32_t k0 = lane * 8; k0 < p.k; k0 += 256) {
+        if (k0 + 8 <= p.k) {
+            const uint4 av = *reinterpret_cast<const uint4*>(A + k0);
+            const float2 a0 = f2(av.x), a1 = f2(av.y), a2 = f2(av.z), a3 = f2(av.w);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j < (int)p.n) {
+                    const uint4 bv = *reinterpret_cast<const uint4*>(B + (size_t)j * p.ldb + k0);
+                    const float2 b0 = f2(bv.x), b1 = f2(bv.y), b2 = f2(bv.z), b3 = f2(bv.w);
+                    float s = acc[j];
+                    s = fmaf(a0.x, b0.x, s);
+                    s = fmaf(a0.y, b0.y, s);
+                    s = fmaf(a1.x, b1.x, s);
+                    s = fmaf(a1.y, b1.y, s);
+                    s = fmaf(a2.x, b2.x, s);
+                    s = fmaf(a2.y, b2.y, s);
+                    s = fmaf(a3.x, b3.x, s);
+                    s = fmaf(a3.y, b3.y, s);
+                    acc[j] = s;
+                }
+            }
+        } else {
+            for (uint32_t kk = k0; kk < p.k; kk++) {
+                const float av = FMT == 0 ? __half2float(__ushort_as_half(A[kk])) : __bfloat162float(__ushort_as_bfloat16(A[kk]));
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (j < (int)p.n) {
+                        const uint16_t bb = B[(size_t)j * p.ldb + kk];
+                        acc[j] = fmaf(av, FMT == 0 ? __half2float(__ushort_as_half(bb)) : __bfloat162float(__ushort_as_bfloat16(bb)), acc[j]);
+                    }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    if (lane < p.n) {
+        float v = acc[0];
+#pragma unroll
+        for (int j = 1; j < 8; j++)
+            if ((int)lane == j) v = acc[j];
+        const float alpha = p.alpha_ptr ? load_scalar(p.alpha_ptr, p.scalar_f16) : p.alpha;
+        const float beta = p.beta_ptr ? load_scalar(p.beta_ptr, p.scalar_f16) : p.beta;
+        void* cz = static_cast<uint8_t*>(p.c) + (size_t)z * p.sc * (p.ct == CFI_R_32F ? 4 : 2);
+        const size_t ci = (size_t)lane * p.ldc + row;
+        float r = alpha * v;
+        if (beta != 0.0f) r += beta * ld_elem(cz, ci, p.ct);
+        st_elem(cz, ci, p.ct, r);
     }
 }
 
@@ -852,6 +943,48 @@ int gemm_common(cfi_blas* h, int transa, int transb, int m, int n, int k, const 
                     compute_type != CFI_COMPUTE_32F_FAST_TF32 && lda % 8 == 0 && ldb % 8 == 0 &&
                     (reinterpret_cast<uintptr_t>(A) & 15) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
                     (batch == 1 || ((sa % 8) == 0 && (sb % 8) == 0 && sa > 0 && sb > 0));
+    // n <= 8 columns (decode attention): the skinny kernel (CFI_GEMM_SKINNY=0 off)
+    const char* sk_env = getenv("CFI_GEMM_SKINNY");
+    const bool skinny = !(sk_env && strcmp(sk_env, "0") == 0) && !ptr_arrays && fmt16 && b_type == a_type &&
+                        transa == CFI_OP_T && transb == CFI_OP_N && n <= 8 && k > 0 && lda % 8 == 0 && ldb % 8 == 0 &&
+                        (reinterpret_cast<uintptr_t>(A) & 15) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
+                        batch <= 65535 && (batch == 1 || ((sa % 8) == 0 && (sb % 8) == 0));
+    if (skinny) {
+        SkinnyArgs q;
+        q.a = A;
+        q.b = B;
+        q.c = C;
+        q.sa = sa;
+        q.sb = sb;
+        q.sc = sc;
+        q.lda = lda;
+        q.ldb = ldb;
+        q.ldc = ldc;
+        q.ct = c_type;
+        q.m = (uint32_t)m;
+        q.n = (uint32_t)n;
+        q.k = (uint32_t)k;
+        q.alpha = al;
+        q.beta = be;
+        q.alpha_ptr = dev_ptrs ? alpha : nullptr;
+        q.beta_ptr = dev_ptrs ? beta : nullptr;
+        q.scalar_f16 = sf16;
+        const char* ep = getenv("CFI_PDL");
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)((m + 7) / 8), (unsigned)batch, 1);
+        cfg.blockDim = dim3(256, 1, 1);
+        cfg.stream = h->stream;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = (ep && strcmp(ep, "0") == 0) ? 0 : 1;
+        cudaError_t e = a_type == CFI_R_16F ? cudaLaunchKernelEx(&cfg, cfi_gemm_skinny<0>, q)
+                                            : cudaLaunchKernelEx(&cfg, cfi_gemm_skinny<1>, q);
+        if (e != cudaSuccess) return CFI_BLAS_EXECUTION_FAILED;
+        h->last_path = 3;
+        return CFI_BLAS_SUCCESS;
+    }
     if (tc) {
         TcGemm d;
         d.a = A;

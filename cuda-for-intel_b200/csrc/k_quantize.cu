@@ -95,6 +95,8 @@ template <int DS4>
 __global__ void __launch_bounds__(128)
     cfi_quantize_mmq_q8_1(const float* __restrict__ x, const int32_t* __restrict__ ids, void* __restrict__ vy,
                           int64_t ne00, int64_t s01, int64_t s02, int64_t s03, int64_t ne0, int ne1, int ne2) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t i0 = ((int64_t)blockIdx.y * 128 + threadIdx.x) * 4;
     if (i0 >= ne0) return;  // whole warps: ne0 % 128 == 0

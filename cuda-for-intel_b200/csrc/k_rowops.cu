@@ -9,6 +9,7 @@
 // inside 1e-3 relative L2 (rsqrtf/expf/sincosf are CUDA's, not bit-identical to libm).
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
+#include "sm100_ptx.cuh"
 
 namespace {
 
@@ -45,6 +46,8 @@ __global__ void __launch_bounds__(CFI_ROWOP_THREADS)
                  int64_t add_stride_row, int64_t add_stride_channel, int64_t add_stride_sample, uint3 add_ncols,
                  uint3 add_nrows, uint3 add_nchannels, uint3 add_nsamples) {
     __shared__ float red[32];
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
     const uint32_t row = blockIdx.x, channel = blockIdx.y, sample = blockIdx.z;
     const uint32_t nrows = gridDim.x, nchannels = gridDim.y;
     x += sample * stride_sample + channel * stride_channel + row * stride_row;
@@ -75,6 +78,8 @@ __global__ void __launch_bounds__(CFI_ROWOP_THREADS)
                        int64_t stride_row, int64_t stride_channel, int64_t stride_sample, float eps) {
     __shared__ float red[32];
     (void)nsamples;
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
     const uint32_t row = blockIdx.x, channel = blockIdx.y, sample = blockIdx.z, nrows = gridDim.x;
     x += sample * stride_sample + channel * stride_channel + row * stride_row;
     dst += (((int64_t)sample * nchannels + channel) * nrows + row) * ncols;
@@ -100,6 +105,8 @@ __global__ void __launch_bounds__(CFI_ROWOP_THREADS)
                   const int32_t* __restrict__ pos, float freq_scale, float ext_factor, float attn_factor,
                   rope_corr_dims corr_dims, float theta_scale, const float* __restrict__ freq_factors,
                   uint32_t nrows) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
     const uint32_t half = (uint32_t)ne0 / 2;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t row_dst = (uint32_t)(gid / half);
@@ -158,6 +165,8 @@ __global__ void __launch_bounds__(CFI_ROWOP_THREADS)
                  float* __restrict__ dst, const soft_max_params p) {
     extern __shared__ float vals[];
     __shared__ float red[32];
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
     const int64_t i03 = blockIdx.z, i02 = blockIdx.y, i01 = blockIdx.x;
     const int64_t rowx = blockIdx.x + (int64_t)blockIdx.y * gridDim.x + (int64_t)blockIdx.z * gridDim.x * gridDim.y;
     const int64_t i11 = i01, i12 = i02 % p.ne12, i13 = i03 % p.ne13;

@@ -563,7 +563,8 @@ static uint32_t env_u32(const char* name, uint32_t dflt, uint32_t lo, uint32_t h
     return (uint32_t)std::min<unsigned long>(hi, std::max<unsigned long>(lo, x));
 }
 
-// Programmatic dependent launch for the decode kernels (CFI_PDL=0 turns it off).
+// Programmatic dependent launch for the native kernels (CFI_PDL=0 turns it off): each one lets
+// its dependents launch early and waits for its predecessor before touching data it may produce.
 static bool pdl_enabled() { return env_u32("CFI_PDL", 1, 0, 1) != 0; }
 
 int mmq_tile_n(uint32_t ncols_dst);  // k_mmq_sm100.cu
@@ -632,6 +633,7 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         nl.fn = cfi_native_quantize_mmq(plan.ty == 1);
         memcpy(nl.grid, grid, sizeof nl.grid);
         nl.block[0] = 128;
+        nl.pdl = pdl_enabled();
         break;
     case CFI_K_MMQ: {
         // mod.rs:542-557: stock 32x8 threads; MoE (ids_dst / expert_bounds) keeps the stock kernel
@@ -654,6 +656,7 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         nl.fn = plan.kernel == CFI_K_RMS_NORM ? cfi_native_rms_norm(plan.aux & 1, (plan.aux >> 1) & 1) : cfi_native_rms_norm_plain();
         memcpy(nl.grid, grid, sizeof nl.grid);
         nl.block[0] = CFI_ROWOP_THREADS;
+        nl.pdl = pdl_enabled();
         break;
     case CFI_K_ROPE_NEOX: {
         if (!block_is(block, 1, 256, 1) || nvals < 7 || grid[2] != 1) return false;
@@ -665,6 +668,7 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         nl.grid[0] = (uint32_t)((pairs + CFI_ROWOP_THREADS - 1) / CFI_ROWOP_THREADS);
         nl.block[0] = CFI_ROWOP_THREADS;
         nl.extra.push_back((uint32_t)nr);
+        nl.pdl = pdl_enabled();
         break;
     }
     case CFI_K_SOFT_MAX: {
@@ -676,6 +680,7 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         memcpy(nl.grid, grid, sizeof nl.grid);
         nl.block[0] = CFI_ROWOP_THREADS;
         nl.smem = (size_t)ncols * 4;
+        nl.pdl = pdl_enabled();
         break;
     }
     default:

@@ -1,0 +1,179 @@
+"""Synthetic decode driver: a Qwen2-architecture layer stack (Qwen2.5-0.5B
+shape, random Q8_0 weights) stepping one token at a time through this library's kernels only.
+
+Per layer, in ggml's order: rms_norm (x attn_norm) -> quantize_q8_1 -> Q/K/V mul_mat_vec_q (+bias)
+-> rope_neox on q and k -> K/V cache store (f16) -> KQ = K^T q (GemmStridedBatchedEx, GQA groups)
+-> soft_max (scale 1/sqrt(d), causal mask) -> KQV = V P -> quantize -> O projection -> residual ->
+rms_norm (x ffn_norm) -> quantize -> gate/up -> swiglu -> quantize -> down -> residual.  Then the
+output norm, the tied Q8_0 embedding as lm_head, and a device-side greedy argmax that advances the
+position.  The substituted kernels (quantize_q8_1, mul_mat_vec_q, rms_norm, rope_neox, soft_max)
+run through the substitution C ABI with ggml's kernelParams; the attention products through the
+cuBLAS-compatible GemmEx; the element-wise steps through include/cfi_glue.h.  Position and token
+live in device memory, so one captured step graph replays for every token.
+
+The model weights are random (seeded), so the generated tokens are meaningless; the KV cache of the
+prompt positions is filled with seeded random values instead of running a prefill.
+"""
+import ctypes as C
+import math
+from dataclasses import dataclass
+
+import cfi_b200 as cfi
+
+
+@dataclass
+class Config:
+    hidden: int = 896
+    layers: int = 24
+    n_head: int = 14
+    n_kv_head: int = 2
+    head_dim: int = 64
+    ffn: int = 4864
+    vocab: int = 151936
+    eps: float = 1e-6
+    theta: float = 1e6
+    prompt: int = 631
+    n_ctx: int = 680  # >= prompt + generated tokens, a multiple of 8
+
+    def weight_bytes_per_token(self):
+        per_layer = (self.hidden * (self.n_head * self.head_dim) * 2 + self.hidden * self.n_kv_head * self.head_dim * 2
+                     + self.hidden * self.ffn * 3)
+        return (per_layer * self.layers + self.vocab * self.hidden) * 34 // 32
+
+
+def random_q8_0(torch, rows, k, gen, device):
+    """Valid Q8_0 blocks of a random matrix with values about N(0, 0.02) (device-side, seeded)."""
+    nb = rows * k // 32
+    q = torch.clamp(torch.round(torch.randn(nb, 32, generator=gen, device=device) * 42.0), -127, 127).to(torch.int8)
+    d = (0.02 / 42.0 * (0.75 + 0.5 * torch.rand(nb, 1, generator=gen, device=device))).to(torch.float16)
+    blk = torch.empty(nb, 34, dtype=torch.uint8, device=device)
+    blk[:, 0:2] = d.view(torch.uint8)
+    blk[:, 2:] = q.view(torch.uint8)
+    return blk.reshape(-1)
+
+
+class DecodeModel:
+    def __init__(self, torch, ctx, device, cfg=None, seed=0x5eed):
+        self.t = torch
+        self.cfg = cfg or Config()
+        self.dev = device
+        self.g = cfi.GgmlCaller(ctx, "all")
+        self.blas = cfi.Blas()
+        self.L = cfi.lib()
+        c, tt = self.cfg, torch
+        gen = tt.Generator(device=device)
+        gen.manual_seed(seed)
+        f32 = dict(dtype=tt.float32, device=device)
+        nq, nkv = c.n_head * c.head_dim, c.n_kv_head * c.head_dim
+        self.layers = []
+        for _ in range(c.layers):
+            self.layers.append(dict(
+                wq=random_q8_0(tt, nq, c.hidden, gen, device), wk=random_q8_0(tt, nkv, c.hidden, gen, device),
+                wv=random_q8_0(tt, nkv, c.hidden, gen, device), wo=random_q8_0(tt, c.hidden, nq, gen, device),
+                wg=random_q8_0(tt, c.ffn, c.hidden, gen, device), wu=random_q8_0(tt, c.ffn, c.hidden, gen, device),
+                wd=random_q8_0(tt, c.hidden, c.ffn, gen, device),
+                bq=tt.randn(nq, generator=gen, **f32) * 0.1, bk=tt.randn(nkv, generator=gen, **f32) * 0.1,
+                bv=tt.randn(nkv, generator=gen, **f32) * 0.1,
+                attn_norm=1.0 + 0.1 * tt.randn(c.hidden, generator=gen, **f32),
+                ffn_norm=1.0 + 0.1 * tt.randn(c.hidden, generator=gen, **f32),
+                kc=tt.zeros(c.n_kv_head, c.n_ctx, c.head_dim, dtype=tt.float16, device=device),
+                vc=tt.zeros(c.n_kv_head, c.head_dim, c.n_ctx, dtype=tt.float16, device=device)))
+            lay = self.layers[-1]
+            lay["kc"][:, :c.prompt] = (tt.randn(c.n_kv_head, c.prompt, c.head_dim, generator=gen, **f32)).half()
+            lay["vc"][:, :, :c.prompt] = (tt.randn(c.n_kv_head, c.head_dim, c.prompt, generator=gen, **f32)).half()
+        self.embd = random_q8_0(tt, c.vocab, c.hidden, gen, device)  # tied with lm_head
+        self.out_norm = 1.0 + 0.1 * tt.randn(c.hidden, generator=gen, **f32)
+        # activations and device-side state
+        z = lambda n: tt.zeros(n, **f32)
+        self.x, self.h, self.q, self.k, self.v = z(c.hidden), z(c.hidden), z(nq), z(nkv), z(nkv)
+        self.qr, self.kr = z(nq), z(nkv)
+        self.attn, self.o = z(nq), z(c.hidden)
+        self.gate, self.up, self.gu, self.dn = z(c.ffn), z(c.ffn), z(c.ffn), z(c.hidden)
+        self.logits = z(c.vocab)
+        self.scores, self.probs = z(c.n_head * c.n_ctx), z(c.n_head * c.n_ctx)
+        self.mask = z(c.n_ctx)
+        self.q16 = tt.zeros(nq, dtype=tt.float16, device=device)
+        self.p16 = tt.zeros(c.n_head * c.n_ctx, dtype=tt.float16, device=device)
+        qb = lambda n: tt.zeros(n // 32 * 36, dtype=tt.uint8, device=device)
+        self.hq, self.aq, self.gq = qb(c.hidden), qb(nq), qb(c.ffn)
+        self.token = tt.zeros(1, dtype=tt.int32, device=device)
+        self.pos = tt.zeros(1, dtype=tt.int32, device=device)
+        self.launches_per_step = 0
+
+    def reset(self, token, pos=None):
+        self.token.fill_(int(token))
+        self.pos.fill_(self.cfg.prompt if pos is None else int(pos))
+
+    def _chk(self, rc, what):
+        if rc != 0:
+            raise RuntimeError("%s failed: %d" % (what, rc))
+        self.launches_per_step += 1
+
+    def step(self, stream):
+        """Enqueue one token step on `stream` (a cudaStream_t)."""
+        c, g, L, s = self.cfg, self.g, self.L, stream
+        P = lambda t: C.c_void_p(t.data_ptr())
+        sv = C.c_void_p(s)
+        nq, nkv, grp = c.n_head * c.head_dim, c.n_kv_head * c.head_dim, c.n_head // c.n_kv_head
+        self.launches_per_step = 0
+        self._chk(L.cfi_glue_get_rows_q8_0(P(self.embd), P(self.token), P(self.x), c.hidden, sv), "get_rows")
+        self._chk(L.cfi_glue_causal_mask(P(self.mask), P(self.pos), c.n_ctx, sv), "mask")
+
+        def gemv(w, xq, out, rows, k):
+            g.mmvq(cfi.Q8_0, 1, w.data_ptr(), xq.data_ptr(), out.data_ptr(), k, rows, stream=s)
+            self.launches_per_step += 1
+
+        def quant(x, xq, k):
+            g.quantize_q8_1(x.data_ptr(), xq.data_ptr(), k, k, 1, stream=s)
+            self.launches_per_step += 1
+
+        B = cfi.Blas
+        self.blas.set_stream(s)
+        for lay in self.layers:
+            g.rms_norm(self.x.data_ptr(), self.h.data_ptr(), c.hidden, 1, mul=lay["attn_norm"].data_ptr(), eps=c.eps,
+                       stream=s)
+            quant(self.h, self.hq, c.hidden)
+            gemv(lay["wq"], self.hq, self.q, nq, c.hidden)
+            gemv(lay["wk"], self.hq, self.k, nkv, c.hidden)
+            gemv(lay["wv"], self.hq, self.v, nkv, c.hidden)
+            self._chk(L.cfi_glue_qkv_bias(P(self.q), P(self.k), P(self.v), P(lay["bq"]), P(lay["bk"]), P(lay["bv"]),
+                                          nq, nkv, sv), "bias")
+            g.rope_neox(self.q.data_ptr(), self.qr.data_ptr(), c.head_dim, c.n_head, 1, c.head_dim, self.pos.data_ptr(),
+                        freq_base=c.theta, stream=s)
+            g.rope_neox(self.k.data_ptr(), self.kr.data_ptr(), c.head_dim, c.n_kv_head, 1, c.head_dim,
+                        self.pos.data_ptr(), freq_base=c.theta, stream=s)
+            self._chk(L.cfi_glue_kv_store(P(self.qr), P(self.kr), P(self.v), P(self.q16), P(lay["kc"]), P(lay["vc"]),
+                                          P(self.pos), nq, nkv, c.head_dim, c.n_ctx, sv), "kv_store")
+            # KQ: per KV head, scores[h][j] = K[j] . q_h for its `grp` query heads
+            rc = self.blas.gemm_strided_batched_ex(
+                B.OP_T, B.OP_N, c.n_ctx, grp, c.head_dim, 1.0, lay["kc"].data_ptr(), B.R_16F, c.head_dim,
+                c.n_ctx * c.head_dim, self.q16.data_ptr(), B.R_16F, c.head_dim, grp * c.head_dim, 0.0,
+                self.scores.data_ptr(), B.R_32F, c.n_ctx, grp * c.n_ctx, c.n_kv_head)
+            self._chk(rc, "KQ")
+            g.soft_max(self.scores.data_ptr(), self.mask.data_ptr(), self.probs.data_ptr(), c.n_ctx, 1, c.n_head,
+                       1.0 / math.sqrt(c.head_dim), stream=s)
+            self._chk(L.cfi_glue_to_f16(P(self.probs), P(self.p16), c.n_head * c.n_ctx, sv), "to_f16")
+            # KQV: out_h = V P_h
+            rc = self.blas.gemm_strided_batched_ex(
+                B.OP_T, B.OP_N, c.head_dim, grp, c.n_ctx, 1.0, lay["vc"].data_ptr(), B.R_16F, c.n_ctx,
+                c.head_dim * c.n_ctx, self.p16.data_ptr(), B.R_16F, c.n_ctx, grp * c.n_ctx, 0.0,
+                self.attn.data_ptr(), B.R_32F, c.head_dim, grp * c.head_dim, c.n_kv_head)
+            self._chk(rc, "KQV")
+            quant(self.attn, self.aq, nq)
+            gemv(lay["wo"], self.aq, self.o, c.hidden, nq)
+            self._chk(L.cfi_glue_add(P(self.x), P(self.o), c.hidden, sv), "add")
+            g.rms_norm(self.x.data_ptr(), self.h.data_ptr(), c.hidden, 1, mul=lay["ffn_norm"].data_ptr(), eps=c.eps,
+                       stream=s)
+            quant(self.h, self.hq, c.hidden)
+            gemv(lay["wg"], self.hq, self.gate, c.ffn, c.hidden)
+            gemv(lay["wu"], self.hq, self.up, c.ffn, c.hidden)
+            self._chk(L.cfi_glue_swiglu(P(self.gate), P(self.up), P(self.gu), c.ffn, sv), "swiglu")
+            quant(self.gu, self.gq, c.ffn)
+            gemv(lay["wd"], self.gq, self.dn, c.hidden, c.ffn)
+            self._chk(L.cfi_glue_add(P(self.x), P(self.dn), c.hidden, sv), "add")
+            self.launches_per_step += 5  # rms_norm x2, rope x2, soft_max
+        g.rms_norm(self.x.data_ptr(), self.h.data_ptr(), c.hidden, 1, mul=self.out_norm.data_ptr(), eps=c.eps, stream=s)
+        quant(self.h, self.hq, c.hidden)
+        gemv(self.embd, self.hq, self.logits, c.vocab, c.hidden)
+        self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
+        self.launches_per_step += 1  # the output rms_norm

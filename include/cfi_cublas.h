@@ -5,8 +5,9 @@
  * in for (cuda-for-intel crates/cublas_shim/src/lib.rs:887-1076, validation plan.rs:160-215):
  * C = alpha * op(A) * op(B) + beta * C.  f16/bf16 inputs with op(A) = A^T and op(B) = B -- the
  * layout ggml uses for its dense and attention GEMMs -- run on the 5th-generation tensor cores
- * (tcgen05, fp32 accumulate in tensor memory, TMA-fed); every other legal combination runs a SIMT
- * kernel with fp32 accumulation.  Calls are asynchronous on the handle's stream.
+ * (tcgen05, fp32 accumulate in tensor memory, TMA-fed) -- or, with at most 8 columns (decode-time
+ * attention), a warp-per-row skinny kernel; every other legal combination runs a SIMT kernel with
+ * fp32 accumulation.  Calls are asynchronous on the handle's stream.
  */
 #ifndef CFI_CUBLAS_H
 #define CFI_CUBLAS_H
@@ -70,7 +71,8 @@ CFI_API int cfi_blas_sgemm(cfi_blas *handle, int transa, int transb, int m, int 
 /* plan::validate (plan.rs:160-215): 0, CFI_BLAS_INVALID_VALUE or CFI_BLAS_NOT_SUPPORTED. */
 CFI_API int cfi_blas_validate(int transa, int transb, int m, int n, int k, int lda, int ldb, int ldc, int a_type,
                               int b_type, int c_type, int compute_type);
-/* Which kernel the last GEMM call of this handle ran: 1 tcgen05, 2 SIMT, 0 none (early return). */
+/* Which kernel the last GEMM call of this handle ran: 1 tcgen05, 2 SIMT, 3 skinny (n <= 8 columns),
+ * 0 none (early return). */
 CFI_API int cfi_blas_last_path(cfi_blas *handle);
 
 #ifdef __cplusplus

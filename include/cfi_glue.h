@@ -1,0 +1,45 @@
+/*
+ * cfi_glue.h -- element-wise helpers of libcfi_b200.so for the synthetic decode driver.
+ *
+ * No counterpart in cuda-for-intel: in a real deployment ggml runs its own get_rows, add, cpy, glu
+ * and argmax kernels between the substituted ones.  These let a whole token step run on this
+ * library's kernels (and be captured as one CUDA graph): positions and token ids are read from
+ * device memory.  All pointers are device pointers; `stream` is a cudaStream_t; each returns 0 or
+ * a CUDA error code.
+ */
+#ifndef CFI_GLUE_H
+#define CFI_GLUE_H
+#include <stdint.h>
+
+#ifndef CFI_API
+#define CFI_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[0..ncols) = row ids[0] of a row-major Q8_0 matrix, dequantised to f32 */
+CFI_API int cfi_glue_get_rows_q8_0(const void *table, const int32_t *ids, float *out, int ncols, void *stream);
+/* q += bq, k += bk, v += bv (nq and nkv values) */
+CFI_API int cfi_glue_qkv_bias(float *q, float *k, float *v, const float *bq, const float *bk, const float *bv, int nq,
+                              int nkv, void *stream);
+/* K cache [kv head][pos][dim] and V cache [kv head][dim][pos] (f16, n_ctx positions) at pos[0];
+ * q16 = f16(q) */
+CFI_API int cfi_glue_kv_store(const float *q, const float *k, const float *v, void *q16, void *kc, void *vc,
+                              const int32_t *pos, int nq, int nkv, int head_dim, int n_ctx, void *stream);
+/* mask[j] = 0 for j <= pos[0], -inf after */
+CFI_API int cfi_glue_causal_mask(float *mask, const int32_t *pos, int n_ctx, void *stream);
+/* y = f16(x) */
+CFI_API int cfi_glue_to_f16(const float *x, void *y, int n, void *stream);
+/* x += y */
+CFI_API int cfi_glue_add(float *x, const float *y, int n, void *stream);
+/* out = silu(g) * u */
+CFI_API int cfi_glue_swiglu(const float *g, const float *u, float *out, int n, void *stream);
+/* token[0] = first index of max(logits[0..n)); pos[0] += 1 */
+CFI_API int cfi_glue_argmax_next(const float *logits, int n, int32_t *token, int32_t *pos, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

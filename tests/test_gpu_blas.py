@@ -49,7 +49,7 @@ def test_gemm_ex_tn_on_tensor_cores(blas, m, n, k, dt):
                       B.R_32F, m)
     assert st == 0
     sync()
-    assert blas.last_path() == 1, "expected the tcgen05 path"
+    assert blas.last_path() == (3 if n <= 8 else 1), "expected the skinny (n <= 8) or the tcgen05 path"
     want = (A.float() @ Bm.float().T).T
     assert rel(Cm, want) < REL_L2
     if m * n <= 5000000 and dt == torch.float16:
@@ -115,7 +115,7 @@ def test_attention_gemms_strided_and_pointer_arrays(blas):
                                       n_tok * n_kv, heads)
     assert st == 0
     sync()
-    assert blas.last_path() == 1
+    assert blas.last_path() == 3  # 7 columns: the skinny kernel
     assert rel(KQ2, want) < REL_L2
     # KQV: V^T (d x n_kv per head, stored n_kv x d column-major... op(A) = A^T with A stored n_kv x d)
     V = torch.randn(heads, d, n_kv, device="cuda").half()      # column-major n_kv x d per head
@@ -128,6 +128,56 @@ def test_attention_gemms_strided_and_pointer_arrays(blas):
     sync()
     wantv = torch.stack([(V[h].float() @ P[h].float().T).T for h in range(heads)])
     assert rel(O16.float(), wantv) < 2e-3
+
+
+@pytest.mark.parametrize("n", [1, 3, 7, 8])
+@pytest.mark.parametrize("k", [64, 63, 680, 1000])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_skinny_gemm_batched_beta_and_tails(blas, n, k, dt):
+    """n <= 8 columns: the warp-per-row kernel, strided batches, k not a multiple of 8 (lda = ldb
+    rounded up to 8 so the rows stay 16-byte aligned), 16-bit output with beta, f32 output."""
+    torch.manual_seed(n * 1000 + k)
+    at = B.R_16F if dt == torch.float16 else B.R_16BF
+    m, batch = 300, 3
+    ld = (k + 7) // 8 * 8
+    A = torch.randn(batch, m, ld, device="cuda").to(dt)
+    Bm = torch.randn(batch, n, ld, device="cuda").to(dt)
+    C0 = torch.randn(batch, n, m, device="cuda").to(dt)  # output in the input type (cuBLAS rule)
+    Cm = C0.clone()
+    st = blas.gemm_strided_batched_ex(B.OP_T, B.OP_N, m, n, k, 0.5, A.data_ptr(), at, ld, m * ld, Bm.data_ptr(), at,
+                                      ld, n * ld, 1.5, Cm.data_ptr(), at, m, n * m, batch)
+    assert st == 0
+    sync()
+    assert blas.last_path() == 3
+    want = torch.stack([0.5 * (A[z, :, :k].float() @ Bm[z, :, :k].float().T).T + 1.5 * C0[z].float()
+                        for z in range(batch)])
+    assert rel(Cm.float(), want) < (2e-3 if dt == torch.float16 else 1e-2)  # output rounding
+    Cf = torch.zeros(batch, n, m, device="cuda")
+    st = blas.gemm_strided_batched_ex(B.OP_T, B.OP_N, m, n, k, 1.0, A.data_ptr(), at, ld, m * ld, Bm.data_ptr(), at,
+                                      ld, n * ld, 0.0, Cf.data_ptr(), B.R_32F, m, n * m, batch)
+    assert st == 0
+    sync()
+    want = torch.stack([(A[z, :, :k].float() @ Bm[z, :, :k].float().T).T for z in range(batch)])
+    assert rel(Cf, want) < 1e-5
+
+
+def test_skinny_switch_routes_to_tensor_cores(blas, monkeypatch):
+    """CFI_GEMM_SKINNY=0 sends n <= 8 to the tcgen05 kernel; both give the same result."""
+    torch.manual_seed(9)
+    m, n, k = 680, 7, 64
+    A = torch.randn(m, k, device="cuda").half()
+    Bm = torch.randn(n, k, device="cuda").half()
+    out = []
+    for env, path in (("1", 3), ("0", 1)):
+        monkeypatch.setenv("CFI_GEMM_SKINNY", env)
+        Cm = torch.zeros(n, m, device="cuda")
+        assert blas.gemm_ex(B.OP_T, B.OP_N, m, n, k, 1.0, A.data_ptr(), B.R_16F, k, Bm.data_ptr(), B.R_16F, k, 0.0,
+                            Cm.data_ptr(), B.R_32F, m) == 0
+        sync()
+        assert blas.last_path() == path
+        out.append(Cm)
+    want = (A.float() @ Bm.float().T).T
+    assert rel(out[0], want) < 1e-5 and rel(out[1], want) < 1e-5
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 1), (0, 1), (1, 0)])

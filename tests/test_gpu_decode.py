@@ -1,0 +1,195 @@
+"""The synthetic decode driver (BASELINE config 4 architecture) on the GPU against a plain PyTorch
+float64 evaluation of the same layer math (weights dequantised from the same Q8_0 blocks,
+activations put through the same q8_1 rounding, the attention operands through the same fp16
+rounding), and captured-graph replays against eager steps.
+
+Each operation is checked teacher-forced -- fed the inputs the kernels themselves produced -- at
+1e-5 relative L2.  A float64 evaluation chained through a whole step drifts further: every q8_1
+activation quantisation turns the ~1e-6 fp32/fp64 differences (rope at large angles, fp16
+rounding of q and the probabilities) into whole-step rounding flips, 5-10x growth per
+quantisation point (measured: attention output 4.5e-5, O projection 4.9e-4, FFN gate 2.3e-3), so
+the chained logits are held to 5e-2."""
+import math
+
+import numpy as np
+import pytest
+
+import cfi_b200 as cfi
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from decode import Config, DecodeModel  # noqa: E402
+
+
+def deq_q8_0(blocks, rows, k):
+    b = blocks.view(-1, 34)
+    d = b[:, 0:2].contiguous().view(torch.float16).float().double()
+    q = b[:, 2:].contiguous().view(torch.int8).double()
+    return (q * d).reshape(rows, k)
+
+
+def q8_1_round(x):
+    """quantize_q8_1 then dequantise (refs.rs:119-147): d = amax/127 stored as fp16, q = roundf(x/d)."""
+    xb = x.float().reshape(-1, 32)
+    amax = xb.abs().amax(dim=1, keepdim=True)
+    d = amax / 127.0
+    q = torch.where(amax > 0, torch.sign(xb / d) * torch.floor(torch.abs(xb / d) + 0.5), torch.zeros_like(xb))
+    return (q.double() * d.half().double()).reshape(-1)
+
+
+def rms(x, w, eps):
+    return x / torch.sqrt((x * x).mean() + eps) * w.double()
+
+
+def rope(x, nh, hd, pos, theta):
+    x = x.reshape(nh, hd)
+    half = hd // 2
+    i = torch.arange(half, dtype=torch.float64, device=x.device)
+    ang = pos * theta ** (-2.0 * i / hd)
+    c, s = torch.cos(ang), torch.sin(ang)
+    a, b = x[:, :half], x[:, half:]
+    return torch.cat([a * c - b * s, a * s + b * c], dim=1).reshape(-1)
+
+
+def reference_step(m, token, pos):
+    c = m.cfg
+    nq = c.n_head * c.head_dim
+    grp = c.n_head // c.n_kv_head
+    E = deq_q8_0(m.embd, c.vocab, c.hidden)
+    x = E[token].clone()
+    for lay in m.layers:
+        W = lambda name, r, k: deq_q8_0(lay[name], r, k)
+        h = q8_1_round(rms(x, lay["attn_norm"], c.eps))
+        q = W("wq", nq, c.hidden) @ h + lay["bq"].double()
+        k = W("wk", c.n_kv_head * c.head_dim, c.hidden) @ h + lay["bk"].double()
+        v = W("wv", c.n_kv_head * c.head_dim, c.hidden) @ h + lay["bv"].double()
+        q = rope(q, c.n_head, c.head_dim, pos, c.theta)
+        k = rope(k, c.n_kv_head, c.head_dim, pos, c.theta)
+        kc = lay["kc"].clone()
+        vc = lay["vc"].clone()
+        kc[:, pos] = k.reshape(c.n_kv_head, c.head_dim).half()
+        vc[:, :, pos] = v.reshape(c.n_kv_head, c.head_dim).half()
+        q16 = q.half().double().reshape(c.n_head, c.head_dim)
+        out = torch.zeros(c.n_head, c.head_dim, dtype=torch.float64, device=x.device)
+        for hh in range(c.n_head):
+            g = hh // grp
+            sc = kc[g].double() @ q16[hh] / math.sqrt(c.head_dim)
+            sc[pos + 1:] = -math.inf
+            p = torch.softmax(sc, dim=0).float().half().double()
+            out[hh] = vc[g].double() @ p
+        a = q8_1_round(out.reshape(-1))
+        x = x + W("wo", c.hidden, nq) @ a
+        h = q8_1_round(rms(x, lay["ffn_norm"], c.eps))
+        gt = W("wg", c.ffn, c.hidden) @ h
+        up = W("wu", c.ffn, c.hidden) @ h
+        gu = q8_1_round(gt / (1 + torch.exp(-gt)) * up)
+        x = x + W("wd", c.hidden, c.ffn) @ gu
+    h = q8_1_round(rms(x, m.out_norm, c.eps))
+    return E @ h
+
+
+@pytest.fixture(scope="module")
+def model():
+    assert torch.cuda.is_available()
+    ctx = cfi.Ctx(0)
+    m = DecodeModel(torch, ctx, torch.device("cuda", 0), Config(layers=2, vocab=2048))
+    yield m
+    ctx.close()
+
+
+@pytest.fixture(scope="module")
+def model1():
+    ctx = cfi.Ctx(0)
+    m = DecodeModel(torch, ctx, torch.device("cuda", 0), Config(layers=1, vocab=2048), seed=0x1234)
+    yield m
+    ctx.close()
+
+
+def rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm())
+
+
+def test_each_operation_of_a_step_teacher_forced(model1):
+    m = model1
+    c = m.cfg
+    lay = m.layers[0]
+    nq, grp, pos = c.n_head * c.head_dim, c.n_head // c.n_kv_head, c.prompt
+    m.reset(token=77)
+    m.step(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert cfi.lib().cfi_device_error() == 0
+    E = deq_q8_0(m.embd, c.vocab, c.hidden)
+    W = lambda name, r, k: deq_q8_0(lay[name], r, k)
+    tol = 1e-5
+    h = q8_1_round(rms(E[77], lay["attn_norm"], c.eps))
+    assert rel(m.q, W("wq", nq, c.hidden) @ h + lay["bq"].double()) < tol
+    assert rel(m.k, W("wk", 128, c.hidden) @ h + lay["bk"].double()) < tol
+    assert rel(m.v, W("wv", 128, c.hidden) @ h + lay["bv"].double()) < tol
+    # fp32 angles near 631 rad: ~6e-6 (the rope kernel's own test bound is 1e-4)
+    assert rel(m.qr, rope(m.q.double(), c.n_head, c.head_dim, pos, c.theta)) < 3e-5
+    assert rel(m.kr, rope(m.k.double(), c.n_kv_head, c.head_dim, pos, c.theta)) < 3e-5
+    kc, vc = lay["kc"].double(), lay["vc"].double()
+    assert torch.equal(lay["kc"][:, pos], m.kr.reshape(2, 64).half())
+    assert torch.equal(lay["vc"][:, :, pos], m.v.reshape(2, 64).half())
+    q16 = m.qr.half().double().reshape(c.n_head, c.head_dim)
+    sc = torch.stack([kc[hh // grp] @ q16[hh] for hh in range(c.n_head)])
+    assert rel(m.scores.reshape(c.n_head, -1)[:, :pos + 1], sc[:, :pos + 1]) < tol
+    sm = m.scores.double().reshape(c.n_head, -1) / math.sqrt(c.head_dim)
+    sm[:, pos + 1:] = -math.inf
+    assert rel(m.probs.reshape(c.n_head, -1), torch.softmax(sm, 1)) < tol
+    p16 = m.probs.half().double().reshape(c.n_head, -1)
+    out = torch.stack([vc[hh // grp] @ p16[hh] for hh in range(c.n_head)]).reshape(-1)
+    assert rel(m.attn, out) < tol
+    assert rel(m.o, W("wo", c.hidden, nq) @ q8_1_round(m.attn.double())) < tol
+    x1 = E[77] + m.o.double()
+    h2 = q8_1_round(rms(x1, lay["ffn_norm"], c.eps))
+    assert rel(m.gate, W("wg", c.ffn, c.hidden) @ h2) < tol
+    assert rel(m.up, W("wu", c.ffn, c.hidden) @ h2) < tol
+    g, u = m.gate.double(), m.up.double()
+    assert rel(m.gu, g / (1 + torch.exp(-g)) * u) < tol
+    assert rel(m.dn, W("wd", c.hidden, c.ffn) @ q8_1_round(m.gu.double())) < tol
+    assert rel(m.x, x1 + m.dn.double()) < tol
+    assert rel(m.logits, E @ q8_1_round(rms(m.x.double(), m.out_norm, c.eps))) < tol
+    assert int(m.token.item()) == int(torch.argmax(m.logits).item())
+    assert int(m.pos.item()) == pos + 1
+
+
+def test_whole_step_against_the_chained_evaluation(model):
+    m = model
+    m.reset(token=77)
+    m.step(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert cfi.lib().cfi_device_error() == 0
+    want = reference_step(m, 77, m.cfg.prompt)
+    assert rel(m.logits, want) < 5e-2
+
+
+def test_graph_replay_equals_eager_steps(model):
+    m = model
+    s = torch.cuda.current_stream()
+    for lay in m.layers:
+        lay["kc"][:, m.cfg.prompt:] = 0
+        lay["vc"][:, :, m.cfg.prompt:] = 0
+    m.reset(token=5)
+    eager = []
+    for _ in range(3):
+        m.step(s.cuda_stream)
+        eager.append((int(m.token.item()), m.logits.clone()))
+    torch.cuda.synchronize()
+    # rewind the KV caches to the prompt (the eager steps wrote positions prompt .. prompt+2)
+    for lay in m.layers:
+        lay["kc"][:, m.cfg.prompt:] = 0
+        lay["vc"][:, :, m.cfg.prompt:] = 0
+    m.reset(token=5)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        m.step(torch.cuda.current_stream().cuda_stream)
+    m.reset(token=5)
+    for tok, logits in eager:
+        gr.replay()
+        torch.cuda.synchronize()
+        assert int(m.token.item()) == tok
+        assert torch.equal(m.logits, logits)
+    assert cfi.lib().cfi_device_error() == 0
+    del gr
