@@ -190,6 +190,141 @@ def prefill_gemm(cfi, g, stream, dev, peak_tf):
                          "frac": round(best / peak_tf, 4), "peak_kind": "measured bf16 dense (burst)"}}
 
 
+def graph_time_us(stream, body, reps=5, calls=1):
+    """Capture `calls` x body(stream_handle) in one CUDA graph; mean device time per body call (µs)
+    over `reps` replays after one warm replay, CUDA events on the launching stream."""
+    import torch
+
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        for i in range(calls):
+            body(i, torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.stream(stream):
+        gr.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+    del gr
+    return us
+
+
+def config1_bench(cfi, g, stream, dev, peak):
+    """Q8_0 mul_mat_vec_q 4864x896 on its own (batch 1), and with its
+    quantize_q8_1 in front, back to back over rotated weight copies (> 3x L2)."""
+    import torch
+
+    rows, k = 4864, 896
+    wb = rows * k // 32 * 34
+    ncopy = int(np.ceil(3 * L2_BYTES / wb))
+    w = torch.from_numpy(cfi.synthetic_weights(cfi.Q8_0, rows, k, seed=11).ravel()).to(dev)
+    wd = torch.empty((ncopy, w.numel()), dtype=torch.uint8, device=dev)
+    wd[:] = w
+    x = torch.from_numpy(np.random.default_rng(3).normal(size=k).astype(np.float32)).to(dev)
+    q = torch.zeros(k // 32 * 36, dtype=torch.uint8, device=dev)
+    y = torch.zeros(rows, dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        g.quantize_q8_1(x.data_ptr(), q.data_ptr(), k, k, 1, stream=stream.cuda_stream)
+        g.mmvq(cfi.Q8_0, 1, wd[0].data_ptr(), q.data_ptr(), y.data_ptr(), k, rows, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    mm = lambda i, st: g.mmvq(cfi.Q8_0, 1, wd[i].data_ptr(), q.data_ptr(), y.data_ptr(), k, rows, stream=st)
+
+    def pair(i, st):
+        g.quantize_q8_1(x.data_ptr(), q.data_ptr(), k, k, 1, stream=st)
+        mm(i, st)
+    us = graph_time_us(stream, mm, calls=ncopy)
+    us_pair = graph_time_us(stream, pair, calls=ncopy)
+    mbytes = wb + k // 32 * 36 + rows * 4                 # 4,650,992
+    qbytes = k * 4 + k // 32 * 36
+    return {"workload": "config1: Q8_0 mul_mat_vec_q 4864x896, batch 1 (weights rotated over %d copies, %.0f MB)"
+                        % (ncopy, ncopy * wb / 1e6),
+            "mmvq_us": round(us, 3), "mmvq_gbs": round(mbytes / us / 1e3, 1),
+            "mmvq_frac": round(mbytes / us / 1e3 / peak, 4),
+            "quantize_plus_mmvq_us": round(us_pair, 3), "quantize_plus_mmvq_gbs": round((mbytes + qbytes) / us_pair / 1e3, 1),
+            "bytes_per_call": mbytes}
+
+
+def config5_bench(cfi, g, stream, dev, peak_gbs, peak_tf):
+    """Qwen2.5-1.5B-architecture weight products, 28 layers of Q4_K matrices
+    (q, o 1536x1536; k, v 256x1536; gate, up 8960x1536; down 1536x8960) and the Q8_0 head
+    151936x1536: (a) a 631-token prefill -- per layer the activations quantised to q8_1_mmq once
+    per distinct input (attention input, attention output, FFN input, FFN hidden) and the seven
+    mul_mat_q products; the head on the last token only (quantize_q8_1 + mul_mat_vec_q), as ggml
+    does; (b) one batch-64 decode step of 64 independent sequences -- the same products with 64
+    columns (mul_mat_q, as ggml uses above 8 columns), the head included.  Attention and the
+    element-wise ops are not in this leg.  Weights random, device-side (seeded)."""
+    import torch
+
+    from decode import random_q4_k, random_q8_0
+
+    H, F, KV, L, V = 1536, 8960, 256, 28, 151936
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    shapes = {"q": (H, H), "k": (KV, H), "v": (KV, H), "o": (H, H), "g": (F, H), "u": (F, H), "d": (H, F)}
+    layers = [{n: random_q4_k(torch, r, c, gen, dev) for n, (r, c) in shapes.items()} for _ in range(L)]
+    head = random_q8_0(torch, V, H, gen, dev)
+    wbytes = sum(t.numel() for lay in layers for t in lay.values()) + head.numel()
+    params = L * sum(r * c for r, c in shapes.values())
+
+    def buffers(n):
+        xf = {kk: torch.randn(n * kk, generator=gen, device=dev) for kk in (H, F)}
+        xq = {kk: torch.zeros(kk // 128 * n * 144, dtype=torch.uint8, device=dev) for kk in (H, F)}
+        out = {nm: torch.zeros(n * r, dtype=torch.float32, device=dev) for nm, (r, c) in shapes.items()}
+        return xf, xq, out
+
+    def layer_products(n, xf, xq, out, st):
+        for lay in layers:
+            for inputs, k in ((("q", "k", "v"), H), (("o",), H), (("g", "u"), H), (("d",), F)):
+                g.quantize_mmq(1, xf[k].data_ptr(), xq[k].data_ptr(), k, k, n, stream=st)
+                for nm in inputs:
+                    r = shapes[nm][0]
+                    g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, r, n, stream=st)
+
+    # (a) prefill, 631 tokens
+    n = 631
+    xf, xq, out = buffers(n)
+    hq = torch.zeros(H // 32 * 36, dtype=torch.uint8, device=dev)
+    logits = torch.zeros(V, dtype=torch.float32, device=dev)
+
+    def prefill(i, st):
+        layer_products(n, xf, xq, out, st)
+        g.quantize_q8_1(xf[H].data_ptr() + (n - 1) * H * 4, hq.data_ptr(), H, H, 1, stream=st)
+        g.mmvq(cfi.Q8_0, 1, head.data_ptr(), hq.data_ptr(), logits.data_ptr(), H, V, stream=st)
+    with torch.cuda.stream(stream):
+        prefill(0, stream.cuda_stream)
+    torch.cuda.synchronize()
+    us_pf = graph_time_us(stream, prefill, reps=3)
+    pf_ops = 2.0 * params * n + 2.0 * V * H
+    # (b) batch-64 decode step
+    n = 64
+    xf, xq, out = buffers(n)
+    hq64 = torch.zeros(H // 128 * n * 144, dtype=torch.uint8, device=dev)
+    logits64 = torch.zeros(n * V, dtype=torch.float32, device=dev)
+
+    def decode64(i, st):
+        layer_products(n, xf, xq, out, st)
+        g.quantize_mmq(0, xf[H].data_ptr(), hq64.data_ptr(), H, H, n, stream=st)
+        g.mmq(cfi.Q8_0, head.data_ptr(), hq64.data_ptr(), logits64.data_ptr(), H, V, n, stream=st)
+    with torch.cuda.stream(stream):
+        decode64(0, stream.cuda_stream)
+    torch.cuda.synchronize()
+    us_dc = graph_time_us(stream, decode64, reps=5)
+    launches = L * (4 + 7) + 2
+    res = {"workload": "config5: Qwen2.5-1.5B-architecture weight products (28 layers Q4_K + Q8_0 head, %d B of "
+                       "weights), 631-token prefill and a batch-64 decode step; attention not included" % wbytes,
+           "prefill": {"ms": round(us_pf / 1e3, 3), "tok_per_s": round(631 / (us_pf * 1e-6), 1),
+                       "tflops": round(pf_ops / us_pf / 1e6, 1), "frac": round(pf_ops / us_pf / 1e6 / peak_tf, 4),
+                       "launches": launches},
+           "decode_b64": {"ms": round(us_dc / 1e3, 3), "tok_per_s": round(64 / (us_dc * 1e-6), 1),
+                          "weights_gbs": round(wbytes / us_dc / 1e3, 1),
+                          "frac": round(wbytes / us_dc / 1e3 / peak_gbs, 4), "launches": launches}}
+    del layers, head
+    return res
+
+
 def decode_bench(stream, dev, ntok=48, warm=3):
     """Qwen2.5-0.5B-architecture decode (24 layers, Q8_0 random weights, 631-token
     seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens."""
@@ -455,10 +590,17 @@ def run_gpu(args, rank, world):
             line["prefill"] = prefill_gemm(cfi, g, stream, dev, tensor_peak())
         if not args.no_decode and world == 1:
             line["decode"] = decode_bench(stream, dev)
+        if not args.no_configs and world == 1:
+            line["config1"] = config1_bench(cfi, g, stream, dev, peak)
+            line["config5"] = config5_bench(cfi, g, stream, dev, peak, tensor_peak())
         if not args.no_cpu and world == 1:
             gbs, used, n, el = cpu_baseline(args.cpu_seconds)
+            gbs1, _, n1, el1 = cpu_baseline(max(1.0, args.cpu_seconds / 2), threads=1)
             line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
-                                    "sample": "%d full steps (4 batches each) in %.1f s" % (n, el)}
+                                    "sample": "%d full steps (4 batches each) in %.1f s, rows split over %d threads"
+                                              % (n, el, used),
+                                    "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
+                                                      "sample": "%d full steps in %.1f s" % (n1, el1)}}
         print(json.dumps(line), flush=True)
     del graphs, ge
     if dist:
@@ -476,6 +618,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 5 legs")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     args = ap.parse_args()
     if args.warmup < 3:

@@ -61,3 +61,12 @@ struct TcGemm {
     int scalar_f16;
 };
 int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream);
+
+// Split-K support of k_gemm_sm100.cu shared with the quantized GEMM: a per-device fp32 workspace
+// (grown outside stream capture; nullptr when it cannot be; replaced buffers stay allocated) and
+// the ordered reduction C[plane][col][row] = sum over splits of ws[split][plane][col][row] (f32 C,
+// alpha 1, beta 0; plane p: channel p % nch, sample p / nch).
+float* cfi_splitk_workspace(size_t bytes, cudaStream_t stream);
+int cfi_splitk_reduce_f32(const float* ws, uint32_t ld_ws, uint32_t m, uint32_t n, uint32_t planes, uint32_t splits,
+                          float* c, long long ldc, long long c_zstride, long long c_wstride, uint32_t nch,
+                          cudaStream_t stream, bool pdl);

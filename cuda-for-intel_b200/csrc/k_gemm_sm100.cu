@@ -23,6 +23,7 @@
 #include <map>
 #include <mutex>
 #include <type_traits>
+#include <vector>
 
 #include "../../include/cfi_cublas.h"
 #include "cfi_common.cuh"
@@ -636,9 +637,11 @@ bool dtype_ok(int t) { return t == CFI_R_32F || t == CFI_R_16F || t == CFI_R_16B
 
 }  // namespace
 
-// Per-device split-K workspace (fp32 partial tiles), grown outside stream capture only.
+// Per-device split-K workspace (fp32 partial tiles), grown outside stream capture only.  A
+// replaced buffer is kept, not freed: graphs captured earlier still name it.
 static std::mutex g_ws_mu;
 static std::map<int, std::pair<void*, size_t>> g_ws;
+static std::vector<void*> g_ws_retired;
 static float* splitk_workspace(size_t bytes, cudaStream_t stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
@@ -647,7 +650,7 @@ static float* splitk_workspace(size_t bytes, cudaStream_t stream) {
     if (w.second < bytes) {
         cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(stream, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone) return nullptr;
-        if (w.first) cudaFree(w.first);
+        if (w.first) g_ws_retired.push_back(w.first);
         w.first = nullptr;
         w.second = 0;
         const size_t want = bytes + bytes / 4;
@@ -846,6 +849,42 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
     }
     return (int)(d.fmt == 0 ? cudaLaunchKernelEx(&cfg, cfi_gemm_tc<0>, ta, tb, tcm, g)
                             : cudaLaunchKernelEx(&cfg, cfi_gemm_tc<1>, ta, tb, tcm, g));
+}
+
+float* cfi_splitk_workspace(size_t bytes, cudaStream_t stream) { return splitk_workspace(bytes, stream); }
+
+int cfi_splitk_reduce_f32(const float* ws, uint32_t ld_ws, uint32_t m, uint32_t n, uint32_t planes, uint32_t splits,
+                          float* c, long long ldc, long long c_zstride, long long c_wstride, uint32_t nch,
+                          cudaStream_t stream, bool pdl) {
+    ReduceArgs r;
+    r.ws = ws;
+    r.ld_ws = ld_ws;
+    r.m = m;
+    r.n = n;
+    r.planes = planes;
+    r.splits = splits;
+    r.c = c;
+    r.c_type = CFI_R_32F;
+    r.ldc = ldc;
+    r.c_zstride = c_zstride;
+    r.c_wstride = c_wstride;
+    r.nch = nch;
+    r.alpha = 1.0f;
+    r.beta = 0.0f;
+    r.alpha_ptr = nullptr;
+    r.beta_ptr = nullptr;
+    r.scalar_f16 = 0;
+    cudaLaunchConfig_t rc = {};
+    const uint64_t nthr = (uint64_t)((m + 3) / 4) * n * planes;
+    rc.gridDim = dim3((uint32_t)((nthr + 255) / 256), 1, 1);
+    rc.blockDim = dim3(256, 1, 1);
+    rc.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    rc.attrs = at;
+    rc.numAttrs = pdl ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&rc, cfi_gemm_splitk_reduce, r);
 }
 
 // Reads and clears the error word of the GEMM kernel's bounded waits (folded into cfi_device_error).

@@ -29,6 +29,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
@@ -392,6 +393,316 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---- quantized GEMM with TMA-staged raw weight tiles (the default prefill path) ----
+// Warp 10 streams the raw weight bytes of one 256-value K chunk for the tile's 128 rows per TMA
+// load (Q4_K: one superblock, 144 B per row; Q8_0: eight blocks, 272 B per row) into a ring of
+// raw slots; warps 0-7 dequantize each 64-value stage of a chunk into the fp16 A ring (two
+// threads per row, one 32-value group each, stored in the 128-byte swizzled K-major layout);
+// warp 9 streams the fp16 activations (Xh) with TMA; one thread of warp 8 issues tcgen05.mma.
+// Q4_K's appended correction stages (half(-dmin m) against the per-group sums) read the
+// superblock headers from global memory.  K may be split over blockIdx.z (plane * splits +
+// split) in whole chunks; split partials go to a workspace through the C tensor map and an
+// ordered reduction kernel sums them.
+constexpr int QMM_THREADS = 352;
+constexpr int QMM_MMA_WARP = 8, QMM_B_WARP = 9, QMM_RAW_WARP = 10;
+constexpr int QMM_MAX_NS = 4, QMM_MAX_RAW = 4;
+
+struct QmmArgs {
+    const uint8_t* x;  // weights (for the Q4_K correction stages)
+    uint32_t K, Kt, nrows, ncols_dst, bn;
+    uint32_t ns, nraw, b_stage;  // A/B ring depth, raw ring depth, bytes of a B stage
+    uint32_t splits, kchunk;     // stages per split (a multiple of 4)
+    uint32_t stride_row_x, stride_channel_x, stride_sample_x;  // blocks
+    uint32_t nchannels_y, channel_ratio, sample_ratio;
+    int tma_c;  // 0: dst stored with plain 16-byte stores (splits == 1 only)
+    float* dst;
+    uint32_t stride_col_dst, stride_channel_dst, stride_sample_dst;
+    unsigned int* err;
+};
+
+template <uint32_t TY>
+constexpr uint32_t qmm_raw_row() { return TY == T_Q4_K ? 144u : 272u; }
+
+// Q8_0 stage s4 of a chunk, block 2 s4 + hh of row r: the block starts 4 s4 + 2 hh bytes into the
+// 16-byte aligned 48-byte window at row + 64 s4 + 32 hh.
+template <int S4>
+CFI_DEV void qmm_dequant_q80(const uint8_t* rowp, int hh, uint8_t* atom, int r) {
+    const uint4* win = reinterpret_cast<const uint4*>(rowp + 64 * S4 + 32 * hh);
+    const uint4 c0 = win[0], c1 = win[1], c2 = win[2];
+    const uint32_t w[12] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x, c2.y, c2.z, c2.w};
+    if (hh == 0) {  // d in the low half of word S4, quants from byte 2 of it
+        const __half2 d2 = __half2half2(__ushort_as_half((uint16_t)(w[S4] & 0xffffu)));
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint32_t q0 = __funnelshift_r(w[S4 + 2 * c], w[S4 + 2 * c + 1], 16);
+            const uint32_t q1 = __funnelshift_r(w[S4 + 2 * c + 1], w[S4 + 2 * c + 2], 16);
+            uint32_t v0, v1, v2, v3;
+            dequant4(q0, d2, v0, v1);
+            dequant4(q1, d2, v2, v3);
+            st_chunk(atom, r, c, v0, v1, v2, v3);
+        }
+    } else {  // d in the high half of word S4, quants word-aligned from word S4 + 1
+        const __half2 d2 = __half2half2(__ushort_as_half((uint16_t)(w[S4] >> 16)));
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            uint32_t v0, v1, v2, v3;
+            dequant4(w[S4 + 1 + 2 * c], d2, v0, v1);
+            dequant4(w[S4 + 2 + 2 * c], d2, v2, v3);
+            st_chunk(atom, r, 4 + c, v0, v1, v2, v3);
+        }
+    }
+}
+
+template <uint32_t TY>
+__global__ void __launch_bounds__(QMM_THREADS, 1)
+    cfi_qmm_tc(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_b,
+               const __grid_constant__ CUtensorMap tmap_c, const QmmArgs a) {
+    constexpr uint32_t RAW_ROW = qmm_raw_row<TY>();
+    constexpr uint32_t RAW_BYTES = BM * RAW_ROW;  // 18 KB / 34 KB (multiples of 1024)
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t NS = a.ns, NR = a.nraw;
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + NS * A_STAGE;
+    uint8_t* sRaw = sB + NS * a.b_stage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sRaw + NR * RAW_BYTES);
+    uint64_t* empty = full + QMM_MAX_NS;
+    uint64_t* raw_full = empty + QMM_MAX_NS;
+    uint64_t* raw_empty = raw_full + QMM_MAX_RAW;
+    uint64_t* done = raw_empty + QMM_MAX_RAW;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* epi_ok = abort_flag + 1;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t bn = a.bn;
+    const uint32_t tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+    const int kmain = (int)(a.K / BK), ktotal = (int)(a.Kt / BK);
+    const uint32_t split = blockIdx.z % a.splits, plane = blockIdx.z / a.splits;
+    const int k0 = (int)(split * a.kchunk);
+    const int k1 = min(ktotal, k0 + (int)a.kchunk);
+    const int nsteps = max(0, k1 - k0);
+    const int nchunks = k0 < kmain ? (min(k1, kmain) - k0 + 3) / 4 : 0;
+    const uint32_t row0 = blockIdx.x * BM, col0 = blockIdx.y * bn;
+    const uint32_t wt = plane / a.nchannels_y, zt = plane - wt * a.nchannels_y;
+    const uint32_t sx = wt / a.sample_ratio, cx = zt / a.channel_ratio;
+
+    if (tid == 0) {
+        for (uint32_t i = 0; i < NS; i++) {
+            mbar_init(&full[i], 8 + 1);  // one arrival per dequantizing warp + the B load's expect_tx
+            mbar_init(&empty[i], 1);     // tcgen05.commit
+        }
+        for (uint32_t i = 0; i < NR; i++) {
+            mbar_init(&raw_full[i], 1);  // the raw load's expect_tx
+            mbar_init(&raw_empty[i], 8);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == QMM_MMA_WARP) {
+        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
+    pdl_wait();  // weights and activations may come from the previous kernel
+
+    if (warp < 8) {
+        // ================= dequantization (256 threads), then the epilogue =================
+        const int r = tid & (BM - 1), hh = tid >> 7;
+        for (int i = 0; i < nsteps; i++) {
+            const int s = k0 + i;
+            const uint32_t slot = (uint32_t)i % NS;
+            const int j = i >> 2;  // chunk of the CTA (k0 is a multiple of 4)
+            bool ok = true;
+            if (s < kmain && (i & 3) == 0) ok = mbar_wait(&raw_full[j % NR], (uint32_t)(j / NR) & 1, abort_flag);
+            if (ok) ok = mbar_wait(&empty[slot], ((uint32_t)(i / NS) & 1) ^ 1, abort_flag);
+            if (!ok) {
+                if (lane == 0) {
+                    cfi_set_error(a.err, 0x800 + (uint32_t)warp);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            uint8_t* atom = sA + slot * A_STAGE;
+            if (s < kmain) {
+                const uint8_t* rowp = sRaw + (j % NR) * RAW_BYTES + r * RAW_ROW;
+                if (TY == T_Q8_0) {
+                    switch (s & 3) {
+                    case 0: qmm_dequant_q80<0>(rowp, hh, atom, r); break;
+                    case 1: qmm_dequant_q80<1>(rowp, hh, atom, r); break;
+                    case 2: qmm_dequant_q80<2>(rowp, hh, atom, r); break;
+                    default: qmm_dequant_q80<3>(rowp, hh, atom, r); break;
+                    }
+                } else {  // Q4_K: sub-block g = 2 (s % 4) + hh of the chunk's superblock
+                    const uint4 h = *reinterpret_cast<const uint4*>(rowp);
+                    const uint4 q0 = *reinterpret_cast<const uint4*>(rowp + 16 + 32 * (s & 3));
+                    const uint4 q1 = *reinterpret_cast<const uint4*>(rowp + 32 + 32 * (s & 3));
+                    const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                    const uint32_t sc[3] = {h.y, h.z, h.w};
+                    const float dd = __half2float(__ushort_as_half((uint16_t)(h.x & 0xffffu)));
+                    const int g = 2 * (s & 3) + hh;
+                    const int scv = g < 4 ? (scale_byte(sc, g) & 63)
+                                          : ((scale_byte(sc, g + 4) & 0xF) | ((scale_byte(sc, g - 4) >> 6) << 4));
+                    // the reference's tile loader stores half(d * sc) (refs.rs:709-712)
+                    const __half2 d2 = __half2half2(__float2half_rn(dd * (float)scv));
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t v0, v1, v2, v3;
+                        dequant4_u4(q[2 * c], 4 * hh, d2, v0, v1);
+                        dequant4_u4(q[2 * c + 1], 4 * hh, d2, v2, v3);
+                        st_chunk(atom, r, 4 * hh + c, v0, v1, v2, v3);
+                    }
+                }
+            } else {  // Q4_K correction stage: A[r][K + g] = half(-dmin * m_g) (refs.rs:712)
+                const int g0 = (s - kmain) * BK;
+                const int ngroups = (int)(a.K / 32);
+                const uint32_t row = row0 + r;
+                const uint8_t* rowg = a.x + ((size_t)sx * a.stride_sample_x + (size_t)cx * a.stride_channel_x +
+                                             (size_t)min(row, a.nrows - 1) * a.stride_row_x) * Q4_K_BYTES;
+#pragma unroll 1
+                for (int sbl = 4 * hh; sbl < 4 * hh + 4; sbl++) {
+                    const int gbase = g0 + 8 * sbl;
+                    uint32_t hw0 = 0, hs[3] = {0, 0, 0};
+                    if (row < a.nrows && gbase < ngroups) {
+                        const uint32_t* H = reinterpret_cast<const uint32_t*>(rowg + (size_t)(gbase / 8) * Q4_K_BYTES);
+                        hw0 = __ldg(H);
+                        hs[0] = __ldg(H + 1);
+                        hs[1] = __ldg(H + 2);
+                        hs[2] = __ldg(H + 3);
+                    }
+                    const float dmin = __half2float(__ushort_as_half((uint16_t)(hw0 >> 16)));
+                    uint32_t v[4];
+#pragma unroll
+                    for (int p = 0; p < 4; p++) {
+                        uint32_t hv[2];
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int gg = 2 * p + e;
+                            const int mv = gg < 4 ? (scale_byte(hs, gg + 4) & 63)
+                                                  : ((scale_byte(hs, gg + 4) >> 4) | ((scale_byte(hs, gg) >> 6) << 4));
+                            hv[e] = gbase < ngroups ? (uint32_t)__half_as_ushort(__float2half_rn(-dmin * (float)mv)) : 0u;
+                        }
+                        v[p] = hv[0] | (hv[1] << 16);
+                    }
+                    st_chunk(atom, r, sbl, v[0], v[1], v[2], v[3]);
+                }
+            }
+            fence_proxy_async_smem();  // this thread's A-tile writes, visible to the tensor core
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&full[slot]);
+                if (s < kmain && ((i & 3) == 3 || s == kmain - 1 || i == nsteps - 1)) mbar_arrive(&raw_empty[j % NR]);
+            }
+        }
+        // ================= epilogue: TMEM -> shared -> TMA stores =================
+        if (tid == 0) {
+            bool got = false;
+            if (!*abort_flag) {
+                got = mbar_wait(done, 0, abort_flag);
+                if (!got) {
+                    cfi_set_error(a.err, 0x900);
+                    *abort_flag = 1;
+                }
+            }
+            *epi_ok = got ? 1 : 0;
+        }
+        named_bar_sync(1, 256);
+        tc_fence_after();
+        if (*epi_ok && a.tma_c) {
+            // every MMA has completed: the A/B rings hold the 8 KB per-warp staging buffers
+            float* tbuf = reinterpret_cast<float*>(sA) + warp * 2048;
+            if (a.splits > 1)  // raw partial sums into the split-K workspace (plane, split)
+                tmem_tile_tma_store(tmem, warp, lane, 8, bn, tbuf, &tmap_c, (int)row0, (int)col0, (int)plane, (int)split,
+                                    [](float v) { return v; });
+            else
+                tmem_tile_tma_store(tmem, warp, lane, 8, bn, tbuf, &tmap_c, (int)row0, (int)col0, (int)zt, (int)wt,
+                                    [](float v) { return v; });
+        } else if (*epi_ok) {
+            float* dst = a.dst + (size_t)wt * a.stride_sample_dst + (size_t)zt * a.stride_channel_dst;
+            float* buf = reinterpret_cast<float*>(sA) + warp * 1024;
+            const bool vec = (a.stride_col_dst & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+            tmem_tile_store(tmem, warp, lane, 8, bn, buf, [&](uint32_t c, uint32_t rr, float4 f) {
+                const uint32_t col = col0 + c, row = row0 + rr;
+                if (col >= a.ncols_dst || row >= a.nrows) return;
+                float* p = dst + (size_t)col * a.stride_col_dst + row;
+                if (vec && row + 3 < a.nrows) {
+                    *reinterpret_cast<float4*>(p) = f;
+                } else {
+                    p[0] = f.x;
+                    if (row + 1 < a.nrows) p[1] = f.y;
+                    if (row + 2 < a.nrows) p[2] = f.z;
+                    if (row + 3 < a.nrows) p[3] = f.w;
+                }
+            });
+        }
+    } else if (warp == QMM_MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BM, bn, 0);
+            for (int i = 0; i < nsteps; i++) {
+                const uint32_t slot = (uint32_t)i % NS;
+                if (!mbar_wait(&full[slot], (uint32_t)(i / NS) & 1, abort_flag)) {
+                    cfi_set_error(a.err, 0xa00 + slot);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t abase = smem_u32(sA + slot * A_STAGE), bbase = smem_u32(sB + slot * a.b_stage);
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++)
+                    mma_f16(tmem, sw128_kmajor_desc(abase + 32 * k), sw128_kmajor_desc(bbase + 32 * k), idesc,
+                            (i > 0 || k > 0) ? 1u : 0u);
+                mma_commit(&empty[slot]);
+            }
+            mma_commit(done);  // also after a failure: `done` then tracks the MMAs already issued
+        }
+        __syncwarp();
+    } else if (warp == QMM_B_WARP) {
+        if (lane == 0) {
+            prefetch_tmap(&tmap_b);
+            const uint32_t bytes = bn * BK * 2;
+            for (int i = 0; i < nsteps; i++) {
+                const uint32_t slot = (uint32_t)i % NS;
+                if (!mbar_wait(&empty[slot], ((uint32_t)(i / NS) & 1) ^ 1, abort_flag)) {
+                    cfi_set_error(a.err, 0xb00 + slot);
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                tma_load_3d(sB + slot * a.b_stage, &tmap_b, (k0 + i) * BK, (int)col0, (int)plane, &full[slot]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ================= raw weight chunks =================
+        if (lane == 0) {
+            prefetch_tmap(&tmap_w);
+            constexpr int XU = TY == T_Q4_K ? 144 : 136;  // chunk width in tensor-map elements (u8 / u16)
+            for (int j = 0; j < nchunks; j++) {
+                const uint32_t rs = (uint32_t)j % NR;
+                if (!mbar_wait(&raw_empty[rs], ((uint32_t)(j / NR) & 1) ^ 1, abort_flag)) {
+                    cfi_set_error(a.err, 0xc00 + rs);
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
+                tma_load_4d(sRaw + rs * RAW_BYTES, &tmap_w, (k0 / 4 + j) * XU, (int)row0, (int)cx, (int)sx, &raw_full[rs]);
+            }
+        }
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == QMM_MMA_WARP) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
 // block_q8_1_mmq -> fp16 K-major rows: Xh[plane][col][k] = fp16(q * d) for k < K; for DS4
 // (Q4_K) Xh[plane][col][K + g] = s_g (the half float sum of group g), zero up to Kt.
 // One warp per (column, 128-value block); lane l handles values 4l..4l+3.
@@ -434,6 +745,8 @@ template <int DS4>
 __global__ void __launch_bounds__(256)
     cfi_mmq_x_to_f16(const uint8_t* __restrict__ y, __half* __restrict__ xh, uint32_t K, uint32_t Kt, uint32_t ncols,
                      uint32_t ncols_y, uint32_t nchannels_y, uint32_t stride_channel_y, uint32_t stride_sample_y) {
+    pdl_launch_dependents();
+    pdl_wait();
     x_to_f16<DS4>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y, stride_sample_y);
 }
 
@@ -554,13 +867,15 @@ PFN_encodeTiled encode_fn() {
     return fn;
 }
 
-// Per-device activation scratch (fp16 copy of X), grown outside stream capture only.
+// Per-device activation scratch (fp16 copy of X), grown outside stream capture only.  A replaced
+// buffer is kept, not freed: graphs captured earlier still name it.
 struct Scratch {
     void* p = nullptr;
     size_t cap = 0;
 };
 std::mutex g_scratch_mu;
 std::map<int, Scratch> g_scratch;
+std::vector<void*> g_scratch_retired;
 
 int scratch_for(size_t bytes, cudaStream_t stream, void** out) {
     int dev = 0;
@@ -571,7 +886,7 @@ int scratch_for(size_t bytes, cudaStream_t stream, void** out) {
         cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(stream, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone)
             return (int)cudaErrorStreamCaptureUnsupported;
-        if (s.p) cudaFree(s.p);
+        if (s.p) g_scratch_retired.push_back(s.p);
         s.p = nullptr;
         s.cap = 0;
         size_t want = bytes + bytes / 4;
@@ -600,6 +915,177 @@ uint32_t tile_n(uint32_t ncols_dst) {
     const uint32_t tiles = (ncols_dst + 255) / 256;
     const uint32_t per = (ncols_dst + tiles - 1) / tiles;
     return tiles > 1 ? (per + 31) / 32 * 32 : (per + 15) / 16 * 16;
+}
+
+// The fused quantized GEMM applies when TMA can address the raw weight chunks: every row, channel
+// and sample start 16-byte aligned.  Q4_K (144-byte superblocks) always; Q8_0 (34-byte blocks)
+// when K and the block strides are multiples of 256 values / 8 blocks.  CFI_MMQ_FUSED=0 off.
+template <uint32_t TY>
+bool qmm_applicable(const uint8_t* x, uint32_t K, uint32_t srx, uint32_t scx, uint32_t ssx, uint32_t nch_x,
+                    uint32_t ns_x) {
+    const char* e = getenv("CFI_MMQ_FUSED");
+    if (e && strcmp(e, "0") == 0) return false;
+    if (reinterpret_cast<uintptr_t>(x) & 15) return false;
+    if (TY == T_Q4_K) return K % 256 == 0;
+    return K % 256 == 0 && srx % 8 == 0 && (nch_x == 1 || scx % 8 == 0) && (ns_x == 1 || ssx % 8 == 0);
+}
+
+constexpr uint32_t QMM_SMEM_LIMIT = 232448;  // 227 KB of dynamic shared memory per CTA
+
+// Activations -> Xh (pre-pass), then cfi_qmm_tc (+ the split-K reduction).  Returns a CUDA error.
+template <uint32_t TY>
+int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_t K, uint32_t Kt, uint32_t nrows,
+               uint32_t ncols_dst, uint32_t srx, uint32_t ncols_y, uint32_t scd, uint32_t chr, uint32_t nch, uint32_t scx,
+               uint32_t scy, uint32_t scdst, uint32_t smr, uint32_t ns, uint32_t ssx, uint32_t ssy, uint32_t ssd,
+               cudaStream_t stream) {
+    PFN_encodeTiled enc = encode_fn();
+    if (!enc) return (int)cudaErrorNotSupported;
+    const char* ep = getenv("CFI_PDL");
+    const bool pdl = !(ep && strcmp(ep, "0") == 0);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    const uint32_t planes = nch * ns, nch_x = nch / chr, ns_x = ns / smr;
+    // 1. activations -> fp16 K-major
+    {
+        const uint32_t warps = ncols_dst * (K / 128);
+        cudaLaunchConfig_t c = {};
+        c.gridDim = dim3((warps * 32 + 255) / 256, planes, 1);
+        c.blockDim = dim3(256, 1, 1);
+        c.stream = stream;
+        c.attrs = at;
+        c.numAttrs = pdl ? 1 : 0;
+        cudaError_t e = TY == T_Q4_K
+                            ? cudaLaunchKernelEx(&c, cfi_mmq_x_to_f16<1>, y, static_cast<__half*>(xh), K, Kt, ncols_dst,
+                                                 ncols_y, nch, scy, ssy)
+                            : cudaLaunchKernelEx(&c, cfi_mmq_x_to_f16<0>, y, static_cast<__half*>(xh), K, Kt, ncols_dst,
+                                                 ncols_y, nch, scy, ssy);
+        if (e != cudaSuccess) return (int)e;
+    }
+    // 2. tensor maps: raw weights (4-D: chunk bytes, rows, channels, samples), Xh, dst
+    constexpr uint32_t RAW_ROW = qmm_raw_row<TY>();
+    constexpr uint32_t BB = TY == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES;
+    CUtensorMap tw, tb, tc;
+    {
+        const uint32_t es = TY == T_Q4_K ? 1 : 2;
+        const cuuint64_t rowb = (cuuint64_t)srx * BB;
+        const cuuint64_t chb = nch_x > 1 ? (cuuint64_t)scx * BB : rowb * nrows;
+        const cuuint64_t smb = ns_x > 1 ? (cuuint64_t)ssx * BB : chb * nch_x;
+        cuuint64_t dw[4] = {(cuuint64_t)(K / 256) * RAW_ROW / es, nrows, nch_x, ns_x};
+        cuuint64_t sw[3] = {rowb, chb, smb};
+        cuuint32_t bw[4] = {RAW_ROW / es, (cuuint32_t)BM, 1, 1}, ew[4] = {1, 1, 1, 1};
+        if (enc(&tw, TY == T_Q4_K ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 4,
+                const_cast<uint8_t*>(x), dw, sw, bw, ew, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    const uint32_t bn = tile_n(ncols_dst);
+    {
+        cuuint64_t gdim[3] = {Kt, ncols_dst, planes};
+        cuuint64_t gstride[2] = {(cuuint64_t)Kt * 2, (cuuint64_t)Kt * 2 * ncols_dst};
+        cuuint32_t box[3] = {BK, bn, 1}, estr[3] = {1, 1, 1};
+        if (enc(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, xh, gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    memset(&tc, 0, sizeof tc);
+    bool tma_c = (scd % 4) == 0 && (nch == 1 || scdst % 4 == 0) && (ns == 1 || ssd % 4 == 0) &&
+                 (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+    // 3. split K (whole 256-value chunks) when the output tiles fill under half the SMs
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    const uint32_t ktotal = Kt / BK;
+    uint32_t splits = 1, kchunk = (ktotal + 3) / 4 * 4;
+    const uint64_t tiles = (uint64_t)((nrows + BM - 1) / BM) * ((ncols_dst + bn - 1) / bn) * planes;
+    float* ws = nullptr;
+    const uint32_t ld_ws = (nrows + 3) / 4 * 4;
+    const char* es = getenv("CFI_GEMM_SPLITK");
+    if (tma_c && !(es && strcmp(es, "0") == 0) && tiles * 2 <= (uint64_t)sms && ktotal >= 16) {
+        uint32_t sp = std::min<uint32_t>((uint32_t)(sms / tiles), ktotal / 8);
+        if (sp >= 2) {
+            const uint32_t kc = ((ktotal + sp - 1) / sp + 3) / 4 * 4;
+            sp = (ktotal + kc - 1) / kc;
+            if (sp >= 2) {
+                ws = cfi_splitk_workspace((size_t)sp * planes * ncols_dst * ld_ws * 4, stream);
+                if (ws) {
+                    splits = sp;
+                    kchunk = kc;
+                }
+            }
+        }
+    }
+    if (splits > 1) {
+        cuuint64_t dw[4] = {nrows, ncols_dst, planes, splits};
+        cuuint64_t sw[3] = {(cuuint64_t)ld_ws * 4, (cuuint64_t)ld_ws * 4 * ncols_dst, (cuuint64_t)ld_ws * 4 * ncols_dst * planes};
+        cuuint32_t bw[4] = {32, 32, 1, 1}, ew[4] = {1, 1, 1, 1};
+        if (enc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws, dw, sw, bw, ew, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            splits = 1;
+            kchunk = (ktotal + 3) / 4 * 4;
+        }
+    }
+    if (splits == 1 && tma_c) {
+        const cuuint64_t s1 = (cuuint64_t)scd * 4;
+        const cuuint64_t s2 = nch > 1 ? (cuuint64_t)scdst * 4 : s1 * ncols_dst;
+        const cuuint64_t s3 = ns > 1 ? (cuuint64_t)ssd * 4 : s2 * nch;
+        cuuint64_t dc[4] = {nrows, ncols_dst, nch, ns};
+        cuuint64_t scs[3] = {s1, (s2 + 15) & ~(cuuint64_t)15, (s3 + 15) & ~(cuuint64_t)15};
+        cuuint32_t boxc[4] = {32, 32, 1, 1}, esc[4] = {1, 1, 1, 1};
+        tma_c = enc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dst, dc, scs, boxc, esc, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    // 4. ring depths within the shared-memory limit
+    const uint32_t ns_ring = bn <= 128 ? 4 : 3, b_stage = bn * BK * 2;
+    constexpr uint32_t RAW_BYTES = BM * RAW_ROW;
+    const size_t fixed = 1024 + (size_t)ns_ring * (A_STAGE + b_stage) + 256;
+    const uint32_t nraw = (uint32_t)std::min<size_t>(QMM_MAX_RAW, (QMM_SMEM_LIMIT - fixed) / RAW_BYTES);
+    if (nraw < 2) return (int)cudaErrorInvalidValue;
+    const size_t smem = fixed + (size_t)nraw * RAW_BYTES;
+    QmmArgs a;
+    a.x = x;
+    a.K = K;
+    a.Kt = Kt;
+    a.nrows = nrows;
+    a.ncols_dst = ncols_dst;
+    a.bn = bn;
+    a.ns = ns_ring;
+    a.nraw = nraw;
+    a.b_stage = b_stage;
+    a.splits = splits;
+    a.kchunk = kchunk;
+    a.stride_row_x = srx;
+    a.stride_channel_x = scx;
+    a.stride_sample_x = ssx;
+    a.nchannels_y = nch;
+    a.channel_ratio = chr;
+    a.sample_ratio = smr;
+    a.tma_c = tma_c ? 1 : 0;
+    a.dst = dst;
+    a.stride_col_dst = scd;
+    a.stride_channel_dst = scdst;
+    a.stride_sample_dst = ssd;
+    a.err = device_error_ptr();
+    static std::once_flag attr;
+    std::call_once(attr, [] {
+        cudaFuncSetAttribute(cfi_qmm_tc<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
+    });
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((nrows + BM - 1) / BM, (ncols_dst + bn - 1) / bn, planes * splits);
+    c.blockDim = dim3(QMM_THREADS, 1, 1);
+    c.dynamicSmemBytes = smem;
+    c.stream = stream;
+    c.attrs = at;
+    c.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&c, cfi_qmm_tc<TY>, tw, tb, tc, a);
+    if (e != cudaSuccess) return (int)e;
+    if (splits > 1)
+        return cfi_splitk_reduce_f32(ws, ld_ws, nrows, ncols_dst, planes, splits, dst, (long long)scd, (long long)scdst,
+                                     (long long)ssd, nch, stream, pdl);
+    return 0;
 }
 
 template <uint32_t TY>
@@ -631,13 +1117,17 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     const size_t xh_pad = (xh_bytes + 255) & ~(size_t)255;
     const size_t wh_bytes = (size_t)planes_x * nrows * Kt * 2;
     int rc = 0;
+    const bool fused = qmm_applicable<TY>(x, K, srx, scx, ssx, nch_x, ns / smr);
     if (fixed_xh) {
         if (xh_bytes > fixed_cap) return (int)cudaErrorInvalidValue;
         xh = fixed_xh;
     } else {
-        rc = scratch_for(xh_pad + wh_bytes, stream, &xh);
+        rc = scratch_for(fused ? xh_pad : xh_pad + wh_bytes, stream, &xh);
     }
     if (rc) return rc;
+    if (fused)
+        return launch_qmm<TY>(x, y, dst, xh, K, Kt, nrows, ncols_dst, srx, ncols_y, scd, chr, nch, scx, scy, scdst, smr, ns,
+                              ssx, ssy, ssd, stream);
     if (!fixed_xh) {
         // 1. activations and weights -> fp16 K-major (one launch), then the shared TMA-fed
         // tcgen05 GEMM (C = Wh Xh^T per plane)

@@ -52,6 +52,17 @@ def random_q8_0(torch, rows, k, gen, device):
     return blk.reshape(-1)
 
 
+def random_q4_k(torch, rows, k, gen, device):
+    """Valid Q4_K superblocks (144 B: fp16 d and dmin, 12 bytes of 6-bit scales/mins, 128 bytes of
+    nibbles) with random scales, mins and quants (device-side, seeded); d, dmin about 2e-4, so
+    weights fall in about [-0.8, 0.9] with most near +-0.1."""
+    nsb = rows * k // 256
+    blk = torch.randint(0, 256, (nsb, 144), generator=gen, device=device, dtype=torch.int32).to(torch.uint8)
+    dd = (2e-4 * (0.75 + 0.5 * torch.rand(nsb, 2, generator=gen, device=device))).to(torch.float16)
+    blk[:, 0:4] = dd.view(torch.uint8)
+    return blk.reshape(-1)
+
+
 class DecodeModel:
     def __init__(self, torch, ctx, device, cfg=None, seed=0x5eed):
         self.t = torch

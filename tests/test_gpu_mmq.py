@@ -58,6 +58,33 @@ def test_mmq_matches_the_oracle(dev, ty, shapes):
         assert err < REL_L2, (ty, ncols_x, nrows, ncols, err)
 
 
+@pytest.mark.parametrize("ty,case", [
+    (cfi.Q4_K, (1536, 1000, 64, 1, 1, 1)),     # split K, ragged rows
+    (cfi.Q4_K, (8960, 300, 200, 1, 1, 1)),     # deep K (split), 200 columns
+    (cfi.Q4_K, (1536, 260, 631, 1, 1, 1)),     # three column tiles
+    (cfi.Q8_0, (1024, 300, 100, 1, 1, 1)),
+    (cfi.Q8_0, (2048, 129, 40, 2, 1, 2)),      # channels x samples
+])
+def test_mmq_fused_and_prepass_paths_agree(dev, monkeypatch, ty, case):
+    """The fused kernel (TMA-staged raw weights dequantised in shared memory, split K) and the
+    pre-pass path (weights to fp16 in HBM, then the shared GEMM) against the oracle and each other."""
+    ctx, g = dev
+    ncols_x, nrows, ncols, nch, ratio, nsamples = case
+    p, x, y, n = O.mmq_case(ty, ncols_x, nrows, ncols, nch, ratio, nsamples, 11 + ncols + ty)
+    want = O.mmq_ref(ty, p, x, y, n)
+    outs = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("CFI_MMQ_FUSED", fused)
+        got = run(g, ty, p, x, y, n)
+        assert O.rel_l2(got, want) < REL_L2, (fused, O.rel_l2(got, want))
+        outs.append(got)
+    # split-K partials are summed in split order by the reduction kernel: repeatable bitwise
+    monkeypatch.setenv("CFI_MMQ_FUSED", "1")
+    assert np.array_equal(run(g, ty, p, x, y, n), outs[0])
+    # same fp16 operands and fp32 tensor-core accumulation: only the split-K summation order differs
+    assert O.rel_l2(outs[0], outs[1]) < 1e-5
+
+
 def dequant_q8_0(w, rows, k):
     b = w.reshape(rows, k // 32, 34)
     d = b[..., :2].copy().view(np.float16).astype(np.float64)
