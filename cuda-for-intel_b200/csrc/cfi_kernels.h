@@ -17,6 +17,7 @@ const void* cfi_native_quantize_mmq(int ds4);
 // `stream` false selects the row kernel for ncols <= 2 as well.
 const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols, bool stream);
 bool cfi_mmvq_streams(uint32_t ncols);
+bool cfi_mmvq_stream_only(uint32_t ty);  // types without the row kernel (Q6_K, Q4_0)
 // streaming kernel: rows per shared-memory stage and dynamic shared memory of a launch
 void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
                             uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,

@@ -40,7 +40,14 @@ using namespace sm100;
 constexpr int NW = CFI_MMVQ_WARPS;   // warps per CTA
 constexpr int WBUF_ROW = 1120;       // Q8_0: one 32-block chunk of a row + alignment slack + read-ahead
 
-template <uint32_t TY> __host__ __device__ constexpr uint32_t block_bytes() { return TY == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES; }
+template <uint32_t TY> __host__ __device__ constexpr uint32_t block_bytes() {
+    return TY == T_Q4_K ? Q4_K_BYTES : TY == T_Q6_K ? Q6_K_BYTES : TY == T_Q4_0 ? Q4_0_BYTES : Q8_0_BYTES;
+}
+template <uint32_t TY> __host__ __device__ constexpr uint32_t block_values() { return (TY == T_Q4_K || TY == T_Q6_K) ? QK_K : 32; }
+__host__ __device__ inline uint32_t block_bytes_of(uint32_t ty) {
+    return ty == T_Q4_K ? Q4_K_BYTES : ty == T_Q6_K ? Q6_K_BYTES : ty == T_Q4_0 ? Q4_0_BYTES : Q8_0_BYTES;
+}
+__host__ __device__ inline uint32_t block_values_of(uint32_t ty) { return (ty == T_Q4_K || ty == T_Q6_K) ? QK_K : 32; }
 template <uint32_t TY, int NCOLS> __host__ __device__ constexpr int rows_per_warp() {
     return TY == T_Q4_K ? (NCOLS == 1 ? 2 : 1) : (NCOLS <= 2 ? 2 : 1);
 }
@@ -70,12 +77,14 @@ CFI_DEV void l2_prefetch(const void* p, uint32_t bytes) {
 }
 
 // Activation stage: ya[c][b] = qs words 0..3, yb[c][b] = qs words 4..7, ym[c][b] = {d (fp32
-// bits), sum of the 32 int8 quants}; 40 bytes per block and column.
+// bits), aux}; 40 bytes per block and column.  aux: the sum of the 32 int8 quants (Q4_K); the
+// block's s as fp32 bits (Q4_0); the sums of quants 0..15 and 16..31 as two int16 (Q6_K).
 struct YStage {
     uint32_t ya, yb, ym;  // shared-space byte addresses
     uint32_t nb32;
 };
 
+template <uint32_t TY = T_Q4_K>
 CFI_DEV YStage stage_y(uint8_t* smem, int ncols, const uint8_t* y0, size_t y_base, uint32_t stride_col_y, uint32_t nb32) {
     uint4* ya = reinterpret_cast<uint4*>(smem);
     uint4* yb = ya + (size_t)ncols * nb32;
@@ -86,12 +95,25 @@ CFI_DEV YStage stage_y(uint8_t* smem, int ncols, const uint8_t* y0, size_t y_bas
         uint32_t q[9];
 #pragma unroll
         for (int i = 0; i < 9; i++) q[i] = __ldg(w + i);
-        int s = 0;
+        uint32_t aux;
+        if (TY == T_Q4_0) {
+            aux = __float_as_uint(h2f_bits((uint16_t)(q[0] >> 16)));
+        } else if (TY == T_Q6_K) {
+            int lo = 0, hi = 0;
 #pragma unroll
-        for (int i = 1; i < 9; i++) s = dp4a(0x01010101, (int)q[i], s);
+            for (int i = 1; i < 5; i++) lo = dp4a(0x01010101, (int)q[i], lo);
+#pragma unroll
+            for (int i = 5; i < 9; i++) hi = dp4a(0x01010101, (int)q[i], hi);
+            aux = ((uint32_t)lo & 0xffffu) | ((uint32_t)hi << 16);
+        } else {
+            int sm = 0;
+#pragma unroll
+            for (int i = 1; i < 9; i++) sm = dp4a(0x01010101, (int)q[i], sm);
+            aux = (uint32_t)sm;
+        }
         ya[idx] = make_uint4(q[1], q[2], q[3], q[4]);
         yb[idx] = make_uint4(q[5], q[6], q[7], q[8]);
-        ym[idx] = make_uint2(__float_as_uint(h2f_bits((uint16_t)(q[0] & 0xffffu))), (uint32_t)s);
+        ym[idx] = make_uint2(__float_as_uint(h2f_bits((uint16_t)(q[0] & 0xffffu))), aux);
     }
     return YStage{smem_u32(ya), smem_u32(yb), smem_u32(ym), nb32};
 }
@@ -548,6 +570,155 @@ CFI_DEV void q80_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0
     }
 }
 
+// 8 consecutive words starting at the 2-byte-aligned shared address a.
+CFI_DEV void lds8w(uint32_t a, uint32_t (&w)[8]) {
+    const uint32_t sh = (a & 3u) * 8, wa = a & ~3u;
+    uint32_t prev = lds32(wa);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t nxt = lds32(wa + 4 * (i + 1));
+        w[i] = __funnelshift_r(prev, nxt, sh);
+        prev = nxt;
+    }
+}
+
+// Q4_0 (never `wide` in the reference: refs.rs vec_dot Q4_0, two threads per block): model lane l
+// takes words kqs = 2 (l & 1), kqs + 1 of block l / 2 + 16 i; one warp per row.
+template <int NCOLS>
+CFI_DEV void q40_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0, uint32_t r1, const YStage& y,
+                       uint32_t lane, uint32_t warp, uintptr_t plane, uint32_t stride_row_x, float* dplane,
+                       uint32_t stride_col_dst) {
+    constexpr int R = NCOLS == 1 ? 4 : 2;
+    const uint32_t nb = y.nb32, kqs = 2 * (lane & 1);
+    for (uint32_t p0 = r0; p0 < r1; p0 += NW * R) {
+        float acc[R][NCOLS];
+        uint32_t rb[R];
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = min(p0 + warp + NW * k, r1 - 1);
+            const uintptr_t rs = plane + (uintptr_t)(dense ? r0 : r) * stride_row_x * Q4_0_BYTES;
+            rb[k] = sbase + (r - r0) * rstride + (uint32_t)(rs & 15);
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) acc[k][c] = 0.0f;
+        }
+        for (uint32_t b = lane >> 1; b < nb; b += 16) {
+            uint32_t v0[R], v1[R];
+            float d4[R];
+#pragma unroll
+            for (int k = 0; k < R; k++) {
+                const uint32_t blk = rb[k] + b * Q4_0_BYTES;
+                d4[k] = h2f_bits((uint16_t)lds16(blk));
+                const uint32_t qo = blk + 2 + 4 * kqs, sh = (qo & 3u) * 8, wa = qo & ~3u;
+                const uint32_t w0 = lds32(wa), w1 = lds32(wa + 4), w2 = lds32(wa + 8);
+                v0[k] = __funnelshift_r(w0, w1, sh);
+                v1[k] = __funnelshift_r(w1, w2, sh);
+            }
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                const uint32_t o = c * nb + b;
+                const uint2 ua = lds64(y.ya + o * 16 + 4 * kqs), ub = lds64(y.yb + o * 16 + 4 * kqs);
+                const uint2 m = lds64(y.ym + o * 8);
+                const float d8 = __uint_as_float(m.x), s8 = __uint_as_float(m.y);
+#pragma unroll
+                for (int k = 0; k < R; k++) {
+                    int sumi = dp4a((int)(v0[k] & 0x0F0F0F0Fu), (int)ua.x, 0);
+                    sumi = dp4a((int)((v0[k] >> 4) & 0x0F0F0F0Fu), (int)ub.x, sumi);
+                    sumi = dp4a((int)(v1[k] & 0x0F0F0F0Fu), (int)ua.y, sumi);
+                    sumi = dp4a((int)((v1[k] >> 4) & 0x0F0F0F0Fu), (int)ub.y, sumi);
+                    const float inner = __fmaf_rn(d8, (float)sumi, __fmul_rn(s8, -4.0f));
+                    acc[k][c] = __fmaf_rn(d4[k], inner, acc[k][c]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = p0 + warp + NW * k;
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                float v = acc[k][c];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane == 0 && r < r1) dplane[(size_t)c * stride_col_dst + r] = v;
+            }
+        }
+    }
+}
+
+// Q6_K (wide, refs.rs vec_dot_wide Q6_K): model lane l takes 32-value group g = l & 7 (half
+// h = g / 4, quarter sub = g % 4) of superblock l / 8 + 4 i; one warp per row.  6-bit quants are
+// the low or high nibble of ql plus 2 bits of qh; per 16 values an int8 scale.
+template <int NCOLS>
+CFI_DEV void q6k_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0, uint32_t r1, const YStage& y,
+                       uint32_t lane, uint32_t warp, uintptr_t plane, uint32_t stride_row_x, float* dplane,
+                       uint32_t stride_col_dst) {
+    constexpr int R = NCOLS == 1 ? 2 : 1;
+    const uint32_t nb32 = y.nb32, nsb = nb32 / 8;
+    const uint32_t g = lane & 7, h = g >> 2, sub = g & 3;
+    for (uint32_t p0 = r0; p0 < r1; p0 += NW * R) {
+        float acc[R][NCOLS];
+        uint32_t rb[R];
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = min(p0 + warp + NW * k, r1 - 1);
+            const uintptr_t rs = plane + (uintptr_t)(dense ? r0 : r) * stride_row_x * Q6_K_BYTES;
+            rb[k] = sbase + (r - r0) * rstride + (uint32_t)(rs & 15);
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) acc[k][c] = 0.0f;
+        }
+        for (uint32_t sb = lane >> 3; sb < nsb; sb += 4) {
+            uint32_t q[R][8];
+            int sc0[R], sc1[R];
+            float dx[R];
+#pragma unroll
+            for (int k = 0; k < R; k++) {
+                const uint32_t blk = rb[k] + sb * Q6_K_BYTES;
+                dx[k] = h2f_bits((uint16_t)lds16(blk + 208));
+                const uint32_t scw = lds16(blk + 192 + 8 * h + 2 * sub);
+                sc0[k] = (int)(int8_t)(scw & 0xffu);
+                sc1[k] = (int)(int8_t)(scw >> 8);
+                uint32_t ql[8], qh[8];
+                lds8w(blk + 64 * h + 32 * (sub & 1), ql);
+                lds8w(blk + 128 + 32 * h, qh);
+                const uint32_t lsh = 4 * (sub >> 1), hsh = 2 * sub;
+#pragma unroll
+                for (int i = 0; i < 8; i++) q[k][i] = ((ql[i] >> lsh) & 0x0F0F0F0Fu) | (((qh[i] >> hsh) & 0x03030303u) << 4);
+            }
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                const uint32_t o = c * nb32 + sb * 8 + g;
+                const uint4 ya = lds128(y.ya + o * 16), yb = lds128(y.yb + o * 16);
+                const uint2 m = lds64(y.ym + o * 8);
+                const float d8 = __uint_as_float(m.x);
+                const int su0 = (int)(int16_t)(m.y & 0xffffu), su1 = (int)(int16_t)(m.y >> 16);
+#pragma unroll
+                for (int k = 0; k < R; k++) {
+                    int s0 = dp4a((int)q[k][0], (int)ya.x, 0);
+                    s0 = dp4a((int)q[k][1], (int)ya.y, s0);
+                    s0 = dp4a((int)q[k][2], (int)ya.z, s0);
+                    s0 = dp4a((int)q[k][3], (int)ya.w, s0);
+                    int s1 = dp4a((int)q[k][4], (int)yb.x, 0);
+                    s1 = dp4a((int)q[k][5], (int)yb.y, s1);
+                    s1 = dp4a((int)q[k][6], (int)yb.z, s1);
+                    s1 = dp4a((int)q[k][7], (int)yb.w, s1);
+                    const int tot = (s0 - (su0 << 5)) * sc0[k] + (s1 - (su1 << 5)) * sc1[k];
+                    acc[k][c] = __fmaf_rn(__fmul_rn(dx[k], d8), (float)tot, acc[k][c]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t r = p0 + warp + NW * k;
+#pragma unroll
+            for (int c = 0; c < NCOLS; c++) {
+                float v = acc[k][c];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane == 0 && r < r1) dplane[(size_t)c * stride_col_dst + r] = v;
+            }
+        }
+    }
+}
+
 template <uint32_t TY, int NCOLS>
 __global__ void __launch_bounds__(NW * 32)
     cfi_mmvq_stream(const void* __restrict__ vx, const void* __restrict__ vy, const int32_t* __restrict__ ids,
@@ -560,7 +731,7 @@ __global__ void __launch_bounds__(NW * 32)
     __shared__ __align__(8) uint64_t full[ST_MAX_STAGES];
     constexpr uint32_t BB = block_bytes<TY>();
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t nb = TY == T_Q4_K ? ncols_x / QK_K : ncols_x / QK8_0;
+    const uint32_t nb = ncols_x / block_values<TY>();
     const uint32_t nb32 = ncols_x / 32;
     const uint32_t row_bytes = nb * BB;
     const bool dense = stride_row_x == nb;
@@ -613,7 +784,7 @@ __global__ void __launch_bounds__(NW * 32)
         uintptr_t a0 = (b0 + 15) & ~(uintptr_t)15, a1 = b1 & ~(uintptr_t)15;
         if (a1 <= a0) a0 = a1 = b1;
         if (issuer && a1 > a0) bulk_g2s(st + (a0 - base), reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0), bar);
-        if (TY != T_Q4_K && hw < 16) {  // Q8_0 rows are 2-byte aligned: at most 7 halfwords per end
+        if (TY != T_Q4_K && hw < 16) {  // Q8_0, Q4_0, Q6_K rows are 2-byte aligned: at most 7 halfwords per end
             const uintptr_t src = hw < 8 ? b0 + 2 * hw : a1 + 2 * (hw - 8);
             if (hw < 8 ? src < a0 : src < b1)
                 *reinterpret_cast<uint16_t*>(st + (src - base)) = __ldg(reinterpret_cast<const unsigned short*>(src));
@@ -644,7 +815,7 @@ __global__ void __launch_bounds__(NW * 32)
         }
     };
     for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
-    const YStage y = stage_y(smem + nst * stage_bytes, NCOLS, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
+    const YStage y = stage_y<TY>(smem + nst * stage_bytes, NCOLS, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
     __syncthreads();
 
     for (uint32_t ch = 0; ch < nchunks; ch++) {
@@ -658,6 +829,10 @@ __global__ void __launch_bounds__(NW * 32)
         const uint32_t sb = smem_u32(smem + s * stage_bytes);
         if constexpr (TY == T_Q4_K)
             q4k_chunk<NCOLS>(sb, rstride, r0, r1, y, tid, dplane, stride_col_dst);
+        else if constexpr (TY == T_Q6_K)
+            q6k_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
+        else if constexpr (TY == T_Q4_0)
+            q40_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
         else
             q80_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
         __syncthreads();
@@ -680,21 +855,41 @@ const void* pick(uint32_t ncols, bool stream) {
     }
 }
 
+template <uint32_t TY>
+const void* pick_stream(uint32_t ncols) {
+    switch (ncols) {
+    case 1: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 1>);
+    case 2: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 2>);
+    case 3: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 3>);
+    case 4: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 4>);
+    case 5: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 5>);
+    case 6: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 6>);
+    case 7: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 7>);
+    case 8: return reinterpret_cast<const void*>(&cfi_mmvq_stream<TY, 8>);
+    default: return nullptr;
+    }
+}
+
 }  // namespace
 
+// Q6_K and Q4_0 have the streaming kernel only (`stream` is ignored for them).
 const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols, bool stream) {
     if (ty == T_Q8_0) return pick<T_Q8_0>(ncols, stream);
     if (ty == T_Q4_K) return pick<T_Q4_K>(ncols, stream);
+    if (ty == T_Q6_K) return pick_stream<T_Q6_K>(ncols);
+    if (ty == T_Q4_0) return pick_stream<T_Q4_0>(ncols);
     return nullptr;
 }
+
+bool cfi_mmvq_stream_only(uint32_t ty) { return ty == T_Q6_K || ty == T_Q4_0; }
 
 bool cfi_mmvq_streams(uint32_t ncols) { return ncols >= 1 && ncols <= 8; }
 
 void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
                             uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,
                             uint32_t* chunk_rows, uint32_t* nstages, size_t* smem) {
-    const uint32_t nb = ty == T_Q4_K ? ncols_x / QK_K : ncols_x / QK8_0;
-    const uint32_t row_bytes = nb * (ty == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES);
+    const uint32_t nb = ncols_x / block_values_of(ty);
+    const uint32_t row_bytes = nb * block_bytes_of(ty);
     const bool dense = stride_row_x == nb;
     const uint32_t per_cta = (nrows + grid_x - 1) / grid_x;
     uint32_t c = std::min(std::max(1u, chunk_target), std::max(1u, per_cta));

@@ -137,13 +137,52 @@ float lane_dot(uint32_t ty, const uint8_t* xb, const uint8_t* yb, int g, float a
     return acc + (t1 - t2);
 }
 
+// Q6_K group g of a superblock, whole-group lane form (refs.rs:414-430).
+float lane_dot_q6k(const uint8_t* xb, const uint8_t* yb, int g, float acc) {
+    const float d8 = h2f(rd16(yb));
+    const int h = g / 4, sub = g % 4;
+    int tot = 0;
+    for (int half = 0; half < 2; half++) {
+        int si = 0, su = 0;
+        for (int i = 4 * half; i < 4 * half + 4; i++) {
+            const uint32_t lo = (rd32(xb + 64 * h + 32 * (sub & 1) + 4 * i) >> (4 * (sub >> 1))) & 0x0F0F0F0F;
+            const uint32_t hi = ((rd32(xb + 128 + 32 * h + 4 * i) >> (2 * sub)) & 0x03030303) << 4;
+            si = dp4a(lo | hi, rd32(yb + 4 + 4 * i), si);
+            su = dp4a(0x01010101, rd32(yb + 4 + 4 * i), su);
+        }
+        tot += (si - (su << 5)) * (int)(int8_t)xb[192 + 8 * h + 2 * sub + half];
+    }
+    return fmaf(h2f(rd16(xb + 208)) * d8, (float)tot, acc);
+}
+
+// Q4_0 half block kqs (words kqs, kqs+1 of the 16 quant bytes; refs.rs:166-259).
+float lane_dot_q40(const uint8_t* xb, const uint8_t* yb, int kqs, float acc) {
+    int sumi = 0;
+    for (int i = 0; i < 2; i++) {
+        const uint32_t v = rd32(xb + 2 + 4 * (kqs + i));
+        sumi = dp4a(v & 0x0F0F0F0F, rd32(yb + 4 + 4 * (kqs + i)), sumi);
+        sumi = dp4a((v >> 4) & 0x0F0F0F0F, rd32(yb + 4 + 4 * (kqs + i + 4)), sumi);
+    }
+    const float inner = fmaf(h2f(rd16(yb)), (float)sumi, h2f(rd16(yb + 2)) * -4.0f);
+    return fmaf(h2f(rd16(xb)), inner, acc);
+}
+
 float row_dot(uint32_t ty, const uint8_t* row, uint32_t ncols_x, const uint8_t* ycol) {
-    const uint32_t qk = ty == 8 ? 32 : 256, tpb = qk / 32, step = 32 / tpb, nb = ncols_x / qk;
+    const uint32_t qk = (ty == 12 || ty == 14) ? 256 : 32, nb = ncols_x / qk;
+    // threads per block: whole 32-value groups (Q8_0, Q4_K, Q6_K), half blocks (Q4_0)
+    const uint32_t tpb = ty == 2 ? 2 : qk / 32, step = 32 / tpb;
     float lanes[32];
     for (uint32_t l = 0; l < 32; l++) {
         float acc = 0.0f;
-        for (uint32_t k = l / tpb; k < nb; k += step)
-            acc = lane_dot(ty, row + k * block_bytes(ty), ycol + (k * tpb + l % tpb) * 36, (int)(l % tpb), acc);
+        for (uint32_t k = l / tpb; k < nb; k += step) {
+            const uint8_t* xb = row + k * block_bytes(ty);
+            if (ty == 2)
+                acc = lane_dot_q40(xb, ycol + k * 36, 2 * (int)(l % 2), acc);
+            else if (ty == 14)
+                acc = lane_dot_q6k(xb, ycol + (k * tpb + l % tpb) * 36, (int)(l % tpb), acc);
+            else
+                acc = lane_dot(ty, xb, ycol + (k * tpb + l % tpb) * 36, (int)(l % tpb), acc);
+        }
         lanes[l] = acc;
     }
     for (int o = 16; o; o >>= 1) {
@@ -233,12 +272,12 @@ int run(const cfi_plan& plan, const uint32_t grid[3], const uint32_t block[3], A
 // probe.rs:353-368 (one channel, one sample, no ids)
 int probe_mmvq(const cfi_plan& plan, void* stream, std::string* why) {
     const uint32_t ty = plan.ty, nc = plan.ncols, nrows = plan.has_fast ? 11 : 5, ncols_x = 512;
-    if (ty != 8 && ty != 12) {
+    if (ty != 8 && ty != 12 && ty != 14 && ty != 2) {
         *why = "no host check for this type";
         return (int)cudaErrorNotSupported;
     }
     Rng rng{0x5eed + ty};
-    const uint32_t qk = ty == 8 ? 32 : 256, bpr = ncols_x / qk, ystride = ncols_x / 32;
+    const uint32_t qk = (ty == 12 || ty == 14) ? 256 : 32, bpr = ncols_x / qk, ystride = ncols_x / 32;
     std::vector<uint8_t> x = random_blocks(ty, (size_t)nrows * bpr, rng);
     std::vector<float> acts((size_t)ncols_x * nc);
     for (auto& v : acts) v = rng.unit() * 3.0f;

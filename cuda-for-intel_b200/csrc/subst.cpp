@@ -579,15 +579,16 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
     case CFI_K_MMVQ: {
         if (!block_is(block, 32, ggml_mmvq_nwarps(plan.ncols), 1) || nvals < 17) return false;
         const uint32_t ncols_x = (uint32_t)vals[4], stride_col_dst = (uint32_t)vals[8];
-        const uint32_t qk = plan.ty == 12 ? 256 : 32;
+        const uint32_t qk = (plan.ty == 12 || plan.ty == 14) ? 256 : 32;
         if (ncols_x == 0 || ncols_x % qk) return false;
         if (plan.ty == 12 && (vals[0] & 15)) return false;  // 16-byte superblock loads
-        if (plan.ty == 8 && (vals[0] & 1)) return false;
+        if (plan.ty != 12 && (vals[0] & 1)) return false;   // 2-byte aligned blocks
         if ((vals[1] & 3)) return false;                       // q8_1 blocks are read as words
         const uint32_t nrows = plan.ncols == 1 ? grid[0] : std::min(2 * grid[0], stride_col_dst);
         const uint32_t planes = std::max(1u, grid[1] * grid[2]);
         // CFI_MMVQ_STREAM=0 selects the row kernel for ncols <= 2 too
-        const bool stream = cfi_mmvq_streams(plan.ncols) && env_u32("CFI_MMVQ_STREAM", 1, 0, 1) != 0;
+        const bool stream = cfi_mmvq_streams(plan.ncols) &&
+                            (cfi_mmvq_stream_only(plan.ty) || env_u32("CFI_MMVQ_STREAM", 1, 0, 1) != 0);
         nl.fn = cfi_native_mmvq(plan.ty, plan.ncols, stream);
         uint32_t chunk = 0, nstages = 0;
         if (stream) {

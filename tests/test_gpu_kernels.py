@@ -93,14 +93,17 @@ def run_mmvq(g, p, x, y, ids, n, use_ids=False):
 
 
 def per_column_decode_model(p, x, y, ids, n):
-    """Each output column through the oracle's one-warp whole-group model (refs.rs:435-497)."""
+    """Each output column through the oracle's one-warp decode model (refs.rs:435-497): whole
+    32-value groups per lane (`wide`) for Q8_0, Q4_K and Q6_K; Q4_0 is never wide in the
+    reference (two lanes per block)."""
+    wide = 0 if p.ty == cfi.Q4_0 else 1
     out = np.zeros(n, dtype=np.float32)
     for c in range(p.ncols_dst):
         q = O.Mmvq.from_buffer_copy(p)
         q.ncols_dst = 1
         ysub = np.ascontiguousarray(y[c * p.stride_col_y * 36:])
         col = np.zeros(n, dtype=np.float32)
-        O.lib().cfo_mmvq_fast(C.byref(q), O.u8(x), O.u8(ysub), O.i32(ids), O.f32(col), 1, 1, 1)
+        O.lib().cfo_mmvq_fast(C.byref(q), O.u8(x), O.u8(ysub), O.i32(ids), O.f32(col), 1, 1, wide)
         for s in range(p.nsamples_dst):
             for ch in range(p.nchannels_dst):
                 base = s * p.stride_sample_dst + ch * p.stride_channel_dst
@@ -108,11 +111,11 @@ def per_column_decode_model(p, x, y, ids, n):
     return out
 
 
-@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K])
+@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K, cfi.Q6_K, cfi.Q4_0])
 @pytest.mark.parametrize("ncols", [1, 2, 3, 4, 5, 6, 7, 8])
 def test_mmvq_matches_the_oracle(dev, ty, ncols):
     ctx, g = dev
-    for nrows, ncols_x in [(5, 512), (11, 2304 if ty == cfi.Q8_0 else 2304 // 256 * 256), (300, 4096)]:
+    for nrows, ncols_x in [(5, 512), (11, 2304), (300, 4096)]:
         p, x, y, ids, n = O.mmvq_case(ty, ncols, nrows, ncols_x, 1, 1, 1, False, 7 + ty + ncols + nrows)
         got = run_mmvq(g, p, x, y, ids, n)
         model = per_column_decode_model(p, x, y, ids, n)
@@ -123,13 +126,13 @@ def test_mmvq_matches_the_oracle(dev, ty, ncols):
         assert np.any(stock != 0)
 
 
-@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K])
+@pytest.mark.parametrize("ty", [cfi.Q8_0, cfi.Q4_K, cfi.Q6_K, cfi.Q4_0])
 def test_mmvq_channels_samples_and_ids(dev, ty):
     ctx, g = dev
     for (nch, ratio, ns, use_ids, seed) in [(4, 2, 2, False, 99), (5, 1, 1, True, 100)]:
         p, x, y, ids, n = O.mmvq_case(ty, 1, 3, 512, nch, ratio, ns, use_ids, seed)
         got = run_mmvq(g, p, x, y, ids, n, use_ids)
-        want = O.mmvq_fast_ref(p, x, y, ids, n, 1, 1, True)
+        want = O.mmvq_fast_ref(p, x, y, ids, n, 1, 1, ty != cfi.Q4_0)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
         assert O.nmse(got, O.mmvq_ref(p, x, y, ids, n)) < 1e-10
 
@@ -271,7 +274,7 @@ def test_soft_max_matches_the_oracle(dev, ncols, ne01, nheads, f16, max_bias):
 def test_every_native_kernel_passes_its_first_use_probe(dev):
     ctx, g = dev
     plans = []
-    for ty in (8, 12):
+    for ty in (8, 12, 14, 2):
         for n in (1, 2, 5, 8):
             plans.append(cfi.decide(cfi.NAMES["mmvq"].format(ty=ty, ncols=n), "mmvq", "all")[1])
     plans.append(cfi.decide(cfi.NAMES["quantize_q8_1"], "quantize_q8_1", "all")[1])
