@@ -325,16 +325,17 @@ def config5_bench(cfi, g, stream, dev, peak_gbs, peak_tf):
     return res
 
 
-def decode_bench(stream, dev, ntok=48, warm=3):
+def decode_bench(stream, dev, ntok=48, warm=3, fused=False):
     """Qwen2.5-0.5B-architecture decode (24 layers, Q8_0 random weights, 631-token
-    seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens."""
+    seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens.  fused: the
+    stacked-weight step with the fused glue kernels (9 launches per layer instead of 25)."""
     import torch
 
     import cfi_b200 as cfi
     from decode import DecodeModel
 
     ctx = cfi.Ctx(dev.index or 0)
-    m = DecodeModel(torch, ctx, dev)
+    m = DecodeModel(torch, ctx, dev, fused=fused)
     m.reset(token=1234)
     with torch.cuda.stream(stream):
         m.step(stream.cuda_stream)  # first-use probes outside the capture
@@ -360,7 +361,9 @@ def decode_bench(stream, dev, ntok=48, warm=3):
     assert int(m.pos.item()) == m.cfg.prompt + ntok and cfi.lib().cfi_device_error() == 0
     bpt = m.cfg.weight_bytes_per_token()
     out = {"workload": "config4: Qwen2.5-0.5B-architecture decode, 24 layers, Q8_0 random weights, 631-token seeded "
-                       "KV cache, %d greedy tokens, one CUDA graph per token" % ntok,
+                       "KV cache, %d greedy tokens, one CUDA graph per token%s"
+                       % (ntok, "; stacked QKV / gate-up weights and fused glue kernels" if fused
+                          else "; ggml's kernel sequence through the substitution ABI"),
            "tok_per_s": round(ntok / (ms * 1e-3), 1), "ms_per_token": round(ms / ntok, 4),
            "launches_per_token": m.launches_per_step, "weight_bytes_per_token": bpt,
            "weights_gbs": round(bpt * ntok / (ms * 1e-3) / 1e9, 1)}
@@ -590,6 +593,7 @@ def run_gpu(args, rank, world):
             line["prefill"] = prefill_gemm(cfi, g, stream, dev, tensor_peak())
         if not args.no_decode and world == 1:
             line["decode"] = decode_bench(stream, dev)
+            line["decode"]["fused"] = decode_bench(stream, dev, fused=True)
         if not args.no_configs and world == 1:
             line["config1"] = config1_bench(cfi, g, stream, dev, peak)
             line["config5"] = config5_bench(cfi, g, stream, dev, peak, tensor_peak())

@@ -109,6 +109,19 @@ def lib():
     L.cfi_blas_sgemm.argtypes = [vp, i, i, i, i, i, vp, vp, i, vp, i, vp, vp, i]
     L.cfi_device_error.restype = C.c_uint
     L.cfi_version.restype = C.c_char_p
+    f = C.c_float
+    L.cfi_glue_get_rows_q8_0.argtypes = [vp, vp, vp, i, vp]
+    L.cfi_glue_qkv_bias.argtypes = [vp, vp, vp, vp, vp, vp, i, i, vp]
+    L.cfi_glue_kv_store.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp]
+    L.cfi_glue_causal_mask.argtypes = [vp, vp, i, vp]
+    L.cfi_glue_to_f16.argtypes = [vp, vp, i, vp]
+    L.cfi_glue_add.argtypes = [vp, vp, i, vp]
+    L.cfi_glue_swiglu.argtypes = [vp, vp, vp, i, vp]
+    L.cfi_glue_argmax_next.argtypes = [vp, i, vp, vp, vp]
+    L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
+    L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
+    L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]
+    L.cfi_fused_swiglu_q8_1.argtypes = [vp, vp, i, vp]
     _lib = L
     return L
 

@@ -8,11 +8,12 @@
 
 // ggml block sizes (ggml-common.h layouts; see the block structs below).
 constexpr int QK8_0 = 32, QK8_1 = 32, QK4_0 = 32, QK_K = 256;
-constexpr int Q8_0_BYTES = 34, Q8_1_BYTES = 36, Q4_0_BYTES = 18, Q4_K_BYTES = 144, Q6_K_BYTES = 210;
+constexpr int Q8_0_BYTES = 34, Q8_1_BYTES = 36, Q4_0_BYTES = 18, Q5_0_BYTES = 22, Q4_K_BYTES = 144, Q5_K_BYTES = 176,
+              Q6_K_BYTES = 210;
 constexpr int MMQ_BLOCK_BYTES = 144;  // block_q8_1_mmq: 4 scales (16 B) + 128 int8
 
 // ggml type ids.
-constexpr uint32_t T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14;
+constexpr uint32_t T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14;
 
 // ggml's fastdiv triple {mp, L, d}: n / d == (umulhi(n, mp) + n) >> L.
 CFI_DEV uint32_t fastdiv(uint32_t n, uint3 v) { return (__umulhi(n, v.x) + n) >> v.y; }

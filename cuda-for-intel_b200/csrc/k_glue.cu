@@ -11,6 +11,7 @@
 #include "sm100_ptx.cuh"
 
 #include <stdlib.h>
+#include <algorithm>
 #include <string.h>
 
 namespace {
@@ -85,22 +86,15 @@ __global__ void swiglu(const float* __restrict__ g, const float* __restrict__ u,
     }
 }
 
-// token[0] = argmax(logits) (first index of the maximum), pos[0] += 1.  One CTA of 1024 threads.
-__global__ void __launch_bounds__(1024) argmax_next(const float* __restrict__ logits, int n, int32_t* __restrict__ token,
-                                                    int32_t* __restrict__ pos) {
-    sm100::pdl_launch_dependents();
-    sm100::pdl_wait();
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = logits[i];
-        if (v > best || (v == best && i < idx)) {
-            best = v;
-            idx = i;
-        }
-    }
+// token[0] = argmax(logits) (first index of the maximum), pos[0] += 1.  AMAX_CTAS CTAs reduce
+// contiguous ranges; the last CTA to finish (device counter) reduces their results in CTA order
+// and resets the counter.  The partials live in device globals: one call at a time per device.
+constexpr int AMAX_CTAS = 148;
+static __device__ float g_amax_val[AMAX_CTAS];
+static __device__ int g_amax_idx[AMAX_CTAS];
+static __device__ unsigned int g_amax_count;
+
+CFI_DEV void amax_pair_reduce(float& best, int& idx) {
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
@@ -109,33 +103,337 @@ __global__ void __launch_bounds__(1024) argmax_next(const float* __restrict__ lo
             idx = oi;
         }
     }
-    if ((threadIdx.x & 31) == 0) {
-        bv[threadIdx.x >> 5] = best;
-        bi[threadIdx.x >> 5] = idx;
+}
+
+__global__ void __launch_bounds__(512) argmax_next(const float* __restrict__ logits, int n, int32_t* __restrict__ token,
+                                                   int32_t* __restrict__ pos) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
+    __shared__ float bv[16];
+    __shared__ int bi[16];
+    __shared__ int last;
+    const int chunk = (n + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = lo + (int)threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > best || (v == best && i < idx)) {
+            best = v;
+            idx = i;
+        }
+    }
+    amax_pair_reduce(best, idx);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        bv[warp] = best;
+        bi[warp] = idx;
     }
     __syncthreads();
-    if (threadIdx.x < 32) {
-        best = threadIdx.x < (blockDim.x >> 5) ? bv[threadIdx.x] : -INFINITY;
-        idx = threadIdx.x < (blockDim.x >> 5) ? bi[threadIdx.x] : 0x7fffffff;
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > best || (ov == best && oi < idx)) {
-                best = ov;
-                idx = oi;
-            }
-        }
-        if (threadIdx.x == 0) {
-            token[0] = idx;
-            pos[0] += 1;
+    if (warp == 0) {
+        best = lane < (int)(blockDim.x >> 5) ? bv[lane] : -INFINITY;
+        idx = lane < (int)(blockDim.x >> 5) ? bi[lane] : 0x7fffffff;
+        amax_pair_reduce(best, idx);
+        if (lane == 0) {
+            g_amax_val[blockIdx.x] = best;
+            g_amax_idx[blockIdx.x] = idx;
+            __threadfence();
+            last = atomicAdd(&g_amax_count, 1u) == gridDim.x - 1;
         }
     }
+    __syncthreads();
+    if (!last || warp != 0) return;
+    __threadfence();
+    best = -INFINITY;
+    idx = 0x7fffffff;
+    for (int b = lane; b < (int)gridDim.x; b += 32) {
+        const float v = __ldcg(&g_amax_val[b]);
+        const int i = __ldcg(&g_amax_idx[b]);
+        if (v > best || (v == best && i < idx)) {
+            best = v;
+            idx = i;
+        }
+    }
+    amax_pair_reduce(best, idx);
+    if (lane == 0) {
+        token[0] = idx;
+        pos[0] += 1;
+        g_amax_count = 0;
+    }
+}
+
+// ---- fused decode steps ----
+
+// q8_1 block of 32 values, one value per lane (the reference's lane form: refs.rs:103-147):
+// amax and sum by the xor butterfly 16..1, d = amax / 127, q = roundf(v / d).
+CFI_DEV void q8_1_store_lane(float v, uint8_t* blk, int lane) {
+    float a = fabsf(v), sm = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    }
+    const float d = __fdiv_rn(a, 127.0f);
+    const int8_t q = a == 0.0f ? (int8_t)0 : (int8_t)(int32_t)roundf(__fdiv_rn(v, d));
+    blk[4 + lane] = (uint8_t)q;
+    if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = (uint32_t)f2h_bits(d) | ((uint32_t)f2h_bits(sm) << 16);
+}
+
+// Block sum over 256 threads in the order of the native rms_norm (thread-strided partials, warp
+// butterfly, then the 8 warp sums by a second butterfly).
+CFI_DEV float block_sum256(float v, float* red) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+// Threads own values c = t, t + blockDim, ...; the sum of squares is formed as the native
+// rms_norm forms it (256 thread-strided fma chains, then the two-level butterfly), so the result
+// is the chain's bit for bit; each warp then quantizes the 32-value blocks it holds.
+__global__ void __launch_bounds__(1024) add_rmsnorm_q81(float* __restrict__ x, const float* __restrict__ y,
+                                                        const float* __restrict__ w, uint8_t* __restrict__ out, int n,
+                                                        float eps) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
+    extern __shared__ float hbuf[];
+    __shared__ float red[32];
+    __shared__ float s_scale;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x;
+    for (int c = tid; c < n; c += nt) {
+        float v = x[c];
+        if (y) {
+            v += y[c];
+            x[c] = v;
+        }
+        hbuf[c] = v;
+    }
+    __syncthreads();
+    if (warp < 8) {
+        float ss = 0.0f;
+        for (int c = tid; c < n; c += 256) ss = __fmaf_rn(hbuf[c], hbuf[c], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const float t = warp_sum(lane < 8 ? red[lane] : 0.0f);
+        if (lane == 0) s_scale = rsqrtf(t / (float)n + eps);
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    for (int c = tid; c < n; c += nt) {
+        float v = scale * hbuf[c];
+        v = v * w[c];
+        q8_1_store_lane(v, out + (size_t)(c / 32) * Q8_1_BYTES, lane);
+    }
+}
+
+// One thread per (head, rotation pair) of q and k, plus the v values.
+__global__ void __launch_bounds__(256) qkv_rope_store(const float* __restrict__ qkv, const float* __restrict__ bias,
+                                                      float* __restrict__ q_out, __half* __restrict__ kc,
+                                                      __half* __restrict__ vc, const int32_t* __restrict__ pos, int nq,
+                                                      int nkv, int head_dim, int n_ctx, float theta_scale) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int half = head_dim / 2, p = pos[0];
+    const int npairs = (nq + nkv) / 2;
+    if (i < npairs) {
+        const int head = i / half, j = i - head * half;
+        const int base = head * head_dim;  // in [q | k]
+        const float x0 = qkv[base + j] + bias[base + j], x1 = qkv[base + j + half] + bias[base + j + half];
+        // rope_neox with freq_scale 1, no extrapolation, attn_factor 1: theta = pos * theta_scale^j
+        const float theta = __fmul_rn((float)p, powf(theta_scale, (float)(2 * j) / 2.0f));
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
+        const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        if (base < nq) {
+            q_out[base + j] = y0;
+            q_out[base + j + half] = y1;
+        } else {
+            const int kh = (base - nq) / head_dim;
+            __half* kr = kc + ((size_t)kh * n_ctx + p) * head_dim;
+            kr[j] = __float2half_rn(y0);
+            kr[j + half] = __float2half_rn(y1);
+        }
+    } else if (i < npairs + nkv) {
+        const int e = i - npairs, kh = e / head_dim, dd = e - kh * head_dim;
+        const float v = qkv[nq + nkv + e] + bias[nq + nkv + e];
+        vc[((size_t)kh * head_dim + dd) * n_ctx + p] = __float2half_rn(v);
+    }
+}
+
+// Split over positions (flash-decoding): CTA (h, s) of grid (n_head, nsplit) takes the positions
+// [s chunk, (s + 1) chunk) that are <= pos[0] for query head h: scores (thread t: position t of the
+// range, the K row read whole with 16-byte loads), the range's max m_s, e_j = exp(score_j - m_s),
+// l_s = sum e_j and o_s[d] = sum e_j V[d][j] (256 / head_dim threads per dim over 8-position runs
+// of the V^T row).  The partials go to device globals; the last CTA of the head (device counter)
+// combines them in split order, out[d] = sum_s o_s[d] e^(m_s - M) / sum_s l_s e^(m_s - M), writes
+// the head_dim / 32 q8_1 blocks and resets the counter.  One call at a time per device.
+constexpr int ATT_MAX_CTX = 8192, ATT_MAX_HEADS = 64, ATT_MAX_SPLIT = 64, ATT_CHUNK = 128;
+static __device__ float g_att_part[ATT_MAX_HEADS * ATT_MAX_SPLIT * (2 + 128)];
+static __device__ unsigned int g_att_count[ATT_MAX_HEADS];
+
+__global__ void __launch_bounds__(256) attention_q81(const float* __restrict__ q, const __half* __restrict__ kc,
+                                                    const __half* __restrict__ vc, const int32_t* __restrict__ pos,
+                                                    uint8_t* __restrict__ out, int n_head, int n_kv_head, int head_dim,
+                                                    int n_ctx, float scale, int chunk) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
+    __shared__ float sc[ATT_CHUNK * 2];
+    __shared__ float red[32];
+    __shared__ __align__(16) float qs[128];
+    __shared__ float o[128];
+    __shared__ int last;
+    const int h = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y, kvh = h / (n_head / n_kv_head);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int npos = min(pos[0] + 1, n_ctx);
+    const int j0 = split * chunk, j1 = min(npos, j0 + chunk);  // j1 <= j0: empty range
+    const __half* K = kc + (size_t)kvh * n_ctx * head_dim;
+    const __half* V = vc + (size_t)kvh * head_dim * n_ctx;
+    if (tid < head_dim) qs[tid] = q[(size_t)h * head_dim + tid];
+    __syncthreads();
+    // ---- scores of the range ----
+    float mx = -INFINITY;
+    const int nv = head_dim / 8;
+    for (int jj = tid; j0 + jj < j1; jj += 256) {
+        const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)(j0 + jj) * head_dim);
+        uint4 kv[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++)
+            if (e < nv) kv[e] = __ldg(kr + e);
+        float acc = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            if (e < nv) {
+                const __half2* hp = reinterpret_cast<const __half2*>(&kv[e]);
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const float2 f = __half22float2(hp[t]);
+                    acc = __fmaf_rn(qs[8 * e + 2 * t], f.x, acc);
+                    acc = __fmaf_rn(qs[8 * e + 2 * t + 1], f.y, acc);
+                }
+            }
+        }
+        const float sj = acc * scale;
+        sc[jj] = sj;
+        mx = fmaxf(mx, sj);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = warp_max(lane < 8 ? red[lane] : -INFINITY);
+    __syncthreads();
+    float sum = 0.0f;
+    const int cnt = max(0, j1 - j0), cpad = (cnt + 7) & ~7;
+    for (int jj = tid; jj < cpad; jj += 256) {
+        const float e = jj < cnt ? expf(sc[jj] - mx) : 0.0f;
+        sc[jj] = e;
+        sum += e;
+    }
+    sum = block_sum256(sum, red);
+    __syncthreads();
+    // ---- unnormalised output of the range ----
+    const int tpd = 256 / head_dim, d = tid / tpd, part = tid % tpd;
+    const uint4* vr = reinterpret_cast<const uint4*>(V + (size_t)d * n_ctx + j0);
+    const int nrun = cpad / 8;
+    float acc = 0.0f;
+    for (int r0 = part; r0 < nrun; r0 += 4 * tpd) {
+        uint4 vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int r = r0 + u * tpd;
+            vv[u] = r < nrun ? __ldg(vr + r) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int r = r0 + u * tpd;
+            if (r < nrun) {
+                const __half2* hp = reinterpret_cast<const __half2*>(&vv[u]);
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const float2 f = __half22float2(hp[t]);
+                    acc = __fmaf_rn(sc[8 * r + 2 * t], f.x, acc);
+                    acc = __fmaf_rn(sc[8 * r + 2 * t + 1], f.y, acc);
+                }
+            }
+        }
+    }
+    for (int off = tpd / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    float* pp = g_att_part + ((size_t)h * ATT_MAX_SPLIT + split) * (2 + 128);
+    if (part == 0) pp[2 + d] = acc;
+    if (tid == 0) {
+        pp[0] = mx;
+        pp[1] = sum;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(&g_att_count[h], 1u) == (unsigned)nsplit - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // ---- combine the splits in order ----
+    const float* hp0 = g_att_part + (size_t)h * ATT_MAX_SPLIT * (2 + 128);
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(hp0 + sp * (2 + 128)));
+    if (tid < head_dim) {
+        float num = 0.0f, den = 0.0f;
+        for (int sp = 0; sp < nsplit; sp++) {
+            const float* ps = hp0 + sp * (2 + 128);
+            const float ms = __ldcg(ps);
+            if (ms == -INFINITY) continue;  // empty range
+            const float f = expf(ms - M);
+            num = __fmaf_rn(__ldcg(ps + 2 + tid), f, num);
+            den = __fmaf_rn(__ldcg(ps + 1), f, den);
+        }
+        o[tid] = num / den;
+    }
+    __syncthreads();
+    for (int b = warp; b < head_dim / 32; b += 8)
+        q8_1_store_lane(o[32 * b + lane], out + ((size_t)h * (head_dim / 32) + b) * Q8_1_BYTES, lane);
+    if (tid == 0) g_att_count[h] = 0;
+}
+
+// One warp per q8_1 block.
+__global__ void __launch_bounds__(256) swiglu_q81(const float* __restrict__ gu, uint8_t* __restrict__ out, int n) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (b >= n / 32) return;
+    const int i = 32 * b + lane;
+    const float a = gu[i];
+    const float v = a / (1.0f + expf(-a)) * gu[n + i];
+    q8_1_store_lane(v, out + (size_t)b * Q8_1_BYTES, lane);
 }
 
 inline dim3 g1(int n) { return dim3((unsigned)((n + 255) / 256)); }
 
 // Launch with programmatic dependent launch unless CFI_PDL=0 (each kernel waits for its predecessor
 // before reading anything).
+template <typename... K, typename... A>
+int launch_smem(void (*k)(K...), dim3 grid, unsigned threads, size_t smem, void* stream, A... args) {
+    static const bool pdl = [] {
+        const char* e = getenv("CFI_PDL");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, k, ((K)args)...);
+}
+
 template <typename... K, typename... A>
 int launch(void (*k)(K...), dim3 grid, unsigned threads, void* stream, A... args) {
     static const bool pdl = [] {
@@ -183,5 +481,39 @@ extern "C" int cfi_glue_swiglu(const float* g, const float* u, float* out, int n
     return launch(swiglu, g1(n), 256, stream, g, u, out, n);
 }
 extern "C" int cfi_glue_argmax_next(const float* logits, int n, int32_t* token, int32_t* pos, void* stream) {
-    return launch(argmax_next, dim3(1), 1024, stream, logits, n, token, pos);
+    return launch(argmax_next, dim3(AMAX_CTAS), 512, stream, logits, n, token, pos);
+}
+
+extern "C" int cfi_fused_add_rmsnorm_q8_1(float* x, const float* y, const float* w, void* out, int n, float eps,
+                                          void* stream) {
+    if (n <= 0 || n % 32 || n > 8192) return (int)cudaErrorInvalidValue;
+    const size_t smem = (size_t)n * 4;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(add_rmsnorm_q81, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const unsigned threads = (unsigned)std::max(256, std::min(1024, n));  // n is a multiple of 32
+    return launch_smem(add_rmsnorm_q81, dim3(1), threads, smem, stream, x, y, w, (uint8_t*)out, n, eps);
+}
+extern "C" int cfi_fused_qkv_rope_store(const float* qkv, const float* bias, float* q_out, void* kc, void* vc,
+                                        const int32_t* pos, int nq, int nkv, int head_dim, int n_ctx, float theta,
+                                        void* stream) {
+    if (head_dim <= 0 || head_dim % 2 || nq % head_dim || nkv % head_dim) return (int)cudaErrorInvalidValue;
+    // theta_scale = theta^(-2 / n_dims), computed on the host as the rope_neox caller does
+    const float theta_scale = powf(theta, -2.0f / (float)head_dim);
+    return launch(qkv_rope_store, g1((nq + nkv) / 2 + nkv), 256, stream, qkv, bias, q_out, (__half*)kc, (__half*)vc,
+                  pos, nq, nkv, head_dim, n_ctx, theta_scale);
+}
+extern "C" int cfi_fused_attention_q8_1(const float* q, const void* kc, const void* vc, const int32_t* pos, void* out,
+                                        int n_head, int n_kv_head, int head_dim, int n_ctx, float scale, void* stream) {
+    if ((head_dim != 64 && head_dim != 128) || n_kv_head <= 0 || n_head % n_kv_head || n_head > ATT_MAX_HEADS ||
+        n_ctx <= 0 || n_ctx % 8 || n_ctx > ATT_MAX_CTX || (reinterpret_cast<uintptr_t>(kc) & 15) ||
+        (reinterpret_cast<uintptr_t>(vc) & 15))
+        return (int)cudaErrorInvalidValue;
+    // position ranges of at most ATT_CHUNK (a multiple of 8, so V^T runs stay 16-byte aligned)
+    const int nsplit = (n_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int chunk = ((n_ctx + nsplit - 1) / nsplit + 7) / 8 * 8;
+    return launch(attention_q81, dim3(n_head, nsplit), 256, stream, q, (const __half*)kc, (const __half*)vc, pos,
+                  (uint8_t*)out, n_head, n_kv_head, head_dim, n_ctx, scale, chunk);
+}
+extern "C" int cfi_fused_swiglu_q8_1(const float* gu, void* out, int n, void* stream) {
+    if (n <= 0 || n % 32) return (int)cudaErrorInvalidValue;
+    return launch(swiglu_q81, dim3((unsigned)((n / 32 + 7) / 8)), 256, stream, gu, (uint8_t*)out, n);
 }

@@ -96,6 +96,28 @@ CFI_DEV void dequant4_u4(uint32_t w, uint32_t shift, __half2 d2, uint32_t& lo, u
     hi = h2_bits(__hmul2(b, d2));
 }
 
+// Per-type mmq traits (refs.rs:641-649): values per weight block, block bytes, the q8_1_mmq
+// activation layout (DS4: half d + half sum per 32 values; else float d) and whether the
+// min term needs appended correction columns (Q4_K, Q5_K).
+template <uint32_t TY> constexpr uint32_t mmq_qk() { return (TY == T_Q4_K || TY == T_Q5_K || TY == T_Q6_K) ? 256u : 32u; }
+template <uint32_t TY> constexpr uint32_t mmq_bb() {
+    return TY == T_Q8_0 ? Q8_0_BYTES : TY == T_Q4_0 ? Q4_0_BYTES : TY == T_Q5_0 ? Q5_0_BYTES
+         : TY == T_Q4_K ? Q4_K_BYTES : TY == T_Q5_K ? Q5_K_BYTES : Q6_K_BYTES;
+}
+template <uint32_t TY> constexpr int mmq_ds4() { return (TY == T_Q4_0 || TY == T_Q4_K || TY == T_Q5_K) ? 1 : 0; }
+template <uint32_t TY> constexpr int mmq_corr() { return (TY == T_Q4_K || TY == T_Q5_K) ? 1 : 0; }
+
+// 4 unsigned bytes (0..255, exact in fp16) -> two half2, scaled by d.
+CFI_DEV void dequant4_ub(uint32_t b, __half2 d2, uint32_t& lo, uint32_t& hi) {
+    const uint32_t p0 = __byte_perm(b, 0x64646464u, 0x4140);
+    const uint32_t p1 = __byte_perm(b, 0x64646464u, 0x4342);
+    const __half2 bias = __float2half2_rn(1024.0f);
+    __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&p0), bias);
+    __half2 c = __hsub2(*reinterpret_cast<const __half2*>(&p1), bias);
+    lo = h2_bits(__hmul2(a, d2));
+    hi = h2_bits(__hmul2(c, d2));
+}
+
 CFI_DEV void st_chunk(uint8_t* atom, int r, int c, uint32_t a, uint32_t b, uint32_t cc, uint32_t d) {
     uint4 v = make_uint4(a, b, cc, d);
     *reinterpret_cast<uint4*>(atom + r * 128 + ((c ^ (r & 7)) << 4)) = v;
@@ -706,7 +728,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
 // block_q8_1_mmq -> fp16 K-major rows: Xh[plane][col][k] = fp16(q * d) for k < K; for DS4
 // (Q4_K) Xh[plane][col][K + g] = s_g (the half float sum of group g), zero up to Kt.
 // One warp per (column, 128-value block); lane l handles values 4l..4l+3.
-template <int DS4>
+template <int DS4, int SUMS>
 CFI_DEV void x_to_f16(uint32_t bx, uint32_t plane, const uint8_t* __restrict__ y, __half* __restrict__ xh, uint32_t K,
                       uint32_t Kt, uint32_t ncols, uint32_t ncols_y, uint32_t nchannels_y, uint32_t stride_channel_y,
                       uint32_t stride_sample_y) {
@@ -733,7 +755,7 @@ CFI_DEV void x_to_f16(uint32_t bx, uint32_t plane, const uint8_t* __restrict__ y
     __half* row = xh + ((size_t)plane * ncols + col) * Kt;
     uint2 out = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
     *reinterpret_cast<uint2*>(row + kb * 128 + 4 * lane) = out;
-    if (DS4) {
+    if (SUMS) {
         if ((lane & 7) == 0) row[K + kb * 4 + (lane >> 3)] = __ushort_as_half((uint16_t)sbits);
         // zero the padding of the appended columns once (block kb == 0 of each column)
         if (kb == 0)
@@ -741,30 +763,134 @@ CFI_DEV void x_to_f16(uint32_t bx, uint32_t plane, const uint8_t* __restrict__ y
     }
 }
 
-template <int DS4>
+template <int DS4, int SUMS>
 __global__ void __launch_bounds__(256)
     cfi_mmq_x_to_f16(const uint8_t* __restrict__ y, __half* __restrict__ xh, uint32_t K, uint32_t Kt, uint32_t ncols,
                      uint32_t ncols_y, uint32_t nchannels_y, uint32_t stride_channel_y, uint32_t stride_sample_y) {
     pdl_launch_dependents();
     pdl_wait();
-    x_to_f16<DS4>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y, stride_sample_y);
+    x_to_f16<DS4, SUMS>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y, stride_sample_y);
 }
 
 // Weights -> fp16 K-major rows: Wh[xplane][row][k].  Q8_0: fp16(q * d).  Q4_K: fp16(q *
 // half(d * sc)) and, in the appended columns K + g, half(-dmin * m_g) (the terms the fused kernel
 // builds in shared memory; refs.rs:709-712), zero up to Kt.  One thread per weight block
 // (Q8_0: 32 values, Q4_K: 256 values), consecutive threads on consecutive blocks of a row.
+// Q4_0 / Q5_0 / Q6_K blocks are only 2-byte aligned: halfword loads.
+CFI_DEV uint32_t ldg_w2(const uint8_t* p) {  // 4 bytes at a 2-byte-aligned address
+    const unsigned short* h = reinterpret_cast<const unsigned short*>(p);
+    return (uint32_t)__ldg(h) | ((uint32_t)__ldg(h + 1) << 16);
+}
+
 template <uint32_t TY>
 CFI_DEV void w_to_f16(uint32_t bx, uint32_t xp, const uint8_t* __restrict__ x, __half* __restrict__ wh, uint32_t K,
                       uint32_t Kt, uint32_t nrows, uint32_t srx, uint32_t nch_x, uint32_t scx, uint32_t ssx) {
-    constexpr uint32_t QKB = TY == T_Q4_K ? QK_K : QK8_0;
+    constexpr uint32_t QKB = mmq_qk<TY>();
     const uint32_t nb = K / QKB;
     const uint64_t t = (uint64_t)bx * blockDim.x + threadIdx.x;
     if (t >= (uint64_t)nrows * nb) return;
     const uint32_t row = (uint32_t)(t / nb), b = (uint32_t)(t - (uint64_t)row * nb);
     const uint32_t sx = xp / nch_x, cx = xp - sx * nch_x;
     __half* out = wh + ((size_t)xp * nrows + row) * Kt;
-    if (TY == T_Q8_0) {
+    const uint8_t* blk = x + ((size_t)sx * ssx + (size_t)cx * scx + (size_t)row * srx + b) * mmq_bb<TY>();
+    if (TY == T_Q4_0 || TY == T_Q5_0) {
+        // Q4_0: q = nibble - 8; Q5_0: q = (nibble | qh bit << 4) - 16; values 0..15 from the low
+        // nibbles of qs, 16..31 from the high; fp16(q * d)
+        const __half2 d2 = __half2half2(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(blk))));
+        const uint32_t qh = TY == T_Q5_0 ? ldg_w2(blk + 2) : 0u;
+        const uint8_t* qs = blk + (TY == T_Q5_0 ? 6 : 2);
+        uint32_t v[16];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t w = ldg_w2(qs + 4 * j);
+#pragma unroll
+            for (int hi = 0; hi < 2; hi++) {
+                uint32_t n = (w >> (4 * hi)) & 0x0F0F0F0Fu;
+                if (TY == T_Q5_0) {
+                    const uint32_t bits = qh >> (16 * hi + 4 * j);
+                    n |= ((bits & 1u) << 4) | ((bits & 2u) << 11) | ((bits & 4u) << 18) | ((bits & 8u) << 25);
+                }
+                const uint32_t q = __vsub4(n, TY == T_Q5_0 ? 0x10101010u : 0x08080808u);
+                uint32_t lo, hh;
+                dequant4(q, d2, lo, hh);
+                v[8 * hi + 2 * j] = lo;
+                v[8 * hi + 2 * j + 1] = hh;
+            }
+        }
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)b * 32);
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else if (TY == T_Q6_K) {
+        // q = (ql nibble | 2 qh bits << 4) - 32, fp16(d * (sc * q)) with an int8 scale per 16 values
+        const float d = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(blk + 208))));
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)b * 256);
+#pragma unroll 1
+        for (int g = 0; g < 8; g++) {
+            const int h = g >> 2, quad = g & 3;
+            const uint32_t scw = __ldg(reinterpret_cast<const unsigned short*>(blk + 192 + 2 * g));
+            const int sc0 = (int)(int8_t)(scw & 0xffu), sc1 = (int)(int8_t)(scw >> 8);
+            uint32_t v[16];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t lw = (ldg_w2(blk + 64 * h + 32 * (quad & 1) + 4 * j) >> (4 * (quad >> 1))) & 0x0F0F0F0Fu;
+                const uint32_t hw = ((ldg_w2(blk + 128 + 32 * h + 4 * j) >> (2 * quad)) & 0x03030303u) << 4;
+                const uint32_t q = lw | hw;
+                const int sc = j < 4 ? sc0 : sc1;
+                float f[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) f[e] = d * (float)(sc * ((int)((q >> (8 * e)) & 0xffu) - 32));
+                const __half2 a = __floats2half2_rn(f[0], f[1]), c = __floats2half2_rn(f[2], f[3]);
+                v[2 * j] = h2_bits(a);
+                v[2 * j + 1] = h2_bits(c);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) o[g * 4 + i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    } else if (TY == T_Q5_K) {
+        // Q4_K's layout plus one high bit per value (qh bit g of byte i): q in 0..31
+        const uint4* b4 = reinterpret_cast<const uint4*>(blk);
+        const uint4 h = __ldg(b4);
+        const uint32_t hs[3] = {h.y, h.z, h.w};
+        const float dd = __half2float(__ushort_as_half((uint16_t)(h.x & 0xffffu)));
+        const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+        const uint4 qh0 = __ldg(b4 + 1), qh1 = __ldg(b4 + 2);
+        const uint32_t qh[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)b * 256);
+        uint32_t corr[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 q0 = __ldg(b4 + 3 + 2 * c), q1 = __ldg(b4 + 4 + 2 * c);
+            const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            uint32_t hv[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int g = 2 * c + e;
+                int scv, mv;
+                if (g < 4) {
+                    scv = scale_byte(hs, g) & 63;
+                    mv = scale_byte(hs, g + 4) & 63;
+                } else {
+                    scv = (scale_byte(hs, g + 4) & 0xF) | ((scale_byte(hs, g - 4) >> 6) << 4);
+                    mv = (scale_byte(hs, g + 4) >> 4) | ((scale_byte(hs, g) >> 6) << 4);
+                }
+                const __half2 d2 = __half2half2(__float2half_rn(dd * (float)scv));
+                hv[e] = (uint32_t)__half_as_ushort(__float2half_rn(-dmin * (float)mv));
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    uint32_t a0, a1, b0, b1;
+                    const uint32_t u0 = ((q[i] >> (4 * e)) & 0x0F0F0F0Fu) | (((qh[i] >> g) & 0x01010101u) << 4);
+                    const uint32_t u1 = ((q[i + 1] >> (4 * e)) & 0x0F0F0F0Fu) | (((qh[i + 1] >> g) & 0x01010101u) << 4);
+                    dequant4_ub(u0, d2, a0, a1);
+                    dequant4_ub(u1, d2, b0, b1);
+                    o[g * 4 + i / 2] = make_uint4(a0, a1, b0, b1);
+                }
+            }
+            corr[c] = hv[0] | (hv[1] << 16);
+        }
+        *reinterpret_cast<uint4*>(out + K + (size_t)b * 8) = make_uint4(corr[0], corr[1], corr[2], corr[3]);
+        if (b == 0)  // the padding of the appended columns, once per row
+            for (uint32_t k = K + K / 32; k < Kt; k++) out[k] = __float2half(0.0f);
+    } else if (TY == T_Q8_0) {
         const uint8_t* blk = x + ((size_t)sx * ssx + (size_t)cx * scx + (size_t)row * srx + b) * Q8_0_BYTES;
         const uint32_t* wa = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(blk) & ~(uintptr_t)3);
         const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(blk) & 3) * 8;  // 0 or 16
@@ -841,7 +967,7 @@ __global__ void __launch_bounds__(256)
     pdl_launch_dependents();
     pdl_wait();
     if (blockIdx.y < planes)
-        x_to_f16<TY == T_Q4_K ? 1 : 0>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y,
+        x_to_f16<mmq_ds4<TY>(), mmq_corr<TY>()>(blockIdx.x, blockIdx.y, y, xh, K, Kt, ncols, ncols_y, nchannels_y, stride_channel_y,
                                        stride_sample_y);
     else
         w_to_f16<TY>(blockIdx.x, blockIdx.y - planes, x, wh, K, Kt, nrows, srx, nch_x, scx, ssx);
@@ -923,6 +1049,7 @@ uint32_t tile_n(uint32_t ncols_dst) {
 template <uint32_t TY>
 bool qmm_applicable(const uint8_t* x, uint32_t K, uint32_t srx, uint32_t scx, uint32_t ssx, uint32_t nch_x,
                     uint32_t ns_x) {
+    if (TY != T_Q4_K && TY != T_Q8_0) return false;
     const char* e = getenv("CFI_MMQ_FUSED");
     if (e && strcmp(e, "0") == 0) return false;
     if (reinterpret_cast<uintptr_t>(x) & 15) return false;
@@ -956,9 +1083,9 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
         c.attrs = at;
         c.numAttrs = pdl ? 1 : 0;
         cudaError_t e = TY == T_Q4_K
-                            ? cudaLaunchKernelEx(&c, cfi_mmq_x_to_f16<1>, y, static_cast<__half*>(xh), K, Kt, ncols_dst,
+                            ? cudaLaunchKernelEx(&c, cfi_mmq_x_to_f16<1, 1>, y, static_cast<__half*>(xh), K, Kt, ncols_dst,
                                                  ncols_y, nch, scy, ssy)
-                            : cudaLaunchKernelEx(&c, cfi_mmq_x_to_f16<0>, y, static_cast<__half*>(xh), K, Kt, ncols_dst,
+                            : cudaLaunchKernelEx(&c, cfi_mmq_x_to_f16<0, 0>, y, static_cast<__half*>(xh), K, Kt, ncols_dst,
                                                  ncols_y, nch, scy, ssy);
         if (e != cudaSuccess) return (int)e;
     }
@@ -1100,13 +1227,15 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     const uint32_t scdst = (uint32_t)v[16], smr = (uint32_t)v[17], ns = (uint32_t)v[18], ssx = (uint32_t)v[19];
     const uint32_t ssy = (uint32_t)v[20], ssd = (uint32_t)v[21];
     if (K % 128 || !nrows || !ncols_dst || !nch || !ns || !chr || !smr) return (int)cudaErrorInvalidValue;
-    if (TY == T_Q4_K && K % 256) return (int)cudaErrorInvalidValue;
+    if (K % mmq_qk<TY>()) return (int)cudaErrorInvalidValue;
     if (TY == T_Q8_0 && ((reinterpret_cast<uintptr_t>(x) & 3) || (srx & 1) || (scx & 1) || (ssx & 1)))
         return (int)cudaErrorInvalidValue;
-    if (TY == T_Q4_K && (reinterpret_cast<uintptr_t>(x) & 3)) return (int)cudaErrorInvalidValue;
-    // the producers address a tile's 128 rows with 32-bit offsets
-    if ((uint64_t)BM * srx * (TY == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES) >= (1ull << 31)) return (int)cudaErrorInvalidValue;
-    const uint32_t Kc = TY == T_Q4_K ? (K / 32 + BK - 1) / BK * BK : 0;
+    // Q4_K / Q5_K superblocks are read as 16-byte words; the other types need 2-byte alignment
+    if ((TY == T_Q4_K || TY == T_Q5_K) && (reinterpret_cast<uintptr_t>(x) & 15)) return (int)cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(x) & 1) return (int)cudaErrorInvalidValue;
+    // the fixed-scratch kernel's producers address a tile's 128 rows with 32-bit offsets
+    if ((uint64_t)BM * srx * mmq_bb<TY>() >= (1ull << 31)) return (int)cudaErrorInvalidValue;
+    const uint32_t Kc = mmq_corr<TY>() ? (K / 32 + BK - 1) / BK * BK : 0;
     const uint32_t Kt = K + Kc;
     const uint32_t planes = nch * ns;
     void* xh = nullptr;
@@ -1132,7 +1261,7 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
         // 1. activations and weights -> fp16 K-major (one launch), then the shared TMA-fed
         // tcgen05 GEMM (C = Wh Xh^T per plane)
         __half* wh = reinterpret_cast<__half*>(static_cast<uint8_t*>(xh) + xh_pad);
-        const uint64_t nblk = (uint64_t)nrows * (K / (TY == T_Q4_K ? QK_K : QK8_0));
+        const uint64_t nblk = (uint64_t)nrows * (K / mmq_qk<TY>());
         const uint32_t gx_w = (uint32_t)((nblk + 255) / 256);
         const uint32_t gx_x = (ncols_dst * (K / 128) * 32 + 255) / 256;
         dim3 pgrid(std::max(gx_w, gx_x), planes + planes_x);
@@ -1170,14 +1299,17 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
         return rc < 0 ? (int)cudaErrorInvalidValue : rc;
     }
     // fixed scratch (no room for the fp16 weights): activations -> fp16, then the fused kernel
-    // dequantizes weight tiles in shared memory
+    // dequantizes weight tiles in shared memory (Q8_0 and Q4_K only)
+    if constexpr (TY != T_Q8_0 && TY != T_Q4_K) {
+        return (int)cudaErrorNotSupported;
+    } else {
     {
         const uint32_t warps = ncols_dst * (K / 128);
         dim3 grid((warps * 32 + 255) / 256, planes);
         if (TY == T_Q4_K)
-            cfi_mmq_x_to_f16<1><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
+            cfi_mmq_x_to_f16<1, 1><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
         else
-            cfi_mmq_x_to_f16<0><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
+            cfi_mmq_x_to_f16<0, 0><<<grid, 256, 0, stream>>>(y, static_cast<__half*>(xh), K, Kt, ncols_dst, ncols_y, nch, scy, ssy);
         rc = (int)cudaGetLastError();
         if (rc) return rc;
     }
@@ -1234,6 +1366,7 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     dim3 grid((nrows + BM - 1) / BM, (ncols_dst + bn - 1) / bn, planes);
     cfi_mmq_tc<TY><<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, tmap_c, a);
     return (int)cudaGetLastError();
+    }
 }
 
 }  // namespace
@@ -1241,15 +1374,23 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
 namespace cfi {
 int mmq_tile_n(uint32_t ncols_dst) { return (int)tile_n(ncols_dst); }
 int mmq_threads() { return THREADS; }
-bool mmq_type_ok(uint32_t ty) { return ty == T_Q8_0 || ty == T_Q4_K; }
+bool mmq_type_ok(uint32_t ty) {
+    return ty == T_Q8_0 || ty == T_Q4_K || ty == T_Q4_0 || ty == T_Q5_0 || ty == T_Q5_K || ty == T_Q6_K;
+}
 
 int mmq_launch(const cfi_plan& plan, void** args, void* stream) {
     std::vector<uint64_t> v = arg_values(plan, args);
     if (v.size() != 23) return (int)cudaErrorInvalidValue;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (plan.ty == T_Q8_0) return launch_tc<T_Q8_0>(v.data(), s);
-    if (plan.ty == T_Q4_K) return launch_tc<T_Q4_K>(v.data(), s);
-    return (int)cudaErrorNotSupported;
+    switch (plan.ty) {
+    case T_Q8_0: return launch_tc<T_Q8_0>(v.data(), s);
+    case T_Q4_K: return launch_tc<T_Q4_K>(v.data(), s);
+    case T_Q4_0: return launch_tc<T_Q4_0>(v.data(), s);
+    case T_Q5_0: return launch_tc<T_Q5_0>(v.data(), s);
+    case T_Q5_K: return launch_tc<T_Q5_K>(v.data(), s);
+    case T_Q6_K: return launch_tc<T_Q6_K>(v.data(), s);
+    default: return (int)cudaErrorNotSupported;
+    }
 }
 }  // namespace cfi
 

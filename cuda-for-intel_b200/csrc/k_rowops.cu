@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(CFI_ROWOP_THREADS)
         dst[idst + p + 1] = x[ix + p + 1];
         return;
     }
-    const float theta_base = (float)pos[channel_x] * powf(theta_scale, (float)i0 / 2.0f);
+    const float theta_base = __fmul_rn((float)pos[channel_x], powf(theta_scale, (float)i0 / 2.0f));
     const float ff = HAS_FF ? freq_factors[p] : 1.0f;
     const float theta_extrap = theta_base / ff;
     float theta = freq_scale * theta_extrap;
@@ -139,8 +139,9 @@ __global__ void __launch_bounds__(CFI_ROWOP_THREADS)
     sn *= mscale;
     if (!FORWARD) sn = -sn;
     const float x0 = x[ix + 0], x1 = x[ix + n_dims / 2];
-    dst[idst + 0] = x0 * cs - x1 * sn;
-    dst[idst + n_dims / 2] = x0 * sn + x1 * cs;
+    // rounded products, then the sum (no fused multiply-add: the fused decode kernel matches it)
+    dst[idst + 0] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+    dst[idst + n_dims / 2] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
 }
 
 // ggml's soft_max_params (128 bytes, tests/gpu/soft_max_generic.rs:10-31).

@@ -427,49 +427,108 @@ int probe_quantize_mmq(const cfi_plan& plan, void* stream, std::string* why) {
     return 0;
 }
 
-// mmq reference (refs.rs:771-834) for Q8_0 and Q4_K, one channel and sample.
+// One 32-value group of a weight block as the mmq tile loaders see it (refs.rs:659-740): signed
+// quants q, the group scale d (K-quants: half(d * sc)) and, for Q4_K / Q5_K, m = half(-dmin * m).
+// Q6_K: the two 16-value int8 scales in sc[] and d = the superblock d.
+struct XGroup {
+    int8_t q[32];
+    float d = 0.0f, m = 0.0f;
+    int sc[2] = {0, 0};
+};
+
+XGroup decode_group(uint32_t ty, const uint8_t* blk, int g) {
+    XGroup r;
+    switch (ty) {
+    case 8:
+        r.d = h2f(rd16(blk));
+        for (int i = 0; i < 32; i++) r.q[i] = (int8_t)blk[2 + i];
+        break;
+    case 2:
+        r.d = h2f(rd16(blk));
+        for (int i = 0; i < 32; i++) r.q[i] = (int8_t)((i < 16 ? (blk[2 + i] & 15) : (blk[2 + i - 16] >> 4)) - 8);
+        break;
+    case 6: {
+        r.d = h2f(rd16(blk));
+        const uint32_t qh = rd32(blk + 2);
+        for (int i = 0; i < 32; i++) {
+            const int nib = i < 16 ? (blk[6 + i] & 15) : (blk[6 + i - 16] >> 4);
+            r.q[i] = (int8_t)((nib | (int)(((qh >> i) & 1) << 4)) - 16);
+        }
+        break;
+    }
+    case 12:
+    case 13: {
+        const uint8_t* s = blk + 4;
+        int scv, mv;
+        if (g < 4) {
+            scv = s[g] & 63;
+            mv = s[g + 4] & 63;
+        } else {
+            scv = (s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4);
+            mv = (s[g + 4] >> 4) | ((s[g] >> 6) << 4);
+        }
+        r.d = h2f(f2h(h2f(rd16(blk)) * (float)scv));
+        r.m = h2f(f2h(-h2f(rd16(blk + 2)) * (float)mv));
+        for (int i = 0; i < 32; i++) {
+            const uint8_t v = blk[(ty == 12 ? 16 : 48) + 32 * (g / 2) + i];
+            const int nib = g % 2 == 0 ? (v & 15) : (v >> 4);
+            const int hi = ty == 13 ? ((blk[16 + i] >> g) & 1) : 0;
+            r.q[i] = (int8_t)(nib | (hi << 4));
+        }
+        break;
+    }
+    default: {  // 14: Q6_K
+        r.d = h2f(rd16(blk + 208));
+        r.sc[0] = (int8_t)blk[192 + 2 * g];
+        r.sc[1] = (int8_t)blk[192 + 2 * g + 1];
+        for (int i = 0; i < 32; i++) {
+            const int v = 32 * g + i, half = v / 128, rr = v % 128, quad = rr / 32, l = rr % 32;
+            int lo = blk[64 * half + 32 * (quad & 1) + l];
+            lo = (quad >> 1) == 0 ? (lo & 15) : (lo >> 4);
+            const int hi = (blk[128 + 32 * half + l] >> (2 * quad)) & 3;
+            r.q[i] = (int8_t)((lo | (hi << 4)) - 32);
+        }
+        break;
+    }
+    }
+    return r;
+}
+
+bool mmq_ds4(uint32_t ty) { return ty == 2 || ty == 12 || ty == 13; }
+uint32_t mmq_groups(uint32_t ty) { return (ty == 12 || ty == 13 || ty == 14) ? 8 : 1; }
+
+// mmq reference (refs.rs:771-834), one channel and sample.
 void mmq_ref(uint32_t ty, const uint8_t* x, const uint8_t* y, uint32_t ncols_x, uint32_t nrows, uint32_t ncols, float* dst) {
-    const uint32_t nb = ncols_x / 32, groups = ty == 12 ? 8 : 1, bb = (uint32_t)block_bytes(ty), srx = nb / groups;
+    const uint32_t nb = ncols_x / 32, groups = mmq_groups(ty), bb = (uint32_t)block_bytes(ty), srx = nb / groups;
     for (uint32_t c = 0; c < ncols; c++)
         for (uint32_t r = 0; r < nrows; r++) {
-            float sum = 0.0f;
+            float sum = 0.0f, tmp = 0.0f;
             for (uint32_t kb = 0; kb < nb; kb++) {
                 const uint8_t* blk = x + ((size_t)r * srx + kb / groups) * bb;
                 const uint8_t* yb = y + ((size_t)(kb / 4) * ncols + c) * 144;
                 const uint8_t* yq = yb + 16 + (kb % 4) * 32;
-                int8_t q[32];
-                float d, m = 0.0f;
-                if (ty == 8) {
-                    d = h2f(rd16(blk));
-                    for (int i = 0; i < 32; i++) q[i] = (int8_t)blk[2 + i];
+                const XGroup xg = decode_group(ty, blk, (int)(kb % groups));
+                int dots[2] = {0, 0};
+                for (int i = 0; i < 32; i++) dots[i / 16] += (int)xg.q[i] * (int)(int8_t)yq[i];
+                const int dot = dots[0] + dots[1];
+                float db, sb = 0.0f;
+                if (mmq_ds4(ty)) {
+                    db = h2f(rd16(yb + 4 * (kb % 4)));
+                    sb = h2f(rd16(yb + 4 * (kb % 4) + 2));
                 } else {
-                    const int g = (int)(kb % 8);
-                    const uint8_t* s = blk + 4;
-                    int scv, mv;
-                    if (g < 4) {
-                        scv = s[g] & 63;
-                        mv = s[g + 4] & 63;
-                    } else {
-                        scv = (s[g + 4] & 0xF) | ((s[g - 4] >> 6) << 4);
-                        mv = (s[g + 4] >> 4) | ((s[g] >> 6) << 4);
-                    }
-                    d = h2f(f2h(h2f(rd16(blk)) * (float)scv));
-                    m = h2f(f2h(-h2f(rd16(blk + 2)) * (float)mv));
-                    for (int i = 0; i < 32; i++) {
-                        uint8_t v = blk[16 + 32 * (g / 2) + i];
-                        q[i] = (int8_t)(g % 2 == 0 ? (v & 15) : (v >> 4));
-                    }
-                }
-                int dot = 0;
-                for (int i = 0; i < 32; i++) dot += (int)q[i] * (int)(int8_t)yq[i];
-                if (ty == 8) {
-                    float db;
                     memcpy(&db, yb + 4 * (kb % 4), 4);
-                    sum = fmaf(d * (float)dot, db, sum);
+                }
+                if (ty == 8 || ty == 2 || ty == 6) {
+                    sum = fmaf(xg.d * (float)dot, db, sum);
+                } else if (ty == 12 || ty == 13) {
+                    sum = fmaf(xg.d * db, (float)dot, sum);
+                    sum = fmaf(xg.m, sb, sum);
                 } else {
-                    float db = h2f(rd16(yb + 4 * (kb % 4))), sb = h2f(rd16(yb + 4 * (kb % 4) + 2));
-                    sum = fmaf(d * db, (float)dot, sum);
-                    sum = fmaf(m, sb, sum);
+                    tmp = fmaf((float)(dots[0] * xg.sc[0] + dots[1] * xg.sc[1]), db, tmp);
+                    if (kb % 4 == 3 || kb == nb - 1) {
+                        sum = fmaf(tmp, xg.d, sum);
+                        tmp = 0.0f;
+                    }
                 }
             }
             dst[(size_t)c * nrows + r] = sum;
@@ -480,17 +539,17 @@ void mmq_ref(uint32_t ty, const uint8_t* x, const uint8_t* y, uint32_t ncols_x, 
 // tensor-core kernel dequantises to fp16, so the bound is nmse < 1e-6 (1e-3 relative L2).
 int probe_mmq(const cfi_plan& plan, void* stream, std::string* why) {
     const uint32_t ty = plan.ty, ncols_x = 256, nrows = 70, ncols = 40;
-    if (ty != 8 && ty != 12) {
+    if (ty != 8 && ty != 12 && ty != 2 && ty != 6 && ty != 13 && ty != 14) {
         *why = "no host check for this type";
         return (int)cudaErrorNotSupported;
     }
     Rng rng{0x3171};
-    const uint32_t groups = ty == 12 ? 8 : 1, nb = ncols_x / 32 / groups;
+    const uint32_t groups = mmq_groups(ty), nb = ncols_x / 32 / groups;
     std::vector<uint8_t> x = random_blocks(ty, (size_t)nrows * nb, rng);
     std::vector<float> acts((size_t)ncols_x * ncols);
     for (auto& v : acts) v = rng.unit() * 2.0f;
     std::vector<uint8_t> y(ncols_x / 128 * ncols * 144);
-    quantize_mmq(ty == 12, acts.data(), ncols_x, ncols, y.data());
+    quantize_mmq(mmq_ds4(ty), acts.data(), ncols_x, ncols, y.data());
     std::vector<float> want((size_t)nrows * ncols), got(want.size());
     mmq_ref(ty, x.data(), y.data(), ncols_x, nrows, ncols, want.data());
     Dev d;

@@ -64,10 +64,16 @@ def random_q4_k(torch, rows, k, gen, device):
 
 
 class DecodeModel:
-    def __init__(self, torch, ctx, device, cfg=None, seed=0x5eed):
+    """fused=False: the ggml op sequence above, kernel by kernel.  fused=True: the same model with
+    Q/K/V and gate/up as stacked weights (one GEMV each) and the include/cfi_glue.h fused steps
+    (add + rms_norm + quantize, bias + rope + cache store, single-token attention to q8_1, SwiGLU +
+    quantize): 9 launches per layer instead of 25."""
+
+    def __init__(self, torch, ctx, device, cfg=None, seed=0x5eed, fused=False):
         self.t = torch
         self.cfg = cfg or Config()
         self.dev = device
+        self.fused = fused
         self.g = cfi.GgmlCaller(ctx, "all")
         self.blas = cfi.Blas()
         self.L = cfi.lib()
@@ -90,6 +96,16 @@ class DecodeModel:
                 kc=tt.zeros(c.n_kv_head, c.n_ctx, c.head_dim, dtype=tt.float16, device=device),
                 vc=tt.zeros(c.n_kv_head, c.head_dim, c.n_ctx, dtype=tt.float16, device=device)))
             lay = self.layers[-1]
+            # stacked Q/K/V and gate/up weights (the per-matrix entries become views of them)
+            lay["wqkv"] = tt.cat([lay["wq"], lay["wk"], lay["wv"]])
+            nqb, nkb = lay["wq"].numel(), lay["wk"].numel()
+            lay["wq"], lay["wk"], lay["wv"] = (lay["wqkv"][:nqb], lay["wqkv"][nqb:nqb + nkb],
+                                               lay["wqkv"][nqb + nkb:])
+            lay["wgu"] = tt.cat([lay["wg"], lay["wu"]])
+            ngb = lay["wg"].numel()
+            lay["wg"], lay["wu"] = lay["wgu"][:ngb], lay["wgu"][ngb:]
+            lay["bqkv"] = tt.cat([lay["bq"], lay["bk"], lay["bv"]])
+            lay["bq"], lay["bk"], lay["bv"] = lay["bqkv"][:nq], lay["bqkv"][nq:nq + nkv], lay["bqkv"][nq + nkv:]
             lay["kc"][:, :c.prompt] = (tt.randn(c.n_kv_head, c.prompt, c.head_dim, generator=gen, **f32)).half()
             lay["vc"][:, :, :c.prompt] = (tt.randn(c.n_kv_head, c.head_dim, c.prompt, generator=gen, **f32)).half()
         self.embd = random_q8_0(tt, c.vocab, c.hidden, gen, device)  # tied with lm_head
@@ -100,6 +116,7 @@ class DecodeModel:
         self.qr, self.kr = z(nq), z(nkv)
         self.attn, self.o = z(nq), z(c.hidden)
         self.gate, self.up, self.gu, self.dn = z(c.ffn), z(c.ffn), z(c.ffn), z(c.hidden)
+        self.qkv, self.gu2 = z(nq + 2 * nkv), z(2 * c.ffn)
         self.logits = z(c.vocab)
         self.scores, self.probs = z(c.n_head * c.n_ctx), z(c.n_head * c.n_ctx)
         self.mask = z(c.n_ctx)
@@ -122,6 +139,8 @@ class DecodeModel:
 
     def step(self, stream):
         """Enqueue one token step on `stream` (a cudaStream_t)."""
+        if self.fused:
+            return self.step_fused(stream)
         c, g, L, s = self.cfg, self.g, self.L, stream
         P = lambda t: C.c_void_p(t.data_ptr())
         sv = C.c_void_p(s)
@@ -188,3 +207,38 @@ class DecodeModel:
         gemv(self.embd, self.hq, self.logits, c.vocab, c.hidden)
         self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
         self.launches_per_step += 1  # the output rms_norm
+
+    def step_fused(self, stream):
+        """One token step with the stacked weights and the fused glue kernels."""
+        c, g, L, s = self.cfg, self.g, self.L, stream
+        P = lambda t: C.c_void_p(t.data_ptr())
+        sv = C.c_void_p(s)
+        nq, nkv = c.n_head * c.head_dim, c.n_kv_head * c.head_dim
+        eps, theta, scale = C.c_float(c.eps), C.c_float(c.theta), C.c_float(1.0 / math.sqrt(c.head_dim))
+        self.launches_per_step = 0
+
+        def gemv(w, xq, out, rows, k):
+            g.mmvq(cfi.Q8_0, 1, w.data_ptr(), xq.data_ptr(), out.data_ptr(), k, rows, stream=s)
+            self.launches_per_step += 1
+
+        self._chk(L.cfi_glue_get_rows_q8_0(P(self.embd), P(self.token), P(self.x), c.hidden, sv), "get_rows")
+        resid = None
+        for lay in self.layers:
+            self._chk(L.cfi_fused_add_rmsnorm_q8_1(P(self.x), resid, P(lay["attn_norm"]), P(self.hq), c.hidden, eps, sv),
+                      "add_rmsnorm")
+            gemv(lay["wqkv"], self.hq, self.qkv, nq + 2 * nkv, c.hidden)
+            self._chk(L.cfi_fused_qkv_rope_store(P(self.qkv), P(lay["bqkv"]), P(self.qr), P(lay["kc"]), P(lay["vc"]),
+                                                 P(self.pos), nq, nkv, c.head_dim, c.n_ctx, theta, sv), "qkv_rope")
+            self._chk(L.cfi_fused_attention_q8_1(P(self.qr), P(lay["kc"]), P(lay["vc"]), P(self.pos), P(self.aq),
+                                                 c.n_head, c.n_kv_head, c.head_dim, c.n_ctx, scale, sv), "attention")
+            gemv(lay["wo"], self.aq, self.o, c.hidden, nq)
+            self._chk(L.cfi_fused_add_rmsnorm_q8_1(P(self.x), P(self.o), P(lay["ffn_norm"]), P(self.hq), c.hidden, eps,
+                                                   sv), "add_rmsnorm")
+            gemv(lay["wgu"], self.hq, self.gu2, 2 * c.ffn, c.hidden)
+            self._chk(L.cfi_fused_swiglu_q8_1(P(self.gu2), P(self.gq), c.ffn, sv), "swiglu")
+            gemv(lay["wd"], self.gq, self.dn, c.hidden, c.ffn)
+            resid = P(self.dn)
+        self._chk(L.cfi_fused_add_rmsnorm_q8_1(P(self.x), resid, P(self.out_norm), P(self.hq), c.hidden, eps, sv),
+                  "add_rmsnorm")
+        gemv(self.embd, self.hq, self.logits, c.vocab, c.hidden)
+        self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")

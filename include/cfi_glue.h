@@ -36,8 +36,33 @@ CFI_API int cfi_glue_to_f16(const float *x, void *y, int n, void *stream);
 CFI_API int cfi_glue_add(float *x, const float *y, int n, void *stream);
 /* out = silu(g) * u */
 CFI_API int cfi_glue_swiglu(const float *g, const float *u, float *out, int n, void *stream);
-/* token[0] = first index of max(logits[0..n)); pos[0] += 1 */
+/* token[0] = first index of max(logits[0..n)); pos[0] += 1 (device-global partials: one call at a
+ * time per device) */
 CFI_API int cfi_glue_argmax_next(const float *logits, int n, int32_t *token, int32_t *pos, void *stream);
+
+/*
+ * Fused decode steps (one launch each where the ggml graph has two to five).  Results equal the
+ * unfused chain where stated; n, nq, nkv multiples of 32.
+ */
+/* x += y (y may be NULL), then q8_1 blocks of rms_norm(x) * w: equal to cfi_glue_add, the native
+ * rms_norm (with the weight multiply) and quantize_q8_1 in sequence, bit for bit.  n <= 8192. */
+CFI_API int cfi_fused_add_rmsnorm_q8_1(float *x, const float *y, const float *w, void *out_q8_1, int n, float eps,
+                                       void *stream);
+/* qkv = [q | k | v] (nq + 2 nkv floats, the output of one GEMV over the stacked Q/K/V weights):
+ * add the stacked biases, rope (NeoX, base theta, all head_dim dims) q into q_out and k, store k
+ * and v (f16) at pos[0] in the caches of cfi_glue_kv_store's layout. */
+CFI_API int cfi_fused_qkv_rope_store(const float *qkv, const float *bias, float *q_out, void *kc, void *vc,
+                                     const int32_t *pos, int nq, int nkv, int head_dim, int n_ctx, float theta,
+                                     void *stream);
+/* Single-token attention over cache positions 0..pos[0]: per query head h (kv head h / (n_head /
+ * n_kv_head)) softmax(scale K q) V in fp32 from the f16 caches, written as q8_1 blocks (head_dim
+ * 64 or 128; n_head <= 64; n_ctx a multiple of 8, at most 8192; caches 16-byte aligned).  Split
+ * over position ranges with device-global partials: one call at a time per device. */
+CFI_API int cfi_fused_attention_q8_1(const float *q, const void *kc, const void *vc, const int32_t *pos,
+                                     void *out_q8_1, int n_head, int n_kv_head, int head_dim, int n_ctx, float scale,
+                                     void *stream);
+/* q8_1 blocks of silu(gu[i]) * gu[n + i], i < n: equal to cfi_glue_swiglu then quantize_q8_1. */
+CFI_API int cfi_fused_swiglu_q8_1(const float *gu, void *out_q8_1, int n, void *stream);
 
 #ifdef __cplusplus
 }

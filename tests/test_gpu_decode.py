@@ -193,3 +193,178 @@ def test_graph_replay_equals_eager_steps(model):
         assert torch.equal(m.logits, logits)
     assert cfi.lib().cfi_device_error() == 0
     del gr
+
+
+# ------------------------------------------------------------------------------------------
+# fused decode steps (include/cfi_glue.h) against the unfused kernel chain they replace
+# ------------------------------------------------------------------------------------------
+def _p(t):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _s():
+    import ctypes
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("n", [896, 1536, 4864])
+def test_fused_add_rmsnorm_quantize_equals_the_chain(n):
+    import ctypes
+    L = cfi.lib()
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    gen = torch.Generator(device="cuda").manual_seed(n)
+    x0 = torch.randn(n, generator=gen, device="cuda")
+    y = torch.randn(n, generator=gen, device="cuda")
+    w = 1.0 + 0.1 * torch.randn(n, generator=gen, device="cuda")
+    xa, xb = x0.clone(), x0.clone()
+    h = torch.zeros(n, device="cuda")
+    qa = torch.zeros(n // 32 * 36, dtype=torch.uint8, device="cuda")
+    qb = torch.zeros_like(qa)
+    s = torch.cuda.current_stream().cuda_stream
+    assert L.cfi_glue_add(_p(xa), _p(y), n, _s()) == 0
+    g.rms_norm(xa.data_ptr(), h.data_ptr(), n, 1, mul=w.data_ptr(), eps=1e-6, stream=s)
+    g.quantize_q8_1(h.data_ptr(), qa.data_ptr(), n, n, 1, stream=s)
+    assert L.cfi_fused_add_rmsnorm_q8_1(_p(xb), _p(y), _p(w), _p(qb), n, ctypes.c_float(1e-6), _s()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(xa, xb)
+    assert torch.equal(qa, qb)
+    # without the residual add
+    assert L.cfi_fused_add_rmsnorm_q8_1(_p(xb), None, _p(w), _p(qb), n, ctypes.c_float(1e-6), _s()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb) and torch.equal(xa, xb)
+    ctx.close()
+
+
+@pytest.mark.parametrize("pos", [0, 631, 679])
+def test_fused_qkv_rope_store_equals_the_chain(pos):
+    import ctypes
+    L = cfi.lib()
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    nh, nkvh, hd, n_ctx, theta = 14, 2, 64, 680, 1e6
+    nq, nkv = nh * hd, nkvh * hd
+    gen = torch.Generator(device="cuda").manual_seed(pos)
+    qkv = torch.randn(nq + 2 * nkv, generator=gen, device="cuda")
+    bias = 0.1 * torch.randn(nq + 2 * nkv, generator=gen, device="cuda")
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    # unfused: bias, rope q and k, cache store
+    q, k, v = qkv[:nq].clone(), qkv[nq:nq + nkv].clone(), qkv[nq + nkv:].clone()
+    qr, kr = torch.zeros(nq, device="cuda"), torch.zeros(nkv, device="cuda")
+    kc_a = torch.zeros(nkvh, n_ctx, hd, dtype=torch.float16, device="cuda")
+    vc_a = torch.zeros(nkvh, hd, n_ctx, dtype=torch.float16, device="cuda")
+    q16 = torch.zeros(nq, dtype=torch.float16, device="cuda")
+    assert L.cfi_glue_qkv_bias(_p(q), _p(k), _p(v), _p(bias[:nq]), _p(bias[nq:nq + nkv]), _p(bias[nq + nkv:]), nq, nkv,
+                               _s()) == 0
+    g.rope_neox(q.data_ptr(), qr.data_ptr(), hd, nh, 1, hd, p.data_ptr(), freq_base=theta, stream=s)
+    g.rope_neox(k.data_ptr(), kr.data_ptr(), hd, nkvh, 1, hd, p.data_ptr(), freq_base=theta, stream=s)
+    assert L.cfi_glue_kv_store(_p(qr), _p(kr), _p(v), _p(q16), _p(kc_a), _p(vc_a), _p(p), nq, nkv, hd, n_ctx, _s()) == 0
+    # fused
+    q_out = torch.zeros(nq, device="cuda")
+    kc_b, vc_b = torch.zeros_like(kc_a), torch.zeros_like(vc_a)
+    assert L.cfi_fused_qkv_rope_store(_p(qkv), _p(bias), _p(q_out), _p(kc_b), _p(vc_b), _p(p), nq, nkv, hd, n_ctx,
+                                      ctypes.c_float(theta), _s()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(q_out, qr)
+    assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+    ctx.close()
+
+
+@pytest.mark.parametrize("nh,nkvh,hd,pos", [(14, 2, 64, 631), (14, 2, 64, 0), (12, 2, 128, 679)])
+def test_fused_attention_against_float64(nh, nkvh, hd, pos):
+    import ctypes
+    L = cfi.lib()
+    n_ctx = 680
+    gen = torch.Generator(device="cuda").manual_seed(nh + hd + pos)
+    q = torch.randn(nh * hd, generator=gen, device="cuda")
+    kc = torch.randn(nkvh, n_ctx, hd, generator=gen, device="cuda").half()
+    vc = torch.randn(nkvh, hd, n_ctx, generator=gen, device="cuda").half()
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    out = torch.zeros(nh * hd // 32 * 36, dtype=torch.uint8, device="cuda")
+    scale = 1.0 / math.sqrt(hd)
+    assert L.cfi_fused_attention_q8_1(_p(q), _p(kc), _p(vc), _p(p), _p(out), nh, nkvh, hd, n_ctx,
+                                      ctypes.c_float(scale), _s()) == 0
+    torch.cuda.synchronize()
+    assert cfi.lib().cfi_device_error() == 0
+    grp = nh // nkvh
+    qd = q.double().reshape(nh, hd)
+    want = []
+    for h in range(nh):
+        s_ = kc[h // grp, :pos + 1].double() @ qd[h] * scale
+        pr = torch.softmax(s_, 0)
+        want.append(vc[h // grp, :, :pos + 1].double() @ pr)
+    want = torch.cat(want)
+    # the q8_1 blocks of the exact output: the kernel's fp32 output is within ~1e-6 of it, so
+    # scales agree closely and quants differ by at most one step (round-half cases), rarely
+    import oracle_py as O
+    ref = torch.from_numpy(O.quantize_q8_1(want.float().cpu().numpy().reshape(1, -1))).reshape(-1, 36)
+    blk = out.cpu().reshape(-1, 36)
+    d = blk[:, 0:2].contiguous().view(torch.float16).double()
+    dr = ref[:, 0:2].contiguous().view(torch.float16).double()
+    assert torch.allclose(d, dr, rtol=2e-3, atol=0)
+    qv = blk[:, 4:].contiguous().view(torch.int8).int()
+    qr = ref[:, 4:].contiguous().view(torch.int8).int()
+    assert int((qv - qr).abs().max()) <= 1
+    assert float((qv != qr).float().mean()) < 0.02
+
+
+def test_fused_swiglu_quantize_equals_the_chain():
+    L = cfi.lib()
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    n = 4864
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    gu = 3 * torch.randn(2 * n, generator=gen, device="cuda")
+    out = torch.zeros(n, device="cuda")
+    qa = torch.zeros(n // 32 * 36, dtype=torch.uint8, device="cuda")
+    qb = torch.zeros_like(qa)
+    assert L.cfi_glue_swiglu(_p(gu[:n]), _p(gu[n:]), _p(out), n, _s()) == 0
+    g.quantize_q8_1(out.data_ptr(), qa.data_ptr(), n, n, 1, stream=torch.cuda.current_stream().cuda_stream)
+    assert L.cfi_fused_swiglu_q8_1(_p(gu), _p(qb), n, _s()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb)
+    ctx.close()
+
+
+def test_fused_step_tracks_the_unfused_step_and_replays():
+    """The fused step runs the same model (same weights, the unfused step's views): its logits stay
+    within the drift the attention's fp16 rounding points allow, and graph replays equal eager steps."""
+    ctx = cfi.Ctx(0)
+    cfg = Config(layers=2, vocab=2048)
+    mu = DecodeModel(torch, ctx, torch.device("cuda", 0), cfg)
+    mf = DecodeModel(torch, ctx, torch.device("cuda", 0), cfg, fused=True)
+    s = torch.cuda.current_stream()
+    mu.reset(token=77)
+    mu.step(s.cuda_stream)
+    mf.reset(token=77)
+    mf.step(s.cuda_stream)
+    torch.cuda.synchronize()
+    assert cfi.lib().cfi_device_error() == 0
+    assert rel(mf.logits, mu.logits) < 5e-2
+    assert mf.launches_per_step == 2 + 9 * cfg.layers + 2
+    # graph replay of the fused step == eager fused steps
+    for lay in mf.layers:
+        lay["kc"][:, cfg.prompt:] = 0
+        lay["vc"][:, :, cfg.prompt:] = 0
+    mf.reset(token=5)
+    eager = []
+    for _ in range(3):
+        mf.step(s.cuda_stream)
+        eager.append((int(mf.token.item()), mf.logits.clone()))
+    for lay in mf.layers:
+        lay["kc"][:, cfg.prompt:] = 0
+        lay["vc"][:, :, cfg.prompt:] = 0
+    mf.reset(token=5)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        mf.step(torch.cuda.current_stream().cuda_stream)
+    mf.reset(token=5)
+    for tok, logits in eager:
+        gr.replay()
+        torch.cuda.synchronize()
+        assert int(mf.token.item()) == tok
+        assert torch.equal(mf.logits, logits)
+    del gr
+    ctx.close()

@@ -46,6 +46,10 @@ def run(g, ty, p, x, y, n):
 @pytest.mark.parametrize("ty,shapes", [
     (cfi.Q8_0, [(256, 70, 40, 2, 1, 1), (384, 65, 9, 4, 2, 2), (128, 3, 1, 1, 1, 1), (512, 300, 300, 1, 1, 1)]),
     (cfi.Q4_K, [(512, 70, 40, 2, 1, 1), (256, 65, 9, 4, 2, 2), (768, 3, 1, 1, 1, 1), (2048, 129, 17, 1, 1, 1)]),
+    (cfi.Q4_0, [(256, 70, 40, 2, 1, 1), (384, 65, 9, 4, 2, 2), (2048, 129, 17, 1, 1, 1)]),
+    (cfi.Q5_0, [(256, 70, 40, 2, 1, 1), (384, 65, 9, 4, 2, 2), (2048, 129, 17, 1, 1, 1)]),
+    (cfi.Q5_K, [(512, 70, 40, 2, 1, 1), (256, 65, 9, 4, 2, 2), (2048, 129, 17, 1, 1, 1)]),
+    (cfi.Q6_K, [(512, 70, 40, 2, 1, 1), (256, 65, 9, 4, 2, 2), (2048, 129, 17, 1, 1, 1)]),
 ])
 def test_mmq_matches_the_oracle(dev, ty, shapes):
     ctx, g = dev
@@ -141,7 +145,7 @@ def test_mmq_quantize_mmq_layouts_are_byte_exact(dev):
 
 def test_mmq_probe_and_fixup_skip(dev):
     ctx, g = dev
-    for ty in (cfi.Q8_0, cfi.Q4_K):
+    for ty in (cfi.Q8_0, cfi.Q4_K, cfi.Q4_0, cfi.Q5_0, cfi.Q5_K, cfi.Q6_K):
         _, p, _ = cfi.decide(cfi.NAMES["mmq"].format(ty=ty, mmq_x=64, check=0), "mmq", "all")
         rc, why = ctx.probe(p, stream())
         assert rc == 0, why
