@@ -156,6 +156,8 @@ LAYOUTS = {
     "rms_norm_plain": [PTR, PTR, U32, U32, U32, U64, U64, U64, F32],
     "rope_neox": [PTR, PTR, U32, U32, U32, U32, U32, PTR, F32, F32, F32, _p(P_WORDS, 2, 4, 0), F32, PTR],
     "soft_max": [PTR, PTR, PTR, PTR, _p(P_WORDS, 32, 8, 0)],
+    "fattn": [PTR] * 8 + [F32, F32, F32, F32, U32, F32] + [U32] * 13 + [U64, U32, U32, U64, U32, U32, U32, U32, U32, U64],
+    "fattn_fixup": [PTR, PTR, U32, U32, U32, U32],
 }
 
 NAMES = {
@@ -168,6 +170,8 @@ NAMES = {
     "rms_norm_plain": "_Z12rms_norm_f32ILi32EEvPKfPfiiilllf",
     "rope_neox": "_Z9rope_neoxILb{fwd}ELb{ff}EfEvPKT1_PS0_iiiiiPKifff14rope_corr_dimsfPKf",
     "soft_max": "_Z12soft_max_f32ILb1ELi0ELi0E{t}EvPKfPKT2_S1_Pf15soft_max_params",
+    "fattn": "_Z18flash_attn_ext_f16ILi{d}ELi{d}ELi32ELi1ELi4ELi2ELb0ELb0EEvPKcS1_S1_S1_S1_PKiPfP6float2ffffjfiiiiiiiiiiiiiliiliiiiil",
+    "fattn_fixup": "_Z25flash_attn_stream_k_fixupILi{d}ELi32ELi1EEvPfPK6float2iiii",
 }
 
 
@@ -466,6 +470,28 @@ class GgmlCaller:
         p = self.plan(("mmq", ty, mmq_x), NAMES["mmq"].format(ty=ty, mmq_x=mmq_x, check=0), "mmq")
         vals = [("ptr", vx), ("ptr", vy), ("ptr", 0), ("ptr", 0), ("ptr", dst), ("ptr", tmp_fixup)] + [("u32", v) for v in words]
         return self._go(p, (148, 1, 1), (32, 8, 1), vals, stream, "mul_mat_q")
+
+    def fattn(self, d, q, k, v, mask, dst, nq, nh, nh_kv, nkv, ns, scale, nq_pad=None, dst_meta=0, q_strides=None,
+              kv_strides=None, stream=0):
+        """flash_attn_ext_f16<d, d, ...> on ggml's contiguous layouts (probe.rs:490-528): Q f32
+        [ns][nh][nq][d], K/V f16 [ns][nh_kv][nkv][d], mask f16 [ns][nq_pad][nkv] (0: none), dst f32
+        [ns][nq][nh][d]."""
+        nq_pad = (nq + 15) // 16 * 16 if nq_pad is None else nq_pad
+        p = self.plan(("fattn", d), NAMES["fattn"].format(d=d), "fattn")
+        nb01, nb02, nb03 = q_strides or (d * 4, d * 4 * nq, d * 4 * nq * nh)
+        nb11, nb12, nb13 = kv_strides or (d * 2, d * 2 * nkv, d * 2 * nkv * nh_kv)
+        vals = [("ptr", q), ("ptr", k), ("ptr", v), ("ptr", mask), ("ptr", 0), ("ptr", 0), ("ptr", dst),
+                ("ptr", dst_meta), ("f32", scale), ("f32", 0.0), ("f32", 1.0), ("f32", 1.0), ("u32", 0), ("f32", 0.0),
+                ("u32", d), ("u32", nq), ("u32", nh), ("u32", ns), ("u32", nb01), ("u32", nb02), ("u32", nb03),
+                ("u32", d), ("u32", nkv), ("u32", nh_kv), ("u32", ns), ("u32", nb11), ("u32", nb12), ("u64", nb13),
+                ("u32", nb11), ("u32", nb12), ("u64", nb13), ("u32", nkv), ("u32", nq_pad), ("u32", ns if mask else 0),
+                ("u32", nkv * 2), ("u32", nkv * 2 * nq_pad), ("u64", nkv * 2 * nq_pad)]
+        return self._go(p, ((nq + 31) // 32, nh, ns), (32, 4, 1), vals, stream, "flash_attn_ext_f16")
+
+    def fattn_fixup(self, d, dst, dst_meta, nq, nh, ns, nkv, stream=0):
+        p = self.plan(("fattn_fixup", d), NAMES["fattn_fixup"].format(d=d), "fattn_fixup")
+        vals = [("ptr", dst), ("ptr", dst_meta), ("i32", nq), ("i32", nh), ("i32", ns), ("i32", nkv)]
+        return self._go(p, (nq, nh, ns), (d, 1, 1), vals, stream, "flash_attn_stream_k_fixup")
 
     def rms_norm(self, x, dst, ncols, nrows, mul=0, add=0, eps=1e-6, nchannels=1, nsamples=1, stream=0):
         m, a = int(bool(mul)), int(bool(add))

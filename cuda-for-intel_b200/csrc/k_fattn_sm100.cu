@@ -1,0 +1,474 @@
+// k_fattn_sm100.cu -- the native flash_attn_ext_f16 (prefill FlashAttention) on the 5th-generation
+// tensor cores of sm_100a.
+//
+// Parameters: ggml-cuda's flash_attn_ext_f16<D, D, ncols1, ncols2, nwarps, ntiles, false, false>
+// (Q, K, V, mask, sinks, KV_max, dst, dst_meta, f32 scale, max_bias, m0, m1, u32 n_head_log2, f32
+// logit_softcap, i32 ne00..ne03, nb01..nb03, ne10..ne13, nb11, nb12, i64 nb13, nb21, nb22, i64 nb23,
+// ne31..ne33, nb31, nb32, i64 nb33; cuda-for-intel src/subst/fattn.rs:45-66, mod.rs:239-242).
+// Q f32 [seq][head][query][D] (byte strides nb01..nb03), K/V f16 [seq][kv head][key][D], mask f16
+// [seq % ne33][query][key] (row stride nb31), dst f32 [seq][query][head][D].  Supported as in the
+// reference (mod.rs:27-54): D = 64 or 128, no sinks, max_bias 0, no softcap, GQA; plus 16-byte
+// aligned K/V rows (TMA).
+//
+// One CTA of 192 threads per (128-query tile, head, sequence):
+//   * warps 0-3 own one query row each thread (TMEM lane = row): they convert Q (x scale) to fp16
+//     in the 128-byte swizzled K-major layout, then per 128-key chunk read the score row from
+//     TMEM, add the mask, run the online softmax (row max, exp, sum in fp32), rescale the output
+//     accumulator in TMEM when the running max grows, and write P (fp16) as the A operand of the
+//     PV product; at the end O / l goes to dst;
+//   * warp 4 streams K and V chunks with TMA (two stages, 128 keys x 64 dims per box, keys past the
+//     end read as zero);
+//   * one thread of warp 5 issues S = Q K^T (M 128, N 128, K = D) into one of two TMEM score
+//     buffers and O += P V (M 128, N = D, K 128; V is the MN-major B operand) into the TMEM output.
+// TMEM: scores at columns 0 and 128, output at 256.  Every wait is bounded (error word + abort).
+// Arithmetic: fp16 Q and P (as ggml's tensor-core kernel rounds them), fp32 scores, softmax and
+// accumulation; results agree with the exact softmax attention to ~1e-3 relative.
+#include <cuda.h>
+
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "cfi_common.cuh"
+#include "cfi_kernels.h"
+#include "sm100_ptx.cuh"
+#include "subst_host.hpp"
+
+static __device__ unsigned int g_fattn_error;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int FA_BM = 128;       // queries per CTA (TMEM lanes)
+constexpr int FA_BN = 128;       // keys per chunk
+constexpr int FA_THREADS = 192;  // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr uint32_t FA_TMEM_COLS = 512;
+
+struct FaArgs {
+    const uint8_t* q;
+    float* dst;
+    const uint8_t* mask;
+    float scale;
+    int ne01, ne02, ne03, ne11, ne12;
+    long long nb01, nb02, nb03;   // Q byte strides
+    long long nb31, nb33;         // mask byte strides (row, sequence)
+    int ne31, ne33;               // mask rows, mask sequences
+    int nchunks;
+    unsigned int* err;
+};
+
+template <int D>
+constexpr size_t fa_smem_bytes() {
+    return 1024 + (size_t)FA_BM * D * 2 + 4 * (size_t)FA_BN * D * 2 + (size_t)FA_BM * FA_BN * 2 + 256;
+}
+
+CFI_DEV void st_chunk16(uint8_t* atom, int r, int c, uint32_t a, uint32_t b, uint32_t cc, uint32_t d) {
+    *reinterpret_cast<uint4*>(atom + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(a, b, cc, d);
+}
+CFI_DEV uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int D>
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    cfi_fattn_tc(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, const FaArgs a) {
+    constexpr int DB = D / 64;                          // 64-dim blocks (one swizzle atom column each)
+    constexpr uint32_t QBYTES = FA_BM * D * 2;
+    constexpr uint32_t KVBYTES = FA_BN * D * 2;         // one K or V stage
+    constexpr uint32_t BLK_Q = FA_BM * 128, BLK_KV = FA_BN * 128;  // bytes of one 64-dim block
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + QBYTES;
+    uint8_t* sV = sK + 2 * KVBYTES;
+    uint8_t* sP = sV + 2 * KVBYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + FA_BM * FA_BN * 2);
+    uint64_t* kv_full = bars;       // [2] TMA bytes of K and V of a chunk
+    uint64_t* kv_empty = bars + 2;  // [2] the PV product of the chunk has read V (and S read K)
+    uint64_t* s_full = bars + 4;    // [2] scores of a chunk in TMEM
+    uint64_t* s_empty = bars + 6;   // [2] softmax warps have read them (4 arrivals)
+    uint64_t* p_full = bars + 8;    // P in shared memory, output rescaled (4 arrivals)
+    uint64_t* pv_done = bars + 9;   // O += P V completed
+    uint64_t* q_ready = bars + 10;  // fp16 Q in shared memory (4 arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q0 = blockIdx.x * FA_BM, head = blockIdx.y, seq = blockIdx.z;
+    const int kvh = head / (a.ne02 / a.ne12);
+    const int nch = a.nchunks;
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_empty[i], 4);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(pv_done, 1);
+        mbar_init(q_ready, 4);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, FA_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
+    pdl_wait();  // Q, K, V and the mask may come from the previous kernel
+
+    if (warp == 4) {
+        // ================= K / V chunks by TMA =================
+        if (lane == 0) {
+            prefetch_tmap(&tk);
+            prefetch_tmap(&tv);
+            for (int j = 0; j < nch; j++) {
+                const int st = j & 1;
+                if (!mbar_wait(&kv_empty[st], ((uint32_t)(j >> 1) & 1) ^ 1, abort_flag)) {
+                    cfi_set_error(a.err, 0xfa100 + st);
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&kv_full[st], 2 * KVBYTES);
+#pragma unroll
+                for (int b = 0; b < DB; b++) {
+                    tma_load_4d(sK + st * KVBYTES + b * BLK_KV, &tk, 64 * b, j * FA_BN, kvh, seq, &kv_full[st]);
+                    tma_load_4d(sV + st * KVBYTES + b * BLK_KV, &tv, 64 * b, j * FA_BN, kvh, seq, &kv_full[st]);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ================= MMA issue =================
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16(FA_BM, FA_BN, 0);
+            const uint32_t id_o = idesc_f16(FA_BM, D, 0) | (1u << 16);  // B (V) MN-major
+            bool ok = mbar_wait(q_ready, 0, abort_flag);
+            for (int j = 0; ok && j <= nch; j++) {
+                if (j < nch) {
+                    const int st = j & 1;
+                    ok = mbar_wait(&kv_full[st], (uint32_t)(j >> 1) & 1, abort_flag);
+                    if (ok && j >= 2) ok = mbar_wait(&s_empty[st], (uint32_t)((j >> 1) - 1) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t qa = smem_u32(sQ), kb = smem_u32(sK + st * KVBYTES);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint32_t off_q = (kk >> 2) * BLK_Q + (kk & 3) * 32, off_k = (kk >> 2) * BLK_KV + (kk & 3) * 32;
+                        mma_f16(tmem + st * FA_BN, sw128_kmajor_desc(qa + off_q), sw128_kmajor_desc(kb + off_k), id_s,
+                                kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&s_full[st]);
+                }
+                if (j >= 1) {
+                    const int jp = j - 1, st = jp & 1;
+                    ok = mbar_wait(p_full, (uint32_t)jp & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t pa = smem_u32(sP), vb = smem_u32(sV + st * KVBYTES);
+#pragma unroll
+                    for (int kk = 0; kk < FA_BN / 16; kk++) {
+                        const uint32_t off_p = (kk >> 2) * BLK_Q + (kk & 3) * 32;
+                        mma_f16(tmem + 256, sw128_kmajor_desc(pa + off_p), sw128_mnmajor_desc(vb + kk * 16 * 128, BLK_KV),
+                                id_o, (jp > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(pv_done);
+                    mma_commit(&kv_empty[st]);
+                }
+            }
+            if (!ok) {
+                cfi_set_error(a.err, 0xfa200);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ================= softmax warps: thread = query row =================
+        const int r = tid, q = q0 + r;
+        const bool qvalid = q < a.ne01;
+        {
+            const float* qrow = reinterpret_cast<const float*>(a.q + (size_t)seq * a.nb03 + (size_t)head * a.nb02 +
+                                                               (size_t)(qvalid ? q : 0) * a.nb01);
+#pragma unroll
+            for (int b = 0; b < DB; b++)
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] = qvalid ? qrow[64 * b + 8 * c + e] * a.scale : 0.0f;
+                    st_chunk16(sQ + b * BLK_Q, r, c, pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                               pack_h2(f[6], f[7]));
+                }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_ready);
+
+        const uint16_t* mrow = nullptr;
+        if (a.mask && q < a.ne31)
+            mrow = reinterpret_cast<const uint16_t*>(a.mask + (size_t)(seq % a.ne33) * a.nb33 + (size_t)q * a.nb31);
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        float m = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nch; j++) {
+            const int st = j & 1, key0 = j * FA_BN;
+            // tcgen05.ld / st are warp-collective: every decision before them is warp-uniform
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (uint32_t)(j >> 1) & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[FA_BN];
+#pragma unroll
+            for (int g = 0; g < FA_BN / 32; g++) {
+                uint32_t v[32];
+                tmem_ld32(trow + st * FA_BN + 32 * g, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) sv[32 * g + i] = __uint_as_float(v[i]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[st]);
+            // mask and keys past the end
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < FA_BN; c++) {
+                const int key = key0 + c;
+                float s = sv[c];
+                if (key >= a.ne11)
+                    s = -INFINITY;
+                else if (mrow)
+                    s += __half2float(__ushort_as_half(mrow[key]));
+                sv[c] = s;
+                mx = fmaxf(mx, s);
+            }
+            const float m_new = fmaxf(m, mx);
+            const bool none = m_new == -INFINITY;  // every key so far masked
+            const float alpha = none ? 1.0f : expf(m - m_new);
+            uint32_t ph[FA_BN / 2];
+            float psum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < FA_BN; c += 2) {
+                const float p0 = none ? 0.0f : expf(sv[c] - m_new), p1 = none ? 0.0f : expf(sv[c + 1] - m_new);
+                const __half2 h = __floats2half2_rn(p0, p1);
+                const float2 hf = __half22float2(h);
+                psum += hf.x + hf.y;  // the normaliser sums the fp16 weights the PV product uses
+                ph[c / 2] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            l = l * alpha + psum;
+            // the previous PV product must be done before O is rescaled and P is overwritten
+            if (j >= 1) {
+                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)(j - 1) & 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+                    for (int g = 0; g < D / 32; g++) {
+                        uint32_t v[32];
+                        tmem_ld32(trow + 256 + 32 * g, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                        tmem_st32(trow + 256 + 32 * g, v);
+                    }
+                    tmem_st_wait();
+                }
+            }
+#pragma unroll
+            for (int kb = 0; kb < FA_BN / 64; kb++)
+#pragma unroll
+                for (int c = 0; c < 8; c++)
+                    st_chunk16(sP + kb * BLK_Q, r, c, ph[32 * kb + 4 * c], ph[32 * kb + 4 * c + 1], ph[32 * kb + 4 * c + 2],
+                               ph[32 * kb + 4 * c + 3]);
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            m = m_new;
+        }
+        if (ok && nch > 0) ok = mbar_wait(pv_done, (uint32_t)(nch - 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+        if (!ok) {
+            if (lane == 0) {
+                cfi_set_error(a.err, 0xfa300 + warp);
+                *abort_flag = 1;
+            }
+        } else {
+            // every lane loads its TMEM row (collective); rows past the queries store nothing
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            float* out = a.dst + (((size_t)seq * a.ne01 + (qvalid ? q : 0)) * a.ne02 + head) * D;
+#pragma unroll
+            for (int g = 0; g < D / 32; g++) {
+                uint32_t v[32];
+                tmem_ld32(trow + 256 + 32 * g, v);
+                tmem_ld_wait();
+                if (qvalid) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(out + 32 * g + i) =
+                            make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
+                                        __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, FA_TMEM_COLS);
+    }
+}
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled encode_fn() {
+    static PFN_encodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+unsigned int* fa_err_ptr() {
+    static unsigned int* p = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_fattn_error) != cudaSuccess) {
+            cudaGetLastError();
+            p = nullptr;
+        }
+    });
+    return p;
+}
+
+template <int D>
+int launch_fa(const uint64_t* v, cudaStream_t stream) {
+    PFN_encodeTiled enc = encode_fn();
+    if (!enc) return (int)cudaErrorNotSupported;
+    auto i32 = [&](int k) { return (int)(uint32_t)v[k]; };
+    auto f32 = [&](int k) {
+        const uint32_t b = (uint32_t)v[k];
+        float f;
+        memcpy(&f, &b, 4);
+        return f;
+    };
+    const int ne01 = i32(15), ne02 = i32(16), ne03 = i32(17), ne11 = i32(22), ne12 = i32(23);
+    const long long nb11 = i32(25), nb12 = i32(26), nb13 = (long long)v[27];
+    const long long nb21 = i32(28), nb22 = i32(29), nb23 = (long long)v[30];
+    CUtensorMap tk, tv;
+    cuuint32_t box[4] = {64, FA_BN, 1, 1}, es[4] = {1, 1, 1, 1};
+    {
+        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)ne11, (cuuint64_t)ne12, (cuuint64_t)ne03};
+        cuuint64_t str[3] = {(cuuint64_t)nb11, (cuuint64_t)nb12, (cuuint64_t)nb13};
+        if (enc(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, reinterpret_cast<void*>(v[1]), dims, str, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    {
+        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)ne11, (cuuint64_t)ne12, (cuuint64_t)ne03};
+        cuuint64_t str[3] = {(cuuint64_t)nb21, (cuuint64_t)nb22, (cuuint64_t)nb23};
+        if (enc(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, reinterpret_cast<void*>(v[2]), dims, str, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    FaArgs a;
+    a.q = reinterpret_cast<const uint8_t*>(v[0]);
+    a.mask = reinterpret_cast<const uint8_t*>(v[3]);
+    a.dst = reinterpret_cast<float*>(v[6]);
+    a.scale = f32(8);
+    a.ne01 = ne01;
+    a.ne02 = ne02;
+    a.ne03 = ne03;
+    a.ne11 = ne11;
+    a.ne12 = ne12;
+    a.nb01 = i32(18);
+    a.nb02 = i32(19);
+    a.nb03 = i32(20);
+    a.ne31 = i32(32);
+    a.ne33 = std::max(1, i32(33));
+    a.nb31 = i32(34);
+    a.nb33 = (long long)v[36];
+    a.nchunks = (ne11 + FA_BN - 1) / FA_BN;
+    a.err = fa_err_ptr();
+    constexpr size_t smem = fa_smem_bytes<D>();
+    static std::once_flag attr;
+    std::call_once(attr, [] { cudaFuncSetAttribute(cfi_fattn_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
+    const char* ep = getenv("CFI_PDL");
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned)((ne01 + FA_BM - 1) / FA_BM), (unsigned)ne02, (unsigned)ne03);
+    c.blockDim = dim3(FA_THREADS, 1, 1);
+    c.dynamicSmemBytes = smem;
+    c.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    c.attrs = at;
+    c.numAttrs = (ep && strcmp(ep, "0") == 0) ? 0 : 1;
+    return (int)cudaLaunchKernelEx(&c, cfi_fattn_tc<D>, tk, tv, a);
+}
+
+}  // namespace
+
+namespace cfi {
+// mod.rs:27-54 plus this kernel's own needs: D 64/128, no sinks / ALiBi / softcap, GQA, at least
+// 16 queries (below that ggml's split-KV kernel keeps decode), Q rows 4-byte aligned, K/V rows and
+// strides 16-byte aligned (TMA), mask rows 2-byte aligned.
+bool fattn_geometry_ok(uint32_t d, const uint64_t* v, int n) {
+    if (n != 37 || (d != 64 && d != 128)) return false;
+    auto u = [&](int k) { return (uint32_t)v[k]; };
+    auto f_is_zero = [&](int k) { return (u(k) & 0x7fffffffu) == 0; };
+    const uint32_t ne00 = u(14), ne01 = u(15), ne02 = u(16), ne03 = u(17), ne11 = u(22), ne12 = u(23);
+    if (v[4] != 0 || !f_is_zero(9) || !f_is_zero(13)) return false;
+    if (ne00 != d || ne01 < 16 || ne02 == 0 || ne03 == 0 || ne11 == 0 || ne12 == 0 || ne02 % ne12 || ne03 > 65535 || ne02 > 65535)
+        return false;
+    if ((v[0] | u(18) | u(19) | u(20)) % 4) return false;
+    if ((v[1] | v[2] | u(25) | u(26) | v[27] | u(28) | u(29) | v[30]) % 16) return false;
+    if (v[3] != 0 && ((v[3] | u(34) | v[36]) % 2 || u(33) == 0)) return false;
+    if (v[6] % 16) return false;  // float4 stores of dst rows
+    return true;
+}
+
+int fattn_launch(const cfi_plan& plan, void** args, void* stream) {
+    std::vector<uint64_t> v = arg_values(plan, args);
+    if (!fattn_geometry_ok(plan.aux, v.data(), (int)v.size())) return (int)cudaErrorInvalidValue;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return plan.aux == 64 ? launch_fa<64>(v.data(), s) : launch_fa<128>(v.data(), s);
+}
+
+int fattn_threads() { return FA_THREADS; }
+int fattn_tile() { return FA_BM; }
+
+unsigned int fattn_error_take() {
+    unsigned int x = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&x, g_fattn_error, sizeof x) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaMemcpyToSymbol(g_fattn_error, &z, sizeof z);
+    return x;
+}
+}  // namespace cfi

@@ -1485,6 +1485,9 @@ extern "C" int cfi_mmq_static_scratch(uint32_t ggml_type, void** kernel_params, 
 }
 
 unsigned int cfi_gemm_error_take();  // k_gemm_sm100.cu
+namespace cfi {
+unsigned int fattn_error_take();     // k_fattn_sm100.cu
+}
 
 extern "C" unsigned int cfi_device_error(void) {
     unsigned int v = 0, z = 0;
@@ -1496,5 +1499,6 @@ extern "C" unsigned int cfi_device_error(void) {
     }
     const unsigned int g = cfi_gemm_error_take();
     const unsigned int m = cfi_mmvq_error_take();
-    return v ? v : (g ? g : m);
+    const unsigned int f = cfi::fattn_error_take();
+    return v ? v : (g ? g : (m ? m : f));
 }

@@ -10,6 +10,7 @@
 // accept or reject a kernel; it never produces results for a caller.
 #include <cuda_runtime.h>
 #include <math.h>
+#include <algorithm>
 #include <string.h>
 
 #include <vector>
@@ -775,8 +776,99 @@ int probe_soft_max(const cfi_plan& plan, void* stream, std::string* why) {
 
 }  // namespace
 
+// probe.rs:379-390: one FlashAttention tile (16 + 3 queries), 4 heads over 2 KV heads, 70 keys
+// (a partial chunk), causal mask with a padded third, seed 0xfa77 (probe.rs:421-446); exact f64
+// attention on the host.  fp16 Q and P on the tensor cores: nmse < 1e-5 (~3e-3 relative).
+int probe_fattn(const cfi_plan& plan, void* stream, std::string* why) {
+    const uint32_t d = plan.aux, nq = 19, nh = 4, nhk = 2, nkv = 70, ns = 1, nq_pad = 32;
+    if (d != 64 && d != 128) {
+        *why = "no host check for this head size";
+        return (int)cudaErrorNotSupported;
+    }
+    Rng rng{0xfa77};
+    std::vector<float> q((size_t)d * nq * nh * ns);
+    std::vector<uint16_t> k((size_t)d * nkv * nhk * ns), v(k.size()), m((size_t)nkv * nq_pad * ns);
+    for (auto& x : q) x = rng.unit();
+    for (auto& x : k) x = f2h(rng.unit());
+    for (auto& x : v) x = f2h(rng.unit());
+    for (uint32_t i = 0; i < nq_pad; i++)
+        for (uint32_t j = 0; j < nkv; j++) {
+            const uint32_t nvis = nkv - nkv / 3;
+            const bool visible = j < nvis && j + nq <= nvis + i;
+            m[(size_t)i * nkv + j] = visible ? f2h(rng.unit() * 0.5f) : (uint16_t)0xfc00;
+        }
+    const float scale = 1.0f / sqrtf((float)d);
+    std::vector<float> want((size_t)d * nh * nq * ns), got(want.size());
+    for (uint32_t h = 0; h < nh; h++)
+        for (uint32_t i = 0; i < nq; i++) {
+            std::vector<double> sc(nkv);
+            double mx = -INFINITY;
+            for (uint32_t j = 0; j < nkv; j++) {
+                double acc = 0;
+                for (uint32_t t = 0; t < d; t++)
+                    acc += (double)(q[((size_t)h * nq + i) * d + t] * scale) * (double)h2f(k[((size_t)(h / 2) * nkv + j) * d + t]);
+                acc += (double)h2f(m[(size_t)i * nkv + j]);
+                sc[j] = acc;
+                mx = std::max(mx, acc);
+            }
+            double l = 0;
+            for (auto& x : sc) l += (x = exp(x - mx));
+            for (uint32_t t = 0; t < d; t++) {
+                double o = 0;
+                for (uint32_t j = 0; j < nkv; j++) o += sc[j] * (double)h2f(v[((size_t)(h / 2) * nkv + j) * d + t]);
+                want[((size_t)i * nh + h) * d + t] = (float)(o / l);
+            }
+        }
+    Dev dv;
+    void* dq = dv.put(q.data(), q.size() * 4);
+    void* dk = dv.put(k.data(), k.size() * 2);
+    void* dvv = dv.put(v.data(), v.size() * 2);
+    void* dm = dv.put(m.data(), m.size() * 2);
+    void* dd = dv.put(nullptr, want.size() * 4);
+    CK(dq && dk && dvv && dm && dd);
+    Args a(37);
+    a.ptr(0, dq);
+    a.ptr(1, dk);
+    a.ptr(2, dvv);
+    a.ptr(3, dm);
+    a.ptr(4, nullptr);
+    a.ptr(5, nullptr);
+    a.ptr(6, dd);
+    a.ptr(7, nullptr);
+    a.f32(8, scale);
+    a.f32(9, 0.0f);
+    a.f32(10, 1.0f);
+    a.f32(11, 1.0f);
+    a.u32(12, 0);
+    a.f32(13, 0.0f);
+    const uint32_t w[] = {d, nq, nh, ns, d * 4, d * 4 * nq, d * 4 * nq * nh, d, nkv, nhk, ns, d * 2, d * 2 * nkv};
+    for (int i = 0; i < 13; i++) a.u32(14 + i, w[i]);
+    a.u64(27, (uint64_t)d * 2 * nkv * nhk);
+    a.u32(28, d * 2);
+    a.u32(29, d * 2 * nkv);
+    a.u64(30, (uint64_t)d * 2 * nkv * nhk);
+    a.u32(31, nkv);
+    a.u32(32, nq_pad);
+    a.u32(33, ns);
+    a.u32(34, nkv * 2);
+    a.u32(35, nkv * 2 * nq_pad);
+    a.u64(36, (uint64_t)nkv * 2 * nq_pad);
+    const uint32_t grid[3] = {2, nh, ns}, block[3] = {32, 4, 1};
+    int rc = run(plan, grid, block, a, stream, why);
+    if (rc) return rc;
+    CK(cudaMemcpy(got.data(), dd, got.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess);
+    const double e = nmse(got, want);
+    if (!(e < 1e-5)) {
+        *why = "fattn probe nmse " + std::to_string(e);
+        return (int)cudaErrorInvalidValue;
+    }
+    return 0;
+}
+
 int probe_validate(const cfi_plan& plan, void* stream, std::string* why) {
     switch (plan.kernel) {
+    case CFI_K_FATTN: return probe_fattn(plan, stream, why);
+    case CFI_K_FATTN_FIXUP: return 0;
     case CFI_K_MMVQ: return probe_mmvq(plan, stream, why);
     case CFI_K_QUANTIZE_Q8_1: return probe_quantize(plan, stream, why);
     case CFI_K_QUANTIZE_MMQ: return probe_quantize_mmq(plan, stream, why);

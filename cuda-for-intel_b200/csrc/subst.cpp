@@ -275,6 +275,15 @@ Layout layout_for(int kernel, uint32_t aux) {
     case CFI_K_SOFT_MAX:  // PKfPKT2_S1_Pf15soft_max_params (128-byte struct, 8-aligned)
         v = {ptr(), ptr(), ptr(), ptr(), P(CFI_P_WORDS, 32, 8, 0)};
         break;
+    case CFI_K_FATTN:  // mod.rs:239-242: 8 pointers, 29 scalars (nb13, nb23, nb33 int64)
+        v.assign(8, ptr());
+        v.insert(v.end(), {f32(), f32(), f32(), f32(), u32(), f32()});
+        v.insert(v.end(), 13, u32());
+        v.insert(v.end(), {u64(), u32(), u32(), u64(), u32(), u32(), u32(), u32(), u32(), u64()});
+        break;
+    case CFI_K_FATTN_FIXUP:  // mod.rs:244-247: dst, dst_fixup, ne01, ne02, ne03, ne11
+        v = {ptr(), ptr(), u32(), u32(), u32(), u32()};
+        break;
     }
     (void)aux;
     return v;
@@ -290,8 +299,8 @@ static bool layout_matches(int kernel, uint32_t ncols, const cfi_param* params, 
     bool exact = true;
     for (int i = 0; i < n; i++) exact = exact && param_eq(params[i], expected[i]);
     if (exact) return true;
-    if (kernel == CFI_K_MMQ || kernel == CFI_K_MMQ_FIXUP) {
-        int lead = kernel == CFI_K_MMQ ? 6 : 4;
+    if (kernel == CFI_K_MMQ || kernel == CFI_K_MMQ_FIXUP || kernel == CFI_K_FATTN || kernel == CFI_K_FATTN_FIXUP) {
+        int lead = kernel == CFI_K_MMQ ? 6 : kernel == CFI_K_MMQ_FIXUP ? 4 : kernel == CFI_K_FATTN ? 8 : 2;
         bool ok = true;
         for (int i = 0; i < n && ok; i++)
             ok = param_eq(params[i], expected[i]) || (i < lead && (params[i].kind == CFI_P_U64 || params[i].kind == CFI_P_PTR));
@@ -467,6 +476,17 @@ int decide(const std::string& name, const cfi_param* params, int nparams, const 
         kernel = CFI_K_SOFT_MAX;
         aux = t[3].name == "__half" ? 1 : 0;
         family = "soft_max";
+    } else if (b == "flash_attn_ext_f16" && t.size() == 8 && is_int(0) && is_int(1) && is_int(2) && is_int(3) &&
+               is_int(4) && is_int(5) && is_int(6) && is_int(7) && t[0].value == t[1].value &&
+               (t[0].value == 64 || t[0].value == 128) && t[6].value == 0 && t[7].value == 0) {
+        // mod.rs:420-425: equal K/Q and V head sizes 64 or 128, no logit softcap, no MLA
+        kernel = CFI_K_FATTN;
+        aux = (uint32_t)t[0].value;
+        family = "fattn";
+    } else if (b == "flash_attn_stream_k_fixup" && t.size() == 3 && is_int(0) && is_int(1) && is_int(2)) {
+        kernel = CFI_K_FATTN_FIXUP;
+        aux = (uint32_t)t[0].value;
+        family = "fattn";
     } else {
         return CFI_NOT_APPLICABLE;
     }
@@ -515,6 +535,8 @@ int decide(const std::string& name, const cfi_param* params, int nparams, const 
     case CFI_K_RMS_NORM_PLAIN: key = "rms_norm_plain"; break;
     case CFI_K_ROPE_NEOX: key = "rope_neox:f" + std::to_string(aux & 1) + "ff" + std::to_string(aux >> 1); break;
     case CFI_K_SOFT_MAX: key = aux ? "soft_max:f16" : "soft_max:f32"; break;
+    case CFI_K_FATTN: key = "fattn:d" + std::to_string(aux); break;
+    case CFI_K_FATTN_FIXUP: key = "fattn_fixup"; break;
     }
     snprintf(out->key, sizeof out->key, "%s", key.c_str());
     return CFI_SUBSTITUTE;
@@ -684,6 +706,18 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         nl.pdl = pdl_enabled();
         break;
     }
+    case CFI_K_FATTN: {
+        // mod.rs:27-54: stock block (32, nwarps); the native grid tiles 128 queries
+        if (block[0] != 32 || block[2] != 1 || !fattn_geometry_ok(plan.aux, vals, nvals)) return false;
+        const uint32_t ne01 = (uint32_t)vals[15], ne02 = (uint32_t)vals[16], ne03 = (uint32_t)vals[17];
+        nl.grid[0] = (ne01 + (uint32_t)fattn_tile() - 1) / (uint32_t)fattn_tile();
+        nl.grid[1] = ne02;
+        nl.grid[2] = ne03;
+        nl.block[0] = (uint32_t)fattn_threads();
+        nl.own_launch = true;
+        nl.fn = reinterpret_cast<const void*>(&fattn_launch);
+        break;
+    }
     default:
         return false;
     }
@@ -704,6 +738,7 @@ const void* native_kernel(const cfi_plan& plan, std::string* why) {
     case CFI_K_RMS_NORM_PLAIN: fn = cfi_native_rms_norm_plain(); break;
     case CFI_K_ROPE_NEOX: fn = cfi_native_rope_neox(plan.aux & 1, (plan.aux >> 1) & 1); break;
     case CFI_K_SOFT_MAX: fn = cfi_native_soft_max(plan.aux & 1); break;
+    case CFI_K_FATTN: fn = (plan.aux == 64 || plan.aux == 128) ? reinterpret_cast<const void*>(&fattn_launch) : nullptr; break;
     default: break;
     }
     if (!fn && why) *why = std::string("no sm_100a kernel for ") + plan.key;
@@ -728,6 +763,8 @@ struct cfi_ctx {
     std::map<std::string, int> natives;
     bool have_pending = false;
     uint64_t pending_dst = 0, pending_tmp = 0;
+    bool fa_pending = false;  // a native FlashAttention ran: its stream-k fixup is a no-op
+    uint64_t fa_dst = 0, fa_meta = 0;
     uint64_t fixup_events = 0;
     cfi_stats stats{};
     cfi::Inject inject[5];
@@ -817,7 +854,7 @@ static int ensure_smem(const void* fn, size_t smem) {
 }
 
 int issue_native(const NativeLaunch& nl, const cfi_plan& plan, void** args, void* stream) {
-    if (nl.own_launch) return mmq_launch(plan, args, stream);
+    if (nl.own_launch) return plan.kernel == CFI_K_FATTN ? fattn_launch(plan, args, stream) : mmq_launch(plan, args, stream);
     std::vector<void*> argv(args, args + nl.nparams);
     std::vector<uint32_t> extra = nl.extra;
     for (auto& w : extra) argv.push_back(&w);
@@ -862,7 +899,17 @@ int launch_to(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t
     if (plan) {
         std::vector<uint64_t> vals = arg_values(*plan, args);
         if (plan->kernel == CFI_K_MMQ) ctx->have_pending = false;
-        if (plan->kernel == CFI_K_MMQ_FIXUP) {
+        if (plan->kernel == CFI_K_FATTN) ctx->fa_pending = false;
+        if (plan->kernel == CFI_K_FATTN_FIXUP) {
+            // [dst, dst_fixup, ...]: the native FlashAttention writes final results (fattn.rs:17-18)
+            const bool skip = vals.size() == 6 && ctx->fa_pending && ctx->fa_dst == vals[0] && ctx->fa_meta == vals[1];
+            if (ctx->fixup_events++ < 40) logf_("fattn fixup %s", skip ? "skipped" : "RUNS");
+            if (skip) {
+                ctx->fa_pending = false;
+                ctx->stats.fixups_skipped++;
+                return 0;
+            }
+        } else if (plan->kernel == CFI_K_MMQ_FIXUP) {
             // [ids, bounds, dst, tmp, ...]: only fixups of a native mul_mat_q are no-ops
             const bool skip = vals.size() == 13 && ctx->have_pending && ctx->pending_dst == vals[2] && ctx->pending_tmp == vals[3];
             if (ctx->fixup_events++ < 40) logf_("mmq fixup %s", skip ? "skipped" : "RUNS");
@@ -886,6 +933,11 @@ int launch_to(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t
                         ctx->have_pending = true;
                         ctx->pending_dst = vals[4];
                         ctx->pending_tmp = vals[5];
+                    }
+                    if (plan->kernel == CFI_K_FATTN) {
+                        ctx->fa_pending = true;
+                        ctx->fa_dst = vals[6];
+                        ctx->fa_meta = vals[7];
                     }
                     return 0;
                 }
@@ -996,6 +1048,7 @@ void cfi_plan_entry_name(const cfi_plan* plan, char* out, size_t len) {
     case CFI_K_RMS_NORM_PLAIN: snprintf(buf, sizeof buf, "cfi_rms_norm_plain"); break;
     case CFI_K_ROPE_NEOX: snprintf(buf, sizeof buf, "cfi_rope_neox_f%u_ff%u", plan->aux & 1, (plan->aux >> 1) & 1); break;
     case CFI_K_SOFT_MAX: snprintf(buf, sizeof buf, "cfi_soft_max_%s", plan->aux ? "f16" : "f32"); break;
+    case CFI_K_FATTN: snprintf(buf, sizeof buf, "cfi_fattn_tc_d%u", plan->aux); break;
     default: break;
     }
     copy_out(buf, out, len);

@@ -87,4 +87,11 @@ int probe_validate(const cfi_plan& plan, void* stream, std::string* why);
 // Launch of the native mmq (k_mmq_sm100.cu), with its own grid and launch attributes.
 int mmq_launch(const cfi_plan& plan, void** args, void* stream);
 
+// Native FlashAttention (k_fattn_sm100.cu): the launch words it serves (plan.aux = head size) and
+// its own launch.
+bool fattn_geometry_ok(uint32_t d, const uint64_t* vals, int n);
+int fattn_launch(const cfi_plan& plan, void** args, void* stream);
+int fattn_threads();
+int fattn_tile();
+
 }  // namespace cfi

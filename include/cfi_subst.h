@@ -47,7 +47,9 @@ enum cfi_kernel {
     CFI_K_RMS_NORM = 6,     /* rms_norm_f32<block, do_multiply, do_add> */
     CFI_K_RMS_NORM_PLAIN = 7, /* rms_norm_f32<block> (older iiilllf parameter list) */
     CFI_K_ROPE_NEOX = 8,    /* rope_neox<forward, has_ff, float> */
-    CFI_K_SOFT_MAX = 9      /* soft_max_f32<use_shared, ncols, block, T> */
+    CFI_K_SOFT_MAX = 9,     /* soft_max_f32<use_shared, ncols, block, T> */
+    CFI_K_FATTN = 10,       /* flash_attn_ext_f16<D, D, ncols1, ncols2, nwarps, ntiles, false, false> */
+    CFI_K_FATTN_FIXUP = 11  /* flash_attn_stream_k_fixup<D, ncols1, ncols2>: skipped after a native one */
 };
 
 /* Decode-fast shape of mmvq (replaces mmvq::Fast, src/subst/mmvq.rs:727-735). */

@@ -994,3 +994,57 @@ void cfo_soft_max(const float *x, const float *mask, const float *sinks, float *
     }
     free(v);
 }
+
+/* ---- src/subst/probe.rs:421-489: FlashAttention case (xorshift64* draws in the reference's
+ * order: Q, K, V, then the mask biases) and the exact f64 softmax attention ---- */
+void cfo_fattn_case(uint32_t d, uint32_t nq, uint32_t nh, uint32_t nh_kv, uint32_t nkv, uint32_t ns, int causal,
+                    uint64_t seed, float *q, uint16_t *k, uint16_t *v, uint16_t *mask) {
+    uint64_t rng = seed;
+    for (size_t i = 0; i < (size_t)d * nq * nh * ns; i++) q[i] = cfo_rng_unit(&rng);
+    for (size_t i = 0; i < (size_t)d * nkv * nh_kv * ns; i++) k[i] = cfo_f32_to_f16(cfo_rng_unit(&rng));
+    for (size_t i = 0; i < (size_t)d * nkv * nh_kv * ns; i++) v[i] = cfo_f32_to_f16(cfo_rng_unit(&rng));
+    if (!causal || !mask) return;
+    size_t nq_pad = (nq + 15) / 16 * 16;
+    for (size_t s = 0; s < ns; s++)
+        for (size_t i = 0; i < nq_pad; i++)
+            for (size_t j = 0; j < nkv; j++) {
+                /* the last third of the keys is padding; query i sees keys up to nvis - nq + i */
+                size_t nvis = nkv - nkv / 3;
+                int visible = j < nvis && j + nq <= nvis + i;
+                mask[(s * nq_pad + i) * nkv + j] = visible ? cfo_f32_to_f16(cfo_rng_unit(&rng) * 0.5f) : 0xfc00;
+            }
+}
+
+void cfo_fattn_reference(uint32_t d, uint32_t nq, uint32_t nh, uint32_t nh_kv, uint32_t nkv, uint32_t ns,
+                         const float *q, const uint16_t *k, const uint16_t *v, const uint16_t *mask, float scale,
+                         float *dst) {
+    size_t gqa = nh / nh_kv, nq_pad = (nq + 15) / 16 * 16;
+    double *sc = (double *)malloc(sizeof(double) * nkv);
+    for (size_t s = 0; s < ns; s++)
+        for (size_t h = 0; h < nh; h++) {
+            size_t kh = h / gqa;
+            for (size_t i = 0; i < nq; i++) {
+                const float *qrow = q + ((s * nh + h) * nq + i) * d;
+                double mx = -INFINITY;
+                for (size_t j = 0; j < nkv; j++) {
+                    const uint16_t *krow = k + ((s * nh_kv + kh) * nkv + j) * d;
+                    double acc = 0;
+                    for (size_t t = 0; t < d; t++) acc += (double)(qrow[t] * scale) * (double)cfo_f16_to_f32(krow[t]);
+                    if (mask) acc += (double)cfo_f16_to_f32(mask[(s * nq_pad + i) * nkv + j]);
+                    sc[j] = acc;
+                    if (acc > mx) mx = acc;
+                }
+                double l = 0;
+                for (size_t j = 0; j < nkv; j++) {
+                    sc[j] = exp(sc[j] - mx);
+                    l += sc[j];
+                }
+                for (size_t t = 0; t < d; t++) {
+                    double o = 0;
+                    for (size_t j = 0; j < nkv; j++) o += sc[j] * (double)cfo_f16_to_f32(v[((s * nh_kv + kh) * nkv + j) * d + t]);
+                    dst[((s * nq + i) * nh + h) * d + t] = (float)(o / l);
+                }
+            }
+        }
+    free(sc);
+}

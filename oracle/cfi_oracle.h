@@ -125,6 +125,15 @@ void cfo_soft_max(const float *x, const float *mask, const float *sinks, float *
                   size_t nheads, size_t rows, float scale, float max_bias);
 
 /* cpu_baseline.c: one host decode step (quantize + row-parallel GEMV); returns threads used */
+/* ---- FlashAttention case and exact reference (src/subst/probe.rs:405-489) ----
+ * Q [ns][nh][nq][d] f32, K/V [ns][nh_kv][nkv][d] f16, mask [ns][nq_pad][nkv] f16 (or none),
+ * dst [ns][nq][nh][d] f32; nq_pad = nq rounded up to 16. */
+void cfo_fattn_case(uint32_t d, uint32_t nq, uint32_t nh, uint32_t nh_kv, uint32_t nkv, uint32_t ns, int causal,
+                    uint64_t seed, float *q, uint16_t *k, uint16_t *v, uint16_t *mask);
+void cfo_fattn_reference(uint32_t d, uint32_t nq, uint32_t nh, uint32_t nh_kv, uint32_t nkv, uint32_t ns,
+                         const float *q, const uint16_t *k, const uint16_t *v, const uint16_t *mask, float scale,
+                         float *dst);
+
 int cfo_cpu_decode_step(uint32_t ty, const uint8_t *w, size_t rows, size_t ncols_x, const float *x,
                         size_t ncols_dst, uint8_t *yq, float *dst, int threads);
 

@@ -59,6 +59,13 @@ def lib():
         _o.cfo_rng_next.restype = C.c_uint64
         _o.cfo_dp4a.restype = C.c_int32
         _o.cfo_dp4a.argtypes = [C.c_uint32, C.c_uint32, C.c_int32]
+        u32 = C.c_uint32
+        _o.cfo_fattn_case.argtypes = [u32, u32, u32, u32, u32, u32, C.c_int, C.c_uint64, f32p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p]
+        _o.cfo_fattn_case.restype = None
+        _o.cfo_fattn_reference.argtypes = [u32, u32, u32, u32, u32, u32, f32p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_float, f32p]
+        _o.cfo_fattn_reference.restype = None
         _o.cfo_fastdiv.restype = C.c_uint32
         _o.cfo_fastmodulo.restype = C.c_uint32
         _o.cfo_gemm_validate.restype = C.c_int
@@ -216,3 +223,26 @@ def cpu_decode_step(ty, w, rows, ncols_x, x, ncols_dst, threads=0):
     dst = np.zeros(ncols_dst * rows, dtype=np.float32)
     used = lib().cfo_cpu_decode_step(C.c_uint32(ty), u8(w), rows, ncols_x, f32(x), ncols_dst, u8(yq), f32(dst), threads)
     return dst, yq, used
+
+
+def fattn_case(d, nq, nh, nh_kv, nkv, ns, causal, seed):
+    """src/subst/probe.rs:421-446: Q f32 [ns][nh][nq][d], K/V f16 bits [ns][nh_kv][nkv][d], mask f16
+    bits [ns][nq_pad][nkv] (None without a mask)."""
+    q = np.zeros(d * nq * nh * ns, dtype=np.float32)
+    k = np.zeros(d * nkv * nh_kv * ns, dtype=np.uint16)
+    v = np.zeros_like(k)
+    nq_pad = (nq + 15) // 16 * 16
+    m = np.zeros(nkv * nq_pad * ns, dtype=np.uint16) if causal else None
+    lib().cfo_fattn_case(d, nq, nh, nh_kv, nkv, ns, int(causal), C.c_uint64(seed), f32(q),
+                         k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p),
+                         m.ctypes.data_as(C.c_void_p) if m is not None else None)
+    return q, k, v, m
+
+
+def fattn_reference(d, nq, nh, nh_kv, nkv, ns, q, k, v, m, scale):
+    """Exact softmax attention in f64 (probe.rs:451-487); dst [ns][nq][nh][d] f32."""
+    out = np.zeros(d * nh * nq * ns, dtype=np.float32)
+    lib().cfo_fattn_reference(d, nq, nh, nh_kv, nkv, ns, f32(q), k.ctypes.data_as(C.c_void_p),
+                              v.ctypes.data_as(C.c_void_p), m.ctypes.data_as(C.c_void_p) if m is not None else None,
+                              C.c_float(scale), f32(out))
+    return out
