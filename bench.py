@@ -325,6 +325,38 @@ def config5_bench(cfi, g, stream, dev, peak_gbs, peak_tf):
     return res
 
 
+def fattn_bench(cfi, g, stream, dev, peak_tf):
+    """The native flash_attn_ext_f16 (tcgen05) on the prefill attention of BASELINE configs 4 and 5:
+    631 queries against a 640-key padded causal cache (14 heads x 64 over 2 KV heads; 12 x 128 over
+    2), CUDA graph of back-to-back calls.  FLOPs counted for the whole score matrix (4 nq nkv D H):
+    masked keys are computed, not skipped."""
+    import torch
+
+    out = {}
+    for d, nh, nhk in ((64, 14, 2), (128, 12, 2)):
+        nq, nkv = 631, 640
+        gen = torch.Generator(device=dev).manual_seed(d)
+        q = torch.randn(nh * nq * d, generator=gen, device=dev)
+        k = torch.randn(nhk * nkv * d, generator=gen, device=dev).half()
+        v = torch.randn(nhk * nkv * d, generator=gen, device=dev).half()
+        nq_pad = (nq + 15) // 16 * 16
+        i = torch.arange(nq_pad, device=dev)[:, None]
+        j = torch.arange(nkv, device=dev)[None, :]
+        mask = torch.where(j <= i, 0.0, float("-inf")).half().contiguous()
+        dst = torch.zeros(nq * nh * d, device=dev)
+        call = lambda n, st: g.fattn(d, q.data_ptr(), k.data_ptr(), v.data_ptr(), mask.data_ptr(), dst.data_ptr(), nq,
+                                     nh, nhk, nkv, 1, 1.0 / d ** 0.5, stream=st)
+        with torch.cuda.stream(stream):
+            call(0, stream.cuda_stream)
+        torch.cuda.synchronize()
+        us = graph_time_us(stream, call, reps=5, calls=20)
+        fl = 4.0 * nq * nkv * d * nh
+        out["d%d_h%d" % (d, nh)] = {"us": round(us, 2), "tflops": round(fl / us / 1e6, 1),
+                                   "frac": round(fl / us / 1e6 / peak_tf, 4)}
+    return {"workload": "flash_attn_ext_f16, 631 queries x 640 keys, causal mask (configs 4 / 5 prefill attention)",
+            "shapes": out}
+
+
 def decode_bench(stream, dev, ntok=48, warm=3, fused=False):
     """Qwen2.5-0.5B-architecture decode (24 layers, Q8_0 random weights, 631-token
     seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens.  fused: the
@@ -597,6 +629,7 @@ def run_gpu(args, rank, world):
         if not args.no_configs and world == 1:
             line["config1"] = config1_bench(cfi, g, stream, dev, peak)
             line["config5"] = config5_bench(cfi, g, stream, dev, peak, tensor_peak())
+            line["fattn"] = fattn_bench(cfi, g, stream, dev, tensor_peak())
         if not args.no_cpu and world == 1:
             gbs, used, n, el = cpu_baseline(args.cpu_seconds)
             gbs1, _, n1, el1 = cpu_baseline(max(1.0, args.cpu_seconds / 2), threads=1)

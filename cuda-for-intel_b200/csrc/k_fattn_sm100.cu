@@ -10,15 +10,19 @@
 // reference (mod.rs:27-54): D = 64 or 128, no sinks, max_bias 0, no softcap, GQA; plus 16-byte
 // aligned K/V rows (TMA).
 //
-// One CTA of 192 threads per (128-query tile, head, sequence):
-//   * warps 0-3 own one query row each thread (TMEM lane = row): they convert Q (x scale) to fp16
-//     in the 128-byte swizzled K-major layout, then per 128-key chunk read the score row from
-//     TMEM, add the mask, run the online softmax (row max, exp, sum in fp32), rescale the output
-//     accumulator in TMEM when the running max grows, and write P (fp16) as the A operand of the
-//     PV product; at the end O / l goes to dst;
-//   * warp 4 streams K and V chunks with TMA (two stages, 128 keys x 64 dims per box, keys past the
+// One CTA of 320 threads per (128-query tile, head, sequence):
+//   * warps 0-7 run the softmax, two warps per TMEM lane quadrant: thread (row, half) owns one
+//     query row (TMEM lane) and 64 of the 128 key columns of a chunk.  They convert Q (x scale) to
+//     fp16 in the 128-byte swizzled K-major layout, then per chunk read their score columns from
+//     TMEM, add the mask (16-byte loads issued before the wait), exchange the half-row maxima through
+//     shared memory, run the online softmax (row max, exp, sum in fp32), rescale their half of the
+//     output accumulator in TMEM when the running max grows, and write their half of P (fp16) as the
+//     A operand of the PV product; at the end O / (l_0 + l_1) goes to dst;
+//   * before the loop the tile's key range is cut to the chunks where some valid query sees some
+//     key (mask not -inf), so a causal prompt skips the chunks above the diagonal;
+//   * warp 9 streams K and V chunks with TMA (two stages, 128 keys x 64 dims per box, keys past the
 //     end read as zero);
-//   * one thread of warp 5 issues S = Q K^T (M 128, N 128, K = D) into one of two TMEM score
+//   * one thread of warp 8 issues S = Q K^T (M 128, N 128, K = D) into one of two TMEM score
 //     buffers and O += P V (M 128, N = D, K 128; V is the MN-major B operand) into the TMEM output.
 // TMEM: scores at columns 0 and 128, output at 256.  Every wait is bounded (error word + abort).
 // Arithmetic: fp16 Q and P (as ggml's tensor-core kernel rounds them), fp32 scores, softmax and
@@ -43,7 +47,9 @@ using namespace sm100;
 
 constexpr int FA_BM = 128;       // queries per CTA (TMEM lanes)
 constexpr int FA_BN = 128;       // keys per chunk
-constexpr int FA_THREADS = 192;  // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int FA_SOFTMAX_WARPS = 8, FA_MMA_WARP = 8, FA_TMA_WARP = 9;
+constexpr int FA_FLAG_WORDS = 8;  // chunk-visibility bits: key ranges up to 256 chunks are cut
+constexpr int FA_THREADS = 320;  // warps 0-7 softmax (two per TMEM sub-partition), 8 MMA, 9 TMA
 constexpr uint32_t FA_TMEM_COLS = 512;
 
 struct FaArgs {
@@ -76,10 +82,14 @@ template <int D>
 __global__ void __launch_bounds__(FA_THREADS, 1)
     cfi_fattn_tc(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, const FaArgs a) {
     constexpr int DB = D / 64;                          // 64-dim blocks (one swizzle atom column each)
+    constexpr int DH = D / 2;                           // output columns per softmax half
     constexpr uint32_t QBYTES = FA_BM * D * 2;
     constexpr uint32_t KVBYTES = FA_BN * D * 2;         // one K or V stage
     constexpr uint32_t BLK_Q = FA_BM * 128, BLK_KV = FA_BN * 128;  // bytes of one 64-dim block
     extern __shared__ uint8_t smem_raw[];
+    __shared__ float xmax[2][2][FA_BM];  // partial row maxima (chunk parity, key half, row)
+    __shared__ float xsum[2][FA_BM];     // final partial row sums (key half, row)
+    __shared__ uint32_t chunk_vis[FA_FLAG_WORDS];  // chunks with a visible key for some valid query
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + QBYTES;
@@ -89,32 +99,32 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     uint64_t* kv_full = bars;       // [2] TMA bytes of K and V of a chunk
     uint64_t* kv_empty = bars + 2;  // [2] the PV product of the chunk has read V (and S read K)
     uint64_t* s_full = bars + 4;    // [2] scores of a chunk in TMEM
-    uint64_t* s_empty = bars + 6;   // [2] softmax warps have read them (4 arrivals)
-    uint64_t* p_full = bars + 8;    // P in shared memory, output rescaled (4 arrivals)
+    uint64_t* s_empty = bars + 6;   // [2] softmax warps have read them (8 arrivals)
+    uint64_t* p_full = bars + 8;    // P in shared memory, output rescaled (8 arrivals)
     uint64_t* pv_done = bars + 9;   // O += P V completed
-    uint64_t* q_ready = bars + 10;  // fp16 Q in shared memory (4 arrivals)
+    uint64_t* q_ready = bars + 10;  // fp16 Q in shared memory (8 arrivals)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q0 = blockIdx.x * FA_BM, head = blockIdx.y, seq = blockIdx.z;
     const int kvh = head / (a.ne02 / a.ne12);
-    const int nch = a.nchunks;
 
     if (tid == 0) {
         for (int i = 0; i < 2; i++) {
             mbar_init(&kv_full[i], 1);
             mbar_init(&kv_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 4);
+            mbar_init(&s_empty[i], FA_SOFTMAX_WARPS);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, FA_SOFTMAX_WARPS);
         mbar_init(pv_done, 1);
-        mbar_init(q_ready, 4);
+        mbar_init(q_ready, FA_SOFTMAX_WARPS);
         *abort_flag = 0;
+        for (int w = 0; w < FA_FLAG_WORDS; w++) chunk_vis[w] = 0u;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == FA_MMA_WARP) {
         tmem_alloc(tmem_slot, FA_TMEM_COLS);
         tmem_relinquish();
     }
@@ -125,7 +135,67 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     pdl_launch_dependents();
     pdl_wait();  // Q, K, V and the mask may come from the previous kernel
 
-    if (warp == 4) {
+    // softmax thread: row r (TMEM lane) and key half h (columns 64 h .. 64 h + 63 of a chunk)
+    const int r = 32 * (warp & 3) + lane, h = (warp >> 2) & 1, q = q0 + r;
+    const bool qvalid = q < a.ne01;
+    const uint16_t* mrow = nullptr;
+    if (warp < FA_SOFTMAX_WARPS && a.mask && q < a.ne31)
+        mrow = reinterpret_cast<const uint16_t*>(a.mask + (size_t)(seq % a.ne33) * a.nb33 + (size_t)q * a.nb31);
+    // ---- the tile's key range: the chunks where some valid query sees some key (mask not -inf);
+    // fully masked chunks before and after are skipped, as the reference skips them
+    // (fattn.rs:258-262).  Every thread tests its row's half of every chunk with independent loads
+    // into register bits, then ORs them into shared flags ----
+    const int nall = a.nchunks;
+    const bool cut = a.mask != nullptr && nall <= 32 * FA_FLAG_WORDS;
+    if (warp < FA_SOFTMAX_WARPS && cut && qvalid) {
+        uint32_t bits[FA_FLAG_WORDS];
+#pragma unroll
+        for (int w = 0; w < FA_FLAG_WORDS; w++) bits[w] = 0u;
+        const bool vec = mrow && ((reinterpret_cast<uintptr_t>(a.mask) | (uintptr_t)a.nb31 | (uintptr_t)a.nb33) & 15) == 0;
+        for (int j = 0; j < nall; j++) {
+            const int k0 = j * FA_BN + 64 * h;
+            bool any = false;
+            if (!mrow) {
+                any = k0 < a.ne11;  // no mask row for this query: every key counts
+            } else if (vec) {
+                uint4 w[8];
+#pragma unroll
+                for (int t = 0; t < 8; t++)
+                    w[t] = k0 + 8 * t < a.ne11 ? __ldg(reinterpret_cast<const uint4*>(mrow + k0 + 8 * t)) : make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    const uint32_t x[4] = {w[t].x, w[t].y, w[t].z, w[t].w};
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const uint32_t hv = (x[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+                        any = any || (k0 + 8 * t + e < a.ne11 && hv != 0xfc00u);
+                    }
+                }
+            } else {
+#pragma unroll 8
+                for (int c = 0; c < 64; c++) any = any || (k0 + c < a.ne11 && mrow[k0 + c] != 0xfc00u);
+            }
+            if (any) bits[j >> 5] |= 1u << (j & 31);
+        }
+#pragma unroll
+        for (int w = 0; w < FA_FLAG_WORDS; w++)
+            if (bits[w]) atomicOr(&chunk_vis[w], bits[w]);
+    }
+    __syncthreads();
+    int jb = 0, je = nall;  // chunks [jb, je)
+    if (cut) {
+        jb = nall;
+        je = 0;
+        for (int j = 0; j < nall; j++)
+            if (chunk_vis[j >> 5] >> (j & 31) & 1u) {
+                jb = min(jb, j);
+                je = j + 1;
+            }
+        if (je <= jb) jb = je = 0;
+    }
+    const int nch = je - jb;
+
+    if (warp == FA_TMA_WARP) {
         // ================= K / V chunks by TMA =================
         if (lane == 0) {
             prefetch_tmap(&tk);
@@ -140,15 +210,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 mbar_arrive_expect_tx(&kv_full[st], 2 * KVBYTES);
 #pragma unroll
                 for (int b = 0; b < DB; b++) {
-                    tma_load_4d(sK + st * KVBYTES + b * BLK_KV, &tk, 64 * b, j * FA_BN, kvh, seq, &kv_full[st]);
-                    tma_load_4d(sV + st * KVBYTES + b * BLK_KV, &tv, 64 * b, j * FA_BN, kvh, seq, &kv_full[st]);
+                    tma_load_4d(sK + st * KVBYTES + b * BLK_KV, &tk, 64 * b, (jb + j) * FA_BN, kvh, seq, &kv_full[st]);
+                    tma_load_4d(sV + st * KVBYTES + b * BLK_KV, &tv, 64 * b, (jb + j) * FA_BN, kvh, seq, &kv_full[st]);
                 }
             }
         }
         __syncwarp();
-    } else if (warp == 5) {
+    } else if (warp == FA_MMA_WARP) {
         // ================= MMA issue =================
-        if (lane == 0) {
+        if (lane == 0 && nch > 0) {
             const uint32_t id_s = idesc_f16(FA_BM, FA_BN, 0);
             const uint32_t id_o = idesc_f16(FA_BM, D, 0) | (1u << 16);  // B (V) MN-major
             bool ok = mbar_wait(q_ready, 0, abort_flag);
@@ -191,46 +261,61 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         }
         __syncwarp();
     } else {
-        // ================= softmax warps: thread = query row =================
-        const int r = tid, q = q0 + r;
-        const bool qvalid = q < a.ne01;
+        // ================= softmax warps: (row, key half) per thread =================
         {
             const float* qrow = reinterpret_cast<const float*>(a.q + (size_t)seq * a.nb03 + (size_t)head * a.nb02 +
                                                                (size_t)(qvalid ? q : 0) * a.nb01);
 #pragma unroll
-            for (int b = 0; b < DB; b++)
+            for (int gi = 0; gi < DH / 8; gi++) {
+                const int g = h * (DH / 8) + gi, b = g / 8, c = g % 8;  // 8-dim group of this half
+                float f[8];
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    float f[8];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) f[e] = qvalid ? qrow[64 * b + 8 * c + e] * a.scale : 0.0f;
-                    st_chunk16(sQ + b * BLK_Q, r, c, pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
-                               pack_h2(f[6], f[7]));
-                }
+                for (int e = 0; e < 8; e++) f[e] = qvalid ? qrow[8 * g + e] * a.scale : 0.0f;
+                st_chunk16(sQ + b * BLK_Q, r, c, pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                           pack_h2(f[6], f[7]));
+            }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(q_ready);
 
-        const uint16_t* mrow = nullptr;
-        if (a.mask && q < a.ne31)
-            mrow = reinterpret_cast<const uint16_t*>(a.mask + (size_t)(seq % a.ne33) * a.nb33 + (size_t)q * a.nb31);
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        const bool mvec = mrow && ((reinterpret_cast<uintptr_t>(a.mask) | (uintptr_t)a.nb31 | (uintptr_t)a.nb33) & 15) == 0;
+        const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
         float m = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int j = 0; j < nch; j++) {
-            const int st = j & 1, key0 = j * FA_BN;
+            const int st = j & 1, key0 = (jb + j) * FA_BN + 64 * h;
+            // this half's 64 mask values, loaded before waiting on the scores
+            float mk[64];
+            if (mvec) {
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    uint4 w = make_uint4(0, 0, 0, 0);
+                    if (key0 + 8 * t < a.ne11) w = __ldg(reinterpret_cast<const uint4*>(mrow + key0 + 8 * t));
+                    const __half2* hp = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float2 f = __half22float2(hp[e]);
+                        mk[8 * t + 2 * e] = f.x;
+                        mk[8 * t + 2 * e + 1] = f.y;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++)
+                    mk[c] = (mrow && key0 + c < a.ne11) ? __half2float(__ushort_as_half(mrow[key0 + c])) : 0.0f;
+            }
             // tcgen05.ld / st are warp-collective: every decision before them is warp-uniform
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (uint32_t)(j >> 1) & 1, abort_flag))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sv[FA_BN];
+            float sv[64];
 #pragma unroll
-            for (int g = 0; g < FA_BN / 32; g++) {
+            for (int g = 0; g < 2; g++) {
                 uint32_t v[32];
-                tmem_ld32(trow + st * FA_BN + 32 * g, v);
+                tmem_ld32(trow + st * FA_BN + 64 * h + 32 * g, v);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; i++) sv[32 * g + i] = __uint_as_float(v[i]);
@@ -238,31 +323,28 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[st]);
-            // mask and keys past the end
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < FA_BN; c++) {
-                const int key = key0 + c;
-                float s = sv[c];
-                if (key >= a.ne11)
-                    s = -INFINITY;
-                else if (mrow)
-                    s += __half2float(__ushort_as_half(mrow[key]));
+            for (int c = 0; c < 64; c++) {
+                const float s = key0 + c < a.ne11 ? sv[c] + mk[c] : -INFINITY;
                 sv[c] = s;
                 mx = fmaxf(mx, s);
             }
-            const float m_new = fmaxf(m, mx);
+            // the row max over both key halves
+            xmax[st][h][r] = mx;
+            named_bar_sync(1, 32 * FA_SOFTMAX_WARPS);
+            const float m_new = fmaxf(m, fmaxf(mx, xmax[st][h ^ 1][r]));
             const bool none = m_new == -INFINITY;  // every key so far masked
-            const float alpha = none ? 1.0f : expf(m - m_new);
-            uint32_t ph[FA_BN / 2];
+            const float alpha = none ? 1.0f : __expf(m - m_new);
+            uint32_t ph[32];
             float psum = 0.0f;
 #pragma unroll
-            for (int c = 0; c < FA_BN; c += 2) {
-                const float p0 = none ? 0.0f : expf(sv[c] - m_new), p1 = none ? 0.0f : expf(sv[c + 1] - m_new);
-                const __half2 h = __floats2half2_rn(p0, p1);
-                const float2 hf = __half22float2(h);
+            for (int c = 0; c < 64; c += 2) {
+                const float p0 = none ? 0.0f : __expf(sv[c] - m_new), p1 = none ? 0.0f : __expf(sv[c + 1] - m_new);
+                const __half2 hh = __floats2half2_rn(p0, p1);
+                const float2 hf = __half22float2(hh);
                 psum += hf.x + hf.y;  // the normaliser sums the fp16 weights the PV product uses
-                ph[c / 2] = *reinterpret_cast<const uint32_t*>(&h);
+                ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
             }
             l = l * alpha + psum;
             // the previous PV product must be done before O is rescaled and P is overwritten
@@ -274,23 +356,20 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-                    for (int g = 0; g < D / 32; g++) {
+                    for (int g = 0; g < DH / 32; g++) {
                         uint32_t v[32];
-                        tmem_ld32(trow + 256 + 32 * g, v);
+                        tmem_ld32(trow + 256 + DH * h + 32 * g, v);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-                        tmem_st32(trow + 256 + 32 * g, v);
+                        tmem_st32(trow + 256 + DH * h + 32 * g, v);
                     }
                     tmem_st_wait();
                 }
             }
 #pragma unroll
-            for (int kb = 0; kb < FA_BN / 64; kb++)
-#pragma unroll
-                for (int c = 0; c < 8; c++)
-                    st_chunk16(sP + kb * BLK_Q, r, c, ph[32 * kb + 4 * c], ph[32 * kb + 4 * c + 1], ph[32 * kb + 4 * c + 2],
-                               ph[32 * kb + 4 * c + 3]);
+            for (int c = 0; c < 8; c++)
+                st_chunk16(sP + h * BLK_Q, r, c, ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
@@ -299,6 +378,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         }
         if (ok && nch > 0) ok = mbar_wait(pv_done, (uint32_t)(nch - 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
+        xsum[h][r] = l;
+        named_bar_sync(1, 32 * FA_SOFTMAX_WARPS);
         tc_fence_after();
         if (!ok) {
             if (lane == 0) {
@@ -307,13 +388,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
         } else {
             // every lane loads its TMEM row (collective); rows past the queries store nothing
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            float* out = a.dst + (((size_t)seq * a.ne01 + (qvalid ? q : 0)) * a.ne02 + head) * D;
+            const float lt = l + xsum[h ^ 1][r];
+            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+            float* out = a.dst + (((size_t)seq * a.ne01 + (qvalid ? q : 0)) * a.ne02 + head) * D + DH * h;
 #pragma unroll
-            for (int g = 0; g < D / 32; g++) {
+            for (int g = 0; g < DH / 32; g++) {
                 uint32_t v[32];
-                tmem_ld32(trow + 256 + 32 * g, v);
-                tmem_ld_wait();
+                if (nch > 0) {
+                    tmem_ld32(trow + 256 + DH * h + 32 * g, v);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = 0u;
+                }
                 if (qvalid) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
@@ -326,7 +413,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == FA_MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, FA_TMEM_COLS);
     }
