@@ -10,7 +10,7 @@
 // reference (mod.rs:27-54): D = 64 or 128, no sinks, max_bias 0, no softcap, GQA; plus 16-byte
 // aligned K/V rows (TMA).
 //
-// One CTA of 320 threads per (128-query tile, head, sequence):
+// One CTA of 352 threads per (128-query tile, head, sequence):
 //   * warps 0-7 run the softmax, two warps per TMEM lane quadrant: thread (row, half) owns one
 //     query row (TMEM lane) and 64 of the 128 key columns of a chunk.  They convert Q (x scale) to
 //     fp16 in the 128-byte swizzled K-major layout, then per chunk read their score columns from
@@ -20,8 +20,9 @@
 //     A operand of the PV product; at the end O / (l_0 + l_1) goes to dst;
 //   * before the loop the tile's key range is cut to the chunks where some valid query sees some
 //     key (mask not -inf), so a causal prompt skips the chunks above the diagonal;
-//   * warp 9 streams K and V chunks with TMA (two stages, 128 keys x 64 dims per box, keys past the
-//     end read as zero);
+//   * warps 9 and 10 stream K and V chunks with TMA (two stages each, 128 keys x 64 dims per box,
+//     keys past the end read as zero); a K stage is free once its S product is done, so K loads run
+//     ahead of the PV products;
 //   * one thread of warp 8 issues S = Q K^T (M 128, N 128, K = D) into one of two TMEM score
 //     buffers and O += P V (M 128, N = D, K 128; V is the MN-major B operand) into the TMEM output.
 // TMEM: scores at columns 0 and 128, output at 256.  Every wait is bounded (error word + abort).
@@ -47,9 +48,9 @@ using namespace sm100;
 
 constexpr int FA_BM = 128;       // queries per CTA (TMEM lanes)
 constexpr int FA_BN = 128;       // keys per chunk
-constexpr int FA_SOFTMAX_WARPS = 8, FA_MMA_WARP = 8, FA_TMA_WARP = 9;
+constexpr int FA_SOFTMAX_WARPS = 8, FA_MMA_WARP = 8, FA_TMA_WARP = 9, FA_TMA_V_WARP = 10;
 constexpr int FA_FLAG_WORDS = 8;  // chunk-visibility bits: key ranges up to 256 chunks are cut
-constexpr int FA_THREADS = 320;  // warps 0-7 softmax (two per TMEM sub-partition), 8 MMA, 9 TMA
+constexpr int FA_THREADS = 352;  // warps 0-7 softmax (two per TMEM sub-partition), 8 MMA, 9-10 TMA
 constexpr uint32_t FA_TMEM_COLS = 512;
 
 struct FaArgs {
@@ -96,14 +97,16 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     uint8_t* sV = sK + 2 * KVBYTES;
     uint8_t* sP = sV + 2 * KVBYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sP + FA_BM * FA_BN * 2);
-    uint64_t* kv_full = bars;       // [2] TMA bytes of K and V of a chunk
-    uint64_t* kv_empty = bars + 2;  // [2] the PV product of the chunk has read V (and S read K)
+    uint64_t* k_full = bars;        // [2] TMA bytes of K of a chunk
+    uint64_t* k_empty = bars + 2;   // [2] the S product of the chunk has read K
     uint64_t* s_full = bars + 4;    // [2] scores of a chunk in TMEM
     uint64_t* s_empty = bars + 6;   // [2] softmax warps have read them (8 arrivals)
     uint64_t* p_full = bars + 8;    // P in shared memory, output rescaled (8 arrivals)
     uint64_t* pv_done = bars + 9;   // O += P V completed
     uint64_t* q_ready = bars + 10;  // fp16 Q in shared memory (8 arrivals)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    uint64_t* v_full = bars + 11;   // [2] TMA bytes of V of a chunk
+    uint64_t* v_empty = bars + 13;  // [2] the PV product of the chunk has read V
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -112,8 +115,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 
     if (tid == 0) {
         for (int i = 0; i < 2; i++) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_empty[i], FA_SOFTMAX_WARPS);
         }
@@ -195,24 +200,26 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
     const int nch = je - jb;
 
-    if (warp == FA_TMA_WARP) {
-        // ================= K / V chunks by TMA =================
+    if (warp == FA_TMA_WARP || warp == FA_TMA_V_WARP) {
+        // ================= K (warp 9) and V (warp 10) chunks by TMA, each ring on its own =================
         if (lane == 0) {
-            prefetch_tmap(&tk);
-            prefetch_tmap(&tv);
+            const bool isk = warp == FA_TMA_WARP;
+            const CUtensorMap* map = isk ? &tk : &tv;
+            uint8_t* ring = isk ? sK : sV;
+            uint64_t* full = isk ? k_full : v_full;
+            uint64_t* empty = isk ? k_empty : v_empty;
+            prefetch_tmap(map);
             for (int j = 0; j < nch; j++) {
                 const int st = j & 1;
-                if (!mbar_wait(&kv_empty[st], ((uint32_t)(j >> 1) & 1) ^ 1, abort_flag)) {
+                if (!mbar_wait(&empty[st], ((uint32_t)(j >> 1) & 1) ^ 1, abort_flag)) {
                     cfi_set_error(a.err, 0xfa100 + st);
                     *abort_flag = 1;
                     break;
                 }
-                mbar_arrive_expect_tx(&kv_full[st], 2 * KVBYTES);
+                mbar_arrive_expect_tx(&full[st], KVBYTES);
 #pragma unroll
-                for (int b = 0; b < DB; b++) {
-                    tma_load_4d(sK + st * KVBYTES + b * BLK_KV, &tk, 64 * b, (jb + j) * FA_BN, kvh, seq, &kv_full[st]);
-                    tma_load_4d(sV + st * KVBYTES + b * BLK_KV, &tv, 64 * b, (jb + j) * FA_BN, kvh, seq, &kv_full[st]);
-                }
+                for (int b = 0; b < DB; b++)
+                    tma_load_4d(ring + st * KVBYTES + b * BLK_KV, map, 64 * b, (jb + j) * FA_BN, kvh, seq, &full[st]);
             }
         }
         __syncwarp();
@@ -225,7 +232,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             for (int j = 0; ok && j <= nch; j++) {
                 if (j < nch) {
                     const int st = j & 1;
-                    ok = mbar_wait(&kv_full[st], (uint32_t)(j >> 1) & 1, abort_flag);
+                    ok = mbar_wait(&k_full[st], (uint32_t)(j >> 1) & 1, abort_flag);
                     if (ok && j >= 2) ok = mbar_wait(&s_empty[st], (uint32_t)((j >> 1) - 1) & 1, abort_flag);
                     if (!ok) break;
                     tc_fence_after();
@@ -237,10 +244,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                                 kk > 0 ? 1u : 0u);
                     }
                     mma_commit(&s_full[st]);
+                    mma_commit(&k_empty[st]);
                 }
                 if (j >= 1) {
                     const int jp = j - 1, st = jp & 1;
                     ok = mbar_wait(p_full, (uint32_t)jp & 1, abort_flag);
+                    if (ok) ok = mbar_wait(&v_full[st], (uint32_t)(jp >> 1) & 1, abort_flag);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t pa = smem_u32(sP), vb = smem_u32(sV + st * KVBYTES);
@@ -251,7 +260,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                                 id_o, (jp > 0 || kk > 0) ? 1u : 0u);
                     }
                     mma_commit(pv_done);
-                    mma_commit(&kv_empty[st]);
+                    mma_commit(&v_empty[st]);
                 }
             }
             if (!ok) {
