@@ -108,7 +108,8 @@ class DecodeModel:
             lay["bq"], lay["bk"], lay["bv"] = lay["bqkv"][:nq], lay["bqkv"][nq:nq + nkv], lay["bqkv"][nq + nkv:]
             lay["kc"][:, :c.prompt] = (tt.randn(c.n_kv_head, c.prompt, c.head_dim, generator=gen, **f32)).half()
             lay["vc"][:, :, :c.prompt] = (tt.randn(c.n_kv_head, c.head_dim, c.prompt, generator=gen, **f32)).half()
-        self.embd = random_q8_0(tt, c.vocab, c.hidden, gen, device)  # tied with lm_head
+        self.embd = random_q8_0(tt, c.vocab, c.hidden, gen, device)
+        self.head = self.embd  # tied lm_head (a GGUF file with output.weight replaces it)
         self.out_norm = 1.0 + 0.1 * tt.randn(c.hidden, generator=gen, **f32)
         # activations and device-side state
         z = lambda n: tt.zeros(n, **f32)
@@ -204,7 +205,7 @@ class DecodeModel:
             self.launches_per_step += 5  # rms_norm x2, rope x2, soft_max
         g.rms_norm(self.x.data_ptr(), self.h.data_ptr(), c.hidden, 1, mul=self.out_norm.data_ptr(), eps=c.eps, stream=s)
         quant(self.h, self.hq, c.hidden)
-        gemv(self.embd, self.hq, self.logits, c.vocab, c.hidden)
+        gemv(self.head, self.hq, self.logits, c.vocab, c.hidden)
         self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
         self.launches_per_step += 1  # the output rms_norm
 
@@ -240,5 +241,84 @@ class DecodeModel:
             resid = P(self.dn)
         self._chk(L.cfi_fused_add_rmsnorm_q8_1(P(self.x), resid, P(self.out_norm), P(self.hq), c.hidden, eps, sv),
                   "add_rmsnorm")
-        gemv(self.embd, self.hq, self.logits, c.vocab, c.hidden)
+        gemv(self.head, self.hq, self.logits, c.vocab, c.hidden)
         self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
+
+
+# ---- GGUF (llama.cpp's qwen2 tensor names; include/cfi_gguf.h reads the file) ----
+GGUF_LAYER = {"attn_norm.weight": "attn_norm", "attn_q.weight": "wq", "attn_q.bias": "bq", "attn_k.weight": "wk",
+              "attn_k.bias": "bk", "attn_v.weight": "wv", "attn_v.bias": "bv", "attn_output.weight": "wo",
+              "ffn_norm.weight": "ffn_norm", "ffn_gate.weight": "wg", "ffn_up.weight": "wu", "ffn_down.weight": "wd"}
+_Q8_0, _F32 = 8, 0
+
+
+def _gguf_shape(name, c):
+    """(ggml type, dims with ne[0] innermost) of a per-layer tensor of config c."""
+    nq, nkv = c.n_head * c.head_dim, c.n_kv_head * c.head_dim
+    mats = {"wq": (c.hidden, nq), "wk": (c.hidden, nkv), "wv": (c.hidden, nkv), "wo": (nq, c.hidden),
+            "wg": (c.hidden, c.ffn), "wu": (c.hidden, c.ffn), "wd": (c.ffn, c.hidden)}
+    vecs = {"bq": nq, "bk": nkv, "bv": nkv, "attn_norm": c.hidden, "ffn_norm": c.hidden}
+    return (_Q8_0, mats[name]) if name in mats else (_F32, (vecs[name],))
+
+
+def save_gguf(model, path):
+    """Writes the model's weights (Q8_0 matrices, f32 norms and biases) as a qwen2 GGUF file."""
+    import gguf as G
+
+    c = model.cfg
+    kv = {"general.architecture": (G.STRING, "qwen2"), "qwen2.block_count": (G.U32, c.layers),
+          "qwen2.embedding_length": (G.U32, c.hidden), "qwen2.feed_forward_length": (G.U32, c.ffn),
+          "qwen2.attention.head_count": (G.U32, c.n_head), "qwen2.attention.head_count_kv": (G.U32, c.n_kv_head),
+          "qwen2.attention.layer_norm_rms_epsilon": (G.F32, c.eps), "qwen2.rope.freq_base": (G.F32, c.theta),
+          "qwen2.context_length": (G.U32, c.n_ctx)}
+    host = lambda t: t.detach().contiguous().cpu().numpy().tobytes()
+    ts = [("token_embd.weight", _Q8_0, (c.hidden, c.vocab), host(model.embd))]
+    for i, lay in enumerate(model.layers):
+        for gname, key in GGUF_LAYER.items():
+            ty, dims = _gguf_shape(key, c)
+            ts.append(("blk.%d.%s" % (i, gname), ty, dims, host(lay[key])))
+    ts.append(("output_norm.weight", _F32, (c.hidden,), host(model.out_norm)))
+    if model.head is not model.embd:
+        ts.append(("output.weight", _Q8_0, (c.hidden, c.vocab), host(model.head)))
+    G.write_gguf(path, kv, ts)
+
+
+def load_gguf(torch, ctx, device, path, fused=False, prompt=None, n_ctx=None, seed=0x5eed):
+    """A DecodeModel with the weights of a qwen2 GGUF file (Q8_0 matrices, f32 norms and biases,
+    as in a Q8_0 model export; other matrix types are refused).  The KV cache of the prompt
+    positions stays seeded random (no prefill is run)."""
+    import gguf as G
+
+    with G.GGUFFile(path) as f:
+        if f.get("general.architecture") != "qwen2":
+            raise G.GGUFError("not a qwen2 model: %r" % f.get("general.architecture"))
+        a = lambda k, default=None: f.get("qwen2." + k, default)
+        _, edims, _ = f.tensor("token_embd.weight")
+        hidden, nh = int(a("embedding_length")), int(a("attention.head_count"))
+        cfg = Config(hidden=hidden, layers=int(a("block_count")), n_head=nh, n_kv_head=int(a("attention.head_count_kv")),
+                     head_dim=hidden // nh, ffn=int(a("feed_forward_length")), vocab=int(edims[1]),
+                     eps=float(a("attention.layer_norm_rms_epsilon")), theta=float(a("rope.freq_base", 1e6)))
+        if prompt is not None:
+            cfg.prompt = prompt
+        if n_ctx is not None:
+            cfg.n_ctx = n_ctx
+        m = DecodeModel(torch, ctx, device, cfg, seed=seed, fused=fused)
+
+        def put(dst, name, ty, dims):
+            gty, gdims, data = f.tensor(name)
+            if gty != ty or tuple(gdims) != tuple(dims):
+                raise G.GGUFError("%s: type %d dims %s, this driver needs type %d dims %s" % (name, gty, gdims, ty, dims))
+            src = torch.from_numpy(data.copy()).to(device)
+            dst.view(torch.uint8).reshape(-1).copy_(src)
+
+        put(m.embd, "token_embd.weight", _Q8_0, (hidden, cfg.vocab))
+        for i, lay in enumerate(m.layers):
+            for gname, key in GGUF_LAYER.items():
+                ty, dims = _gguf_shape(key, cfg)
+                put(lay[key], "blk.%d.%s" % (i, gname), ty, dims)
+        put(m.out_norm, "output_norm.weight", _F32, (hidden,))
+        names = f.tensor_names()
+        if "output.weight" in names:
+            m.head = torch.empty_like(m.embd)
+            put(m.head, "output.weight", _Q8_0, (hidden, cfg.vocab))
+    return m

@@ -368,3 +368,39 @@ def test_fused_step_tracks_the_unfused_step_and_replays():
         assert torch.equal(mf.logits, logits)
     del gr
     ctx.close()
+
+
+def test_gguf_export_and_load_give_the_same_model(tmp_path):
+    """A model written as a qwen2 GGUF file (include/cfi_gguf.h reader) and loaded back steps to
+    bit-identical logits, fused and unfused; a separate output.weight becomes the lm_head."""
+    from decode import load_gguf, save_gguf
+
+    ctx = cfi.Ctx(0)
+    cfg = Config(layers=2, vocab=2048)
+    m0 = DecodeModel(torch, ctx, torch.device("cuda", 0), cfg)
+    path = tmp_path / "qwen2-mini.gguf"
+    save_gguf(m0, path)
+    # another seed: every weight differs until the file's are loaded; the caches are copied over
+    m1 = load_gguf(torch, ctx, torch.device("cuda", 0), path, seed=1234)
+    assert m1.cfg.hidden == cfg.hidden and m1.cfg.layers == 2 and m1.cfg.vocab == 2048
+    assert torch.equal(m1.layers[1]["wqkv"], m0.layers[1]["wqkv"]) and torch.equal(m1.layers[0]["bqkv"], m0.layers[0]["bqkv"])
+    s = torch.cuda.current_stream().cuda_stream
+    for fused in (False, True):
+        m0.fused = m1.fused = fused
+        for l0, l1 in zip(m0.layers, m1.layers):
+            l0["kc"][:, cfg.prompt:] = 0
+            l0["vc"][:, :, cfg.prompt:] = 0
+            l1["kc"].copy_(l0["kc"])
+            l1["vc"].copy_(l0["vc"])
+        for m in (m0, m1):
+            m.reset(token=11)
+            m.step(s)
+        torch.cuda.synchronize()
+        assert torch.equal(m0.logits, m1.logits)
+    # a separate lm_head
+    m0.head = m0.embd.clone()
+    m0.head[:34] = 0  # first block of row 0 zeroed: d = 0
+    save_gguf(m0, tmp_path / "b.gguf")
+    m2 = load_gguf(torch, ctx, torch.device("cuda", 0), tmp_path / "b.gguf")
+    assert m2.head is not m2.embd and torch.equal(m2.head, m0.head)
+    ctx.close()
