@@ -122,6 +122,9 @@ def lib():
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_swiglu_q8_1.argtypes = [vp, vp, i, vp]
+    L.cfi_fused_mmvq_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, i, i, vp, vp, vp, f, vp]
+    L.cfi_fused_mmvq_swiglu_q8_1.argtypes = [vp, vp, vp, i, i, vp, vp]
+    L.cfi_fused_mmvq_qkv_rope_store.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     _lib = L
     return L
 

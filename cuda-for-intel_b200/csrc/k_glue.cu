@@ -9,6 +9,7 @@
 #include "../../include/cfi_glue.h"
 #include "cfi_common.cuh"
 #include "sm100_ptx.cuh"
+#include "decode_epi.cuh"
 
 #include <stdlib.h>
 #include <algorithm>
@@ -162,22 +163,7 @@ __global__ void __launch_bounds__(512) argmax_next(const float* __restrict__ log
     }
 }
 
-// ---- fused decode steps ----
-
-// q8_1 block of 32 values, one value per lane (the reference's lane form: refs.rs:103-147):
-// amax and sum by the xor butterfly 16..1, d = amax / 127, q = roundf(v / d).
-CFI_DEV void q8_1_store_lane(float v, uint8_t* blk, int lane) {
-    float a = fabsf(v), sm = v;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-        sm += __shfl_xor_sync(0xffffffffu, sm, o);
-    }
-    const float d = __fdiv_rn(a, 127.0f);
-    const int8_t q = a == 0.0f ? (int8_t)0 : (int8_t)(int32_t)roundf(__fdiv_rn(v, d));
-    blk[4 + lane] = (uint8_t)q;
-    if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = (uint32_t)f2h_bits(d) | ((uint32_t)f2h_bits(sm) << 16);
-}
+// ---- fused decode steps (block-level bodies in decode_epi.cuh) ----
 
 // Block sum over 256 threads in the order of the native rms_norm (thread-strided partials, warp
 // butterfly, then the 8 warp sums by a second butterfly).
@@ -191,81 +177,23 @@ CFI_DEV float block_sum256(float v, float* red) {
     return warp_sum(t);
 }
 
-// Threads own values c = t, t + blockDim, ...; the sum of squares is formed as the native
-// rms_norm forms it (256 thread-strided fma chains, then the two-level butterfly), so the result
-// is the chain's bit for bit; each warp then quantizes the 32-value blocks it holds.
 __global__ void __launch_bounds__(1024) add_rmsnorm_q81(float* __restrict__ x, const float* __restrict__ y,
                                                         const float* __restrict__ w, uint8_t* __restrict__ out, int n,
                                                         float eps) {
     sm100::pdl_launch_dependents();
     sm100::pdl_wait();
     extern __shared__ float hbuf[];
-    __shared__ float red[32];
-    __shared__ float s_scale;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x;
-    for (int c = tid; c < n; c += nt) {
-        float v = x[c];
-        if (y) {
-            v += y[c];
-            x[c] = v;
-        }
-        hbuf[c] = v;
-    }
-    __syncthreads();
-    if (warp < 8) {
-        float ss = 0.0f;
-        for (int c = tid; c < n; c += 256) ss = __fmaf_rn(hbuf[c], hbuf[c], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const float t = warp_sum(lane < 8 ? red[lane] : 0.0f);
-        if (lane == 0) s_scale = rsqrtf(t / (float)n + eps);
-    }
-    __syncthreads();
-    const float scale = s_scale;
-    for (int c = tid; c < n; c += nt) {
-        float v = scale * hbuf[c];
-        v = v * w[c];
-        q8_1_store_lane(v, out + (size_t)(c / 32) * Q8_1_BYTES, lane);
-    }
+    epi_add_rmsnorm_q81(x, y, w, out, n, eps, hbuf);
 }
 
-// One thread per (head, rotation pair) of q and k, plus the v values.
 __global__ void __launch_bounds__(256) qkv_rope_store(const float* __restrict__ qkv, const float* __restrict__ bias,
                                                       float* __restrict__ q_out, __half* __restrict__ kc,
                                                       __half* __restrict__ vc, const int32_t* __restrict__ pos, int nq,
                                                       int nkv, int head_dim, int n_ctx, float theta_scale) {
     sm100::pdl_launch_dependents();
     sm100::pdl_wait();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    const int half = head_dim / 2, p = pos[0];
-    const int npairs = (nq + nkv) / 2;
-    if (i < npairs) {
-        const int head = i / half, j = i - head * half;
-        const int base = head * head_dim;  // in [q | k]
-        const float x0 = qkv[base + j] + bias[base + j], x1 = qkv[base + j + half] + bias[base + j + half];
-        // rope_neox with freq_scale 1, no extrapolation, attn_factor 1: theta = pos * theta_scale^j
-        const float theta = __fmul_rn((float)p, powf(theta_scale, (float)(2 * j) / 2.0f));
-        float sn, cs;
-        sincosf(theta, &sn, &cs);
-        const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-        const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-        if (base < nq) {
-            q_out[base + j] = y0;
-            q_out[base + j + half] = y1;
-        } else {
-            const int kh = (base - nq) / head_dim;
-            __half* kr = kc + ((size_t)kh * n_ctx + p) * head_dim;
-            kr[j] = __float2half_rn(y0);
-            kr[j + half] = __float2half_rn(y1);
-        }
-    } else if (i < npairs + nkv) {
-        const int e = i - npairs, kh = e / head_dim, dd = e - kh * head_dim;
-        const float v = qkv[nq + nkv + e] + bias[nq + nkv + e];
-        vc[((size_t)kh * head_dim + dd) * n_ctx + p] = __float2half_rn(v);
-    }
+    epi_qkv_rope_store(qkv, bias, q_out, kc, vc, pos, nq, nkv, head_dim, n_ctx, theta_scale,
+                       blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
 
 // Split over positions (flash-decoding): CTA (h, s) of grid (n_head, nsplit) takes the positions
@@ -403,12 +331,7 @@ __global__ void __launch_bounds__(256) attention_q81(const float* __restrict__ q
 __global__ void __launch_bounds__(256) swiglu_q81(const float* __restrict__ gu, uint8_t* __restrict__ out, int n) {
     sm100::pdl_launch_dependents();
     sm100::pdl_wait();
-    const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (b >= n / 32) return;
-    const int i = 32 * b + lane;
-    const float a = gu[i];
-    const float v = a / (1.0f + expf(-a)) * gu[n + i];
-    q8_1_store_lane(v, out + (size_t)b * Q8_1_BYTES, lane);
+    epi_swiglu_q81(gu, out, n, blockIdx.x * 8 + (threadIdx.x >> 5), gridDim.x * 8);
 }
 
 inline dim3 g1(int n) { return dim3((unsigned)((n + 255) / 256)); }

@@ -30,6 +30,8 @@
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
+#include "decode_epi.cuh"
+#include "../../include/cfi_glue.h"
 
 #include <algorithm>
 
@@ -719,14 +721,19 @@ CFI_DEV void q6k_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0
     }
 }
 
+#define MMVQ_STREAM_PARAMS                                                                                           \
+    const void *__restrict__ vx, const void *__restrict__ vy, const int32_t *__restrict__ ids, float *__restrict__ dst,     \
+        uint32_t ncols_x, uint3 nchannels_y, uint32_t stride_row_x, uint32_t stride_col_y, uint32_t stride_col_dst,        \
+        uint3 channel_ratio, uint32_t stride_channel_x, uint32_t stride_channel_y, uint32_t stride_channel_dst,            \
+        uint3 sample_ratio, uint32_t stride_sample_x, uint32_t stride_sample_y, uint32_t stride_sample_dst, uint32_t nrows, \
+        uint32_t chunk_rows, uint32_t nst
+#define MMVQ_STREAM_ARGS                                                                                              \
+    vx, vy, ids, dst, ncols_x, nchannels_y, stride_row_x, stride_col_y, stride_col_dst, channel_ratio, stride_channel_x, \
+        stride_channel_y, stride_channel_dst, sample_ratio, stride_sample_x, stride_sample_y, stride_sample_dst, nrows,  \
+        chunk_rows, nst
+
 template <uint32_t TY, int NCOLS>
-__global__ void __launch_bounds__(NW * 32)
-    cfi_mmvq_stream(const void* __restrict__ vx, const void* __restrict__ vy, const int32_t* __restrict__ ids,
-                    float* __restrict__ dst, uint32_t ncols_x, uint3 nchannels_y, uint32_t stride_row_x,
-                    uint32_t stride_col_y, uint32_t stride_col_dst, uint3 channel_ratio, uint32_t stride_channel_x,
-                    uint32_t stride_channel_y, uint32_t stride_channel_dst, uint3 sample_ratio, uint32_t stride_sample_x,
-                    uint32_t stride_sample_y, uint32_t stride_sample_dst, uint32_t nrows, uint32_t chunk_rows,
-                    uint32_t nst) {
+CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[ST_MAX_STAGES];
     constexpr uint32_t BB = block_bytes<TY>();
@@ -840,6 +847,36 @@ __global__ void __launch_bounds__(NW * 32)
     }
 }
 
+template <uint32_t TY, int NCOLS>
+__global__ void __launch_bounds__(NW * 32) cfi_mmvq_stream(MMVQ_STREAM_PARAMS) {
+    mmvq_stream_body<TY, NCOLS>(MMVQ_STREAM_ARGS);
+}
+
+// Q8_0 GEMV (one column) followed, in its last CTA to finish, by one fused decode step on the
+// output (decode_epi.cuh).  Every CTA counts itself done after its rows are stored (fence, then
+// the device counter); the last one runs the step over the whole output and resets the counter.
+template <int EPI>
+__global__ void __launch_bounds__(NW * 32) cfi_mmvq_epi(MMVQ_STREAM_PARAMS, const DecodeEpi e) {
+    mmvq_stream_body<T_Q8_0, 1>(MMVQ_STREAM_ARGS);
+    __shared__ int last;
+    __syncthreads();
+    __threadfence();
+    if (threadIdx.x == 0) last = atomicAdd(e.counter, 1u) == gridDim.x * gridDim.y * gridDim.z - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    extern __shared__ __align__(128) uint8_t smem[];
+    if (EPI == EPI_ADD_RMSNORM_Q81)
+        epi_add_rmsnorm_q81(e.x, dst, e.w, e.q, e.n, e.eps, reinterpret_cast<float*>(smem));
+    else if (EPI == EPI_SWIGLU_Q81)
+        epi_swiglu_q81(dst, e.q, e.n, threadIdx.x >> 5, NW);
+    else
+        epi_qkv_rope_store(dst, e.bias, e.q_out, e.kc, e.vc, e.pos, e.nq, e.nkv, e.head_dim, e.n_ctx, e.theta_scale,
+                           threadIdx.x, NW * 32);
+    __syncthreads();
+    if (threadIdx.x == 0) *e.counter = 0u;
+}
+
 template <uint32_t TY>
 const void* pick(uint32_t ncols, bool stream) {
     switch (ncols) {
@@ -920,4 +957,87 @@ unsigned int cfi_mmvq_error_take() {
     }
     cudaMemcpyToSymbol(g_mmvq_error, &z, sizeof z);
     return v;
+}
+
+// ---- GEMV + fused decode step (include/cfi_glue.h) ----
+static __device__ unsigned int g_epi_count[4];
+
+namespace {
+template <int EPI>
+int launch_epi(const void* w, const void* xq, float* y, int rows, int k, DecodeEpi e, size_t epi_smem, void* stream) {
+    if (rows <= 0 || k <= 0 || k % 32 || (reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(xq) & 3))
+        return (int)cudaErrorInvalidValue;
+    static unsigned int* counters = nullptr;
+    if (!counters && cudaGetSymbolAddress(reinterpret_cast<void**>(&counters), g_epi_count) != cudaSuccess)
+        return (int)cudaErrorInvalidSymbol;
+    e.counter = counters + EPI;
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t nb = (uint32_t)k / 32, grid = std::max(1u, std::min((uint32_t)rows, 2u * (uint32_t)sms));
+    uint32_t chunk = 0, nst = 0;
+    size_t smem = 0;
+    cfi_mmvq_stream_layout(T_Q8_0, 1, (uint32_t)k, (uint32_t)rows, grid, nb, 32, 48 * 1024, 3, &chunk, &nst, &smem);
+    smem = std::max(smem, epi_smem);
+    static size_t attr_set[4] = {0, 0, 0, 0};
+    if (smem > 48 * 1024 && attr_set[EPI] < smem) {
+        if (cudaFuncSetAttribute(cfi_mmvq_epi<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return (int)cudaErrorInvalidValue;
+        attr_set[EPI] = smem;
+    }
+    const uint3 none = make_uint3(0, 0, 0), fd1 = make_uint3(1, 0, 1);  // fastdiv triple of 1 (ggml's)
+    const char* ep = getenv("CFI_PDL");
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3(grid, 1, 1);
+    c.blockDim = dim3(NW * 32, 1, 1);
+    c.dynamicSmemBytes = smem;
+    c.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    c.attrs = at;
+    c.numAttrs = (ep && strcmp(ep, "0") == 0) ? 0 : 1;
+    const uint32_t r = (uint32_t)rows;
+    return (int)cudaLaunchKernelEx(&c, cfi_mmvq_epi<EPI>, w, xq, (const int32_t*)nullptr, y, (uint32_t)k, none, nb, nb, r,
+                                   fd1, r * nb, nb, r, fd1, r * nb, nb, r, r, chunk, nst, e);
+}
+}  // namespace
+
+extern "C" int cfi_fused_mmvq_add_rmsnorm_q8_1(const void* w, const void* xq, float* y, int rows, int k, float* x,
+                                               const float* norm_w, void* out_q8_1, float eps, void* stream) {
+    if (rows % 32 || rows > 8192) return (int)cudaErrorInvalidValue;
+    DecodeEpi e = {};
+    e.x = x;
+    e.w = norm_w;
+    e.q = static_cast<uint8_t*>(out_q8_1);
+    e.n = rows;
+    e.eps = eps;
+    return launch_epi<EPI_ADD_RMSNORM_Q81>(w, xq, y, rows, k, e, (size_t)rows * 4, stream);
+}
+
+extern "C" int cfi_fused_mmvq_swiglu_q8_1(const void* w, const void* xq, float* y, int rows, int k, void* out_q8_1,
+                                          void* stream) {
+    if (rows % 64) return (int)cudaErrorInvalidValue;
+    DecodeEpi e = {};
+    e.q = static_cast<uint8_t*>(out_q8_1);
+    e.n = rows / 2;
+    return launch_epi<EPI_SWIGLU_Q81>(w, xq, y, rows, k, e, 0, stream);
+}
+
+extern "C" int cfi_fused_mmvq_qkv_rope_store(const void* w, const void* xq, float* y, int k, const float* bias,
+                                             float* q_out, void* kc, void* vc, const int32_t* pos, int nq, int nkv,
+                                             int head_dim, int n_ctx, float theta, void* stream) {
+    if (head_dim <= 0 || head_dim % 2 || nq % head_dim || nkv % head_dim) return (int)cudaErrorInvalidValue;
+    DecodeEpi e = {};
+    e.bias = bias;
+    e.q_out = q_out;
+    e.kc = static_cast<__half*>(kc);
+    e.vc = static_cast<__half*>(vc);
+    e.pos = pos;
+    e.nq = nq;
+    e.nkv = nkv;
+    e.head_dim = head_dim;
+    e.n_ctx = n_ctx;
+    e.theta_scale = powf(theta, -2.0f / (float)head_dim);
+    return launch_epi<EPI_QKV_ROPE_STORE>(w, xq, y, nq + 2 * nkv, k, e, 0, stream);
 }

@@ -74,6 +74,8 @@ class DecodeModel:
         self.cfg = cfg or Config()
         self.dev = device
         self.fused = fused
+        # fused == 2: which GEMVs also carry their element-wise step (the add + rms_norm ones always)
+        self.epi_qkv = self.epi_swiglu = False
         self.g = cfi.GgmlCaller(ctx, "all")
         self.blas = cfi.Blas()
         self.L = cfi.lib()
@@ -210,7 +212,11 @@ class DecodeModel:
         self.launches_per_step += 1  # the output rms_norm
 
     def step_fused(self, stream):
-        """One token step with the stacked weights and the fused glue kernels."""
+        """One token step with the stacked weights and the fused glue kernels.  fused == 2: the
+        element-wise steps after the QKV, O, gate/up and down GEMVs run in those GEMVs' last CTAs
+        (5 launches per layer); fused == 1: as separate launches (9 per layer)."""
+        if self.fused == 2:
+            return self.step_fused_epi(stream)
         c, g, L, s = self.cfg, self.g, self.L, stream
         P = lambda t: C.c_void_p(t.data_ptr())
         sv = C.c_void_p(s)
@@ -242,6 +248,47 @@ class DecodeModel:
         self._chk(L.cfi_fused_add_rmsnorm_q8_1(P(self.x), resid, P(self.out_norm), P(self.hq), c.hidden, eps, sv),
                   "add_rmsnorm")
         gemv(self.head, self.hq, self.logits, c.vocab, c.hidden)
+        self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
+
+    def step_fused_epi(self, stream):
+        c, L = self.cfg, self.L
+        P = lambda t: C.c_void_p(t.data_ptr())
+        sv = C.c_void_p(stream)
+        nq, nkv = c.n_head * c.head_dim, c.n_kv_head * c.head_dim
+        eps, theta, scale = C.c_float(c.eps), C.c_float(c.theta), C.c_float(1.0 / math.sqrt(c.head_dim))
+        self.launches_per_step = 0
+        self._chk(L.cfi_glue_get_rows_q8_0(P(self.embd), P(self.token), P(self.x), c.hidden, sv), "get_rows")
+        self._chk(L.cfi_fused_add_rmsnorm_q8_1(P(self.x), None, P(self.layers[0]["attn_norm"]), P(self.hq), c.hidden, eps,
+                                               sv), "add_rmsnorm")
+        for i, lay in enumerate(self.layers):
+            if self.epi_qkv:
+                self._chk(L.cfi_fused_mmvq_qkv_rope_store(P(lay["wqkv"]), P(self.hq), P(self.qkv), c.hidden,
+                                                          P(lay["bqkv"]), P(self.qr), P(lay["kc"]), P(lay["vc"]),
+                                                          P(self.pos), nq, nkv, c.head_dim, c.n_ctx, theta, sv), "qkv")
+            else:
+                self.g.mmvq(cfi.Q8_0, 1, lay["wqkv"].data_ptr(), self.hq.data_ptr(), self.qkv.data_ptr(), c.hidden,
+                            nq + 2 * nkv, stream=stream)
+                self.launches_per_step += 1
+                self._chk(L.cfi_fused_qkv_rope_store(P(self.qkv), P(lay["bqkv"]), P(self.qr), P(lay["kc"]), P(lay["vc"]),
+                                                     P(self.pos), nq, nkv, c.head_dim, c.n_ctx, theta, sv), "qkv_rope")
+            self._chk(L.cfi_fused_attention_q8_1(P(self.qr), P(lay["kc"]), P(lay["vc"]), P(self.pos), P(self.aq),
+                                                 c.n_head, c.n_kv_head, c.head_dim, c.n_ctx, scale, sv), "attention")
+            self._chk(L.cfi_fused_mmvq_add_rmsnorm_q8_1(P(lay["wo"]), P(self.aq), P(self.o), c.hidden, nq, P(self.x),
+                                                        P(lay["ffn_norm"]), P(self.hq), eps, sv), "o")
+            if self.epi_swiglu:
+                self._chk(L.cfi_fused_mmvq_swiglu_q8_1(P(lay["wgu"]), P(self.hq), P(self.gu2), 2 * c.ffn, c.hidden,
+                                                       P(self.gq), sv), "gate_up")
+            else:
+                self.g.mmvq(cfi.Q8_0, 1, lay["wgu"].data_ptr(), self.hq.data_ptr(), self.gu2.data_ptr(), c.hidden,
+                            2 * c.ffn, stream=stream)
+                self.launches_per_step += 1
+                self._chk(L.cfi_fused_swiglu_q8_1(P(self.gu2), P(self.gq), c.ffn, sv), "swiglu")
+            nxt = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.out_norm
+            self._chk(L.cfi_fused_mmvq_add_rmsnorm_q8_1(P(lay["wd"]), P(self.gq), P(self.dn), c.hidden, c.ffn, P(self.x),
+                                                        P(nxt), P(self.hq), eps, sv), "down")
+        self.g.mmvq(cfi.Q8_0, 1, self.head.data_ptr(), self.hq.data_ptr(), self.logits.data_ptr(), c.hidden, c.vocab,
+                    stream=stream)
+        self.launches_per_step += 1
         self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
 
 
@@ -322,3 +369,4 @@ def load_gguf(torch, ctx, device, path, fused=False, prompt=None, n_ctx=None, se
             m.head = torch.empty_like(m.embd)
             put(m.head, "output.weight", _Q8_0, (hidden, cfg.vocab))
     return m
+

@@ -64,6 +64,23 @@ CFI_API int cfi_fused_attention_q8_1(const float *q, const void *kc, const void 
 /* q8_1 blocks of silu(gu[i]) * gu[n + i], i < n: equal to cfi_glue_swiglu then quantize_q8_1. */
 CFI_API int cfi_fused_swiglu_q8_1(const float *gu, void *out_q8_1, int n, void *stream);
 
+/*
+ * GEMV + fused step in one launch: y = W xq (W: rows x k Q8_0, row-major; xq: q8_1 blocks of one
+ * column) through the streaming GEMV, whose last CTA to finish then runs the step on y.  Results
+ * equal the GEMV followed by the standalone step, bit for bit.  A device counter per step kind
+ * is shared: one call of a kind at a time per device.
+ */
+/* ... then cfi_fused_add_rmsnorm_q8_1(x, y, norm_w, out, rows, eps); rows <= 8192 */
+CFI_API int cfi_fused_mmvq_add_rmsnorm_q8_1(const void *w, const void *xq, float *y, int rows, int k, float *x,
+                                            const float *norm_w, void *out_q8_1, float eps, void *stream);
+/* ... then cfi_fused_swiglu_q8_1(y, out, rows / 2) */
+CFI_API int cfi_fused_mmvq_swiglu_q8_1(const void *w, const void *xq, float *y, int rows, int k, void *out_q8_1,
+                                       void *stream);
+/* ... then cfi_fused_qkv_rope_store(y, ...) (rows = nq + 2 nkv) */
+CFI_API int cfi_fused_mmvq_qkv_rope_store(const void *w, const void *xq, float *y, int k, const float *bias,
+                                          float *q_out, void *kc, void *vc, const int32_t *pos, int nq, int nkv,
+                                          int head_dim, int n_ctx, float theta, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

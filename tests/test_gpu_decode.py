@@ -404,3 +404,42 @@ def test_gguf_export_and_load_give_the_same_model(tmp_path):
     m2 = load_gguf(torch, ctx, torch.device("cuda", 0), tmp_path / "b.gguf")
     assert m2.head is not m2.embd and torch.equal(m2.head, m0.head)
     ctx.close()
+
+
+def test_gemv_epilogue_step_equals_the_fused_step():
+    """fused=2 (add + rms_norm + quantize in the O and down GEMVs' last CTAs, 7 launches per layer;
+    with the QKV and gate/up steps too, 5) gives the same bits as fused=1 (separate launches), over
+    three graph-replayed tokens."""
+    ctx = cfi.Ctx(0)
+    cfg = Config(layers=2, vocab=2048)
+    ms = [DecodeModel(torch, ctx, torch.device("cuda", 0), cfg, fused=f) for f in (1, 2, 2)]
+    ms[2].epi_qkv = ms[2].epi_swiglu = True
+    out = []
+    for m in ms:
+        for lay in m.layers:
+            lay["kc"][:, cfg.prompt:] = 0
+            lay["vc"][:, :, cfg.prompt:] = 0
+        m.reset(token=9)
+        m.step(torch.cuda.current_stream().cuda_stream)  # first-use probes, eager
+        for lay in m.layers:
+            lay["kc"][:, cfg.prompt:] = 0
+            lay["vc"][:, :, cfg.prompt:] = 0
+        m.reset(token=9)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            m.step(torch.cuda.current_stream().cuda_stream)
+        m.reset(token=9)
+        toks = []
+        for _ in range(3):
+            gr.replay()
+            torch.cuda.synchronize()
+            toks.append((int(m.token.item()), m.logits.clone()))
+        out.append(toks)
+        del gr
+    assert cfi.lib().cfi_device_error() == 0
+    assert ms[1].launches_per_step == 1 + 1 + 7 * cfg.layers + 2
+    assert ms[2].launches_per_step == 1 + 1 + 5 * cfg.layers + 2
+    for k in (1, 2):
+        for (t1, l1), (t2, l2) in zip(out[0], out[k]):
+            assert t1 == t2 and torch.equal(l1, l2)
+    ctx.close()
