@@ -609,8 +609,12 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         const uint32_t nrows = plan.ncols == 1 ? grid[0] : std::min(2 * grid[0], stride_col_dst);
         const uint32_t planes = std::max(1u, grid[1] * grid[2]);
         // CFI_MMVQ_STREAM=0 selects the row kernel for ncols <= 2 too
+        // CFI_MMVQ_STREAM_MIN_KB: weight matrices smaller than this take the row kernel
+        const uint64_t wkb = (uint64_t)nrows * (uint64_t)vals[6] * (plan.ty == 12 ? 144 : plan.ty == 14 ? 210 :
+                                                                     plan.ty == 2 ? 18 : 34) / 1024;
         const bool stream = cfi_mmvq_streams(plan.ncols) &&
-                            (cfi_mmvq_stream_only(plan.ty) || env_u32("CFI_MMVQ_STREAM", 1, 0, 1) != 0);
+                            (cfi_mmvq_stream_only(plan.ty) ||
+                             (env_u32("CFI_MMVQ_STREAM", 1, 0, 1) != 0 && wkb >= env_u32("CFI_MMVQ_STREAM_MIN_KB", 0, 0, 1u << 30)));
         nl.fn = cfi_native_mmvq(plan.ty, plan.ncols, stream);
         uint32_t chunk = 0, nstages = 0;
         if (stream) {

@@ -74,6 +74,7 @@ class DecodeModel:
         self.cfg = cfg or Config()
         self.dev = device
         self.fused = fused
+        self.row_gemv_below_kb = 16384
         # fused == 2: which GEMVs also carry their element-wise step (the add + rms_norm ones always)
         self.epi_qkv = self.epi_swiglu = False
         self.g = cfi.GgmlCaller(ctx, "all")
@@ -141,7 +142,24 @@ class DecodeModel:
         self.launches_per_step += 1
 
     def step(self, stream):
-        """Enqueue one token step on `stream` (a cudaStream_t)."""
+        """Enqueue one token step on `stream` (a cudaStream_t).  GEMVs over weight matrices under
+        `row_gemv_below_kb` (default 16 MB) take the substitution layer's row kernel
+        (CFI_MMVQ_STREAM_MIN_KB, set for the duration of the call unless the environment sets it):
+        between the short kernels of a decode step it measured faster than the streaming kernel,
+        which still serves the lm_head."""
+        import os
+
+        key = "CFI_MMVQ_STREAM_MIN_KB"
+        prev = os.environ.get(key)
+        if prev is None and self.row_gemv_below_kb:
+            os.environ[key] = str(int(self.row_gemv_below_kb))
+        try:
+            return self._step(stream)
+        finally:
+            if prev is None and self.row_gemv_below_kb:
+                del os.environ[key]
+
+    def _step(self, stream):
         if self.fused:
             return self.step_fused(stream)
         c, g, L, s = self.cfg, self.g, self.L, stream
