@@ -4,6 +4,7 @@ cuda-for-intel src/subst/tests.rs:165-221, 363-399, 599-636 and src/cuda/streams
 import ctypes as C
 import os
 
+import numpy as np
 import pytest
 
 import cfi_b200 as cfi
@@ -269,3 +270,48 @@ def test_decide_reads_the_environment(monkeypatch):
     monkeypatch.setenv("CFI_SUBST_NWARPS", "8")
     L.cfi_subst_decide(mmvq_name(8, 2).encode(), lay, 17, None, C.byref(plan), None, 0)
     assert plan.nwarps == 8 and plan.key == b"mmvq:t8:c2:w8"
+
+
+def fattn_vals(d=64, nq=631, nh=14, nhk=2, nkv=640, sinks=0, max_bias=0.0, softcap=0.0, k_ptr=0x10000, mask=0x30000):
+    """The 37 words of a flash_attn_ext_f16 launch on contiguous layouts (probe.rs:490-528)."""
+    f = lambda x: int(np.float32(x).view(np.uint32))
+    return [0x1000, k_ptr, 0x20000, mask, sinks, 0, 0x40000, 0x50000, f(1 / 8), f(max_bias), f(1.0), f(1.0), 0, f(softcap),
+            d, nq, nh, 1, d * 4, d * 4 * nq, d * 4 * nq * nh, d, nkv, nhk, 1, d * 2, d * 2 * nkv, d * 2 * nkv * nhk,
+            d * 2, d * 2 * nkv, d * 2 * nkv * nhk, nkv, 640, 1, nkv * 2, nkv * 2 * 640, nkv * 2 * 640]
+
+
+def test_fattn_decisions_and_geometry():
+    """flash_attn_ext_f16<D, D, ..., false, false> with D 64 / 128 is substituted (mod.rs:420-425);
+    other head sizes, softcap or MLA are not; the native geometry tiles 128 queries and refuses
+    sinks, ALiBi, softcap, fewer than 16 queries and K/V rows TMA cannot address."""
+    for d in (64, 128):
+        code, p, _ = cfi.decide(cfi.NAMES["fattn"].format(d=d), "fattn", "all")
+        assert code == cfi.SUBSTITUTE and p.key == ("fattn:d%d" % d).encode()
+        assert cfi.map_launch(p, (20, 14, 1), (32, 4, 1), fattn_vals(d)) == ((5, 14, 1), (352, 1, 1))
+    name96 = cfi.NAMES["fattn"].format(d=96)
+    assert cfi.decide(name96, "fattn", "all")[0] == cfi.NOT_APPLICABLE
+    soft = cfi.NAMES["fattn"].format(d=64).replace("ELb0ELb0EE", "ELb1ELb0EE")
+    assert cfi.decide(soft, "fattn", "all")[0] == cfi.NOT_APPLICABLE
+    assert cfi.decide(cfi.NAMES["fattn_fixup"].format(d=64), "fattn_fixup", "all")[0] == cfi.SUBSTITUTE
+    _, p, _ = cfi.decide(cfi.NAMES["fattn"].format(d=64), "fattn", "all")
+    for bad in (dict(sinks=0x60000), dict(max_bias=8.0), dict(softcap=30.0), dict(nq=8), dict(k_ptr=0x10008),
+                dict(nh=14, nhk=4), dict(mask=0x30001)):
+        assert cfi.map_launch(p, (20, 14, 1), (32, 4, 1), fattn_vals(**bad)) is None, bad
+    assert cfi.map_launch(p, (20, 14, 1), (32, 4, 1), fattn_vals(mask=0)) is not None  # no mask
+
+
+def test_fattn_fixup_is_skipped_only_after_a_native_fattn():
+    """ggml launches flash_attn_stream_k_fixup after a stream-k FlashAttention; the native kernel
+    writes final results, so the fixup that follows it (same dst and meta buffers) is a no-op."""
+    ctx, g = fake_caller()
+    g.fattn_fixup(64, 0x40000, 0x50000, 631, 14, 1, 640)  # nothing native before: stock
+    assert ctx.stats()["stock_launches"] == 1 and ctx.stats()["fixups_skipped"] == 0
+    g.fattn(64, 0x1000, 0x10000, 0x20000, 0x30000, 0x40000, 631, 14, 2, 640, 1, 0.125, dst_meta=0x50000)
+    assert ctx.stats()["native_launches"] == 1
+    g.fattn_fixup(64, 0x70000, 0x50000, 631, 14, 1, 640)  # another destination: runs
+    assert ctx.stats()["stock_launches"] == 2 and ctx.stats()["fixups_skipped"] == 0
+    g.fattn(64, 0x1000, 0x10000, 0x20000, 0x30000, 0x40000, 631, 14, 2, 640, 1, 0.125, dst_meta=0x50000)
+    g.fattn_fixup(64, 0x40000, 0x50000, 631, 14, 1, 640)
+    assert ctx.stats()["fixups_skipped"] == 1 and ctx.stats()["stock_launches"] == 2
+    g.fattn_fixup(64, 0x40000, 0x50000, 631, 14, 1, 640)  # only the one right after the native launch
+    assert ctx.stats()["fixups_skipped"] == 1 and ctx.stats()["stock_launches"] == 3
