@@ -108,12 +108,13 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def traffic_per_launch():
-    """dram bytes per mmvq launch from the committed ncu summary, if one exists."""
+def traffic_per_launch(fused=False):
+    """dram bytes per launch of the roofline kernel (the GEMV, or the GEMV that absorbed its
+    quantize_q8_1) from the committed ncu summary, if one exists."""
     p = os.path.join(ROOT, "profiles", "mmvq_q4k_8192x2048_traffic.json")
     try:
         with open(p) as f:
-            return float(json.load(f)["dram_bytes_per_launch_b1"])
+            return float(json.load(f)["dram_bytes_per_launch_b1_fused" if fused else "dram_bytes_per_launch_b1"])
     except Exception:
         return None
 
@@ -212,7 +213,7 @@ def graph_time_us(stream, body, reps=5, calls=1):
     return us
 
 
-def config1_bench(cfi, g, stream, dev, peak):
+def config1_bench(cfi, g, stream, dev, peak, gf=None):
     """Q8_0 mul_mat_vec_q 4864x896 on its own (batch 1), and with its
     quantize_q8_1 in front, back to back over rotated weight copies (> 3x L2)."""
     import torch
@@ -239,7 +240,18 @@ def config1_bench(cfi, g, stream, dev, peak):
     us_pair = graph_time_us(stream, pair, calls=ncopy)
     mbytes = wb + k // 32 * 36 + rows * 4                 # 4,650,992
     qbytes = k * 4 + k // 32 * 36
-    return {"workload": "config1: Q8_0 mul_mat_vec_q 4864x896, batch 1 (weights rotated over %d copies, %.0f MB)"
+    fused = {}
+    if gf is not None:
+        def fpair(i, st):
+            gf.quantize_q8_1(x.data_ptr(), q.data_ptr(), k, k, 1, stream=st)
+            gf.mmvq(cfi.Q8_0, 1, wd[i].data_ptr(), q.data_ptr(), y.data_ptr(), k, rows, stream=st)
+        with torch.cuda.stream(stream):
+            fpair(0, stream.cuda_stream)  # first use outside the capture
+        torch.cuda.synchronize()
+        us_f = graph_time_us(stream, fpair, calls=ncopy)
+        fused = {"fused_quantize_plus_mmvq_us": round(us_f, 3),
+                 "fused_quantize_plus_mmvq_gbs": round((mbytes + qbytes) / us_f / 1e3, 1)}
+    return {**fused, "workload": "config1: Q8_0 mul_mat_vec_q 4864x896, batch 1 (weights rotated over %d copies, %.0f MB)"
                         % (ncopy, ncopy * wb / 1e6),
             "mmvq_us": round(us, 3), "mmvq_gbs": round(mbytes / us / 1e3, 1),
             "mmvq_frac": round(mbytes / us / 1e3 / peak, 4),
@@ -357,25 +369,33 @@ def fattn_bench(cfi, g, stream, dev, peak_tf):
             "shapes": out}
 
 
-def decode_bench(stream, dev, ntok=48, warm=3, fused=False):
+def decode_bench(stream, dev, ntok=48, warm=3, fused=False, defer=False, const_weights=False):
     """Qwen2.5-0.5B-architecture decode (24 layers, Q8_0 random weights, 631-token
     seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens.  fused: the
-    stacked-weight step with the fused glue kernels (9 launches per layer instead of 25)."""
+    stacked-weight step with the fused glue kernels (9 launches per layer instead of 25).  defer:
+    ggml's sequence on a context that holds each quantize_q8_1 back for the GEMV reading it (every
+    GEMV on the streaming kernel, which is the one that absorbs it).  const_weights: the GEMVs copy
+    their weights before waiting on the previous kernel (CFI_CTX_CONST_WEIGHTS)."""
     import torch
 
     import cfi_b200 as cfi
     from decode import DecodeModel
 
-    ctx = cfi.Ctx(dev.index or 0)
+    ctx = cfi.Ctx(dev.index or 0, defer_q8_1=defer, const_weights=const_weights)
     m = DecodeModel(torch, ctx, dev, fused=fused)
+    if defer:
+        m.row_gemv_below_kb = 0
     m.reset(token=1234)
     with torch.cuda.stream(stream):
         m.step(stream.cuda_stream)  # first-use probes outside the capture
     torch.cuda.synchronize()
     m.reset(token=1234)
     gr = torch.cuda.CUDAGraph()
+    before = ctx.stats()["fused_q8_1"]
     with torch.cuda.graph(gr, stream=stream):
         m.step(torch.cuda.current_stream().cuda_stream)
+        ctx.flush()
+    fused_in_capture = ctx.stats()["fused_q8_1"] - before
     m.reset(token=1234)
     with torch.cuda.stream(stream):
         for _ in range(warm):
@@ -396,10 +416,15 @@ def decode_bench(stream, dev, ntok=48, warm=3, fused=False):
                        "KV cache, %d greedy tokens, one CUDA graph per token%s"
                        % (ntok, {0: "; ggml's kernel sequence through the substitution ABI",
                                  1: "; stacked QKV / gate-up weights and fused glue kernels",
-                                 2: "; stacked weights, element-wise steps in the GEMVs' last CTAs"}[int(fused)]),
+                                 2: "; stacked weights, element-wise steps in the GEMVs' last CTAs"}[int(fused)]
+                          + ("; quantize_q8_1 held back into the GEMVs (CFI_CTX_DEFER_Q8_1)" if defer else "")
+                          + ("; weights fetched before the dependent-launch wait (CFI_CTX_CONST_WEIGHTS)"
+                             if const_weights else "")),
            "tok_per_s": round(ntok / (ms * 1e-3), 1), "ms_per_token": round(ms / ntok, 4),
            "launches_per_token": m.launches_per_step, "weight_bytes_per_token": bpt,
            "weights_gbs": round(bpt * ntok / (ms * 1e-3) / 1e9, 1)}
+    if defer:
+        out["launches_per_token"] -= fused_in_capture
     del gr
     ctx.close()
     return out
@@ -454,8 +479,17 @@ def run_gpu(args, rank, world):
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # rank 0's stdout carries only the JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
-    ctx = cfi.Ctx(local)
+    # the step's router holds each quantize_q8_1 back for the GEMV that reads it (one kernel per
+    # pair); --separate-quantize keeps them two launches
+    defer = not args.separate_quantize
+    ctx = cfi.Ctx(local, defer_q8_1=defer, const_weights=True)
     g = cfi.GgmlCaller(ctx, "all")
+    # comparison legs (1 GPU): the same step launched separately, with and without the early
+    # weight copies
+    ctx_sep = cfi.Ctx(local, const_weights=True) if world == 1 else None
+    g_sep = cfi.GgmlCaller(ctx_sep, "all") if ctx_sep else None
+    ctx_plain = cfi.Ctx(local) if world == 1 else None
+    g_plain = cfi.GgmlCaller(ctx_plain, "all") if ctx_plain else None
     stream = torch.cuda.Stream(device=dev)
 
     ncopy = max(8, int(np.ceil(3 * L2_BYTES / W_BYTES / 4.0)) * 4)   # > 3x L2 of weight copies
@@ -482,11 +516,13 @@ def run_gpu(args, rank, world):
     ys_host = torch.zeros(y_all.numel(), dtype=torch.float32).pin_memory()
     comm = torch.cuda.Stream(device=dev) if world > 1 else None
 
-    def step(phase, s, parity=0):
+    def step(phase, s, parity=0, gg=None):
+        gg = gg or g
         for j, b in enumerate(BATCHES):
-            g.quantize_q8_1(xs[b].data_ptr(), qs[b].data_ptr(), K, K, b, stream=s)
+            gg.quantize_q8_1(xs[b].data_ptr(), qs[b].data_ptr(), K, K, b, stream=s)
             wcopy = wd[(phase * len(BATCHES) + j) % ncopy]
-            g.mmvq(cfi.Q4_K, b, wcopy.data_ptr(), qs[b].data_ptr(), y_views_p[parity][b].data_ptr(), K, ROWS, stream=s)
+            gg.mmvq(cfi.Q4_K, b, wcopy.data_ptr(), qs[b].data_ptr(), y_views_p[parity][b].data_ptr(), K, ROWS, stream=s)
+        gg.ctx.flush()
 
     def step_pipelined(phase, parity):
         """Inside a capture: the all-gather of the other output set on the comm stream (one exchange
@@ -512,17 +548,29 @@ def run_gpu(args, rank, world):
             if dist:
                 dist.all_gather_into_tensor(gathered, y_all)
     torch.cuda.synchronize()
-    graphs = {}
-    for ph in range(nphase):
-        for par in (0, 1):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr, stream=stream):
-                step_pipelined(ph, par)
-            graphs[(ph, par)] = gr
-    launches_per_step = 2 * len(BATCHES)
+    # Step i uses weight phase i % nphase and output set i % 2; that pattern repeats every
+    # `period` steps, so one CUDA graph holds a whole period (programmatic dependent launch then
+    # overlaps consecutive steps too, which separate graph launches would not) and a second graph
+    # the first K % period steps, so the timed region runs exactly K steps.
+    period = nphase if nphase % 2 == 0 else 2 * nphase
+
+    def capture(nsteps):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for i in range(nsteps):
+                step_pipelined(i % nphase, i % 2)
+        return gr
+
+    fused_before = ctx.stats()["fused_q8_1"]
+    graph_period = capture(period)
+    # GEMVs that absorbed their quantize, per captured step
+    launches_per_step = 2 * len(BATCHES) - (ctx.stats()["fused_q8_1"] - fused_before) // period
+    fused_step = launches_per_step < 2 * len(BATCHES)
+    rest = args.steps % period
+    graph_rest = capture(rest) if rest else None
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            graphs[(i % nphase, i % 2)].replay()
+        for _ in range((args.warmup + period - 1) // period):
+            graph_period.replay()
     torch.cuda.synchronize()
 
     # ---- timed region: device time, max over ranks ----
@@ -533,8 +581,10 @@ def run_gpu(args, rank, world):
     with Clocks(local) as clk:
         with torch.cuda.stream(stream):
             e0.record(stream)
-            for i in range(args.steps):
-                graphs[(i % nphase, i % 2)].replay()
+            for _ in range(args.steps // period):
+                graph_period.replay()
+            if graph_rest is not None:
+                graph_rest.replay()
             e1.record(stream)
         torch.cuda.synchronize()
     if dist:
@@ -548,13 +598,31 @@ def run_gpu(args, rank, world):
     ms_step = ms / args.steps
     value = world * STEP_BYTES / (ms_step * 1e-3) / 1e9
 
+    legs = {}
+    for leg, gg, note in (("separate_launches", g_sep, "quantize_q8_1 and mul_mat_vec_q launched separately, "
+                           "weights fetched before the wait (CFI_CTX_CONST_WEIGHTS)"),
+                          ("plain_router", g_plain, "separate launches, no context flags (weights fetched "
+                           "after the wait)")):
+        if gg is None:
+            continue
+        with torch.cuda.stream(stream):
+            step(0, stream.cuda_stream, 0, gg)  # first use outside the capture
+        torch.cuda.synchronize()
+        us_l = graph_time_us(stream, lambda i, st: step(i % nphase, st, 0, gg), reps=max(3, args.steps // 10),
+                             calls=nphase)
+        legs[leg] = {"value": round(STEP_BYTES / us_l / 1e3, 2), "ms_per_step": round(us_l * 1e-3, 5),
+                     "launches_per_step": 2 * len(BATCHES), "router": note}
+
     # ---- dominant kernel: mmvq Q4_K batch 1, back to back (one graph of ncopy launches over the
     # rotated weight copies), CUDA events on the launching stream around the replays ----
     gk = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gk, stream=stream):
         for i in range(ncopy):
+            if fused_step:  # the step's kernel: quantize_q8_1 absorbed by the GEMV
+                g.quantize_q8_1(xs[1].data_ptr(), qs[1].data_ptr(), K, K, 1, stream=torch.cuda.current_stream().cuda_stream)
             g.mmvq(cfi.Q4_K, 1, wd[i].data_ptr(), qs[1].data_ptr(), y_views[1].data_ptr(), K, ROWS,
                    stream=torch.cuda.current_stream().cuda_stream)
+        ctx.flush()
     reps = max(3, args.steps // 10)
     with torch.cuda.stream(stream):
         gk.replay()
@@ -566,7 +634,8 @@ def run_gpu(args, rank, world):
     torch.cuda.synchronize()
     kms = k0.elapsed_time(k1) / (reps * ncopy)
     peak, peak_kind = peaks()
-    achieved = MMVQ_BYTES(1) / (kms * 1e-3) / 1e9
+    kbytes = MMVQ_BYTES(1) + (QUANT_BYTES(1) if fused_step else 0)
+    achieved = kbytes / (kms * 1e-3) / 1e9
 
     # ---- end to end: host activations in, outputs back to the host, every step ----
     h2d = sum(xs_host[b].numel() * 4 for b in BATCHES)
@@ -601,7 +670,7 @@ def run_gpu(args, rank, world):
     e2e = world * STEP_BYTES * args.steps / e2e_s / 1e9
 
     stats = ctx.stats()
-    ok = stats["stock_launches"] == 0 and stats["native_failures"] == 0
+    ok = stats["stock_launches"] == 0 and stats["native_failures"] == 0 and (not defer or stats["fused_q8_1"] > 0)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
@@ -611,24 +680,34 @@ def run_gpu(args, rank, world):
                            "rows_per_gpu": ROWS, "k": K, "batches": list(BATCHES), "weight_copies": ncopy,
                            "l2": "inputs larger than L2: %d weight copies (%.0f MB) rotated" % (ncopy, ncopy * W_BYTES / 1e6),
                            "parallelism": "row-sharded x%d + NCCL all-gather" % world if world > 1 else "single GPU",
-                           "bytes_per_step_per_gpu": STEP_BYTES, "cuda_graph": True},
+                           "bytes_per_step_per_gpu": STEP_BYTES,
+                           "cuda_graph": "%d steps per graph (one period of the weight rotation)" % period,
+                           "router": ("weights fetched before the dependent-launch wait (CFI_CTX_CONST_WEIGHTS)"
+                                      + ("; quantize_q8_1 held back into its GEMV where the prologue is small "
+                                         "(CFI_CTX_DEFER_Q8_1)" if defer else ""))},
                 "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "note": "host fp32 activations in and fp32 outputs out every step (weights resident), "
                                 "stream synchronized per step"},
                 "gpu_launches": launches_per_step * args.steps,
                 "collectives_per_step": 1 if world > 1 else 0,
-                "roofline": {"bound": "hbm", "kernel": "mul_mat_vec_q<Q4_K,1> 8192x2048", "achieved": round(achieved, 1),
+                "roofline": {"bound": "hbm",
+                             "kernel": ("cfi_mmvq_stream_q81<Q4_K,1> (quantize_q8_1 + mul_mat_vec_q) 8192x2048"
+                                        if fused_step else "cfi_mmvq_stream<Q4_K,1> (mul_mat_vec_q) 8192x2048"),
+                             "achieved": round(achieved, 1),
                              "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                             "traffic": traffic_per_launch(), "launch_us": round(kms * 1e3, 3),
-                             "bytes_per_launch": MMVQ_BYTES(1)},
+                             "traffic": traffic_per_launch(fused_step), "launch_us": round(kms * 1e3, 3),
+                             "bytes_per_launch": kbytes},
                 "clocks": clk.summary(), "native_only": ok}
+        line.update(legs)
         if not args.no_prefill and world == 1:
             line["prefill"] = prefill_gemm(cfi, g, stream, dev, tensor_peak())
         if not args.no_decode and world == 1:
             line["decode"] = decode_bench(stream, dev)
-            line["decode"]["fused"] = decode_bench(stream, dev, fused=1)
+            line["decode"]["const_weights"] = decode_bench(stream, dev, const_weights=True)
+            line["decode"]["deferred_quantize"] = decode_bench(stream, dev, defer=True, const_weights=True)
+            line["decode"]["fused"] = decode_bench(stream, dev, fused=1, const_weights=True)
         if not args.no_configs and world == 1:
-            line["config1"] = config1_bench(cfi, g, stream, dev, peak)
+            line["config1"] = config1_bench(cfi, g_sep or g, stream, dev, peak, gf=g if defer else None)
             line["config5"] = config5_bench(cfi, g, stream, dev, peak, tensor_peak())
             line["fattn"] = fattn_bench(cfi, g, stream, dev, tensor_peak())
         if not args.no_cpu and world == 1:
@@ -640,11 +719,14 @@ def run_gpu(args, rank, world):
                                     "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
                                                       "sample": "%d full steps in %.1f s" % (n1, el1)}}
         print(json.dumps(line), flush=True)
-    del graphs, ge
+    del graph_period, graph_rest, ge
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     ctx.close()
+    for c in (ctx_sep, ctx_plain):
+        if c:
+            c.close()
 
 
 def main():
@@ -658,6 +740,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 5 legs")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--separate-quantize", action="store_true",
+                    help="launch quantize_q8_1 and mul_mat_vec_q separately (no CFI_CTX_DEFER_Q8_1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

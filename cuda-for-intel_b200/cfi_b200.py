@@ -24,7 +24,7 @@ QK = {Q4_0: 32, Q5_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
 P_U8, P_U16, P_U32, P_F32, P_U64, P_PTR, P_WORDS, P_STAGED = range(8)
 SUBSTITUTE, MISMATCH, NOT_APPLICABLE = 0, 1, 2
 K_MMVQ, K_QUANTIZE_Q8_1, K_MMQ, K_MMQ_FIXUP, K_QUANTIZE_MMQ, K_RMS_NORM, K_RMS_NORM_PLAIN, K_ROPE_NEOX, K_SOFT_MAX = range(1, 10)
-CTX_FAKE = 1
+CTX_FAKE, CTX_DEFER_Q8_1, CTX_CONST_WEIGHTS = 1, 2, 4
 SITE_NATIVE_LAUNCH, SITE_PROBE, SITE_STOCK_LAUNCH, SITE_BUILD = 1, 2, 3, 4
 
 
@@ -47,7 +47,8 @@ class Plan(C.Structure):
 
 class Stats(C.Structure):
     _fields_ = [("native_launches", C.c_uint64), ("stock_launches", C.c_uint64), ("fixups_skipped", C.c_uint64),
-                ("probes_run", C.c_uint64), ("probes_failed", C.c_uint64), ("native_failures", C.c_uint64)]
+                ("probes_run", C.c_uint64), ("probes_failed", C.c_uint64), ("native_failures", C.c_uint64),
+                ("fused_q8_1", C.c_uint64)]
 
 
 _lib = None
@@ -85,6 +86,7 @@ def lib():
     L.cfi_ctx_create.restype = C.c_void_p
     L.cfi_ctx_destroy.argtypes = [C.c_void_p]
     L.cfi_ctx_destroy.restype = None
+    L.cfi_ctx_flush.argtypes = [C.c_void_p]
     L.cfi_subst_launch.argtypes = [C.c_void_p, C.POINTER(Plan), C.c_void_p, u32p, u32p, C.c_uint32, C.c_void_p,
                                    C.POINTER(C.c_void_p)]
     L.cfi_subst_probe.argtypes = [C.c_void_p, C.POINTER(Plan), C.c_void_p, C.c_char_p, C.c_size_t]
@@ -288,8 +290,13 @@ class KernelArgs:
 class Ctx:
     """A cfi_ctx: per-device native registry, router and statistics."""
 
-    def __init__(self, device=0, fake=False):
-        self.h = lib().cfi_ctx_create(device, CTX_FAKE if fake else 0)
+    def __init__(self, device=0, fake=False, defer_q8_1=False, const_weights=False):
+        """defer_q8_1: hold each quantize_q8_1 back for the GEMV that reads it (one fused kernel);
+        call flush() before reading its output by anything but a launch through this context.
+        const_weights: no kernel writes the GEMVs' weight matrices, so each GEMV copies its
+        weights before waiting on the previous kernel."""
+        flags = (CTX_FAKE if fake else 0) | (CTX_DEFER_Q8_1 if defer_q8_1 else 0)
+        self.h = lib().cfi_ctx_create(device, flags | (CTX_CONST_WEIGHTS if const_weights else 0))
         if not self.h:
             raise RuntimeError("cfi_ctx_create failed")
 
@@ -307,6 +314,9 @@ class Ctx:
     def launch(self, plan, grid, block, args, stream=0, stock_fn=None, shared=0):
         return lib().cfi_subst_launch(self.h, C.byref(plan) if plan is not None else None, stock_fn, _u3(*grid),
                                       _u3(*block), shared, C.c_void_p(stream), args.ptrs)
+
+    def flush(self):
+        check(lib().cfi_ctx_flush(self.h), "cfi_ctx_flush")
 
     def probe(self, plan, stream=0):
         why = C.create_string_buffer(512)

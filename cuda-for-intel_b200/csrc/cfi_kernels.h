@@ -22,12 +22,32 @@ bool cfi_mmvq_stream_only(uint32_t ty);  // types without the row kernel (Q6_K, 
 void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
                             uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,
                             uint32_t* chunk_rows, uint32_t* nstages, size_t* smem);
+// direct-fill kernel (cfi_native_mmvq_direct, `nstages` 0): plain global loads into two
+// register-fed stages of at most 16 KB.  False when the rows are strided or one row is larger than a stage.
+bool cfi_mmvq_direct_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
+                            uint32_t stride_row_x, uint32_t* chunk_rows, size_t* smem);
 // row kernel (ncols >= 3): dynamic shared memory of a launch
 size_t cfi_mmvq_smem_bytes(uint32_t ty, uint32_t ncols, uint32_t ncols_x);
 // Rows a warp of the row kernel computes at once (all loads of an iteration issued together).
 inline uint32_t cfi_mmvq_rows_per_warp(uint32_t ty, uint32_t ncols) {
     return ty == 12 ? (ncols == 1 ? 2 : 1) : (ncols <= 2 ? 2 : 1);
 }
+// A deferred quantize_q8_1 absorbed by the streaming GEMV (the router's CFI_CTX_DEFER_Q8_1 mode):
+// the fp32 activations x (column c at x + c * s01, ne00 real values), the q8_1 buffer the quantize
+// would have written (nbq = ne0 / 32 blocks per column, columns contiguous) and nothing else.  The
+// GEMV quantizes x in its prologue with the quantizer's own arithmetic and its CTAs together store
+// every block of vy, so memory ends up as after quantize_q8_1 + mul_mat_vec_q.  Passed by value
+// after the three trailing words.
+struct CfiFuseQ {
+    const float* x;
+    uint8_t* vy;
+    int64_t ne00, s01;
+    uint32_t nbq, pad;
+};
+// the GEMV with the quantize in its prologue, on the direct-fill or the bulk-copy layout (the
+// same trailing words as that layout's kernel, then the CfiFuseQ); nullptr above 4 columns
+const void* cfi_native_mmvq_q81(uint32_t ty, uint32_t ncols, bool direct);
+const void* cfi_native_mmvq_direct(uint32_t ty, uint32_t ncols);  // the direct-fill kernel (nstages 0)
 int cfi_mmvq_max_smem_bytes();
 unsigned int cfi_mmvq_error_take();
 constexpr int CFI_MMVQ_THREADS = 256;

@@ -31,6 +31,7 @@
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
 #include "decode_epi.cuh"
+#include "q81_block.cuh"
 #include "../../include/cfi_glue.h"
 
 #include <algorithm>
@@ -117,6 +118,66 @@ CFI_DEV YStage stage_y(uint8_t* smem, int ncols, const uint8_t* y0, size_t y_bas
         yb[idx] = make_uint4(q[5], q[6], q[7], q[8]);
         ym[idx] = make_uint2(__float_as_uint(h2f_bits((uint16_t)(q[0] & 0xffffu))), aux);
     }
+    return YStage{smem_u32(ya), smem_u32(yb), smem_u32(ym), nb32};
+}
+
+// The activation stage of a GEMV that absorbed a deferred quantize_q8_1, built by a cluster of
+// CTAs together: CTA `rank` of the cluster quantizes blocks rank, rank + cs, ... (one 8-thread
+// group per 32-value block of x, q81_block.cuh: the quantizer's arithmetic) and stores each one
+// into the stage of every CTA of the cluster (distributed shared memory), so the stage holds
+// exactly what stage_y would have read from the quantizer's output.  The first cluster also
+// stores every block, padding blocks (b >= nb32) included, to vy.  Ends with a cluster barrier:
+// no CTA leaves while a peer may still store into its shared memory.  The kernel arrives at the
+// cluster barrier on entry (mmvq_stream_body); the wait here completes that phase.
+template <uint32_t TY>
+CFI_DEV YStage stage_y_q81(uint8_t* smem, int ncols, const CfiFuseQ& f, uint32_t nb32) {
+    uint4* ya = reinterpret_cast<uint4*>(smem);
+    uint4* yb = ya + (size_t)ncols * nb32;
+    uint2* ym = reinterpret_cast<uint2*>(yb + (size_t)ncols * nb32);
+    const uint32_t cs = cluster_nctarank(), rank = cluster_ctarank();
+    const bool writer = blockIdx.x < cs;  // the first cluster
+    cluster_wait();  // every CTA of the cluster has started (arrived at kernel entry)
+    const uint32_t total = (uint32_t)ncols * f.nbq;
+    const uint32_t j = threadIdx.x & 7, groups = blockDim.x / 8;
+    for (uint32_t base = 0; base * cs < total; base += groups) {
+        const uint32_t idx = (base + threadIdx.x / 8) * cs + rank;
+        const uint32_t c = idx / f.nbq, b = idx - c * f.nbq;
+        const bool need = idx < total && (b < nb32 || writer);  // uniform over the 8-thread group
+        const unsigned mask = __ballot_sync(0xffffffffu, need);
+        if (!need) continue;
+        const Q81Part p = q81_quantize4(q81_load4(f.x + (size_t)c * f.s01, (int64_t)b * 32 + 4 * j, f.ne00), mask);
+        uint32_t qw;
+        memcpy(&qw, &p.q, 4);
+        // aux word of the stage (stage_y): quant sums as exact integer adds over the group
+        int part = dp4a(0x01010101, (int)qw, 0);
+        part += __shfl_xor_sync(mask, part, 1);
+        part += __shfl_xor_sync(mask, part, 2);          // words 0-3 on threads 0-3, 4-7 on 4-7
+        const int other = __shfl_xor_sync(mask, part, 4);
+        uint32_t aux;
+        if (TY == T_Q4_0)
+            aux = __float_as_uint(h2f_bits((uint16_t)(p.ds >> 16)));
+        else if (TY == T_Q6_K)
+            aux = ((uint32_t)part & 0xffffu) | ((uint32_t)other << 16);
+        else
+            aux = (uint32_t)(part + other);
+        if (writer) {
+            uint8_t* blk = f.vy + (size_t)idx * Q8_1_BYTES;
+            *reinterpret_cast<uint32_t*>(blk + 4 + 4 * j) = qw;
+            if (j == 0) *reinterpret_cast<uint32_t*>(blk) = p.ds;
+        }
+        if (b < nb32) {
+            const uint32_t s = c * nb32 + b;
+            const uint32_t wa = j < 4 ? smem_u32(ya + s) + 4 * j : smem_u32(yb + s) + 4 * (j - 4);
+            const uint32_t ma = smem_u32(ym + s);
+            const uint32_t dbits = __float_as_uint(h2f_bits((uint16_t)(p.ds & 0xffffu)));
+            for (uint32_t t = 0; t < cs; t++) {
+                st_cluster_u32(mapa_shared(wa, t), qw);
+                if (j == 0) st_cluster_v2(mapa_shared(ma, t), dbits, aux);
+            }
+        }
+    }
+    __syncwarp();
+    cluster_sync();
     return YStage{smem_u32(ya), smem_u32(yb), smem_u32(ym), nb32};
 }
 
@@ -374,6 +435,7 @@ __global__ void __launch_bounds__(NW * 32)
 //   * Q8_0: one warp per row, lane l = model lane l.
 // R rows per team are computed together so their loads and butterflies interleave.
 constexpr uint32_t ST_MAX_STAGES = 4;
+constexpr int DIRECT_U = 4;  // 16-byte pieces per thread and chunk of the direct fill
 
 // Shared-memory layout of one stage.  Dense rows (stride_row_x == blocks per row) are copied as
 // one contiguous range, row k of the chunk at (address of its first row & 15) + k * row_bytes;
@@ -732,8 +794,13 @@ CFI_DEV void q6k_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0
         stride_channel_y, stride_channel_dst, sample_ratio, stride_sample_x, stride_sample_y, stride_sample_dst, nrows,  \
         chunk_rows, nst
 
-template <uint32_t TY, int NCOLS>
-CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS) {
+template <uint32_t TY, int NCOLS, bool FQ = false, bool DIRECT = false>
+CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) {
+    // nst bit 8 (CFI_CTX_CONST_WEIGHTS): the weights are not written by any kernel, so their
+    // first stages are fetched before waiting on the previous kernel (programmatic dependent
+    // launch), overlapping its tail; only the activations (and an ids table) wait
+    const bool early = (nst & 0x100u) != 0 && !(NCOLS == 1 && ids != nullptr);
+    nst &= 0xffu;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[ST_MAX_STAGES];
     constexpr uint32_t BB = block_bytes<TY>();
@@ -750,12 +817,13 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS) {
     const uint32_t rbeg = (uint32_t)((uint64_t)blockIdx.x * nrows / gridDim.x);
     const uint32_t rend = (uint32_t)((uint64_t)(blockIdx.x + 1) * nrows / gridDim.x);
     const uint32_t nchunks = (rend - rbeg + chunk_rows - 1) / chunk_rows;
+    if constexpr (FQ) cluster_arrive_relaxed();  // completed in stage_y_q81
 
     if (tid == 0) {
         for (uint32_t s = 0; s < nst; s++) mbar_init(&full[s], 1);
         fence_mbar_init();
         // L2 hint for this CTA's rows (the ids table may come from the previous kernel: skip)
-        if (!use_ids && rend > rbeg) {
+        if (!use_ids && !early && rend > rbeg) {
             const uint32_t channel_x = fastdiv(channel_dst, channel_ratio);
             const uint8_t* pl = static_cast<const uint8_t*>(vx) +
                                 ((size_t)sample_x * stride_sample_x + (size_t)channel_x * stride_channel_x) * BB;
@@ -768,16 +836,17 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS) {
             }
         }
     }
-    pdl_launch_dependents();
-    pdl_wait();
-    __syncthreads();
-
-    const uint32_t channel_x = use_ids ? (uint32_t)ids[channel_dst] : fastdiv(channel_dst, channel_ratio);
-    const uint32_t channel_y = use_ids ? fastmodulo(channel_dst, nchannels_y) : channel_dst;
-    const size_t y_base = (size_t)sample_dst * stride_sample_y + (size_t)channel_y * stride_channel_y;
-    const uintptr_t plane = reinterpret_cast<uintptr_t>(vx) +
-                            ((size_t)sample_x * stride_sample_x + (size_t)channel_x * stride_channel_x) * BB;
-    float* dplane = dst + (size_t)sample_dst * stride_sample_dst + (size_t)channel_dst * stride_channel_dst;
+    // operand addresses of this CTA's plane (an ids table is read only after the wait)
+    size_t y_base = 0;
+    uintptr_t plane = 0;
+    float* dplane = nullptr;
+    auto resolve = [&]() {
+        const uint32_t channel_x = use_ids ? (uint32_t)ids[channel_dst] : fastdiv(channel_dst, channel_ratio);
+        const uint32_t channel_y = use_ids ? fastmodulo(channel_dst, nchannels_y) : channel_dst;
+        y_base = (size_t)sample_dst * stride_sample_y + (size_t)channel_y * stride_channel_y;
+        plane = reinterpret_cast<uintptr_t>(vx) + ((size_t)sample_x * stride_sample_x + (size_t)channel_x * stride_channel_x) * BB;
+        dplane = dst + (size_t)sample_dst * stride_sample_dst + (size_t)channel_dst * stride_channel_dst;
+    };
 
     // copies one byte range [b0, b1) (2-byte aligned) to shared memory at st + (x - (b0 & ~15)):
     // the 16-byte-aligned interior by one bulk copy (issued by `issuer`), the ragged ends as
@@ -821,8 +890,101 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS) {
             }
         }
     };
-    for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
-    const YStage y = stage_y<TY>(smem + nst * stage_bytes, NCOLS, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
+    auto stage_act = [&](uint8_t* at) -> YStage {
+        if constexpr (FQ)
+            return stage_y_q81<TY>(at, NCOLS, *fq, nb32);
+        else
+            return stage_y<TY>(at, NCOLS, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
+    };
+    auto compute = [&](uint32_t sb, uint32_t r0, uint32_t r1, const YStage& y) {
+        if constexpr (TY == T_Q4_K)
+            q4k_chunk<NCOLS>(sb, rstride, r0, r1, y, tid, dplane, stride_col_dst);
+        else if constexpr (TY == T_Q6_K)
+            q6k_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
+        else if constexpr (TY == T_Q4_0)
+            q40_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
+        else
+            q80_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
+    };
+
+    if constexpr (DIRECT) {
+        // Direct fill (dense rows; the host sizes a chunk to at most DIRECT_U x 16 bytes per
+        // thread): every thread loads its 16-byte pieces of the chunk's byte range into
+        // registers with plain global loads -- all of them in flight at once, served from L2
+        // after the prefetch above -- and stores them into the stage, two stages alternating,
+        // so chunk k+1 is in flight while chunk k is computed.  Same stage layout as the bulk
+        // copies: the range from its first 16-byte boundary, ragged ends as halfwords.
+        uint4 reg[DIRECT_U];
+        uint32_t hwv = 0;
+        auto piece = [&](uint32_t ch, uintptr_t& b0, uintptr_t& b1, uintptr_t& a0, uintptr_t& a1) {
+            const uint32_t r0 = rbeg + ch * chunk_rows, r1 = min(r0 + chunk_rows, rend);
+            b0 = plane + (uintptr_t)r0 * row_bytes;
+            b1 = plane + (uintptr_t)r1 * row_bytes;
+            a0 = (b0 + 15) & ~(uintptr_t)15;
+            a1 = b1 & ~(uintptr_t)15;
+            if (a1 <= a0) a0 = a1 = b1;
+        };
+        auto load = [&](uint32_t ch) {
+            uintptr_t b0, b1, a0, a1;
+            piece(ch, b0, b1, a0, a1);
+#pragma unroll
+            for (int u = 0; u < DIRECT_U; u++) {
+                const uintptr_t src = a0 + 16u * (tid + NW * 32u * u);
+                reg[u] = src < a1 ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0, 0, 0, 0);
+            }
+            if (TY != T_Q4_K && tid < 16) {  // 2-byte aligned rows: at most 7 halfwords per end
+                const uintptr_t src = tid < 8 ? b0 + 2 * tid : a1 + 2 * (tid - 8);
+                if (tid < 8 ? src < a0 : src < b1) hwv = __ldg(reinterpret_cast<const unsigned short*>(src));
+            }
+        };
+        auto store = [&](uint32_t ch, uint8_t* st) {
+            uintptr_t b0, b1, a0, a1;
+            piece(ch, b0, b1, a0, a1);
+            const uintptr_t base = b0 & ~(uintptr_t)15;
+#pragma unroll
+            for (int u = 0; u < DIRECT_U; u++) {
+                const uintptr_t src = a0 + 16u * (tid + NW * 32u * u);
+                if (src < a1) *reinterpret_cast<uint4*>(st + (src - base)) = reg[u];
+            }
+            if (TY != T_Q4_K && tid < 16) {
+                const uintptr_t src = tid < 8 ? b0 + 2 * tid : a1 + 2 * (tid - 8);
+                if (tid < 8 ? src < a0 : src < b1) *reinterpret_cast<uint16_t*>(st + (src - base)) = (uint16_t)hwv;
+            }
+        };
+        if (early) {
+            resolve();
+            if (nchunks > 0) load(0);
+        }
+        pdl_launch_dependents();
+        pdl_wait();
+        if (!early) {
+            resolve();
+            if (nchunks > 0) load(0);
+        }
+        const YStage y = stage_act(smem + 2 * stage_bytes);
+        for (uint32_t ch = 0; ch < nchunks; ch++) {
+            uint8_t* st = smem + (ch & 1) * stage_bytes;
+            store(ch, st);
+            __syncthreads();
+            if (ch + 1 < nchunks) load(ch + 1);
+            const uint32_t r0 = rbeg + ch * chunk_rows;
+            compute(smem_u32(st), r0, min(r0 + chunk_rows, rend), y);
+        }
+        return;
+    } else {
+    if (early) {
+        __syncthreads();  // the barrier inits precede the fills' waits in other threads
+        resolve();
+        for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    __syncthreads();
+    if (!early) {
+        resolve();
+        for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
+    }
+    const YStage y = stage_act(smem + nst * stage_bytes);
     __syncthreads();
 
     for (uint32_t ch = 0; ch < nchunks; ch++) {
@@ -833,23 +995,34 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS) {
             return;
         }
         const uint32_t r0 = rbeg + ch * chunk_rows, r1 = min(r0 + chunk_rows, rend);
-        const uint32_t sb = smem_u32(smem + s * stage_bytes);
-        if constexpr (TY == T_Q4_K)
-            q4k_chunk<NCOLS>(sb, rstride, r0, r1, y, tid, dplane, stride_col_dst);
-        else if constexpr (TY == T_Q6_K)
-            q6k_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
-        else if constexpr (TY == T_Q4_0)
-            q40_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
-        else
-            q80_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
+        compute(smem_u32(smem + s * stage_bytes), r0, r1, y);
         __syncthreads();
         if (ch + nst < nchunks) fill(ch + nst, s);
+    }
     }
 }
 
 template <uint32_t TY, int NCOLS>
 __global__ void __launch_bounds__(NW * 32) cfi_mmvq_stream(MMVQ_STREAM_PARAMS) {
     mmvq_stream_body<TY, NCOLS>(MMVQ_STREAM_ARGS);
+}
+
+// The direct-fill GEMV (nst == 0 from the host): 4 CTAs per SM for one or two columns.
+template <int NCOLS> constexpr int direct_min_ctas() { return NCOLS <= 2 ? 4 : 2; }
+template <uint32_t TY, int NCOLS>
+__global__ void __launch_bounds__(NW * 32, direct_min_ctas<NCOLS>()) cfi_mmvq_direct(MMVQ_STREAM_PARAMS) {
+    mmvq_stream_body<TY, NCOLS, false, true>(MMVQ_STREAM_ARGS);
+}
+
+// GEMV that absorbed the quantize_q8_1 launched before it (single channel/sample plane), on the
+// direct-fill and on the bulk-copy layout.
+template <uint32_t TY, int NCOLS>
+__global__ void __launch_bounds__(NW * 32, direct_min_ctas<NCOLS>()) cfi_mmvq_direct_q81(MMVQ_STREAM_PARAMS, const CfiFuseQ fq) {
+    mmvq_stream_body<TY, NCOLS, true, true>(MMVQ_STREAM_ARGS, &fq);
+}
+template <uint32_t TY, int NCOLS>
+__global__ void __launch_bounds__(NW * 32) cfi_mmvq_stream_q81(MMVQ_STREAM_PARAMS, const CfiFuseQ fq) {
+    mmvq_stream_body<TY, NCOLS, true, false>(MMVQ_STREAM_ARGS, &fq);
 }
 
 // Q8_0 GEMV (one column) followed, in its last CTA to finish, by one fused decode step on the
@@ -907,7 +1080,50 @@ const void* pick_stream(uint32_t ncols) {
     }
 }
 
+template <uint32_t TY>
+const void* pick_direct(uint32_t ncols) {
+    switch (ncols) {
+    case 1: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 1>);
+    case 2: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 2>);
+    case 3: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 3>);
+    case 4: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 4>);
+    case 5: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 5>);
+    case 6: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 6>);
+    case 7: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 7>);
+    case 8: return reinterpret_cast<const void*>(&cfi_mmvq_direct<TY, 8>);
+    default: return nullptr;
+    }
+}
+
+// fused kernels exist for up to 4 columns (the router absorbs a quantize only there)
+template <uint32_t TY>
+const void* pick_q81(uint32_t ncols, bool direct) {
+    switch (ncols) {
+    case 1: return direct ? reinterpret_cast<const void*>(&cfi_mmvq_direct_q81<TY, 1>) : reinterpret_cast<const void*>(&cfi_mmvq_stream_q81<TY, 1>);
+    case 2: return direct ? reinterpret_cast<const void*>(&cfi_mmvq_direct_q81<TY, 2>) : reinterpret_cast<const void*>(&cfi_mmvq_stream_q81<TY, 2>);
+    case 3: return direct ? reinterpret_cast<const void*>(&cfi_mmvq_direct_q81<TY, 3>) : reinterpret_cast<const void*>(&cfi_mmvq_stream_q81<TY, 3>);
+    case 4: return direct ? reinterpret_cast<const void*>(&cfi_mmvq_direct_q81<TY, 4>) : reinterpret_cast<const void*>(&cfi_mmvq_stream_q81<TY, 4>);
+    default: return nullptr;
+    }
+}
+
 }  // namespace
+
+const void* cfi_native_mmvq_direct(uint32_t ty, uint32_t ncols) {
+    if (ty == T_Q8_0) return pick_direct<T_Q8_0>(ncols);
+    if (ty == T_Q4_K) return pick_direct<T_Q4_K>(ncols);
+    if (ty == T_Q6_K) return pick_direct<T_Q6_K>(ncols);
+    if (ty == T_Q4_0) return pick_direct<T_Q4_0>(ncols);
+    return nullptr;
+}
+
+const void* cfi_native_mmvq_q81(uint32_t ty, uint32_t ncols, bool direct) {
+    if (ty == T_Q8_0) return pick_q81<T_Q8_0>(ncols, direct);
+    if (ty == T_Q4_K) return pick_q81<T_Q4_K>(ncols, direct);
+    if (ty == T_Q6_K) return pick_q81<T_Q6_K>(ncols, direct);
+    if (ty == T_Q4_0) return pick_q81<T_Q4_0>(ncols, direct);
+    return nullptr;
+}
 
 // Q6_K and Q4_0 have the streaming kernel only (`stream` is ignored for them).
 const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols, bool stream) {
@@ -937,6 +1153,20 @@ void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint3
     *nstages = nst;
     const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127;
     *smem = (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys;
+}
+
+bool cfi_mmvq_direct_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
+                            uint32_t stride_row_x, uint32_t* chunk_rows, size_t* smem) {
+    const uint32_t nb = ncols_x / block_values_of(ty);
+    const uint32_t row_bytes = nb * block_bytes_of(ty);
+    const uint32_t cap = (uint32_t)DIRECT_U * 16u * (uint32_t)(NW * 32);
+    if (stride_row_x != nb || row_bytes == 0 || row_bytes > cap) return false;
+    const uint32_t per_cta = (nrows + grid_x - 1) / grid_x;
+    const uint32_t c = std::max(1u, std::min(per_cta, cap / row_bytes));
+    *chunk_rows = c;
+    const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127;
+    *smem = 2 * (size_t)st_stage_bytes(c, row_bytes, true) + ys;
+    return true;
 }
 
 size_t cfi_mmvq_smem_bytes(uint32_t ty, uint32_t ncols, uint32_t ncols_x) {

@@ -14,28 +14,7 @@
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
-
-// The 32-lane butterfly (offsets 16,8,4,2,1) of the reference, evaluated when thread t of an
-// 8-thread group holds values 4t..4t+3: offsets 16/8/4 pair threads (xor 4/2/1), offsets 2/1 pair
-// components inside a thread.  Returns lane 0's value of the 32-lane form on every thread.
-CFI_DEV float butterfly32_from4(float4 v, unsigned mask) {
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-        v.x += __shfl_xor_sync(mask, v.x, o);
-        v.y += __shfl_xor_sync(mask, v.y, o);
-        v.z += __shfl_xor_sync(mask, v.z, o);
-        v.w += __shfl_xor_sync(mask, v.w, o);
-    }
-    float t0 = __fadd_rn(v.x, v.z), t1 = __fadd_rn(v.y, v.w);
-    return __fadd_rn(t0, t1);
-}
-
-CFI_DEV float amax8_from4(float4 v, unsigned mask) {
-    float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(mask, a, o));
-    return a;
-}
+#include "q81_block.cuh"
 
 // Native quantize_q8_1: 256 threads x 4 values = 1024 values of one row per CTA in x.
 // Grid (ceil(ne0/1024), ne1, ne2*ne3); ne0 % 32 == 0 (ggml pads rows to 512).
@@ -56,35 +35,12 @@ extern "C" __global__ void __launch_bounds__(256)
     const uint32_t i2 = bz - i3 * ne2.z;
     const int64_t i1 = blockIdx.y;
     const float* row = x + (int64_t)i3 * s03 + (int64_t)i2 * s02 + i1 * s01;
-    float4 v;
-    if (i0 + 3 < ne00 && ((reinterpret_cast<uintptr_t>(row + i0) & 15) == 0)) {
-        v = *reinterpret_cast<const float4*>(row + i0);
-    } else {
-        v.x = i0 + 0 < ne00 ? row[i0 + 0] : 0.0f;
-        v.y = i0 + 1 < ne00 ? row[i0 + 1] : 0.0f;
-        v.z = i0 + 2 < ne00 ? row[i0 + 2] : 0.0f;
-        v.w = i0 + 3 < ne00 ? row[i0 + 3] : 0.0f;
-    }
-    const float amax = amax8_from4(v, mask);
-    const float sum = butterfly32_from4(v, mask);
-    const float d = __fdiv_rn(amax, 127.0f);
-    char4 q;
-    if (amax == 0.0f) {
-        q = make_char4(0, 0, 0, 0);
-    } else {
-        q.x = (int8_t)(int32_t)roundf(__fdiv_rn(v.x, d));
-        q.y = (int8_t)(int32_t)roundf(__fdiv_rn(v.y, d));
-        q.z = (int8_t)(int32_t)roundf(__fdiv_rn(v.z, d));
-        q.w = (int8_t)(int32_t)roundf(__fdiv_rn(v.w, d));
-    }
+    const Q81Part p = q81_quantize4(q81_load4(row, i0, ne00), mask);
     const int64_t i_cont = (((int64_t)i3 * ne2.z + i2) * ne1 + i1) * ne0 + i0;
     uint8_t* blk = static_cast<uint8_t*>(vy) + (i_cont / QK8_1) * Q8_1_BYTES;
     const int iqs = (int)(i_cont % QK8_1);
-    *reinterpret_cast<char4*>(blk + 4 + iqs) = q;
-    if (iqs == 0) {
-        uint32_t ds = (uint32_t)f2h_bits(d) | ((uint32_t)f2h_bits(sum) << 16);
-        *reinterpret_cast<uint32_t*>(blk) = ds;
-    }
+    *reinterpret_cast<char4*>(blk + 4 + iqs) = p.q;
+    if (iqs == 0) *reinterpret_cast<uint32_t*>(blk) = p.ds;
 }
 
 // Native quantize_mmq_q8_1<layout>: parameter list of ggml-cuda's quantize_mmq_q8_1 (x, ids, vy,

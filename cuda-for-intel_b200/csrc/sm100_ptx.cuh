@@ -204,6 +204,22 @@ CFI_DEV uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
     return r;
 }
+CFI_DEV uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+// stores into the shared memory of a CTA of the cluster (address from mapa_shared)
+CFI_DEV void st_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+CFI_DEV void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
+    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+// split cluster barrier: arrive early (no memory ordering), wait before the first access to a
+// peer's shared memory (all CTAs of the cluster have then started)
+CFI_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+CFI_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 // every thread of every CTA of the cluster; orders the barrier inits of both CTAs before use
 CFI_DEV void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");

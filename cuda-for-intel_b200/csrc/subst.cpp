@@ -593,6 +593,26 @@ int mmq_tile_n(uint32_t ncols_dst);  // k_mmq_sm100.cu
 int mmq_threads();
 bool mmq_type_ok(uint32_t ty);
 
+static int ensure_smem(const void* fn, size_t smem);
+
+// CTAs of `fn` resident per SM at `threads` threads and `smem` dynamic shared memory (cached);
+// 8 without a device (host-only contexts), so the layout does not depend on one.
+static uint32_t resident_ctas(const void* fn, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, size_t>, uint32_t> memo;
+    std::lock_guard<std::mutex> g(mu);
+    auto key = std::make_pair(fn, smem);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+    int n = 0;
+    if (ensure_smem(fn, smem) != 0 || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        n = 8;
+    }
+    memo[key] = (uint32_t)n;
+    return (uint32_t)n;
+}
+
 bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t block[3], const uint64_t* vals, int nvals,
                 void** args, NativeLaunch* out) {
     NativeLaunch nl;
@@ -617,7 +637,29 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
                              (env_u32("CFI_MMVQ_STREAM", 1, 0, 1) != 0 && wkb >= env_u32("CFI_MMVQ_STREAM_MIN_KB", 0, 0, 1u << 30)));
         nl.fn = cfi_native_mmvq(plan.ty, plan.ncols, stream);
         uint32_t chunk = 0, nstages = 0;
-        if (stream) {
+        bool direct = false;
+        if (stream && env_u32("CFI_MMVQ_DIRECT", 0, 0, 1)) {
+            // direct fill (nstages 0; CFI_MMVQ_DIRECT=1): measured slower than the bulk copies for
+            // Q4_K, and no faster for Q8_0 once the weights are fetched before the wait.
+            // CFI_MMVQ_DIRECT_CTAS CTAs per SM (default 2, fewer when the kernel's registers or
+            // shared memory do not allow them), chunks of at most 16 KB of rows
+            const uint32_t want = env_u32("CFI_MMVQ_DIRECT_CTAS", 2, 1, 8);
+            uint32_t c0 = 0;
+            size_t s0 = 0;
+            const uint32_t g0 = std::max(1u, std::min(nrows, (uint32_t)(sm_count() * want) / planes));
+            const void* dfn = cfi_native_mmvq_direct(plan.ty, plan.ncols);
+            if (dfn && cfi_mmvq_direct_layout(plan.ty, plan.ncols, ncols_x, nrows, g0, (uint32_t)vals[6], &c0, &s0)) {
+                const uint32_t per_sm = std::min(want, resident_ctas(dfn, CFI_MMVQ_THREADS, s0));
+                if (per_sm > 0) {
+                    nl.fn = dfn;
+                    nl.grid[0] = std::max(1u, std::min(nrows, (uint32_t)(sm_count() * per_sm) / planes));
+                    direct = cfi_mmvq_direct_layout(plan.ty, plan.ncols, ncols_x, nrows, nl.grid[0], (uint32_t)vals[6],
+                                                    &chunk, &nl.smem);
+                    nstages = 0;
+                }
+            }
+        }
+        if (stream && !direct) {
             // CFI_MMVQ_STREAM_CTAS CTAs per SM shared by the channel/sample planes; chunks of
             // CFI_MMVQ_CHUNK rows within CFI_MMVQ_STAGE_KB per stage, CFI_MMVQ_STAGES stages
             const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", 2, 1, 8);
@@ -626,7 +668,7 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
             cfi_mmvq_stream_layout(plan.ty, plan.ncols, ncols_x, nrows, nl.grid[0], (uint32_t)vals[6],
                                    env_u32("CFI_MMVQ_CHUNK", 32, 1, 256), 1024 * env_u32("CFI_MMVQ_STAGE_KB", 48, 4, 112),
                                    env_u32("CFI_MMVQ_STAGES", 3, 1, 4), &chunk, &nstages, &nl.smem);
-        } else {
+        } else if (!stream) {
             const uint32_t per_sm = env_u32("CFI_MMVQ_CTAS", 4, 1, 8);
             const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
             const uint32_t rows_per_pass = CFI_MMVQ_WARPS * cfi_mmvq_rows_per_warp(plan.ty, plan.ncols);
@@ -758,6 +800,20 @@ struct Inject {
     int nth = 0, code = 0, calls = 0;
 };
 
+// A native quantize_q8_1 held back (CFI_CTX_DEFER_Q8_1) for the mul_mat_vec_q that reads its
+// output: the launch as the caller made it, with its parameters copied (16 bytes each).
+struct DeferredQ81 {
+    bool on = false;
+    cfi_plan plan{};
+    NativeLaunch nl;
+    void* stock_fn = nullptr;
+    uint32_t grid[3] = {}, block[3] = {}, shmem = 0;
+    void* stream = nullptr;
+    std::vector<uint64_t> vals;
+    alignas(16) uint8_t raw[9 * 16] = {};
+    void* argv[9] = {};
+};
+
 }  // namespace cfi
 
 struct cfi_ctx {
@@ -770,6 +826,7 @@ struct cfi_ctx {
     bool fa_pending = false;  // a native FlashAttention ran: its stream-k fixup is a no-op
     uint64_t fa_dst = 0, fa_meta = 0;
     uint64_t fixup_events = 0;
+    cfi::DeferredQ81 dq;
     cfi_stats stats{};
     cfi::Inject inject[5];
 };
@@ -897,11 +954,153 @@ static int launch_stock(cfi_ctx* ctx, void* stock_fn, const uint32_t grid[3], co
                   static_cast<CUstream>(stream), args, nullptr);
 }
 
+// ---- deferred quantize_q8_1 (CFI_CTX_DEFER_Q8_1) ----
+// quantize_q8_1 values: [x, vy, ne00, s01, s02, s03, ne0, ne1, ne2]; mul_mat_vec_q values:
+// [x, y, ids, dst, ncols_x, nchannels_y, stride_row_x, stride_col_y, stride_col_dst, ...].
+
+// Launches the held-back quantize as it would have run (native, else stock).  Returns 0 or an error.
+static int flush_deferred(cfi_ctx* ctx) {
+    DeferredQ81& d = ctx->dq;
+    if (!d.on) return 0;
+    d.on = false;
+    int code = 0, rc = 0;
+    if (injected(ctx, CFI_SITE_NATIVE_LAUNCH, &code))
+        rc = code;
+    else if (!(ctx->flags & CFI_CTX_FAKE))
+        rc = issue_native(d.nl, d.plan, d.argv, d.stream);
+    if (rc == 0) {
+        ctx->stats.native_launches++;
+        return 0;
+    }
+    logf_("native %s launch failed (%d); using the stock kernel", d.plan.key, rc);
+    if (!(ctx->flags & CFI_CTX_FAKE)) cudaGetLastError();
+    ctx->natives[d.plan.key] = NS_FAILED;
+    ctx->stats.native_failures++;
+    return launch_stock(ctx, d.stock_fn, d.grid, d.block, d.shmem, d.stream, d.argv);
+}
+
+// Holds back a native quantize_q8_1 of up to 8 columns in one plane.  False: launch it now.
+static bool defer_q81(cfi_ctx* ctx, const cfi_plan& plan, void* stock_fn, const uint32_t grid[3], const uint32_t block[3],
+                      uint32_t shmem, void* stream, void** args, const std::vector<uint64_t>& v) {
+    if (!(ctx->flags & CFI_CTX_DEFER_Q8_1) || v.size() != 9 || !args) return false;
+    const uint64_t ne00 = v[2], ne0 = v[6], ne1 = (uint32_t)v[7];
+    if (grid[2] != 1 || ne1 < 1 || ne1 > 8 || grid[1] != ne1 || ne0 == 0 || ne0 % 32 || ne00 > ne0 || (v[0] & 3) || (v[1] & 3))
+        return false;
+    NativeLaunch nl;
+    if (!map_launch(plan, grid, block, v.data(), (int)v.size(), args, &nl) || !native_ready(ctx, plan, stream)) return false;
+    DeferredQ81& d = ctx->dq;
+    Layout l = layout_for(plan.kernel, plan.aux);
+    if (l.size() != 9) return false;
+    for (size_t i = 0; i < 9; i++) {
+        const size_t n = param_bytes(l[i]);
+        if (n == 0 || n > 16 || !args[i]) return false;
+        memcpy(d.raw + 16 * i, args[i], n);
+        d.argv[i] = d.raw + 16 * i;
+    }
+    d.plan = plan;
+    d.nl = nl;
+    d.stock_fn = stock_fn;
+    memcpy(d.grid, grid, sizeof d.grid);
+    memcpy(d.block, block, sizeof d.block);
+    d.shmem = shmem;
+    d.stream = stream;
+    d.vals = v;
+    d.on = true;
+    return true;
+}
+
+// Runs the held-back quantize inside this GEMV launch (cfi_mmvq_stream_q81) when the GEMV reads
+// exactly its output: same stream, one plane, no ids, its columns = the quantized columns, laid
+// out as the quantizer writes them.  Returns 0 when launched, -1 when not applicable, else the
+// launch error.
+static int absorb_q81(cfi_ctx* ctx, const cfi_plan& plan, const NativeLaunch& nl, const std::vector<uint64_t>& v,
+                      void** args, void* stream) {
+    const DeferredQ81& d = ctx->dq;
+    const uint64_t ne0 = d.vals[6];
+    const bool direct = nl.fn == cfi_native_mmvq_direct(plan.ty, plan.ncols);
+    if (stream != d.stream || v.size() < 17 || v[1] != d.vals[1] || v[2] != 0 || plan.ncols != (uint32_t)d.vals[7] ||
+        nl.grid[1] != 1 || nl.grid[2] != 1 || (uint32_t)v[7] != ne0 / 32 || v[4] > ne0 || nl.own_launch ||
+        !(direct || nl.fn == cfi_native_mmvq(plan.ty, plan.ncols, true)))
+        return -1;
+    // the prologue quantizes all ncols x ne0 values in every CTA: absorbed only up to
+    // CFI_DEFER_MAX_VALUES of them (default 1024, one pass of the CTA's 32 eight-thread groups),
+    // where that measured cheaper than a separate launch (Q8_0 4864 x 896: 3.58 against 4.92 us
+    // per pair; Q4_K 8192 x 2048, two passes: slower)
+    if ((uint64_t)plan.ncols * ne0 > env_u32("CFI_DEFER_MAX_VALUES", 1024, 0, 1u << 20)) return -1;
+    const void* fn = cfi_native_mmvq_q81(plan.ty, plan.ncols, direct);
+    if (!fn) return -1;
+    int code = 0;
+    if (injected(ctx, CFI_SITE_NATIVE_LAUNCH, &code)) return code;
+    if (ctx->flags & CFI_CTX_FAKE) return 0;
+    CfiFuseQ fq = {};
+    fq.x = reinterpret_cast<const float*>(d.vals[0]);
+    fq.vy = reinterpret_cast<uint8_t*>(d.vals[1]);
+    fq.ne00 = (int64_t)d.vals[2];
+    fq.s01 = (int64_t)d.vals[3];
+    fq.nbq = (uint32_t)(ne0 / 32);
+    NativeLaunch f = nl;
+    f.fn = fn;
+    if ((ctx->flags & CFI_CTX_CONST_WEIGHTS) && f.extra.size() == 3) f.extra[2] |= 0x100u;
+    // CFI_DEFER_CLUSTER CTAs (1, 2, 4 or 8; default 1) share the quantize work of the prologue
+    // through distributed shared memory (measured slower than every CTA quantizing alone)
+    uint32_t cs = env_u32("CFI_DEFER_CLUSTER", 1, 1, 8);
+    while (cs & (cs - 1)) cs &= cs - 1;
+    f.grid[0] = (f.grid[0] + cs - 1) / cs * cs;
+    std::vector<void*> argv(args, args + f.nparams);
+    std::vector<uint32_t> extra = f.extra;
+    for (auto& w : extra) argv.push_back(&w);
+    argv.push_back(&fq);
+    int e = ensure_smem(f.fn, f.smem);
+    if (e) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(f.grid[0], f.grid[1], f.grid[2]);
+    cfg.blockDim = dim3(f.block[0], f.block[1], f.block[2]);
+    cfg.dynamicSmemBytes = f.smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (f.pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na++].val.programmaticStreamSerializationAllowed = 1;
+    }
+    if (cs > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = cs;
+        attr[na].val.clusterDim.y = 1;
+        attr[na++].val.clusterDim.z = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return (int)cudaLaunchKernelExC(&cfg, f.fn, argv.data());
+}
+
 int launch_to(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t grid[3], const uint32_t block[3],
               uint32_t shmem, void* stream, void** args) {
     std::lock_guard<std::mutex> g(ctx->mu);
     if (plan) {
         std::vector<uint64_t> vals = arg_values(*plan, args);
+        if (ctx->dq.on) {
+            NativeLaunch nl;
+            if (plan->kernel == CFI_K_MMVQ && map_launch(*plan, grid, block, vals.data(), (int)vals.size(), args, &nl) &&
+                native_ready(ctx, *plan, stream)) {
+                const int rc = absorb_q81(ctx, *plan, nl, vals, args, stream);
+                if (rc == 0) {
+                    ctx->dq.on = false;
+                    ctx->stats.native_launches += 2;
+                    ctx->stats.fused_q8_1++;
+                    return 0;
+                }
+                if (rc > 0) {
+                    logf_("fused quantize_q8_1 + %s launch failed (%d); launching them separately", plan->key, rc);
+                    if (!(ctx->flags & CFI_CTX_FAKE)) cudaGetLastError();
+                    ctx->flags &= ~CFI_CTX_DEFER_Q8_1;
+                }
+            }
+            const int rc = flush_deferred(ctx);
+            if (rc) return rc;
+        }
+        if (plan->kernel == CFI_K_QUANTIZE_Q8_1 && defer_q81(ctx, *plan, stock_fn, grid, block, shmem, stream, args, vals))
+            return 0;
         if (plan->kernel == CFI_K_MMQ) ctx->have_pending = false;
         if (plan->kernel == CFI_K_FATTN) ctx->fa_pending = false;
         if (plan->kernel == CFI_K_FATTN_FIXUP) {
@@ -925,6 +1124,8 @@ int launch_to(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t
         } else {
             NativeLaunch nl;
             if (map_launch(*plan, grid, block, vals.data(), (int)vals.size(), args, &nl) && native_ready(ctx, *plan, stream)) {
+                if ((ctx->flags & CFI_CTX_CONST_WEIGHTS) && plan->kernel == CFI_K_MMVQ && nl.extra.size() == 3 && vals[2] == 0)
+                    nl.extra[2] |= 0x100u;  // fetch the weights before waiting on the previous kernel
                 int code = 0;
                 int rc = 0;
                 if (injected(ctx, CFI_SITE_NATIVE_LAUNCH, &code))
@@ -951,6 +1152,9 @@ int launch_to(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t
                 ctx->stats.native_failures++;
             }
         }
+    } else if (ctx->dq.on) {
+        const int rc = flush_deferred(ctx);
+        if (rc) return rc;
     }
     return launch_stock(ctx, stock_fn, grid, block, shmem, stream, args);
 }
@@ -1103,7 +1307,20 @@ cfi_ctx* cfi_ctx_create(int device, int flags) {
     return c;
 }
 
-void cfi_ctx_destroy(cfi_ctx* ctx) { delete ctx; }
+void cfi_ctx_destroy(cfi_ctx* ctx) {
+    if (!ctx) return;
+    {
+        std::lock_guard<std::mutex> g(ctx->mu);
+        flush_deferred(ctx);
+    }
+    delete ctx;
+}
+
+int cfi_ctx_flush(cfi_ctx* ctx) {
+    if (!ctx) return (int)cudaErrorInvalidValue;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    return flush_deferred(ctx);
+}
 
 int cfi_subst_launch(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t grid[3], const uint32_t block[3],
                      uint32_t shared_bytes, void* stream, void** kernel_params) {

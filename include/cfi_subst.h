@@ -111,12 +111,30 @@ CFI_API int cfi_plan_extra_word(const cfi_plan *plan, const uint32_t grid[3], ui
 
 /* ---- per-context native registry and launch router (replaces cuda/subst_hook.rs) ---- */
 typedef struct cfi_ctx cfi_ctx;
-enum { CFI_CTX_FAKE = 1 }; /* host-only backend: launches are recorded, never executed */
+/* CFI_CTX_FAKE: host-only backend, launches are recorded, never executed.
+ * CFI_CTX_DEFER_Q8_1: a native quantize_q8_1 (up to 8 columns, one plane) is held back until the
+ * next launch on the context; when that launch is the native streaming mul_mat_vec_q reading
+ * exactly its output on the same stream, one kernel does both (the GEMV quantizes the activations
+ * in its prologue with the quantizer's arithmetic and stores the q8_1 buffer too, so memory ends
+ * up byte-identical), saving one dependent launch per GEMV.  Any other launch, cfi_ctx_flush and
+ * cfi_ctx_destroy launch the held-back quantize first.  No counterpart in the reference, whose
+ * hook sees every driver call: a caller of this ABI must call cfi_ctx_flush before any operation
+ * that is not a launch through this context (memcpy, event record, stream sync, end of capture)
+ * whenever the last launch may have been a quantize_q8_1. */
+/* CFI_CTX_CONST_WEIGHTS: the caller promises that no kernel writes a weight matrix (the `x`
+ * operand of mul_mat_vec_q) while launches through the context may read it -- true for inference
+ * on loaded weights, false for example for a quantized KV cache multiplied by mul_mat_vec_q.  The
+ * native GEMV then copies its first weight rows into shared memory before waiting on the previous
+ * kernel of its stream (programmatic dependent launch), so that copy overlaps the previous
+ * kernel instead of following it; activations are still read only after the wait. */
+enum { CFI_CTX_FAKE = 1, CFI_CTX_DEFER_Q8_1 = 2, CFI_CTX_CONST_WEIGHTS = 4 };
 
 /* Natives::default (subst_hook.rs:14-24) for `device`; NULL on failure. */
 CFI_API cfi_ctx *cfi_ctx_create(int device, int flags);
-/* Natives::destroy (subst_hook.rs:32-38). */
+/* Natives::destroy (subst_hook.rs:32-38); launches a held-back quantize_q8_1 first. */
 CFI_API void cfi_ctx_destroy(cfi_ctx *ctx);
+/* Launches a held-back quantize_q8_1 (CFI_CTX_DEFER_Q8_1), if any.  Returns 0 or a CUDA error. */
+CFI_API int cfi_ctx_flush(cfi_ctx *ctx);
 
 /* launch / launch_to (subst_hook.rs:99-197): runs the native kernel when `plan` is non-NULL, the
  * launch has the expected shape and the native kernel passed its first-use probe; otherwise (and
@@ -133,8 +151,11 @@ CFI_API int cfi_subst_probe(cfi_ctx *ctx, const cfi_plan *plan, void *stream, ch
 /* Native state of a module key: 0 not built, 1 ready, 2 failed (subst_hook.rs:9-12). */
 CFI_API int cfi_ctx_native_state(cfi_ctx *ctx, const char *key);
 
+/* fused_q8_1: GEMV launches that absorbed a held-back quantize_q8_1 (each also counts as two
+ * native launches, the quantize's and the GEMV's). */
 typedef struct cfi_stats {
     uint64_t native_launches, stock_launches, fixups_skipped, probes_run, probes_failed, native_failures;
+    uint64_t fused_q8_1;
 } cfi_stats;
 CFI_API void cfi_ctx_stats(cfi_ctx *ctx, cfi_stats *out);
 

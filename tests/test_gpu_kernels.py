@@ -75,6 +75,29 @@ def test_quantize_q8_1_large_magnitudes_and_ties(dev):
     assert np.array_equal(dy.cpu().numpy(), ref)
 
 
+def test_quantize_q8_1_near_ties(dev):
+    """Quotients x/d within 1e-4 of a half-integer, where the quantizer's reciprocal fast path
+    must hand over to the IEEE divide (plus exact ties and subnormal / huge scales)."""
+    ctx, g = dev
+    rng = np.random.default_rng(31)
+    nblk = 32768
+    d = np.float32(2.0) ** rng.integers(-30, 30, size=nblk).astype(np.float32) * rng.uniform(0.5, 1.0, nblk).astype(np.float32)
+    k = rng.integers(-127, 127, size=(nblk, 32)).astype(np.float64)
+    eps = rng.uniform(-1e-4, 1e-4, size=(nblk, 32)) * (rng.random((nblk, 32)) < 0.9)
+    x = ((k + 0.5 + eps) * d[:, None].astype(np.float64)).astype(np.float32)
+    x[:, 0] = np.float32(127.0) * d                        # amax sets the block's scale
+    x[:64] = np.float32(1e-41) * (np.arange(32) - 15.5)   # subnormal scales
+    x[64:128] = np.float32(3e38) * (np.arange(32) / 32.0 - 0.5)
+    x = x.ravel()
+    ref = O.quantize_q8_1(x)
+    dx = to_dev(x)
+    dy = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+    g.quantize_q8_1(dx.data_ptr(), dy.data_ptr(), x.size, x.size, 1, stream=stream())
+    sync()
+    got = dy.cpu().numpy()
+    assert np.array_equal(got, ref), "%d of %d bytes differ" % ((got != ref).sum(), ref.size)
+
+
 # ------------------------------------------------------------------------------------------
 # mul_mat_vec_q
 # ------------------------------------------------------------------------------------------

@@ -315,3 +315,70 @@ def test_fattn_fixup_is_skipped_only_after_a_native_fattn():
     assert ctx.stats()["fixups_skipped"] == 1 and ctx.stats()["stock_launches"] == 2
     g.fattn_fixup(64, 0x40000, 0x50000, 631, 14, 1, 640)  # only the one right after the native launch
     assert ctx.stats()["fixups_skipped"] == 1 and ctx.stats()["stock_launches"] == 3
+
+
+def test_deferred_quantize_is_absorbed_only_by_its_gemv(monkeypatch):
+    """CFI_CTX_DEFER_Q8_1: a quantize_q8_1 is held back; the streaming mul_mat_vec_q that reads its
+    output on the same stream runs both (two native launches, one fused) when the prologue is
+    small (CFI_DEFER_MAX_VALUES, default 1024 values); anything else launches the held-back
+    quantize first."""
+    ctx = cfi.Ctx(fake=True, defer_q8_1=True)
+    g = cfi.GgmlCaller(ctx, "all")
+    k, rows = 2048, 8192
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 2)
+    assert ctx.stats()["native_launches"] == 0  # held back
+    g.mmvq(cfi.Q4_K, 2, 0x100000, 0x20000, 0x300000, k, rows)  # 4096 values: launched separately
+    s = ctx.stats()
+    assert s["native_launches"] == 2 and s["fused_q8_1"] == 0
+    monkeypatch.setenv("CFI_DEFER_MAX_VALUES", "4096")
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 2)
+    g.mmvq(cfi.Q4_K, 2, 0x100000, 0x20000, 0x300000, k, rows)
+    monkeypatch.delenv("CFI_DEFER_MAX_VALUES")
+    s = ctx.stats()
+    assert s["native_launches"] == 4 and s["fused_q8_1"] == 1
+    ctx.close()
+    ctx = cfi.Ctx(fake=True, defer_q8_1=True)
+    g = cfi.GgmlCaller(ctx, "all")
+    k = 1024
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 1)
+    g.mmvq(cfi.Q4_K, 1, 0x100000, 0x20000, 0x300000, k, rows)
+    s = ctx.stats()
+    assert s["native_launches"] == 2 and s["fused_q8_1"] == 1
+    # another GEMV input: the quantize runs on its own first
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 1)
+    g.mmvq(cfi.Q4_K, 1, 0x100000, 0x40000, 0x300000, k, rows)
+    s = ctx.stats()
+    assert s["native_launches"] == 4 and s["fused_q8_1"] == 1
+    # column count, stream or padded column stride that do not match: not absorbed
+    g.quantize_q8_1(0x1000, 0x20000, k // 2, k // 2, 2)
+    g.mmvq(cfi.Q4_K, 1, 0x100000, 0x20000, 0x300000, k // 2, rows)  # 2 columns quantized, 1 read
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 1, stream=0x77)
+    g.mmvq(cfi.Q4_K, 1, 0x100000, 0x20000, 0x300000, k, rows)
+    g.quantize_q8_1(0x1000, 0x20000, 896, 1024, 1)
+    g.mmvq(cfi.Q8_0, 1, 0x100000, 0x20000, 0x300000, 896, 4864)  # stride_col_y 28 != 1024 / 32
+    assert ctx.stats()["fused_q8_1"] == 1 and ctx.stats()["native_launches"] == 10
+    # a padded activation with the matching column stride is absorbed
+    g.quantize_q8_1(0x1000, 0x20000, 896, 1024, 1)
+    g.mmvq(cfi.Q8_0, 1, 0x100000, 0x20000, 0x300000, 896, 4864, stride_col_y=32)
+    assert ctx.stats()["fused_q8_1"] == 2
+    # flush, a plain (stock) launch and more than 8 columns
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 1)
+    ctx.flush()
+    assert ctx.stats()["native_launches"] == 13
+    ctx.flush()  # nothing held: no-op
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 1)
+    args = cfi.KernelArgs([("ptr", 0)])
+    assert ctx.launch(None, (1, 1, 1), (32, 1, 1), args) == 0
+    s = ctx.stats()
+    assert s["native_launches"] == 14 and s["stock_launches"] == 1
+    g.quantize_q8_1(0x1000, 0x20000, k, k, 9)  # launched at once
+    assert ctx.stats()["native_launches"] == 15
+    ctx.close()
+
+
+def test_quantize_is_not_deferred_without_the_flag():
+    ctx, g = fake_caller()
+    g.quantize_q8_1(0x1000, 0x20000, 2048, 2048, 1)
+    assert ctx.stats()["native_launches"] == 1
+    g.mmvq(cfi.Q4_K, 1, 0x100000, 0x20000, 0x300000, 2048, 8192)
+    assert ctx.stats()["native_launches"] == 2 and ctx.stats()["fused_q8_1"] == 0
