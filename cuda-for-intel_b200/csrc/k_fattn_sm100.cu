@@ -10,20 +10,22 @@
 // reference (mod.rs:27-54): D = 64 or 128, no sinks, max_bias 0, no softcap, GQA; plus 16-byte
 // aligned K/V rows (TMA).
 //
-// One CTA of 352 threads per (128-query tile, head, sequence):
-//   * warps 0-7 run the softmax, two warps per TMEM lane quadrant: thread (row, half) owns one
-//     query row (TMEM lane) and 64 of the 128 key columns of a chunk.  They convert Q (x scale) to
-//     fp16 in the 128-byte swizzled K-major layout, then per chunk read their score columns from
-//     TMEM, add the mask (16-byte loads issued before the wait), exchange the half-row maxima through
-//     shared memory, run the online softmax (row max, exp, sum in fp32), rescale their half of the
-//     output accumulator in TMEM when the running max grows, and write their half of P (fp16) as the
-//     A operand of the PV product; at the end O / (l_0 + l_1) goes to dst;
+// One CTA of 608 threads per (128-query tile, head, sequence):
+//   * warps 0-15 run the softmax, four warps per TMEM lane quadrant: thread (row, quarter) owns one
+//     query row (TMEM lane) and 32 of the 128 key columns of a chunk.  They convert Q (x scale x
+//     log2 e) to fp16 in the 128-byte swizzled K-major layout, then per chunk read their score
+//     columns from TMEM, add the mask (16-byte loads issued before the wait), exchange the
+//     quarter-row maxima through shared memory (one named barrier per quadrant), run the online
+//     softmax in log2 units (row max, ex2, sum in fp32) with lazy rescaling -- the output
+//     accumulator in TMEM and the sum are rescaled only when the row max grows by more than 2^8 --
+//     and write their quarter of P (fp16) as the A operand of the PV product, alternating between
+//     two P buffers for D 64; at the end O / l goes to dst;
 //   * before the loop the tile's key range is cut to the chunks where some valid query sees some
 //     key (mask not -inf), so a causal prompt skips the chunks above the diagonal;
-//   * warps 9 and 10 stream K and V chunks with TMA (two stages each, 128 keys x 64 dims per box,
+//   * warps 17 and 18 stream K and V chunks with TMA (two stages each, 128 keys x 64 dims per box,
 //     keys past the end read as zero); a K stage is free once its S product is done, so K loads run
 //     ahead of the PV products;
-//   * one thread of warp 8 issues S = Q K^T (M 128, N 128, K = D) into one of two TMEM score
+//   * one thread of warp 16 issues S = Q K^T (M 128, N 128, K = D) into one of two TMEM score
 //     buffers and O += P V (M 128, N = D, K 128; V is the MN-major B operand) into the TMEM output.
 // TMEM: scores at columns 0 and 128, output at 256.  Every wait is bounded (error word + abort).
 // Arithmetic: fp16 Q and P (as ggml's tensor-core kernel rounds them), fp32 scores, softmax and
@@ -48,10 +50,20 @@ using namespace sm100;
 
 constexpr int FA_BM = 128;       // queries per CTA (TMEM lanes)
 constexpr int FA_BN = 128;       // keys per chunk
-constexpr int FA_SOFTMAX_WARPS = 8, FA_MMA_WARP = 8, FA_TMA_WARP = 9, FA_TMA_V_WARP = 10;
+constexpr int FA_SOFTMAX_WARPS = 16, FA_MMA_WARP = 16, FA_TMA_WARP = 17, FA_TMA_V_WARP = 18;
+constexpr int FA_NQ = 4;                 // softmax threads per query row (key quarters)
+constexpr int FA_KQ = FA_BN / FA_NQ;     // keys per softmax thread and chunk
 constexpr int FA_FLAG_WORDS = 8;  // chunk-visibility bits: key ranges up to 256 chunks are cut
-constexpr int FA_THREADS = 352;  // warps 0-7 softmax (two per TMEM sub-partition), 8 MMA, 9-10 TMA
+constexpr int FA_THREADS = 608;  // warps 0-15 softmax (four per TMEM sub-partition), 16 MMA, 17-18 TMA
 constexpr uint32_t FA_TMEM_COLS = 512;
+constexpr float FA_LOG2E = 1.4426950408889634f;
+constexpr float FA_RESCALE_LOG2 = 8.0f;  // rescale O and l only when the row max grows by more than 2^8
+
+CFI_DEV float ex2_approx(float x) {  // 2^x (PTX ex2.approx; -inf -> +0)
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 struct FaArgs {
     const uint8_t* q;
@@ -66,9 +78,13 @@ struct FaArgs {
     unsigned int* err;
 };
 
+// P buffers: two for D 64 (chunk j's P is written while the PV product of chunk j-1 runs); one for
+// D 128, where a second 32 KB buffer does not fit next to the 128 KB of K/V stages
+template <int D> constexpr int fa_pbufs() { return D == 64 ? 2 : 1; }
+
 template <int D>
 constexpr size_t fa_smem_bytes() {
-    return 1024 + (size_t)FA_BM * D * 2 + 4 * (size_t)FA_BN * D * 2 + (size_t)FA_BM * FA_BN * 2 + 256;
+    return 1024 + (size_t)FA_BM * D * 2 + 4 * (size_t)FA_BN * D * 2 + fa_pbufs<D>() * (size_t)FA_BM * FA_BN * 2 + 256;
 }
 
 CFI_DEV void st_chunk16(uint8_t* atom, int r, int c, uint32_t a, uint32_t b, uint32_t cc, uint32_t d) {
@@ -83,30 +99,32 @@ template <int D>
 __global__ void __launch_bounds__(FA_THREADS, 1)
     cfi_fattn_tc(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, const FaArgs a) {
     constexpr int DB = D / 64;                          // 64-dim blocks (one swizzle atom column each)
-    constexpr int DH = D / 2;                           // output columns per softmax half
+    constexpr int DQ = D / FA_NQ;                       // output columns per softmax thread
     constexpr uint32_t QBYTES = FA_BM * D * 2;
     constexpr uint32_t KVBYTES = FA_BN * D * 2;         // one K or V stage
     constexpr uint32_t BLK_Q = FA_BM * 128, BLK_KV = FA_BN * 128;  // bytes of one 64-dim block
     extern __shared__ uint8_t smem_raw[];
-    __shared__ float xmax[2][2][FA_BM];  // partial row maxima (chunk parity, key half, row)
-    __shared__ float xsum[2][FA_BM];     // final partial row sums (key half, row)
+    __shared__ float xmax[2][FA_NQ][FA_BM];  // partial row maxima (chunk parity, key quarter, row)
+    __shared__ float xsum[FA_NQ][FA_BM];     // final partial row sums (key quarter, row)
     __shared__ uint32_t chunk_vis[FA_FLAG_WORDS];  // chunks with a visible key for some valid query
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + QBYTES;
     uint8_t* sV = sK + 2 * KVBYTES;
-    uint8_t* sP = sV + 2 * KVBYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + FA_BM * FA_BN * 2);
+    constexpr int NPB = fa_pbufs<D>();
+    uint8_t* sP = sV + 2 * KVBYTES;  // NPB P buffers; chunk j uses buffer j % NPB
+    constexpr uint32_t PBYTES = FA_BM * FA_BN * 2;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + NPB * PBYTES);
     uint64_t* k_full = bars;        // [2] TMA bytes of K of a chunk
     uint64_t* k_empty = bars + 2;   // [2] the S product of the chunk has read K
     uint64_t* s_full = bars + 4;    // [2] scores of a chunk in TMEM
     uint64_t* s_empty = bars + 6;   // [2] softmax warps have read them (8 arrivals)
-    uint64_t* p_full = bars + 8;    // P in shared memory, output rescaled (8 arrivals)
-    uint64_t* pv_done = bars + 9;   // O += P V completed
-    uint64_t* q_ready = bars + 10;  // fp16 Q in shared memory (8 arrivals)
-    uint64_t* v_full = bars + 11;   // [2] TMA bytes of V of a chunk
-    uint64_t* v_empty = bars + 13;  // [2] the PV product of the chunk has read V
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* p_full = bars + 8;    // [NPB] P of a chunk in its buffer, output rescaled if needed (8 arrivals)
+    uint64_t* pv_done = bars + 10;  // [NPB] O += P V of a chunk completed (its P buffer is free again)
+    uint64_t* q_ready = bars + 12;  // fp16 Q in shared memory (8 arrivals)
+    uint64_t* v_full = bars + 13;   // [2] TMA bytes of V of a chunk
+    uint64_t* v_empty = bars + 15;  // [2] the PV product of the chunk has read V
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -121,9 +139,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_empty[i], FA_SOFTMAX_WARPS);
+            mbar_init(&p_full[i], FA_SOFTMAX_WARPS);  // (the second pair is unused when NPB == 1)
+            mbar_init(&pv_done[i], 1);
         }
-        mbar_init(p_full, FA_SOFTMAX_WARPS);
-        mbar_init(pv_done, 1);
         mbar_init(q_ready, FA_SOFTMAX_WARPS);
         *abort_flag = 0;
         for (int w = 0; w < FA_FLAG_WORDS; w++) chunk_vis[w] = 0u;
@@ -140,8 +158,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     pdl_launch_dependents();
     pdl_wait();  // Q, K, V and the mask may come from the previous kernel
 
-    // softmax thread: row r (TMEM lane) and key half h (columns 64 h .. 64 h + 63 of a chunk)
-    const int r = 32 * (warp & 3) + lane, h = (warp >> 2) & 1, q = q0 + r;
+    // softmax thread: row r (TMEM lane) and key quarter h (columns 32 h .. 32 h + 31 of a chunk)
+    const int r = 32 * (warp & 3) + lane, h = (warp >> 2) & 3, q = q0 + r;
     const bool qvalid = q < a.ne01;
     const uint16_t* mrow = nullptr;
     if (warp < FA_SOFTMAX_WARPS && a.mask && q < a.ne31)
@@ -157,18 +175,28 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
         for (int w = 0; w < FA_FLAG_WORDS; w++) bits[w] = 0u;
         const bool vec = mrow && ((reinterpret_cast<uintptr_t>(a.mask) | (uintptr_t)a.nb31 | (uintptr_t)a.nb33) & 15) == 0;
+        // vector path: the loads of chunk j+1 are issued before chunk j is tested
+        const uint4 ninf4 = make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+        auto load_chunk = [&](int j, uint4 (&w)[FA_KQ / 8]) {
+            const int k0 = j * FA_BN + FA_KQ * h;
+#pragma unroll
+            for (int t = 0; t < FA_KQ / 8; t++)
+                w[t] = (j < nall && k0 + 8 * t < a.ne11) ? __ldg(reinterpret_cast<const uint4*>(mrow + k0 + 8 * t)) : ninf4;
+        };
+        uint4 wn[FA_KQ / 8];
+        if (vec) load_chunk(0, wn);
         for (int j = 0; j < nall; j++) {
-            const int k0 = j * FA_BN + 64 * h;
+            const int k0 = j * FA_BN + FA_KQ * h;
             bool any = false;
             if (!mrow) {
                 any = k0 < a.ne11;  // no mask row for this query: every key counts
             } else if (vec) {
-                uint4 w[8];
+                uint4 w[FA_KQ / 8];
 #pragma unroll
-                for (int t = 0; t < 8; t++)
-                    w[t] = k0 + 8 * t < a.ne11 ? __ldg(reinterpret_cast<const uint4*>(mrow + k0 + 8 * t)) : make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+                for (int t = 0; t < FA_KQ / 8; t++) w[t] = wn[t];
+                load_chunk(j + 1, wn);
 #pragma unroll
-                for (int t = 0; t < 8; t++) {
+                for (int t = 0; t < FA_KQ / 8; t++) {
                     const uint32_t x[4] = {w[t].x, w[t].y, w[t].z, w[t].w};
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
@@ -178,7 +206,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 }
             } else {
 #pragma unroll 8
-                for (int c = 0; c < 64; c++) any = any || (k0 + c < a.ne11 && mrow[k0 + c] != 0xfc00u);
+                for (int c = 0; c < FA_KQ; c++) any = any || (k0 + c < a.ne11 && mrow[k0 + c] != 0xfc00u);
             }
             if (any) bits[j >> 5] |= 1u << (j & 31);
         }
@@ -247,19 +275,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     mma_commit(&k_empty[st]);
                 }
                 if (j >= 1) {
-                    const int jp = j - 1, st = jp & 1;
-                    ok = mbar_wait(p_full, (uint32_t)jp & 1, abort_flag);
+                    const int jp = j - 1, st = jp & 1, pb = jp % NPB;
+                    ok = mbar_wait(&p_full[pb], (uint32_t)(jp / NPB) & 1, abort_flag);
                     if (ok) ok = mbar_wait(&v_full[st], (uint32_t)(jp >> 1) & 1, abort_flag);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t pa = smem_u32(sP), vb = smem_u32(sV + st * KVBYTES);
+                    const uint32_t pa = smem_u32(sP + pb * PBYTES), vb = smem_u32(sV + st * KVBYTES);
 #pragma unroll
                     for (int kk = 0; kk < FA_BN / 16; kk++) {
                         const uint32_t off_p = (kk >> 2) * BLK_Q + (kk & 3) * 32;
                         mma_f16(tmem + 256, sw128_kmajor_desc(pa + off_p), sw128_mnmajor_desc(vb + kk * 16 * 128, BLK_KV),
                                 id_o, (jp > 0 || kk > 0) ? 1u : 0u);
                     }
-                    mma_commit(pv_done);
+                    mma_commit(&pv_done[pb]);
                     mma_commit(&v_empty[st]);
                 }
             }
@@ -271,17 +299,33 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         __syncwarp();
     } else {
         // ================= softmax warps: (row, key half) per thread =================
+        // scores are kept in log2 units: Q is scaled by scale * log2(e) and the mask by log2(e),
+        // so every softmax weight is one ex2
+        const float qscale = a.scale * FA_LOG2E;
         {
+            // this half of the row: every load issued before any conversion or store
             const float* qrow = reinterpret_cast<const float*>(a.q + (size_t)seq * a.nb03 + (size_t)head * a.nb02 +
-                                                               (size_t)(qvalid ? q : 0) * a.nb01);
+                                                               (size_t)(qvalid ? q : 0) * a.nb01) + DQ * h;
+            float f[DQ];
+            if (qvalid && (reinterpret_cast<uintptr_t>(qrow) & 15) == 0) {
 #pragma unroll
-            for (int gi = 0; gi < DH / 8; gi++) {
-                const int g = h * (DH / 8) + gi, b = g / 8, c = g % 8;  // 8-dim group of this half
-                float f[8];
+                for (int i = 0; i < DQ / 4; i++) {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(qrow) + i);
+                    f[4 * i] = t.x;
+                    f[4 * i + 1] = t.y;
+                    f[4 * i + 2] = t.z;
+                    f[4 * i + 3] = t.w;
+                }
+            } else {
 #pragma unroll
-                for (int e = 0; e < 8; e++) f[e] = qvalid ? qrow[8 * g + e] * a.scale : 0.0f;
-                st_chunk16(sQ + b * BLK_Q, r, c, pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
-                           pack_h2(f[6], f[7]));
+                for (int i = 0; i < DQ; i++) f[i] = qvalid ? __ldg(qrow + i) : 0.0f;
+            }
+#pragma unroll
+            for (int gi = 0; gi < DQ / 8; gi++) {
+                const int g = h * (DQ / 8) + gi, b = g / 8, c = g % 8;  // 8-dim group of this quarter
+                const float* e = f + 8 * gi;
+                st_chunk16(sQ + b * BLK_Q, r, c, pack_h2(e[0] * qscale, e[1] * qscale), pack_h2(e[2] * qscale, e[3] * qscale),
+                           pack_h2(e[4] * qscale, e[5] * qscale), pack_h2(e[6] * qscale, e[7] * qscale));
             }
         }
         fence_proxy_async_smem();
@@ -290,15 +334,33 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 
         const bool mvec = mrow && ((reinterpret_cast<uintptr_t>(a.mask) | (uintptr_t)a.nb31 | (uintptr_t)a.nb33) & 15) == 0;
         const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-        float m = -INFINITY, l = 0.0f;
+        const int quad_bar = 1 + (warp & 3);  // the four warps (key quarters) of this TMEM quadrant
+        // this thread's DQ output columns in TMEM: ld / st of 16 or 32 columns
+        auto o_ld = [&](uint32_t (&v)[DQ]) {
+            if constexpr (DQ == 16) tmem_ld16(trow + 256 + DQ * h, v); else tmem_ld32(trow + 256 + DQ * h, v);
+        };
+        auto o_st = [&](const uint32_t (&v)[DQ]) {
+            if constexpr (DQ == 16) tmem_st16(trow + 256 + DQ * h, v); else tmem_st32(trow + 256 + DQ * h, v);
+        };
+        // Online softmax with lazy rescaling: P = 2^(s - m_used) with m_used the row max at the last
+        // rescale; O and l are rescaled only when the chunk's max exceeds m_used by more than
+        // FA_RESCALE_LOG2 (P then stays below 2^FA_RESCALE_LOG2, far inside fp16), so most chunks
+        // neither touch O nor wait for the previous PV product.  With two P buffers, chunk j's P
+        // is written while the PV product of chunk j-1 runs.
+        float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int j = 0; j < nch; j++) {
-            const int st = j & 1, key0 = (jb + j) * FA_BN + 64 * h;
-            // this half's 64 mask values, loaded before waiting on the scores
-            float mk[64];
-            if (mvec) {
+            const int st = j & 1, key0 = (jb + j) * FA_BN + FA_KQ * h;
+            // this quarter's 32 mask values, loaded before waiting on the scores (none without a
+            // mask row); `full`: all 32 keys exist, so no per-key range test
+            const bool full = key0 + FA_KQ <= a.ne11;
+            float mk[FA_KQ];
+            if (!mrow) {
 #pragma unroll
-                for (int t = 0; t < 8; t++) {
+                for (int c = 0; c < FA_KQ; c++) mk[c] = 0.0f;
+            } else if (mvec) {
+#pragma unroll
+                for (int t = 0; t < FA_KQ / 8; t++) {
                     uint4 w = make_uint4(0, 0, 0, 0);
                     if (key0 + 8 * t < a.ne11) w = __ldg(reinterpret_cast<const uint4*>(mrow + key0 + 8 * t));
                     const __half2* hp = reinterpret_cast<const __half2*>(&w);
@@ -311,8 +373,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < 64; c++)
-                    mk[c] = (mrow && key0 + c < a.ne11) ? __half2float(__ushort_as_half(mrow[key0 + c])) : 0.0f;
+                for (int c = 0; c < FA_KQ; c++)
+                    mk[c] = key0 + c < a.ne11 ? __half2float(__ushort_as_half(mrow[key0 + c])) : 0.0f;
             }
             // tcgen05.ld / st are warp-collective: every decision before them is warp-uniform
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (uint32_t)(j >> 1) & 1, abort_flag))) {
@@ -320,75 +382,96 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            float sv[64];
-#pragma unroll
-            for (int g = 0; g < 2; g++) {
+            float sv[FA_KQ];
+            {
                 uint32_t v[32];
-                tmem_ld32(trow + st * FA_BN + 64 * h + 32 * g, v);
+                tmem_ld32(trow + st * FA_BN + FA_KQ * h, v);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i++) sv[32 * g + i] = __uint_as_float(v[i]);
+                for (int i = 0; i < 32; i++) sv[i] = __uint_as_float(v[i]);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[st]);
-            float mx = -INFINITY;
+            float mx8[8];
 #pragma unroll
-            for (int c = 0; c < 64; c++) {
-                const float s = key0 + c < a.ne11 ? sv[c] + mk[c] : -INFINITY;
-                sv[c] = s;
-                mx = fmaxf(mx, s);
+            for (int i = 0; i < 8; i++) mx8[i] = -INFINITY;
+            if (full) {
+#pragma unroll
+                for (int c = 0; c < FA_KQ; c++) {
+                    sv[c] = fmaf(mk[c], FA_LOG2E, sv[c]);
+                    mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < FA_KQ; c++) {
+                    sv[c] = key0 + c < a.ne11 ? fmaf(mk[c], FA_LOG2E, sv[c]) : -INFINITY;
+                    mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+                }
             }
-            // the row max over both key halves
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            // the row max over the four key quarters
             xmax[st][h][r] = mx;
-            named_bar_sync(1, 32 * FA_SOFTMAX_WARPS);
-            const float m_new = fmaxf(m, fmaxf(mx, xmax[st][h ^ 1][r]));
-            const bool none = m_new == -INFINITY;  // every key so far masked
-            const float alpha = none ? 1.0f : __expf(m - m_new);
-            uint32_t ph[32];
-            float psum = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-                const float p0 = none ? 0.0f : __expf(sv[c] - m_new), p1 = none ? 0.0f : __expf(sv[c + 1] - m_new);
-                const __half2 hh = __floats2half2_rn(p0, p1);
-                const float2 hf = __half22float2(hh);
-                psum += hf.x + hf.y;  // the normaliser sums the fp16 weights the PV product uses
-                ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+            named_bar_sync(quad_bar, 32 * FA_NQ);
+            const float m_chunk = fmaxf(fmaxf(xmax[st][0][r], xmax[st][1][r]), fmaxf(xmax[st][2][r], xmax[st][3][r]));
+            // all four quarters of a row see the same values, so they take the same decision
+            const bool grow = m_chunk > m_used + FA_RESCALE_LOG2 || (m_used == -INFINITY && m_chunk != -INFINITY);
+            float alpha = 1.0f;
+            if (grow) {
+                alpha = m_used == -INFINITY ? 0.0f : ex2_approx(m_used - m_chunk);
+                m_used = m_chunk;
             }
-            l = l * alpha + psum;
-            // the previous PV product must be done before O is rescaled and P is overwritten
-            if (j >= 1) {
-                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)(j - 1) & 1, abort_flag))) {
+            if (j >= 1 && __any_sync(0xffffffffu, grow)) {
+                // O holds products up to chunk j-1: wait for the last one, then rescale this quarter
+                if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) % NPB], (uint32_t)((j - 1) / NPB) & 1, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                uint32_t v[DQ];
+                o_ld(v);
+                tmem_ld_wait();
 #pragma unroll
-                    for (int g = 0; g < DH / 32; g++) {
-                        uint32_t v[32];
-                        tmem_ld32(trow + 256 + DH * h + 32 * g, v);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-                        tmem_st32(trow + 256 + DH * h + 32 * g, v);
-                    }
-                    tmem_st_wait();
-                }
+                for (int i = 0; i < DQ; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                o_st(v);
+                tmem_st_wait();
             }
+            // every key so far masked: m_used is -inf and so is every score, and 2^(-inf - 0) = 0
+            const float msub = m_used == -INFINITY ? 0.0f : m_used;
+            uint32_t ph[FA_KQ / 2];
+            float ps8[8];
 #pragma unroll
-            for (int c = 0; c < 8; c++)
-                st_chunk16(sP + h * BLK_Q, r, c, ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+            for (int i = 0; i < 8; i++) ps8[i] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < FA_KQ; c += 2) {
+                const float p0 = ex2_approx(sv[c] - msub), p1 = ex2_approx(sv[c + 1] - msub);
+                const __half2 hh = __floats2half2_rn(p0, p1);
+                ps8[(c >> 1) & 7] += p0 + p1;
+                ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+            l = l * alpha + psum;
+            // P buffer j % NPB was last read by the PV product of chunk j - NPB
+            const int pb = j % NPB;
+            if (j >= NPB && !__all_sync(0xffffffffu, mbar_wait(&pv_done[pb], (uint32_t)((j - NPB) / NPB) & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            // keys 32 h .. 32 h + 31: 64-key block h / 2, 16-byte chunks 4 (h & 1) .. 4 (h & 1) + 3
+            uint8_t* pblk = sP + pb * PBYTES + (h >> 1) * BLK_Q;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                st_chunk16(pblk, r, 4 * (h & 1) + c, ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            m = m_new;
+            if (lane == 0) mbar_arrive(&p_full[pb]);
         }
-        if (ok && nch > 0) ok = mbar_wait(pv_done, (uint32_t)(nch - 1) & 1, abort_flag);
+        if (ok && nch > 0) ok = mbar_wait(&pv_done[(nch - 1) % NPB], (uint32_t)((nch - 1) / NPB) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         xsum[h][r] = l;
-        named_bar_sync(1, 32 * FA_SOFTMAX_WARPS);
+        named_bar_sync(quad_bar, 32 * FA_NQ);
         tc_fence_after();
         if (!ok) {
             if (lane == 0) {
@@ -397,26 +480,23 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
         } else {
             // every lane loads its TMEM row (collective); rows past the queries store nothing
-            const float lt = l + xsum[h ^ 1][r];
+            const float lt = (xsum[0][r] + xsum[1][r]) + (xsum[2][r] + xsum[3][r]);
             const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-            float* out = a.dst + (((size_t)seq * a.ne01 + (qvalid ? q : 0)) * a.ne02 + head) * D + DH * h;
+            float* out = a.dst + (((size_t)seq * a.ne01 + (qvalid ? q : 0)) * a.ne02 + head) * D + DQ * h;
+            uint32_t v[DQ];
+            if (nch > 0) {
+                o_ld(v);
+                tmem_ld_wait();
+            } else {
 #pragma unroll
-            for (int g = 0; g < DH / 32; g++) {
-                uint32_t v[32];
-                if (nch > 0) {
-                    tmem_ld32(trow + 256 + DH * h + 32 * g, v);
-                    tmem_ld_wait();
-                } else {
+                for (int i = 0; i < DQ; i++) v[i] = 0u;
+            }
+            if (qvalid) {
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = 0u;
-                }
-                if (qvalid) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(out + 32 * g + i) =
-                            make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
-                                        __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
-                }
+                for (int i = 0; i < DQ; i += 4)
+                    *reinterpret_cast<float4*>(out + i) =
+                        make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
+                                    __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
             }
         }
     }

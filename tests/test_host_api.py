@@ -287,7 +287,7 @@ def test_fattn_decisions_and_geometry():
     for d in (64, 128):
         code, p, _ = cfi.decide(cfi.NAMES["fattn"].format(d=d), "fattn", "all")
         assert code == cfi.SUBSTITUTE and p.key == ("fattn:d%d" % d).encode()
-        assert cfi.map_launch(p, (20, 14, 1), (32, 4, 1), fattn_vals(d)) == ((5, 14, 1), (352, 1, 1))
+        assert cfi.map_launch(p, (20, 14, 1), (32, 4, 1), fattn_vals(d)) == ((5, 14, 1), (608, 1, 1))
     name96 = cfi.NAMES["fattn"].format(d=96)
     assert cfi.decide(name96, "fattn", "all")[0] == cfi.NOT_APPLICABLE
     soft = cfi.NAMES["fattn"].format(d=64).replace("ELb0ELb0EE", "ELb1ELb0EE")
