@@ -1106,7 +1106,39 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return (int)cudaErrorInvalidValue;
     }
-    const uint32_t bn = tile_n(ncols_dst);
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    constexpr uint32_t RAW_BYTES = BM * qmm_raw_row<TY>();
+    // Column tile and ring depths.  Default: tile_n's tile, one CTA per SM with 3-4 A/B stages and
+    // up to 4 raw slots.  When that needs more than one wave, the widest tile of at most 160
+    // columns whose grid fits two CTAs per SM is used instead, with 2-deep rings (about 110 KB of
+    // shared memory, so two CTAs share an SM and hide each other's latencies): Q4_K 8960 x 1536 x
+    // 631, 210 CTAs in 1.4 waves -> 280 in one, measured 45.7 -> 32.5 us.  CFI_QMM_BN (a multiple of
+    // 16, 16..256), CFI_QMM_STAGES and CFI_QMM_RAW (2..4) override.
+    auto env_in = [](const char* n, uint32_t dflt, uint32_t lo, uint32_t hi) {
+        const char* e = getenv(n);
+        const int v = e ? atoi(e) : 0;
+        return (v >= (int)lo && v <= (int)hi && (v % 16 == 0 || hi <= 16)) ? (uint32_t)v : dflt;
+    };
+    const uint32_t rtiles = (nrows + BM - 1) / BM;
+    uint32_t bn = tile_n(ncols_dst), ns_dflt = bn <= 128 ? 4 : 3, raw_dflt = QMM_MAX_RAW;
+    if ((uint64_t)rtiles * ((ncols_dst + bn - 1) / bn) * planes > (uint64_t)sms) {
+        for (uint32_t ct = (ncols_dst + 159) / 160; ct <= (ncols_dst + 63) / 64; ct++) {
+            const uint32_t b2 = ((ncols_dst + ct - 1) / ct + 15) / 16 * 16;
+            const size_t sm2 = 1024 + 2 * (size_t)(A_STAGE + b2 * BK * 2) + 256 + 2 * (size_t)RAW_BYTES;
+            if ((uint64_t)rtiles * ct * planes <= 2 * (uint64_t)sms && sm2 <= QMM_SMEM_LIMIT / 2 - 3 * 1024) {
+                bn = b2;
+                ns_dflt = 2;
+                raw_dflt = 2;
+                break;
+            }
+        }
+    }
+    bn = env_in("CFI_QMM_BN", bn, 16, 256);
     {
         cuuint64_t gdim[3] = {Kt, ncols_dst, planes};
         cuuint64_t gstride[2] = {(cuuint64_t)Kt * 2, (cuuint64_t)Kt * 2 * ncols_dst};
@@ -1119,12 +1151,6 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     bool tma_c = (scd % 4) == 0 && (nch == 1 || scdst % 4 == 0) && (ns == 1 || ssd % 4 == 0) &&
                  (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
     // 3. split K (whole 256-value chunks) when the output tiles fill under half the SMs
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-    }
     const uint32_t ktotal = Kt / BK;
     uint32_t splits = 1, kchunk = (ktotal + 3) / 4 * 4;
     const uint64_t tiles = (uint64_t)((nrows + BM - 1) / BM) * ((ncols_dst + bn - 1) / bn) * planes;
@@ -1166,10 +1192,10 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     // 4. ring depths within the shared-memory limit
-    const uint32_t ns_ring = bn <= 128 ? 4 : 3, b_stage = bn * BK * 2;
-    constexpr uint32_t RAW_BYTES = BM * RAW_ROW;
+    const uint32_t ns_ring = env_in("CFI_QMM_STAGES", ns_dflt, 2, QMM_MAX_NS), b_stage = bn * BK * 2;
     const size_t fixed = 1024 + (size_t)ns_ring * (A_STAGE + b_stage) + 256;
-    const uint32_t nraw = (uint32_t)std::min<size_t>(QMM_MAX_RAW, (QMM_SMEM_LIMIT - fixed) / RAW_BYTES);
+    const uint32_t nraw = std::min<uint32_t>(env_in("CFI_QMM_RAW", raw_dflt, 2, QMM_MAX_RAW),
+                                             (uint32_t)std::min<size_t>(QMM_MAX_RAW, (QMM_SMEM_LIMIT - fixed) / RAW_BYTES));
     if (nraw < 2) return (int)cudaErrorInvalidValue;
     const size_t smem = fixed + (size_t)nraw * RAW_BYTES;
     QmmArgs a;
