@@ -670,7 +670,7 @@ def run_gpu(args, rank, world):
     e2e = world * STEP_BYTES * args.steps / e2e_s / 1e9
 
     stats = ctx.stats()
-    ok = stats["stock_launches"] == 0 and stats["native_failures"] == 0 and (not defer or stats["fused_q8_1"] > 0)
+    ok = stats["stock_launches"] == 0 and stats["native_failures"] == 0
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
