@@ -580,23 +580,26 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
                         st_chunk(atom, r, 4 * hh + c, v0, v1, v2, v3);
                     }
                 }
-            } else {  // Q4_K correction stage: A[r][K + g] = half(-dmin * m_g) (refs.rs:712)
+            } else if constexpr (TY == T_Q4_K) {  // Q4_K correction stage: A[r][K + g] = half(-dmin * m_g) (refs.rs:712)
                 const int g0 = (s - kmain) * BK;
                 const int ngroups = (int)(a.K / 32);
                 const uint32_t row = row0 + r;
                 const uint8_t* rowg = a.x + ((size_t)sx * a.stride_sample_x + (size_t)cx * a.stride_channel_x +
                                              (size_t)min(row, a.nrows - 1) * a.stride_row_x) * Q4_K_BYTES;
-#pragma unroll 1
-                for (int sbl = 4 * hh; sbl < 4 * hh + 4; sbl++) {
+                // the four superblock headers of this thread, all loads issued before any use
+                uint4 hdr[4];
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const int gbase = g0 + 8 * (4 * hh + t);
+                    hdr[t] = (row < a.nrows && gbase < ngroups)
+                                 ? __ldg(reinterpret_cast<const uint4*>(rowg + (size_t)(gbase / 8) * Q4_K_BYTES))
+                                 : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const int sbl = 4 * hh + t;
                     const int gbase = g0 + 8 * sbl;
-                    uint32_t hw0 = 0, hs[3] = {0, 0, 0};
-                    if (row < a.nrows && gbase < ngroups) {
-                        const uint32_t* H = reinterpret_cast<const uint32_t*>(rowg + (size_t)(gbase / 8) * Q4_K_BYTES);
-                        hw0 = __ldg(H);
-                        hs[0] = __ldg(H + 1);
-                        hs[1] = __ldg(H + 2);
-                        hs[2] = __ldg(H + 3);
-                    }
+                    const uint32_t hw0 = hdr[t].x, hs[3] = {hdr[t].y, hdr[t].z, hdr[t].w};
                     const float dmin = __half2float(__ushort_as_half((uint16_t)(hw0 >> 16)));
                     uint32_t v[4];
 #pragma unroll

@@ -82,7 +82,9 @@ CFI_DEV void tmem_tile_tma_store(uint32_t tmem, int warp, int lane, int nwarps, 
             bulk_commit();
         }
     }
-    if (lane == 0) bulk_wait<0>();
+    // the staging buffers must not be reused or released before the engine has read them; the
+    // global writes themselves complete before the grid does
+    if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
 }
 
