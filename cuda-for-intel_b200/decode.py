@@ -74,7 +74,7 @@ class DecodeModel:
         self.cfg = cfg or Config()
         self.dev = device
         self.fused = fused
-        self.row_gemv_below_kb = 16384
+        self.row_gemv_below_kb = 8192
         # fused == 2: which GEMVs also carry their element-wise step (the add + rms_norm ones always)
         self.epi_qkv = self.epi_swiglu = False
         self.g = cfi.GgmlCaller(ctx, "all")
@@ -143,10 +143,11 @@ class DecodeModel:
 
     def step(self, stream):
         """Enqueue one token step on `stream` (a cudaStream_t).  GEMVs over weight matrices under
-        `row_gemv_below_kb` (default 16 MB) take the substitution layer's row kernel
+        `row_gemv_below_kb` (default 8 MB) take the substitution layer's row kernel
         (CFI_MMVQ_STREAM_MIN_KB, set for the duration of the call unless the environment sets it):
         between the short kernels of a decode step it measured faster than the streaming kernel,
-        which still serves the lm_head."""
+        which serves the stacked gate/up matrix (9 MB, its weights fetched before the dependent-launch
+        wait on a const-weights context) and the lm_head."""
         import os
 
         key = "CFI_MMVQ_STREAM_MIN_KB"
