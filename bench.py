@@ -641,108 +641,100 @@ def run_gpu(args, rank, world):
     # ---- end to end: host activations in, outputs back to the host, every step ----
     h2d = sum(xs_host[b].numel() * 4 for b in BATCHES)
     d2h = y_all.numel() * 4
-    ge = []
-    e2e_note = ("host fp32 activations in and fp32 outputs out every step (weights resident), stream "
-                "synchronized per step")
-    if world == 1:
-        # Pipelined as a serving loop would run it: step i's activation copy and output copy run on
-        # copy streams (one per direction) while steps i-1 / i+1 compute, with double-buffered device inputs and
-        # outputs (parity i % 2) and event edges: H2D(i) after step i-2 has read its input buffer,
-        # step i after H2D(i) and after D2H(i-2) has read its output buffer, D2H(i) after step i.
-        # One CUDA graph holds a whole rotation period; the timed region ends when the last output
-        # is on the host.
-        nx = sum(b * K for b in BATCHES)
-        x_host_all = torch.empty(nx, dtype=torch.float32).pin_memory()
-        o = 0
+    # Pipelined as a serving loop would run it: step i's activation copy and output copy run on
+    # copy streams (one per direction) while steps i-1 / i+1 compute, with double-buffered device inputs and
+    # outputs (parity i % 2) and event edges: H2D(i) after step i-2 has read its input buffer,
+    # step i after H2D(i) and after D2H(i-2) has read its output buffer, D2H(i) after step i.
+    # One CUDA graph holds a whole rotation period; the timed region ends when the last output
+    # is on the host.
+    nx = sum(b * K for b in BATCHES)
+    x_host_all = torch.empty(nx, dtype=torch.float32).pin_memory()
+    o = 0
+    for b in BATCHES:
+        x_host_all[o:o + b * K].copy_(xs_host[b].reshape(-1))
+        o += b * K
+    x_dev = [torch.empty(nx, dtype=torch.float32, device=dev) for _ in range(2)]
+    x_views = []
+    for xd in x_dev:
+        vv, o = {}, 0
         for b in BATCHES:
-            x_host_all[o:o + b * K].copy_(xs_host[b].reshape(-1))
+            vv[b] = xd[o:o + b * K]
             o += b * K
-        x_dev = [torch.empty(nx, dtype=torch.float32, device=dev) for _ in range(2)]
-        x_views = []
-        for xd in x_dev:
-            vv, o = {}, 0
-            for b in BATCHES:
-                vv[b] = xd[o:o + b * K]
-                o += b * K
-            x_views.append(vv)
-        y_host = [torch.empty(y_all.numel(), dtype=torch.float32).pin_memory() for _ in range(2)]
-        copy_s = torch.cuda.Stream(device=dev)   # host -> device
-        copy_o = torch.cuda.Stream(device=dev)   # device -> host (the other direction's copy engine)
-        ev_h2d = [torch.cuda.Event() for _ in range(2)]
-        ev_comp = [torch.cuda.Event() for _ in range(2)]
-        ev_d2h = [torch.cuda.Event() for _ in range(2)]
+        x_views.append(vv)
+    y_host = [torch.empty(y_all.numel(), dtype=torch.float32).pin_memory() for _ in range(2)]
+    copy_s = torch.cuda.Stream(device=dev)   # host -> device
+    copy_o = torch.cuda.Stream(device=dev)   # device -> host (the other direction's copy engine)
+    ev_h2d = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_d2h = [torch.cuda.Event() for _ in range(2)]
+    # with N > 1 GPUs: step i's outputs are all-gathered on the comm stream after its kernels;
+    # step i+2 waits for that collective before it rewrites the same output buffer
+    ev_ag = [torch.cuda.Event() for _ in range(2)]
+    gathered2 = [gathered, torch.zeros_like(gathered)] if dist else None
 
-        def capture_e2e(nsteps):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr, stream=stream):
-                cur = torch.cuda.current_stream()
-                fork = torch.cuda.Event()
-                fork.record(cur)
-                copy_s.wait_event(fork)
-                copy_o.wait_event(fork)
-                for i in range(nsteps):
-                    p = i % 2
-                    with torch.cuda.stream(copy_s):
-                        if i >= 2:
-                            copy_s.wait_event(ev_comp[p])
-                        x_dev[p].copy_(x_host_all, non_blocking=True)
-                        ev_h2d[p].record(copy_s)
-                    cur.wait_event(ev_h2d[p])
-                    if i >= 2:
-                        cur.wait_event(ev_d2h[p])
-                    step(i % nphase, cur.cuda_stream, p, xsrc=x_views[p])
-                    ev_comp[p].record(cur)
-                    with torch.cuda.stream(copy_o):
-                        copy_o.wait_event(ev_comp[p])
-                        y_host[p].copy_(y_sets[p], non_blocking=True)
-                        ev_d2h[p].record(copy_o)
-                for cs in (copy_s, copy_o):
-                    join = torch.cuda.Event()
-                    join.record(cs)
-                    cur.wait_event(join)
-            return gr
-
-        ge = [capture_e2e(period)]
-        e_rest = args.steps % period
-        if e_rest:
-            ge.append(capture_e2e(e_rest))
-        with torch.cuda.stream(stream):
-            ge[0].replay()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        with torch.cuda.stream(stream):
-            for _ in range(args.steps // period):
-                ge[0].replay()
-            if e_rest:
-                ge[1].replay()
-        stream.synchronize()
-        e2e_s = time.perf_counter() - t0
-        e2e_note = ("host fp32 activations in (one pinned buffer) and fp32 outputs out (two pinned buffers) every "
-                    "step, weights resident; the copies (one stream per direction) overlap the neighbouring steps' kernels "
-                    "(double-buffered device inputs and outputs, event-ordered), %d steps per CUDA graph, wall clock "
-                    "until the last output is on the host" % period)
-        ge = []
-    for ph in range(nphase if world > 1 else 0):
+    def capture_e2e(nsteps):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr, stream=stream):
-            for b in BATCHES:
-                xs[b].copy_(xs_host[b], non_blocking=True)
-            step(ph, torch.cuda.current_stream().cuda_stream)
-            ys_host.copy_(y_all, non_blocking=True)
-        ge.append(gr)
-    if world > 1:
-        with torch.cuda.stream(stream):
-            for i in range(args.warmup):
-                ge[i % nphase].replay()
-        torch.cuda.synchronize()
+            cur = torch.cuda.current_stream()
+            fork = torch.cuda.Event()
+            fork.record(cur)
+            copy_s.wait_event(fork)
+            copy_o.wait_event(fork)
+            if dist:
+                comm.wait_event(fork)
+            for i in range(nsteps):
+                p = i % 2
+                with torch.cuda.stream(copy_s):
+                    if i >= 2:
+                        copy_s.wait_event(ev_comp[p])
+                    x_dev[p].copy_(x_host_all, non_blocking=True)
+                    ev_h2d[p].record(copy_s)
+                cur.wait_event(ev_h2d[p])
+                if i >= 2:
+                    cur.wait_event(ev_d2h[p])
+                    if dist:
+                        cur.wait_event(ev_ag[p])
+                step(i % nphase, cur.cuda_stream, p, xsrc=x_views[p])
+                ev_comp[p].record(cur)
+                if dist:
+                    comm.wait_event(ev_comp[p])
+                    with torch.cuda.stream(comm):
+                        dist.all_gather_into_tensor(gathered2[p], y_sets[p])
+                    ev_ag[p].record(comm)
+                with torch.cuda.stream(copy_o):
+                    copy_o.wait_event(ev_comp[p])
+                    y_host[p].copy_(y_sets[p], non_blocking=True)
+                    ev_d2h[p].record(copy_o)
+            for cs in (copy_s, copy_o) + ((comm,) if dist else ()):
+                join = torch.cuda.Event()
+                join.record(cs)
+                cur.wait_event(join)
+        return gr
+
+    ge = [capture_e2e(period)]
+    e_rest = args.steps % period
+    if e_rest:
+        ge.append(capture_e2e(e_rest))
+    with torch.cuda.stream(stream):
+        ge[0].replay()
+    torch.cuda.synchronize()
+    if dist:
         dist.barrier()
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            with torch.cuda.stream(stream):
-                ge[i % nphase].replay()
-                dist.all_gather_into_tensor(gathered, y_all)
-            stream.synchronize()
-        e2e_s = time.perf_counter() - t0
+        torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps // period):
+            ge[0].replay()
+        if e_rest:
+            ge[1].replay()
+    stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    e2e_note = ("host fp32 activations in (one pinned buffer) and fp32 outputs out (two pinned buffers) every "
+                "step, weights resident; the copies (one stream per direction) overlap the neighbouring steps' kernels "
+                "(double-buffered device inputs and outputs, event-ordered)%s, %d steps per CUDA graph, wall clock "
+                "until the last output is on the host" % (", outputs all-gathered over NCCL on a third stream" if dist
+                                                           else "", period))
+    ge = []
     if dist:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
