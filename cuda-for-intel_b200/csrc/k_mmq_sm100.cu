@@ -1067,7 +1067,7 @@ template <uint32_t TY>
 int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_t K, uint32_t Kt, uint32_t nrows,
                uint32_t ncols_dst, uint32_t srx, uint32_t ncols_y, uint32_t scd, uint32_t chr, uint32_t nch, uint32_t scx,
                uint32_t scy, uint32_t scdst, uint32_t smr, uint32_t ns, uint32_t ssx, uint32_t ssy, uint32_t ssd,
-               cudaStream_t stream) {
+               cudaStream_t stream, bool may_allocate = true) {
     PFN_encodeTiled enc = encode_fn();
     if (!enc) return (int)cudaErrorNotSupported;
     const char* ep = getenv("CFI_PDL");
@@ -1160,7 +1160,8 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     float* ws = nullptr;
     const uint32_t ld_ws = (nrows + 3) / 4 * 4;
     const char* es = getenv("CFI_GEMM_SPLITK");
-    if (tma_c && !(es && strcmp(es, "0") == 0) && tiles * 2 <= (uint64_t)sms && ktotal >= 16) {
+    // (split K needs a device workspace: never on the allocation-free entry point)
+    if (may_allocate && tma_c && !(es && strcmp(es, "0") == 0) && tiles * 2 <= (uint64_t)sms && ktotal >= 16) {
         uint32_t sp = std::min<uint32_t>((uint32_t)(sms / tiles), ktotal / 8);
         if (sp >= 2) {
             const uint32_t kc = ((ktotal + sp - 1) / sp + 3) / 4 * 4;
@@ -1285,7 +1286,7 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     if (rc) return rc;
     if (fused)
         return launch_qmm<TY>(x, y, dst, xh, K, Kt, nrows, ncols_dst, srx, ncols_y, scd, chr, nch, scx, scy, scdst, smr, ns,
-                              ssx, ssy, ssd, stream);
+                              ssx, ssy, ssd, stream, fixed_xh == nullptr);
     if (!fixed_xh) {
         // 1. activations and weights -> fp16 K-major (one launch), then the shared TMA-fed
         // tcgen05 GEMM (C = Wh Xh^T per plane)

@@ -186,7 +186,9 @@ CFI_API void cfi_ctx_inject(cfi_ctx *ctx, int site, int nth, int code);
  * Every call uses the same array and leaves its contents behind (nothing in it has to start at
  * zero), so two calls whose work overlaps on the GPU -- on different streams without ordering
  * between them -- race on it.  The entry point itself calls no cudaMalloc, cudaFree or other
- * allocating routine.  Returns 0 or a CUDA error code. */
+ * allocating routine; in particular it never splits K (a split-K launch needs a device
+ * workspace), so its results match cfi_subst_launch's whenever that one does not split K and
+ * agree within fp32 summation order otherwise.  Returns 0 or a CUDA error code. */
 #define CFI_MMQ_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
 CFI_API int cfi_mmq_static_scratch(uint32_t ggml_type, void **kernel_params, void *stream, char *why, size_t why_len);
 
