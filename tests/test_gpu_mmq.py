@@ -65,6 +65,7 @@ def test_mmq_matches_the_oracle(dev, ty, shapes):
 @pytest.mark.parametrize("ty,case", [
     (cfi.Q4_K, (1536, 1000, 64, 1, 1, 1)),     # split K, ragged rows
     (cfi.Q4_K, (8960, 300, 200, 1, 1, 1)),     # deep K (split), 200 columns
+    (cfi.Q4_K, (8960, 1536, 64, 1, 1, 1)),     # batch-64 down product: 19 splits, two CTAs per SM
     (cfi.Q4_K, (1536, 260, 631, 1, 1, 1)),     # three column tiles
     (cfi.Q8_0, (1024, 300, 100, 1, 1, 1)),
     (cfi.Q8_0, (2048, 129, 40, 2, 1, 2)),      # channels x samples
