@@ -1215,7 +1215,12 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     // 4. ring depths within the shared-memory limit
-    const uint32_t ns_ring = env_in("CFI_QMM_STAGES", ns_dflt, 2, QMM_MAX_NS), b_stage = bn * BK * 2;
+    const uint32_t b_stage = bn * BK * 2;
+    uint32_t ns_ring = env_in("CFI_QMM_STAGES", ns_dflt, 2, QMM_MAX_NS);
+    // a CFI_QMM_BN wider than the automatic tile may leave no room for two raw slots at the
+    // default depth: give up A/B stages first
+    while (ns_ring > 2 && 1024 + (size_t)ns_ring * (A_STAGE + b_stage) + 256 + 2 * (size_t)RAW_BYTES > QMM_SMEM_LIMIT)
+        ns_ring--;
     const size_t fixed = 1024 + (size_t)ns_ring * (A_STAGE + b_stage) + 256;
     const uint32_t nraw = std::min<uint32_t>(env_in("CFI_QMM_RAW", raw_dflt, 2, QMM_MAX_RAW),
                                              (uint32_t)std::min<size_t>(QMM_MAX_RAW, (QMM_SMEM_LIMIT - fixed) / RAW_BYTES));

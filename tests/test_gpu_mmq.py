@@ -164,3 +164,23 @@ def test_mmq_probe_and_fixup_skip(dev):
     assert after["fixups_skipped"] == before["fixups_skipped"] + 1
     assert after["native_launches"] == before["native_launches"] + 1 and after["stock_launches"] == before["stock_launches"]
     assert O.rel_l2(dd.cpu().numpy(), O.mmq_ref(cfi.Q8_0, p, x, y, n)) < REL_L2
+
+
+@pytest.mark.parametrize("bn", ["192", "256"])
+def test_mmq_forced_tile_width_keeps_two_raw_slots(monkeypatch, bn):
+    """CFI_QMM_BN wider than the automatic tile: the fused kernel gives up A/B ring stages so that
+    two raw weight slots still fit (Q8_0's 34 KB slots at 192 / 256 columns), instead of the
+    launch being refused; a fresh context, so the first-use probe runs under the override too."""
+    monkeypatch.setenv("CFI_QMM_BN", bn)
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    try:
+        for ty in (cfi.Q8_0, cfi.Q4_K):
+            for (ncols_x, nrows, ncols) in ((512, 300, 40), (4864, 896, 200)):
+                p, x, y, n = O.mmq_case(ty, ncols_x, nrows, ncols, 1, 1, 1, 3 + ncols + ty)
+                got = run(g, ty, p, x, y, n)
+                assert O.rel_l2(got, O.mmq_ref(ty, p, x, y, n)) < REL_L2, (ty, ncols_x, nrows, ncols)
+        st = ctx.stats()
+        assert st["native_failures"] == 0 and st["stock_launches"] == 0
+    finally:
+        ctx.close()
