@@ -1160,20 +1160,20 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     float* ws = nullptr;
     const uint32_t ld_ws = (nrows + 3) / 4 * 4;
     const char* es = getenv("CFI_GEMM_SPLITK");
-    // Split-K CTAs per SM: 2 (default) -- down to one 256-value chunk per split, up to two CTAs per
-    // SM on 2-deep rings when those fit in half the shared memory (batch-64 Q4_K products 1536 x
-    // 1536: 14.0 -> 9.6 us, 256 x 1536: 13.5 -> 9.2, 8960 x 1536: 18.8 -> 16.4, 1536 x 8960: 21.8
-    // -> 20.3); 1 -- at least 8 stages per split, at most one CTA per SM.  CFI_QMM_SPLIT_CTAS
-    // overrides.
-    uint32_t per_sm = env_in("CFI_QMM_SPLIT_CTAS", 2, 1, 2);
-    if (per_sm == 2 && 1024 + 2 * (size_t)(A_STAGE + bn * BK * 2) + 256 + 2 * (size_t)RAW_BYTES > QMM_SMEM_LIMIT / 2 - 3 * 1024)
-        per_sm = 1;
+    // Split K in whole 256-value chunks, down to one chunk per split: up to two CTAs per SM on
+    // 2-deep rings when those fit in half the shared memory, else up to one (batch-64 Q4_K products
+    // 1536 x 1536: 14.0 -> 9.6 us, 256 x 1536: 13.5 -> 9.2, 8960 x 1536: 18.8 -> 16.4, 1536 x 8960:
+    // 21.8 -> 20.3; at 631 columns, one CTA per SM, 1536 x 1536: 18.1 -> 16.4, 256 x 1536: 16.2 -> 11.9).
+    // CFI_QMM_SPLIT_CTAS=1 restores the coarser split (at least 8 stages per split, one CTA per SM).
+    const bool fine = env_in("CFI_QMM_SPLIT_CTAS", 2, 1, 2) == 2;
+    const uint32_t per_sm =
+        fine && 1024 + 2 * (size_t)(A_STAGE + bn * BK * 2) + 256 + 2 * (size_t)RAW_BYTES <= QMM_SMEM_LIMIT / 2 - 3 * 1024 ? 2 : 1;
     // (split K needs a device workspace: never on the allocation-free entry point)
     if (may_allocate && tma_c && !(es && strcmp(es, "0") == 0) && tiles * 2 <= (uint64_t)sms && ktotal >= 16) {
         uint32_t sp, kc;
-        if (per_sm == 2) {
+        if (fine) {
             const uint32_t nck = (ktotal + 3) / 4;
-            sp = std::min<uint32_t>((uint32_t)(2 * sms / tiles), nck);
+            sp = std::min<uint32_t>((uint32_t)(per_sm * sms / tiles), nck);
             kc = 4 * ((nck + sp - 1) / sp);
         } else {
             sp = std::min<uint32_t>((uint32_t)(sms / tiles), ktotal / 8);
