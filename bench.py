@@ -5,13 +5,20 @@ Workload: quantize_q8_1 of fp32 activations + Q4_K mul_mat_v
 (quantize, GEMV) pairs.  Metric: GB/s of algorithmic bytes (weights + q8_1 activations + fp32
 outputs + quantizer traffic) against the measured HBM peak.  Weights rotate over enough copies
 that every GEMV reads from HBM (inputs larger than L2).  Kernels are launched through the
-substitution C ABI (cfi_subst_launch with ggml kernelParams) and each step is replayed as a
-CUDA graph.  With --gpus N (torchrun) every rank owns an 8192-row shard of an (8192 N) x 2048
-matrix (weak scaling) and the outputs are all-gathered over NCCL each step (step i gathers
-step i-1's outputs on a second stream while its own kernels run, all inside the step's graph).
+substitution C ABI (cfi_subst_launch with ggml kernelParams); the timed region replays one CUDA
+graph of exactly --steps steps, replayed once before timing.  With --gpus N (torchrun) every rank
+owns an 8192-row shard of an (8192 N) x 2048 matrix (weak scaling) and the outputs are
+all-gathered over NCCL each step (step i gathers step i-1's outputs on a second stream while its
+own kernels run, all inside the graph).  Every N also runs config 5's batch-64 decode step with
+the rows of every matrix split over the ranks and an all-gather of every product's outputs.
+
+Further legs (1 GPU): per-batch GEMV kernel times, large GEMV shapes (65536 x 2048 Q4_K, the
+151936 x 896 Q8_0 lm_head), the row kernels (rms_norm, rope_neox, soft_max, quantize_q8_1),
+config 1, config 3 (prefill mul_mat_q and GemmEx), config 4 decode, config 5 prefill, the prefill
+FlashAttention and the CPU baseline.  --legs selects them.
 
 --impl reference times the CPU evaluation of the same step (the oracle port of the reference's
-host math, row-parallel over every host core) on rank 0.
+host math, built -O3 -march=native on the host, row-parallel over every host core) on rank 0.
 """
 import argparse
 import json
@@ -35,6 +42,7 @@ QUANT_BYTES = lambda b: b * (K * 4 + Q81(1))
 STEP_BYTES = sum(MMVQ_BYTES(b) + QUANT_BYTES(b) for b in BATCHES)
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "Q4_K decode GEMV + quantize_q8_1 throughput (8192x2048, batch 1/2/4/8)"
+ALL_LEGS = ("gemv", "rowops", "prefill", "decode", "config1", "config5", "fattn", "cpu")
 
 
 def peaks():
@@ -119,81 +127,9 @@ def traffic_per_launch(fused=False):
         return None
 
 
-def prefill_gemm(cfi, g, stream, dev, peak_tf):
-    """BASELINE config 3: Q8_0 weights (4864x896 and 896x4864) x 631 tokens quantised to
-    q8_1_mmq, through the native mul_mat_q (tcgen05).  CUDA graph of back-to-back calls."""
-    import torch
-
-    out = {}
-    for m, k in ((4864, 896), (896, 4864)):
-        n = 631
-        w = torch.from_numpy(cfi.synthetic_weights(cfi.Q8_0, m, k, seed=m)).to(dev)
-        xf = torch.from_numpy(np.random.default_rng(k).normal(size=(n, k)).astype(np.float32)).to(dev)
-        q = torch.zeros(k // 128 * n * 144, dtype=torch.uint8, device=dev)
-        d = torch.zeros(n * m, dtype=torch.float32, device=dev)
-        with torch.cuda.stream(stream):
-            g.quantize_mmq(0, xf.data_ptr(), q.data_ptr(), k, k, n, stream=stream.cuda_stream)
-            g.mmq(cfi.Q8_0, w.data_ptr(), q.data_ptr(), d.data_ptr(), k, m, n, stream=stream.cuda_stream)
-        torch.cuda.synchronize()
-        reps, calls = 5, 20
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            for _ in range(calls):
-                g.mmq(cfi.Q8_0, w.data_ptr(), q.data_ptr(), d.data_ptr(), k, m, n,
-                      stream=torch.cuda.current_stream().cuda_stream)
-        with torch.cuda.stream(stream):
-            gr.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(reps):
-                gr.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
-        out["%dx%dx%d" % (m, k, n)] = {"us": round(us, 2), "tflops": round(2.0 * m * n * k / us / 1e6, 1)}
-        del gr
-    # the cuBLAS-compatible GemmEx path on the same shapes (ggml's T,N f16 -> f32 call)
-    blas = cfi.Blas(stream.cuda_stream)
-    gemm = {}
-    for m, k in ((4864, 896), (896, 4864)):
-        n = 631
-        A = torch.randn(m, k, device=dev).half()
-        B = torch.randn(n, k, device=dev).half()
-        C = torch.zeros(n, m, device=dev)
-        def call(st):
-            blas.set_stream(st)
-            blas.gemm_ex(1, 0, m, n, k, 1.0, A.data_ptr(), 2, k, B.data_ptr(), 2, k, 0.0, C.data_ptr(), 0, m)
-        with torch.cuda.stream(stream):
-            call(stream.cuda_stream)
-        torch.cuda.synchronize()
-        reps, calls = 5, 20
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            for _ in range(calls):
-                call(torch.cuda.current_stream().cuda_stream)
-        with torch.cuda.stream(stream):
-            gr.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(reps):
-                gr.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
-        gemm["%dx%dx%d" % (m, n, k)] = {"us": round(us, 2), "tflops": round(2.0 * m * n * k / us / 1e6, 1),
-                                         "path": "tcgen05" if blas.last_path() == 1 else "simt"}
-        del gr
-    blas.close()
-    best = max(v["tflops"] for v in out.values())
-    return {"workload": "config3: Q8_0 W x 631 q8_1_mmq tokens -> f32 (mul_mat_q on tcgen05, incl. activation pre-pass)",
-            "shapes": out, "gemm_ex_f16": gemm,
-            "roofline": {"bound": "tensor", "achieved": best, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": round(best / peak_tf, 4), "peak_kind": "measured bf16 dense (burst)"}}
-
-
 def graph_time_us(stream, body, reps=5, calls=1):
-    """Capture `calls` x body(stream_handle) in one CUDA graph; mean device time per body call (µs)
-    over `reps` replays after one warm replay, CUDA events on the launching stream."""
+    """Capture `calls` x body(i, stream_handle) in one CUDA graph; mean device time per body call
+    (µs) over `reps` replays after one warm replay, CUDA events on the launching stream."""
     import torch
 
     gr = torch.cuda.CUDAGraph()
@@ -213,6 +149,173 @@ def graph_time_us(stream, body, reps=5, calls=1):
     return us
 
 
+def rotated(torch, dev, host_bytes, min_total):
+    """Copies of one weight matrix on the device, enough that they exceed `min_total` bytes."""
+    n = max(2, int(np.ceil(min_total / host_bytes.size)))
+    wd = torch.empty((n, host_bytes.size), dtype=torch.uint8, device=dev)
+    wd[0].copy_(torch.from_numpy(np.ascontiguousarray(host_bytes).ravel()))
+    for i in range(1, n):
+        wd[i].copy_(wd[0])
+    return wd
+
+
+def prefill_gemm(cfi, g, stream, dev, peak_tf):
+    """BASELINE config 3: Q8_0 weights (4864x896 and 896x4864) x 631 tokens quantised to
+    q8_1_mmq, through the native mul_mat_q (tcgen05), plus the reference's own mmq throughput shape
+    4096x4096x512 (Q8_0 and Q4_K) and the cuBLAS-compatible GemmEx path on config 3's shapes.
+    CUDA graph of back-to-back calls.  Flat keys: <type>_<rows>x<k>x<cols>_us / _tflops."""
+    import torch
+
+    out = {}
+    for ty, m, k, n in ((cfi.Q8_0, 4864, 896, 631), (cfi.Q8_0, 896, 4864, 631), (cfi.Q8_0, 4096, 4096, 512),
+                        (cfi.Q4_K, 4096, 4096, 512)):
+        w = torch.from_numpy(cfi.synthetic_weights(ty, m, k, seed=m).ravel()).to(dev)
+        xf = torch.from_numpy(np.random.default_rng(k).normal(size=(n, k)).astype(np.float32)).to(dev)
+        q = torch.zeros(k // 128 * n * 144, dtype=torch.uint8, device=dev)
+        d = torch.zeros(n * m, dtype=torch.float32, device=dev)
+        ds4 = 1 if ty == cfi.Q4_K else 0
+        torch.cuda.synchronize()  # inputs written on torch's stream, used on `stream`
+        with torch.cuda.stream(stream):
+            g.quantize_mmq(ds4, xf.data_ptr(), q.data_ptr(), k, k, n, stream=stream.cuda_stream)
+            g.mmq(ty, w.data_ptr(), q.data_ptr(), d.data_ptr(), k, m, n, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        us = graph_time_us(stream, lambda i, st: g.mmq(ty, w.data_ptr(), q.data_ptr(), d.data_ptr(), k, m, n,
+                                                        stream=st), reps=5, calls=20)
+        tag = "%s_%dx%dx%d" % ("q8_0" if ty == cfi.Q8_0 else "q4_k", m, k, n)
+        out[tag + "_us"] = round(us, 2)
+        out[tag + "_tflops"] = round(2.0 * m * n * k / us / 1e6, 1)
+    # the cuBLAS-compatible GemmEx path on the same shapes (ggml's T,N f16 -> f32 call)
+    blas = cfi.Blas(stream.cuda_stream)
+    for m, k in ((4864, 896), (896, 4864)):
+        n = 631
+        A = torch.randn(m, k, device=dev).half()
+        B = torch.randn(n, k, device=dev).half()
+        Cm = torch.zeros(n, m, device=dev)
+        torch.cuda.synchronize()
+
+        def call(i, st):
+            blas.set_stream(st)
+            blas.gemm_ex(1, 0, m, n, k, 1.0, A.data_ptr(), 2, k, B.data_ptr(), 2, k, 0.0, Cm.data_ptr(), 0, m)
+        with torch.cuda.stream(stream):
+            call(0, stream.cuda_stream)
+        torch.cuda.synchronize()
+        us = graph_time_us(stream, call, reps=5, calls=20)
+        tag = "gemm_ex_f16_%dx%dx%d" % (m, n, k)
+        out[tag + "_us"] = round(us, 2)
+        out[tag + "_tflops"] = round(2.0 * m * n * k / us / 1e6, 1)
+        out[tag + "_path"] = "tcgen05" if blas.last_path() == 1 else "simt"
+    blas.close()
+    c3 = max(out["q8_0_4864x896x631_tflops"], out["q8_0_896x4864x631_tflops"])
+    return {"workload": "config3: Q8_0 W x 631 q8_1_mmq tokens -> f32 (mul_mat_q on tcgen05, incl. activation "
+                        "pre-pass); also 4096x4096x512",
+            "config3_best_tflops": c3, "config3_frac": round(c3 / peak_tf, 4),
+            "peak_tflops": peak_tf, "peak_kind": "measured bf16 dense (burst)", **out}
+
+
+def gemv_legs(cfi, g, stream, dev, peak):
+    """Q4_K mul_mat_vec_q 8192x2048 at batch 1/2/4/8 on their own, and the large shapes (65536 x
+    2048 Q4_K, the 151936 x 896 Q8_0 lm_head) at batch 1: graphs of back-to-back launches over
+    rotated weight copies (> 3x L2), on a context that fetches weights before the dependent-launch
+    wait.  µs per launch and the fraction of HBM of the algorithmic bytes."""
+    import torch
+
+    out = {}
+    for ty, rows, k, batches, tag in ((cfi.Q4_K, ROWS, K, BATCHES, "q4k_8192x2048"),
+                                      (cfi.Q4_K, 65536, 2048, (1, 8), "q4k_65536x2048"),
+                                      (cfi.Q8_0, 151936, 896, (1,), "q8_0_151936x896")):
+        w = cfi.synthetic_weights(ty, rows, k, seed=rows)
+        wd = rotated(torch, dev, w, 3 * L2_BYTES)
+        ncopy = wd.shape[0]
+        for b in batches:
+            x = torch.from_numpy(np.random.default_rng(b).normal(size=(b, k)).astype(np.float32)).to(dev)
+            q = torch.zeros(b * k // 32 * 36, dtype=torch.uint8, device=dev)
+            y = torch.zeros(b * rows, dtype=torch.float32, device=dev)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                g.quantize_q8_1(x.data_ptr(), q.data_ptr(), k, k, b, stream=stream.cuda_stream)
+                g.mmvq(ty, b, wd[0].data_ptr(), q.data_ptr(), y.data_ptr(), k, rows, stream=stream.cuda_stream)
+            torch.cuda.synchronize()
+            calls = max(ncopy, 8)
+            us = graph_time_us(stream, lambda i, st: g.mmvq(ty, b, wd[i % ncopy].data_ptr(), q.data_ptr(), y.data_ptr(),
+                                                            k, rows, stream=st), reps=5, calls=calls)
+            byts = w.size + b * (k // 32 * 36 + rows * 4)
+            out["%s_b%d_us" % (tag, b)] = round(us, 3)
+            out["%s_b%d_frac" % (tag, b)] = round(byts / us / 1e3 / peak, 4)
+        del wd
+    return out
+
+
+def rowops_bench(cfi, g, stream, dev, peak):
+    """The row kernels at the decode shapes of configs 4/5 (µs per launch: one row or one token, the
+    reference's profiled launches) and at a batched shape that streams from HBM (GB/s of
+    read + write bytes, inputs rotated over > 2x L2): rms_norm_f32 with the weight multiply (rows of
+    896 and 1536), rope_neox (14 heads x 64 and 12 heads x 128, theta 1e6), soft_max_f32 (rows of
+    632 keys with an f32 mask, 14 heads), quantize_q8_1 (896 / 1536 values)."""
+    import torch
+
+    out = {}
+
+    def timed(fn, nbuf):
+        torch.cuda.synchronize()  # inputs written on torch's stream, used on `stream`
+        with torch.cuda.stream(stream):
+            fn(0, stream.cuda_stream)
+        torch.cuda.synchronize()
+        return graph_time_us(stream, lambda i, st: fn(i % nbuf, st), reps=5, calls=max(nbuf, 32))
+
+    for ncols in (896, 1536):
+        wv = torch.randn(ncols, device=dev)
+        for nrows, tag in ((1, "dec"), (16384, "big")):
+            nbuf = 1 if nrows == 1 else max(2, int(np.ceil(2 * L2_BYTES / (nrows * ncols * 8))))
+            xs = torch.randn(nbuf, nrows * ncols, device=dev)
+            ys = torch.zeros_like(xs)
+            us = timed(lambda i, st: g.rms_norm(xs[i].data_ptr(), ys[i].data_ptr(), ncols, nrows, mul=wv.data_ptr(),
+                                                stream=st), nbuf)
+            out["rms_norm_%d_%s_us" % (ncols, tag)] = round(us, 3)
+            if nrows > 1:
+                byts = nrows * ncols * 8 + ncols * 4
+                out["rms_norm_%d_big_gbs" % ncols] = round(byts / us / 1e3, 1)
+                out["rms_norm_%d_big_frac" % ncols] = round(byts / us / 1e3 / peak, 4)
+    for nh, hd in ((14, 64), (12, 128)):
+        for ntok, tag in ((1, "dec"), (4096, "big")):
+            n = nh * hd * ntok
+            nbuf = 1 if ntok == 1 else max(2, int(np.ceil(2 * L2_BYTES / (n * 8))))
+            xs = torch.randn(nbuf, n, device=dev)
+            ys = torch.zeros_like(xs)
+            pos = torch.arange(ntok, dtype=torch.int32, device=dev) + 631
+            us = timed(lambda i, st: g.rope_neox(xs[i].data_ptr(), ys[i].data_ptr(), hd, nh, ntok, hd, pos.data_ptr(),
+                                                 stream=st), nbuf)
+            out["rope_%dx%d_%s_us" % (nh, hd, tag)] = round(us, 3)
+            if ntok > 1:
+                byts = n * 8 + ntok * 4
+                out["rope_%dx%d_big_gbs" % (nh, hd)] = round(byts / us / 1e3, 1)
+                out["rope_%dx%d_big_frac" % (nh, hd)] = round(byts / us / 1e3 / peak, 4)
+    ncols, nh = 632, 14
+    for ne01, tag in ((1, "dec"), (631 * 8, "big")):
+        nbuf = 1 if ne01 == 1 else max(2, int(np.ceil(2 * L2_BYTES / (ne01 * nh * ncols * 8))))
+        xs = torch.randn(nbuf, ne01 * nh * ncols, device=dev)
+        ys = torch.zeros_like(xs)
+        mask = torch.zeros(ne01 * ncols, device=dev)
+        us = timed(lambda i, st: g.soft_max(xs[i].data_ptr(), mask.data_ptr(), ys[i].data_ptr(), ncols, ne01, nh, 0.125,
+                                            stream=st), nbuf)
+        out["soft_max_%s_us" % tag] = round(us, 3)
+        if ne01 > 1:
+            byts = ne01 * nh * ncols * 8 + ne01 * ncols * 4
+            out["soft_max_big_gbs"] = round(byts / us / 1e3, 1)
+            out["soft_max_big_frac"] = round(byts / us / 1e3 / peak, 4)
+    for k in (896, 1536):
+        for ncol, tag in ((1, "dec"), (16384, "big")):
+            nbuf = 1 if ncol == 1 else max(2, int(np.ceil(2 * L2_BYTES / (ncol * k * 5))))
+            xs = torch.randn(nbuf, ncol * k, device=dev)
+            qs = torch.zeros(nbuf, ncol * k // 32 * 36, dtype=torch.uint8, device=dev)
+            us = timed(lambda i, st: g.quantize_q8_1(xs[i].data_ptr(), qs[i].data_ptr(), k, k, ncol, stream=st), nbuf)
+            out["quantize_q8_1_%d_%s_us" % (k, tag)] = round(us, 3)
+            if ncol > 1:
+                byts = ncol * k * 4 + ncol * k // 32 * 36
+                out["quantize_q8_1_%d_big_gbs" % k] = round(byts / us / 1e3, 1)
+                out["quantize_q8_1_%d_big_frac" % k] = round(byts / us / 1e3 / peak, 4)
+    return out
+
+
 def config1_bench(cfi, g, stream, dev, peak, gf=None):
     """Q8_0 mul_mat_vec_q 4864x896 on its own (batch 1), and with its
     quantize_q8_1 in front, back to back over rotated weight copies (> 3x L2)."""
@@ -220,13 +323,12 @@ def config1_bench(cfi, g, stream, dev, peak, gf=None):
 
     rows, k = 4864, 896
     wb = rows * k // 32 * 34
-    ncopy = int(np.ceil(3 * L2_BYTES / wb))
-    w = torch.from_numpy(cfi.synthetic_weights(cfi.Q8_0, rows, k, seed=11).ravel()).to(dev)
-    wd = torch.empty((ncopy, w.numel()), dtype=torch.uint8, device=dev)
-    wd[:] = w
+    wd = rotated(torch, dev, cfi.synthetic_weights(cfi.Q8_0, rows, k, seed=11), 3 * L2_BYTES)
+    ncopy = wd.shape[0]
     x = torch.from_numpy(np.random.default_rng(3).normal(size=k).astype(np.float32)).to(dev)
     q = torch.zeros(k // 32 * 36, dtype=torch.uint8, device=dev)
     y = torch.zeros(rows, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         g.quantize_q8_1(x.data_ptr(), q.data_ptr(), k, k, 1, stream=stream.cuda_stream)
         g.mmvq(cfi.Q8_0, 1, wd[0].data_ptr(), q.data_ptr(), y.data_ptr(), k, rows, stream=stream.cuda_stream)
@@ -259,81 +361,214 @@ def config1_bench(cfi, g, stream, dev, peak, gf=None):
             "bytes_per_call": mbytes}
 
 
-def config5_bench(cfi, g, stream, dev, peak_gbs, peak_tf):
-    """Qwen2.5-1.5B-architecture weight products, 28 layers of Q4_K matrices
-    (q, o 1536x1536; k, v 256x1536; gate, up 8960x1536; down 1536x8960) and the Q8_0 head
-    151936x1536: (a) a 631-token prefill -- per layer the activations quantised to q8_1_mmq once
-    per distinct input (attention input, attention output, FFN input, FFN hidden) and the seven
-    mul_mat_q products; the head on the last token only (quantize_q8_1 + mul_mat_vec_q), as ggml
-    does; (b) one batch-64 decode step of 64 independent sequences -- the same products with 64
-    columns (mul_mat_q, as ggml uses above 8 columns), the head included.  Attention and the
-    element-wise ops are not in this leg.  Weights random, device-side (seeded)."""
+C5_H, C5_F, C5_KV, C5_L, C5_V = 1536, 8960, 256, 28, 151936
+C5_SHAPES = {"q": (C5_H, C5_H), "k": (C5_KV, C5_H), "v": (C5_KV, C5_H), "o": (C5_H, C5_H), "g": (C5_F, C5_H),
+             "u": (C5_F, C5_H), "d": (C5_H, C5_F)}
+# products grouped by the activation they read, in model order: each group's input depends on the
+# previous group's outputs (attention input -> q, k, v; attention output -> o; FFN input -> gate,
+# up; FFN hidden -> down; the next layer's attention input)
+C5_GROUPS = ((("q", "k", "v"), C5_H), (("o",), C5_H), (("g", "u"), C5_H), (("d",), C5_F))
+
+
+def config5_prefill(cfi, g, stream, dev, peak_tf):
+    """BASELINE config 5 prefill: Qwen2.5-1.5B-architecture weight products, 28 layers of Q4_K
+    matrices (q, o 1536x1536; k, v 256x1536; gate, up 8960x1536; down 1536x8960) and the Q8_0 head
+    151936x1536, over a 631-token prompt: per layer the activations quantised to q8_1_mmq once per
+    distinct input and the seven mul_mat_q products; the head on the last token only
+    (quantize_q8_1 + mul_mat_vec_q), as ggml does.  Attention and the element-wise ops are not in
+    this leg.  Weights random, device-side (seeded)."""
     import torch
 
     from decode import random_q4_k, random_q8_0
 
-    H, F, KV, L, V = 1536, 8960, 256, 28, 151936
+    H, F, L, V = C5_H, C5_F, C5_L, C5_V
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
-    shapes = {"q": (H, H), "k": (KV, H), "v": (KV, H), "o": (H, H), "g": (F, H), "u": (F, H), "d": (H, F)}
-    layers = [{n: random_q4_k(torch, r, c, gen, dev) for n, (r, c) in shapes.items()} for _ in range(L)]
+    layers = [{nm: random_q4_k(torch, r, c, gen, dev) for nm, (r, c) in C5_SHAPES.items()} for _ in range(L)]
     head = random_q8_0(torch, V, H, gen, dev)
-    wbytes = sum(t.numel() for lay in layers for t in lay.values()) + head.numel()
-    params = L * sum(r * c for r, c in shapes.values())
-
-    def buffers(n):
-        xf = {kk: torch.randn(n * kk, generator=gen, device=dev) for kk in (H, F)}
-        xq = {kk: torch.zeros(kk // 128 * n * 144, dtype=torch.uint8, device=dev) for kk in (H, F)}
-        out = {nm: torch.zeros(n * r, dtype=torch.float32, device=dev) for nm, (r, c) in shapes.items()}
-        return xf, xq, out
-
-    def layer_products(n, xf, xq, out, st):
-        for lay in layers:
-            for inputs, k in ((("q", "k", "v"), H), (("o",), H), (("g", "u"), H), (("d",), F)):
-                g.quantize_mmq(1, xf[k].data_ptr(), xq[k].data_ptr(), k, k, n, stream=st)
-                for nm in inputs:
-                    r = shapes[nm][0]
-                    g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, r, n, stream=st)
-
-    # (a) prefill, 631 tokens
+    params = L * sum(r * c for r, c in C5_SHAPES.values())
     n = 631
-    xf, xq, out = buffers(n)
+    xf = {kk: torch.randn(n * kk, generator=gen, device=dev) for kk in (H, F)}
+    xq = {kk: torch.zeros(kk // 128 * n * 144, dtype=torch.uint8, device=dev) for kk in (H, F)}
+    out = {nm: torch.zeros(n * r, dtype=torch.float32, device=dev) for nm, (r, c) in C5_SHAPES.items()}
     hq = torch.zeros(H // 32 * 36, dtype=torch.uint8, device=dev)
     logits = torch.zeros(V, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
 
     def prefill(i, st):
-        layer_products(n, xf, xq, out, st)
+        for lay in layers:
+            for inputs, k in C5_GROUPS:
+                g.quantize_mmq(1, xf[k].data_ptr(), xq[k].data_ptr(), k, k, n, stream=st)
+                for nm in inputs:
+                    g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, C5_SHAPES[nm][0], n,
+                          stream=st)
         g.quantize_q8_1(xf[H].data_ptr() + (n - 1) * H * 4, hq.data_ptr(), H, H, 1, stream=st)
         g.mmvq(cfi.Q8_0, 1, head.data_ptr(), hq.data_ptr(), logits.data_ptr(), H, V, stream=st)
     with torch.cuda.stream(stream):
         prefill(0, stream.cuda_stream)
     torch.cuda.synchronize()
-    us_pf = graph_time_us(stream, prefill, reps=3)
-    pf_ops = 2.0 * params * n + 2.0 * V * H
-    # (b) batch-64 decode step
-    n = 64
-    xf, xq, out = buffers(n)
-    hq64 = torch.zeros(H // 128 * n * 144, dtype=torch.uint8, device=dev)
-    logits64 = torch.zeros(n * V, dtype=torch.float32, device=dev)
-
-    def decode64(i, st):
-        layer_products(n, xf, xq, out, st)
-        g.quantize_mmq(0, xf[H].data_ptr(), hq64.data_ptr(), H, H, n, stream=st)
-        g.mmq(cfi.Q8_0, head.data_ptr(), hq64.data_ptr(), logits64.data_ptr(), H, V, n, stream=st)
-    with torch.cuda.stream(stream):
-        decode64(0, stream.cuda_stream)
-    torch.cuda.synchronize()
-    us_dc = graph_time_us(stream, decode64, reps=5)
-    launches = L * (4 + 7) + 2
-    res = {"workload": "config5: Qwen2.5-1.5B-architecture weight products (28 layers Q4_K + Q8_0 head, %d B of "
-                       "weights), 631-token prefill and a batch-64 decode step; attention not included" % wbytes,
-           "prefill": {"ms": round(us_pf / 1e3, 3), "tok_per_s": round(631 / (us_pf * 1e-6), 1),
-                       "tflops": round(pf_ops / us_pf / 1e6, 1), "frac": round(pf_ops / us_pf / 1e6 / peak_tf, 4),
-                       "launches": launches},
-           "decode_b64": {"ms": round(us_dc / 1e3, 3), "tok_per_s": round(64 / (us_dc * 1e-6), 1),
-                          "weights_gbs": round(wbytes / us_dc / 1e3, 1),
-                          "frac": round(wbytes / us_dc / 1e3 / peak_gbs, 4), "launches": launches}}
+    us = graph_time_us(stream, prefill, reps=3)
+    ops = 2.0 * params * n + 2.0 * V * H
     del layers, head
+    return {"ms": round(us / 1e3, 3), "tok_per_s": round(631 / (us * 1e-6), 1), "tflops": round(ops / us / 1e6, 1),
+            "frac": round(ops / us / 1e6 / peak_tf, 4), "launches": L * (4 + 7) + 2}
+
+
+def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
+    """BASELINE config 5 decode: one batch-64 step (64 independent sequences) over the 28 Q4_K
+    layers and the Q8_0 head, the rows of every matrix split over the `world` ranks
+    (shard.row_split, weak in memory, strong in work).  Per product: quantize_q8_1_mmq of its input
+    (once per group), the native mul_mat_q on the rank's rows, and with N > 1 an NCCL all-gather of
+    the 64-column outputs on a comm stream followed by cfi_glue_gather_row_shards into ggml's
+    column-major dst.  A group's quantize waits for the previous group's gathers (its input is
+    computed from them in a real model), so collective latency is exposed as it would be.
+    Reported: the step time, the same step without collectives (kernels only), the collectives
+    alone, and a check of rank 0's gathered logits against the unsharded head product on rank 0."""
+    import torch
+
+    import shard
+    from decode import random_q4_k, random_q8_0
+
+    H, F, L, V, n = C5_H, C5_F, C5_L, C5_V, 64
+    L_ = cfi.lib()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+
+    def rows_of(full, rows, sh):
+        return full.view(rows, -1)[sh.row0:sh.row0 + sh.rows].contiguous().view(-1)
+
+    sh = {nm: shard.row_split(r, world, rank) for nm, (r, c) in C5_SHAPES.items()}
+    sh["head"] = shard.row_split(V, world, rank)
+    layers = []
+    for _ in range(L):
+        lay = {}
+        for nm, (r, c) in C5_SHAPES.items():
+            lay[nm] = rows_of(random_q4_k(torch, r, c, gen, dev), r, sh[nm])  # the same draws on every rank
+        layers.append(lay)
+    head_full = random_q8_0(torch, V, H, gen, dev)
+    head = rows_of(head_full, V, sh["head"])
+    if rank != 0:
+        del head_full
+        head_full = None
+    wbytes = L * sum(r * c // 256 * 144 for r, c in C5_SHAPES.values()) + V * H // 32 * 34
+    xf = {kk: torch.randn(n * kk, generator=gen, device=dev) for kk in (H, F)}
+    xq = {kk: torch.zeros(kk // 128 * n * 144, dtype=torch.uint8, device=dev) for kk in (H, F)}
+    hq = torch.zeros(H // 128 * n * 144, dtype=torch.uint8, device=dev)
+    names = list(C5_SHAPES) + ["head"]
+    nrows = {**{nm: r for nm, (r, c) in C5_SHAPES.items()}, "head": V}
+    out = {nm: torch.zeros(n * sh[nm].rows_padded, dtype=torch.float32, device=dev) for nm in names}
+    gath = {nm: torch.zeros(world * n * sh[nm].rows_padded, dtype=torch.float32, device=dev) for nm in names} \
+        if world > 1 else None
+    full = {nm: torch.zeros(n * nrows[nm], dtype=torch.float32, device=dev) for nm in names} if world > 1 else None
+
+    def gathers(cur, nms):
+        """all-gather + assembly of the named outputs on the comm stream after `cur`'s work so far;
+        returns the event that marks their completion."""
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        comm.wait_event(ev)
+        with torch.cuda.stream(comm):
+            for nm in nms:
+                dist.all_gather_into_tensor(gath[nm], out[nm])
+                rc = L_.cfi_glue_gather_row_shards(gath[nm].data_ptr(), full[nm].data_ptr(), nrows[nm], n, world,
+                                                   comm.cuda_stream)
+                assert rc == 0, rc
+        done = torch.cuda.Event()
+        done.record(comm)
+        return done
+
+    def step(kernels=True, collectives=True):
+        cur = torch.cuda.current_stream()
+        st = cur.cuda_stream
+        coll = collectives and world > 1
+        prev = None
+        if coll:
+            fork = torch.cuda.Event()
+            fork.record(cur)
+            comm.wait_event(fork)
+        for lay in layers:
+            for inputs, k in C5_GROUPS:
+                if kernels:
+                    if prev is not None:
+                        cur.wait_event(prev)
+                    g.quantize_mmq(1, xf[k].data_ptr(), xq[k].data_ptr(), k, k, n, stream=st)
+                    for nm in inputs:
+                        g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, sh[nm].rows, n,
+                              stream=st, stride_col_dst=sh[nm].rows_padded)
+                if coll:
+                    prev = gathers(cur, inputs)
+        if kernels:
+            if prev is not None:
+                cur.wait_event(prev)
+            g.quantize_mmq(0, xf[H].data_ptr(), hq.data_ptr(), H, H, n, stream=st)
+            g.mmq(cfi.Q8_0, head.data_ptr(), hq.data_ptr(), out["head"].data_ptr(), H, sh["head"].rows, n, stream=st,
+                  stride_col_dst=sh["head"].rows_padded)
+        if coll:
+            prev = gathers(cur, ["head"])
+            cur.wait_event(prev)
+
+    def timed(**kw):
+        torch.cuda.synchronize()  # inputs written on torch's stream, used on `stream`
+        with torch.cuda.stream(stream):
+            step(**kw)  # first use (probes) outside the capture
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step(**kw)
+        with torch.cuda.stream(stream):
+            gr.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        reps = 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        del gr
+        return ms
+
+    ms_step = timed()
+    ms_kern = timed(collectives=False) if world > 1 else ms_step
+    ms_coll = timed(kernels=False) if world > 1 else 0.0
+    # check: rank 0's gathered logits against the unsharded head product on rank 0
+    check = {}
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    if rank == 0:
+        got = (full["head"] if world > 1 else out["head"]).view(n, V)
+        ref = torch.zeros(n * V, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            g.quantize_mmq(0, xf[H].data_ptr(), hq.data_ptr(), H, H, n, stream=stream.cuda_stream)
+            g.mmq(cfi.Q8_0, head_full.data_ptr(), hq.data_ptr(), ref.data_ptr(), H, V, n, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        ref = ref.view(n, V)
+        diff = (got.double() - ref.double()).norm() / ref.double().norm()
+        check = {"logits_bitwise_equal": bool(torch.equal(got, ref)), "logits_rel_l2": float(diff),
+                 "logits_nonfinite": int((~torch.isfinite(got)).sum()), "ref_nonfinite": int((~torch.isfinite(ref)).sum())}
+    if dist:
+        dist.barrier()
+    launches = L * (4 + 7) + 2 + (L * 7 + 1 if world > 1 else 0)
+    res = {"ms": round(ms_step, 4), "tok_per_s": round(64 / (ms_step * 1e-3), 1),
+           "weights_gbs": round(wbytes / ms_step / 1e6, 1),
+           "frac": round(wbytes / ms_step / 1e6 / (peak_gbs * world), 4),
+           "kernels_only_ms": round(ms_kern, 4), "collectives_only_ms": round(ms_coll, 4),
+           "all_gathers_per_step": (L * 7 + 1) if world > 1 else 0,
+           "gathered_bytes_per_gpu": (world - 1) * n * 4 * (L * sum(sh[nm].rows_padded for nm in C5_SHAPES) +
+                                                            sh["head"].rows_padded),
+           "launches": launches, "gpus": world, **check}
+    del layers, head, head_full, out, gath, full
     return res
 
 
@@ -356,6 +591,7 @@ def fattn_bench(cfi, g, stream, dev, peak_tf):
         j = torch.arange(nkv, device=dev)[None, :]
         mask = torch.where(j <= i, 0.0, float("-inf")).half().contiguous()
         dst = torch.zeros(nq * nh * d, device=dev)
+        torch.cuda.synchronize()
         call = lambda n, st: g.fattn(d, q.data_ptr(), k.data_ptr(), v.data_ptr(), mask.data_ptr(), dst.data_ptr(), nq,
                                      nh, nhk, nkv, 1, 1.0 / d ** 0.5, stream=st)
         with torch.cuda.stream(stream):
@@ -363,10 +599,11 @@ def fattn_bench(cfi, g, stream, dev, peak_tf):
         torch.cuda.synchronize()
         us = graph_time_us(stream, call, reps=5, calls=20)
         fl = 4.0 * nq * nkv * d * nh
-        out["d%d_h%d" % (d, nh)] = {"us": round(us, 2), "tflops": round(fl / us / 1e6, 1),
-                                   "frac": round(fl / us / 1e6 / peak_tf, 4)}
+        out["d%d_h%d_us" % (d, nh)] = round(us, 2)
+        out["d%d_h%d_tflops" % (d, nh)] = round(fl / us / 1e6, 1)
+        out["d%d_h%d_frac" % (d, nh)] = round(fl / us / 1e6 / peak_tf, 4)
     return {"workload": "flash_attn_ext_f16, 631 queries x 640 keys, causal mask (configs 4 / 5 prefill attention)",
-            "shapes": out}
+            **out}
 
 
 def decode_bench(stream, dev, ntok=48, warm=3, fused=False, defer=False, const_weights=False):
@@ -412,30 +649,23 @@ def decode_bench(stream, dev, ntok=48, warm=3, fused=False, defer=False, const_w
     ms = e0.elapsed_time(e1)
     assert int(m.pos.item()) == m.cfg.prompt + ntok and cfi.lib().cfi_device_error() == 0
     bpt = m.cfg.weight_bytes_per_token()
-    out = {"workload": "config4: Qwen2.5-0.5B-architecture decode, 24 layers, Q8_0 random weights, 631-token seeded "
-                       "KV cache, %d greedy tokens, one CUDA graph per token%s"
-                       % (ntok, {0: "; ggml's kernel sequence through the substitution ABI",
-                                 1: "; stacked QKV / gate-up weights and fused glue kernels",
-                                 2: "; stacked weights, element-wise steps in the GEMVs' last CTAs"}[int(fused)]
-                          + ("; quantize_q8_1 held back into the GEMVs (CFI_CTX_DEFER_Q8_1)" if defer else "")
-                          + ("; weights fetched before the dependent-launch wait (CFI_CTX_CONST_WEIGHTS)"
-                             if const_weights else "")),
-           "tok_per_s": round(ntok / (ms * 1e-3), 1), "ms_per_token": round(ms / ntok, 4),
-           "launches_per_token": m.launches_per_step, "weight_bytes_per_token": bpt,
+    out = {"tok_per_s": round(ntok / (ms * 1e-3), 1), "ms_per_token": round(ms / ntok, 4),
+           "launches_per_token": m.launches_per_step - (fused_in_capture if defer else 0),
            "weights_gbs": round(bpt * ntok / (ms * 1e-3) / 1e9, 1)}
-    if defer:
-        out["launches_per_token"] -= fused_in_capture
     del gr
     ctx.close()
     return out
 
 
 def cpu_baseline(seconds, threads=0):
-    """The oracle's CPU decode step (reference host math, row-parallel) on a bounded sample."""
+    """The oracle's CPU decode step (reference host math, row-parallel) on a bounded sample, from
+    the copy of the oracle built -O3 -march=native on this host."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import cfi_b200 as cfi
     import oracle_py as O
 
+    if O._o is None:
+        O.use_native_build()
     w = cfi.synthetic_weights(cfi.Q4_K, ROWS, K, seed=7)
     xs = {b: np.random.default_rng(b).normal(size=(b, K)).astype(np.float32) for b in BATCHES}
     O.cpu_decode_step(cfi.Q4_K, w, ROWS, K, xs[1], 1, threads)
@@ -459,7 +689,7 @@ def run_reference(args, rank, world):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic", "config": {"workload": "config2: Q4_K 8192x2048 GEMV + quantize_q8_1, batch 1/2/4/8"},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
-                             "sample": "%d full steps in %.1f s" % (n, el)},
+                             "sample": "%d full steps in %.1f s (oracle built -O3 -march=native)" % (n, el)},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -469,6 +699,12 @@ def run_gpu(args, rank, world):
 
     import cfi_b200 as cfi
 
+    legs_on = set(ALL_LEGS if args.legs == "all" else [x for x in args.legs.split(",") if x])
+    for flag, leg in (("no_cpu", "cpu"), ("no_prefill", "prefill"), ("no_decode", "decode")):
+        if getattr(args, flag):
+            legs_on.discard(leg)
+    if args.no_configs:
+        legs_on -= {"config1", "config5", "fattn"}
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist = None
@@ -494,15 +730,12 @@ def run_gpu(args, rank, world):
 
     ncopy = max(8, int(np.ceil(3 * L2_BYTES / W_BYTES / 4.0)) * 4)   # > 3x L2 of weight copies
     w = cfi.synthetic_weights(cfi.Q4_K, ROWS, K, seed=7 + rank)
-    wd = torch.empty((ncopy, w.size), dtype=torch.uint8, device=dev)
-    wd[0].copy_(torch.from_numpy(w.ravel()))
-    for i in range(1, ncopy):
-        wd[i].copy_(wd[0])
+    wd = rotated(torch, dev, w, ncopy * W_BYTES)
+    ncopy = wd.shape[0]
     xs_host = {b: torch.from_numpy(np.random.default_rng(b).normal(size=(b, K)).astype(np.float32)).pin_memory()
                for b in BATCHES}
     xs = {b: xs_host[b].to(dev) for b in BATCHES}
     qs = {b: torch.zeros(Q81(b), dtype=torch.uint8, device=dev) for b in BATCHES}
-    ys = {b: torch.zeros(b * ROWS, dtype=torch.float32, device=dev) for b in BATCHES}
     # two output sets: with N > 1 step i all-gathers step i-1's outputs while it computes its own
     y_sets = [torch.zeros(sum(b for b in BATCHES) * ROWS, dtype=torch.float32, device=dev) for _ in range(2)]
     y_all = y_sets[0]
@@ -513,8 +746,8 @@ def run_gpu(args, rank, world):
     y_views_p = [{b: ya[offs[b]:offs[b] + b * ROWS] for b in BATCHES} for ya in y_sets]
     y_views = y_views_p[0]
     gathered = torch.zeros(world * y_all.numel(), dtype=torch.float32, device=dev) if world > 1 else None
-    ys_host = torch.zeros(y_all.numel(), dtype=torch.float32).pin_memory()
     comm = torch.cuda.Stream(device=dev) if world > 1 else None
+    torch.cuda.synchronize()  # everything above was written on torch's stream; the steps run on `stream`
 
     def step(phase, s, parity=0, gg=None, xsrc=None):
         gg = gg or g
@@ -549,29 +782,19 @@ def run_gpu(args, rank, world):
             if dist:
                 dist.all_gather_into_tensor(gathered, y_all)
     torch.cuda.synchronize()
-    # Step i uses weight phase i % nphase and output set i % 2; that pattern repeats every
-    # `period` steps, so one CUDA graph holds a whole period (programmatic dependent launch then
-    # overlaps consecutive steps too, which separate graph launches would not) and a second graph
-    # the first K % period steps, so the timed region runs exactly K steps.
-    period = nphase if nphase % 2 == 0 else 2 * nphase
-
-    def capture(nsteps):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            for i in range(nsteps):
-                step_pipelined(i % nphase, i % 2)
-        return gr
-
+    # One CUDA graph holds exactly the K timed steps (step i: weight phase i % nphase, output set
+    # i % 2; programmatic dependent launch overlaps consecutive steps inside it).  It is replayed
+    # once before the timed replay, so the timed region runs a warmed graph.
     fused_before = ctx.stats()["fused_q8_1"]
-    graph_period = capture(period)
+    graph_k = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_k, stream=stream):
+        for i in range(args.steps):
+            step_pipelined(i % nphase, i % 2)
     # GEMVs that absorbed their quantize, per captured step
-    launches_per_step = 2 * len(BATCHES) - (ctx.stats()["fused_q8_1"] - fused_before) // period
+    launches_per_step = 2 * len(BATCHES) - (ctx.stats()["fused_q8_1"] - fused_before) // args.steps
     fused_step = launches_per_step < 2 * len(BATCHES)
-    rest = args.steps % period
-    graph_rest = capture(rest) if rest else None
     with torch.cuda.stream(stream):
-        for _ in range((args.warmup + period - 1) // period):
-            graph_period.replay()
+        graph_k.replay()
     torch.cuda.synchronize()
 
     # ---- timed region: device time, max over ranks ----
@@ -582,10 +805,7 @@ def run_gpu(args, rank, world):
     with Clocks(local) as clk:
         with torch.cuda.stream(stream):
             e0.record(stream)
-            for _ in range(args.steps // period):
-                graph_period.replay()
-            if graph_rest is not None:
-                graph_rest.replay()
+            graph_k.replay()
             e1.record(stream)
         torch.cuda.synchronize()
     if dist:
@@ -598,6 +818,7 @@ def run_gpu(args, rank, world):
         ms = float(t.item())
     ms_step = ms / args.steps
     value = world * STEP_BYTES / (ms_step * 1e-3) / 1e9
+    del graph_k
 
     legs = {}
     for leg, gg, note in (("separate_launches", g_sep, "quantize_q8_1 and mul_mat_vec_q launched separately, "
@@ -616,24 +837,13 @@ def run_gpu(args, rank, world):
 
     # ---- dominant kernel: mmvq Q4_K batch 1, back to back (one graph of ncopy launches over the
     # rotated weight copies), CUDA events on the launching stream around the replays ----
-    gk = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gk, stream=stream):
-        for i in range(ncopy):
-            if fused_step:  # the step's kernel: quantize_q8_1 absorbed by the GEMV
-                g.quantize_q8_1(xs[1].data_ptr(), qs[1].data_ptr(), K, K, 1, stream=torch.cuda.current_stream().cuda_stream)
-            g.mmvq(cfi.Q4_K, 1, wd[i].data_ptr(), qs[1].data_ptr(), y_views[1].data_ptr(), K, ROWS,
-                   stream=torch.cuda.current_stream().cuda_stream)
-        ctx.flush()
-    reps = max(3, args.steps // 10)
-    with torch.cuda.stream(stream):
-        gk.replay()
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record(stream)
-        for _ in range(reps):
-            gk.replay()
-        k1.record(stream)
-    torch.cuda.synchronize()
-    kms = k0.elapsed_time(k1) / (reps * ncopy)
+    def roof_body(i, st):
+        if fused_step:  # the step's kernel: quantize_q8_1 absorbed by the GEMV
+            g.quantize_q8_1(xs[1].data_ptr(), qs[1].data_ptr(), K, K, 1, stream=st)
+        g.mmvq(cfi.Q4_K, 1, wd[i].data_ptr(), qs[1].data_ptr(), y_views[1].data_ptr(), K, ROWS, stream=st)
+        if i == ncopy - 1:
+            ctx.flush()
+    kms = graph_time_us(stream, roof_body, reps=max(3, args.steps // 10), calls=ncopy) * 1e-3
     peak, peak_kind = peaks()
     kbytes = MMVQ_BYTES(1) + (QUANT_BYTES(1) if fused_step else 0)
     achieved = kbytes / (kms * 1e-3) / 1e9
@@ -642,11 +852,11 @@ def run_gpu(args, rank, world):
     h2d = sum(xs_host[b].numel() * 4 for b in BATCHES)
     d2h = y_all.numel() * 4
     # Pipelined as a serving loop would run it: step i's activation copy and output copy run on
-    # copy streams (one per direction) while steps i-1 / i+1 compute, with double-buffered device inputs and
-    # outputs (parity i % 2) and event edges: H2D(i) after step i-2 has read its input buffer,
-    # step i after H2D(i) and after D2H(i-2) has read its output buffer, D2H(i) after step i.
-    # One CUDA graph holds a whole rotation period; the timed region ends when the last output
-    # is on the host.
+    # copy streams (one per direction) while steps i-1 / i+1 compute, with double-buffered device
+    # inputs and outputs (parity i % 2) and event edges: H2D(i) after step i-2 has read its input
+    # buffer, step i after H2D(i) and after D2H(i-2) has read its output buffer, D2H(i) after step
+    # i.  One CUDA graph holds exactly the K steps (replayed once before timing); the timed region
+    # ends when the last output is on the host.
     nx = sum(b * K for b in BATCHES)
     x_host_all = torch.empty(nx, dtype=torch.float32).pin_memory()
     o = 0
@@ -662,6 +872,7 @@ def run_gpu(args, rank, world):
             o += b * K
         x_views.append(vv)
     y_host = [torch.empty(y_all.numel(), dtype=torch.float32).pin_memory() for _ in range(2)]
+    torch.cuda.synchronize()
     copy_s = torch.cuda.Stream(device=dev)   # host -> device
     copy_o = torch.cuda.Stream(device=dev)   # device -> host (the other direction's copy engine)
     ev_h2d = [torch.cuda.Event() for _ in range(2)]
@@ -672,69 +883,58 @@ def run_gpu(args, rank, world):
     ev_ag = [torch.cuda.Event() for _ in range(2)]
     gathered2 = [gathered, torch.zeros_like(gathered)] if dist else None
 
-    def capture_e2e(nsteps):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            cur = torch.cuda.current_stream()
-            fork = torch.cuda.Event()
-            fork.record(cur)
-            copy_s.wait_event(fork)
-            copy_o.wait_event(fork)
-            if dist:
-                comm.wait_event(fork)
-            for i in range(nsteps):
-                p = i % 2
-                with torch.cuda.stream(copy_s):
-                    if i >= 2:
-                        copy_s.wait_event(ev_comp[p])
-                    x_dev[p].copy_(x_host_all, non_blocking=True)
-                    ev_h2d[p].record(copy_s)
-                cur.wait_event(ev_h2d[p])
+    ge = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ge, stream=stream):
+        cur = torch.cuda.current_stream()
+        fork = torch.cuda.Event()
+        fork.record(cur)
+        copy_s.wait_event(fork)
+        copy_o.wait_event(fork)
+        if dist:
+            comm.wait_event(fork)
+        for i in range(args.steps):
+            p = i % 2
+            with torch.cuda.stream(copy_s):
                 if i >= 2:
-                    cur.wait_event(ev_d2h[p])
-                    if dist:
-                        cur.wait_event(ev_ag[p])
-                step(i % nphase, cur.cuda_stream, p, xsrc=x_views[p])
-                ev_comp[p].record(cur)
+                    copy_s.wait_event(ev_comp[p])
+                x_dev[p].copy_(x_host_all, non_blocking=True)
+                ev_h2d[p].record(copy_s)
+            cur.wait_event(ev_h2d[p])
+            if i >= 2:
+                cur.wait_event(ev_d2h[p])
                 if dist:
-                    comm.wait_event(ev_comp[p])
-                    with torch.cuda.stream(comm):
-                        dist.all_gather_into_tensor(gathered2[p], y_sets[p])
-                    ev_ag[p].record(comm)
-                with torch.cuda.stream(copy_o):
-                    copy_o.wait_event(ev_comp[p])
-                    y_host[p].copy_(y_sets[p], non_blocking=True)
-                    ev_d2h[p].record(copy_o)
-            for cs in (copy_s, copy_o) + ((comm,) if dist else ()):
-                join = torch.cuda.Event()
-                join.record(cs)
-                cur.wait_event(join)
-        return gr
-
-    ge = [capture_e2e(period)]
-    e_rest = args.steps % period
-    if e_rest:
-        ge.append(capture_e2e(e_rest))
+                    cur.wait_event(ev_ag[p])
+            step(i % nphase, cur.cuda_stream, p, xsrc=x_views[p])
+            ev_comp[p].record(cur)
+            if dist:
+                comm.wait_event(ev_comp[p])
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(gathered2[p], y_sets[p])
+                ev_ag[p].record(comm)
+            with torch.cuda.stream(copy_o):
+                copy_o.wait_event(ev_comp[p])
+                y_host[p].copy_(y_sets[p], non_blocking=True)
+                ev_d2h[p].record(copy_o)
+        for cs in (copy_s, copy_o) + ((comm,) if dist else ()):
+            join = torch.cuda.Event()
+            join.record(cs)
+            cur.wait_event(join)
     with torch.cuda.stream(stream):
-        ge[0].replay()
+        ge.replay()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
         torch.cuda.synchronize()
     t0 = time.perf_counter()
     with torch.cuda.stream(stream):
-        for _ in range(args.steps // period):
-            ge[0].replay()
-        if e_rest:
-            ge[1].replay()
+        ge.replay()
     stream.synchronize()
     e2e_s = time.perf_counter() - t0
     e2e_note = ("host fp32 activations in (one pinned buffer) and fp32 outputs out (two pinned buffers) every "
-                "step, weights resident; the copies (one stream per direction) overlap the neighbouring steps' kernels "
-                "(double-buffered device inputs and outputs, event-ordered)%s, %d steps per CUDA graph, wall clock "
-                "until the last output is on the host" % (", outputs all-gathered over NCCL on a third stream" if dist
-                                                           else "", period))
-    ge = []
+                "step, weights resident; copies on one stream per direction overlap the neighbouring steps' kernels%s; "
+                "one CUDA graph of the K steps, replayed once before timing; wall clock until the last output is on "
+                "the host" % (", outputs all-gathered over NCCL on a third stream" if dist else ""))
+    del ge
     if dist:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -743,20 +943,19 @@ def run_gpu(args, rank, world):
 
     stats = ctx.stats()
     ok = stats["stock_launches"] == 0 and stats["native_failures"] == 0
+    line = {}
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,0.02) weights quantized to Q4_K, "
                 "N(0,1) activations)",
                 "config": {"workload": "config2: Q4_K 8192x2048 GEMV + quantize_q8_1, batch 1/2/4/8",
-                           "rows_per_gpu": ROWS, "k": K, "batches": list(BATCHES), "weight_copies": ncopy,
+                           "rows_per_gpu": ROWS, "k": K, "batches": "1,2,4,8", "weight_copies": ncopy,
                            "l2": "inputs larger than L2: %d weight copies (%.0f MB) rotated" % (ncopy, ncopy * W_BYTES / 1e6),
                            "parallelism": "row-sharded x%d + NCCL all-gather" % world if world > 1 else "single GPU",
                            "bytes_per_step_per_gpu": STEP_BYTES,
-                           "cuda_graph": "%d steps per graph (one period of the weight rotation)" % period,
-                           "router": ("weights fetched before the dependent-launch wait (CFI_CTX_CONST_WEIGHTS)"
-                                      + ("; quantize_q8_1 held back into its GEMV where the prologue is small "
-                                         "(CFI_CTX_DEFER_Q8_1)" if defer else ""))},
+                           "cuda_graph": "one graph of exactly the K timed steps, replayed once before timing",
+                           "router": "CFI_CTX_CONST_WEIGHTS" + (" + CFI_CTX_DEFER_Q8_1" if defer else "")},
                 "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "note": e2e_note},
                 "gpu_launches": launches_per_step * args.steps,
@@ -770,27 +969,51 @@ def run_gpu(args, rank, world):
                              "bytes_per_launch": kbytes},
                 "clocks": clk.summary(), "native_only": ok}
         line.update(legs)
-        if not args.no_prefill and world == 1:
+    summary = {}
+    if world == 1:
+        if "gemv" in legs_on:
+            line["gemv"] = gemv_legs(cfi, g_sep, stream, dev, peak)
+            summary.update({k: v for k, v in line["gemv"].items() if k.endswith("_us")})
+        if "rowops" in legs_on:
+            line["rowops"] = rowops_bench(cfi, g_sep, stream, dev, peak)
+        if "prefill" in legs_on:
             line["prefill"] = prefill_gemm(cfi, g, stream, dev, tensor_peak())
-        if not args.no_decode and world == 1:
-            line["decode"] = decode_bench(stream, dev)
-            line["decode"]["const_weights"] = decode_bench(stream, dev, const_weights=True)
-            line["decode"]["deferred_quantize"] = decode_bench(stream, dev, defer=True, const_weights=True)
-            line["decode"]["fused"] = decode_bench(stream, dev, fused=1, const_weights=True)
-        if not args.no_configs and world == 1:
+            summary["config3_tflops"] = line["prefill"]["config3_best_tflops"]
+        if "decode" in legs_on:
+            dec = {"workload": "config4: Qwen2.5-0.5B-architecture decode, 24 layers, Q8_0 random weights, 631-token "
+                               "seeded KV cache, 48 greedy tokens, one CUDA graph per token"}
+            dec["ggml_sequence"] = decode_bench(stream, dev)
+            dec["ggml_const_weights"] = decode_bench(stream, dev, const_weights=True)
+            dec["ggml_deferred_quantize"] = decode_bench(stream, dev, defer=True, const_weights=True)
+            dec["fused"] = decode_bench(stream, dev, fused=1, const_weights=True)
+            line["decode"] = dec
+            summary["config4_tok_s"] = dec["fused"]["tok_per_s"]
+        if "config1" in legs_on:
             line["config1"] = config1_bench(cfi, g_sep or g, stream, dev, peak, gf=g if defer else None)
-            line["config5"] = config5_bench(cfi, g, stream, dev, peak, tensor_peak())
+        if "fattn" in legs_on:
             line["fattn"] = fattn_bench(cfi, g, stream, dev, tensor_peak())
-        if not args.no_cpu and world == 1:
-            gbs, used, n, el = cpu_baseline(args.cpu_seconds)
-            gbs1, _, n1, el1 = cpu_baseline(max(1.0, args.cpu_seconds / 2), threads=1)
-            line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
-                                    "sample": "%d full steps (4 batches each) in %.1f s, rows split over %d threads"
-                                              % (n, el, used),
-                                    "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
-                                                      "sample": "%d full steps in %.1f s" % (n1, el1)}}
+    if "config5" in legs_on:
+        c5 = {"workload": "config5: Qwen2.5-1.5B-architecture weight products (28 layers Q4_K + Q8_0 head, "
+                          "984944640 B of weights); attention not included"}
+        if world == 1:
+            c5["prefill_631"] = config5_prefill(cfi, g, stream, dev, tensor_peak())
+            summary["config5_prefill_ms"] = c5["prefill_631"]["ms"]
+        c5["decode_b64"] = config5_b64(cfi, g, stream, dev, peak, world, rank, dist, comm)
+        summary["config5_b64_ms"] = c5["decode_b64"]["ms"]
+        summary["config5_b64_kernels_ms"] = c5["decode_b64"]["kernels_only_ms"]
+        line["config5"] = c5
+    if world == 1 and "cpu" in legs_on:
+        gbs, used, n, el = cpu_baseline(args.cpu_seconds)
+        gbs1, _, n1, el1 = cpu_baseline(max(1.0, args.cpu_seconds / 2), threads=1)
+        line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
+                                "sample": "%d full steps (4 batches each) in %.1f s, rows split over %d threads, "
+                                          "oracle built -O3 -march=native" % (n, el, used),
+                                "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
+                                                  "sample": "%d full steps in %.1f s" % (n1, el1)}}
+    if rank == 0:
+        summary.update({"value": line["value"], "e2e": line["e2e"]["value"], "frac": line["roofline"]["frac"]})
+        line["summary"] = summary
         print(json.dumps(line), flush=True)
-    del graph_period, graph_rest, ge
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -806,10 +1029,11 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--legs", default="all", help="comma list of %s (default all)" % ",".join(ALL_LEGS))
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 5 legs")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1, config 5 and FlashAttention legs")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--separate-quantize", action="store_true",
                     help="launch quantize_q8_1 and mul_mat_vec_q separately (no CFI_CTX_DEFER_Q8_1)")

@@ -120,6 +120,7 @@ def lib():
     L.cfi_glue_add.argtypes = [vp, vp, i, vp]
     L.cfi_glue_swiglu.argtypes = [vp, vp, vp, i, vp]
     L.cfi_glue_argmax_next.argtypes = [vp, i, vp, vp, vp]
+    L.cfi_glue_gather_row_shards.argtypes = [vp, vp, i, i, i, vp]
     L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]
@@ -465,14 +466,16 @@ class GgmlCaller:
                 ("i64", ne0), ("i32", ne1), ("i32", ne2)]
         return self._go(p, (ne1, (ne0 + 511) // 512, ne2 * ne3), (128, 1, 1), vals, stream, "quantize_mmq_q8_1")
 
-    def mmq(self, ty, vx, vy, dst, ncols_x, nrows, ncols_dst, mmq_x=128, stream=0, tmp_fixup=0):
-        """mul_mat_q<ty> non-MoE, one channel and sample: dst[col][row] (column stride nrows)."""
+    def mmq(self, ty, vx, vy, dst, ncols_x, nrows, ncols_dst, mmq_x=128, stream=0, tmp_fixup=0, stride_col_dst=None):
+        """mul_mat_q<ty> non-MoE, one channel and sample: dst[col][row] (column stride nrows unless
+        given)."""
         groups = 8 if ty in (Q4_K, Q5_K, Q6_K) else 1
         nb = ncols_x // 32 // groups
         ychan = ncols_x // 128 * ncols_dst * 36
+        scd = nrows if stride_col_dst is None else stride_col_dst
         p = self.plan(("mmq", ty, mmq_x), NAMES["mmq"].format(ty=ty, mmq_x=mmq_x, check=0), "mmq")
-        w = [ncols_x, nrows, ncols_dst, nb, ncols_dst, nrows, 1, 1, nrows * nb, ychan, nrows * ncols_dst, 1, 1,
-             nrows * nb, ychan, nrows * ncols_dst, ncols_dst]
+        w = [ncols_x, nrows, ncols_dst, nb, ncols_dst, scd, 1, 1, nrows * nb, ychan, scd * ncols_dst, 1, 1,
+             nrows * nb, ychan, scd * ncols_dst, ncols_dst]
         vals = [("ptr", vx), ("ptr", vy), ("ptr", 0), ("ptr", 0), ("ptr", dst), ("ptr", tmp_fixup)] + [("u32", v) for v in w]
         return self._go(p, (148, 1, 1), (32, 8, 1), vals, stream, "mul_mat_q")
 

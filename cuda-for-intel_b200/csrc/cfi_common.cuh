@@ -4,7 +4,66 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <utility>
+
 #define CFI_DEV __device__ __forceinline__
+
+// ---- host side: state that belongs to one device ----
+// Kernel attributes (cudaFuncSetAttribute) and the addresses of __device__ symbols
+// (cudaGetSymbolAddress) are per device, so one process driving several GPUs sets and looks them
+// up once for each device, keyed by the current device's index.
+constexpr int CFI_MAX_DEVICES = 64;
+
+// Index of the current device, or -1 when it cannot be queried or is past CFI_MAX_DEVICES (the
+// callers then redo the per-device work on every call instead of caching it).
+inline int cfi_device_index() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return d >= 0 && d < CFI_MAX_DEVICES ? d : -1;
+}
+
+struct CfiPerDeviceOnce {
+    std::once_flag f[CFI_MAX_DEVICES];
+};
+
+// Runs fn() once for each device it is called with current.
+template <class F> void cfi_once_per_device(CfiPerDeviceOnce& o, F&& fn) {
+    const int d = cfi_device_index();
+    if (d < 0)
+        fn();
+    else
+        std::call_once(o.f[d], std::forward<F>(fn));
+}
+
+// Device address of the __device__ symbol `sym` on the current device (nullptr if the lookup
+// fails), looked up once per device.
+template <class T> struct CfiSymbolPtr {
+    T* ptr[CFI_MAX_DEVICES] = {};
+    CfiPerDeviceOnce once;
+    T* get(const T& sym) {
+        const int d = cfi_device_index();
+        T* p = nullptr;
+        auto look = [&p, &sym] {
+            if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), sym) != cudaSuccess) {
+                cudaGetLastError();
+                p = nullptr;
+            }
+        };
+        if (d < 0) {
+            look();
+            return p;
+        }
+        std::call_once(once.f[d], [&] {
+            look();
+            ptr[d] = p;
+        });
+        return ptr[d];
+    }
+};
 
 // ggml block sizes (ggml-common.h layouts; see the block structs below).
 constexpr int QK8_0 = 32, QK8_1 = 32, QK4_0 = 32, QK_K = 256;

@@ -78,6 +78,7 @@ CFI_DEV void epi_qkv_rope_store(const float* __restrict__ qkv, const float* __re
                                 __half* __restrict__ kc, __half* __restrict__ vc, const int32_t* __restrict__ pos,
                                 int nq, int nkv, int head_dim, int n_ctx, float theta_scale, int i0, int nt) {
     const int half = head_dim / 2, p = pos[0];
+    const bool in_cache = p >= 0 && p < n_ctx;  // a position outside the cache stores nothing
     const int npairs = (nq + nkv) / 2;
     for (int i = i0; i < npairs + nkv; i += nt) {
         if (i < npairs) {
@@ -94,13 +95,13 @@ CFI_DEV void epi_qkv_rope_store(const float* __restrict__ qkv, const float* __re
             if (base < nq) {
                 q_out[base + j] = y0;
                 q_out[base + j + half] = y1;
-            } else {
+            } else if (in_cache) {
                 const int kh = (base - nq) / head_dim;
                 __half* kr = kc + ((size_t)kh * n_ctx + p) * head_dim;
                 kr[j] = __float2half_rn(y0);
                 kr[j + half] = __float2half_rn(y1);
             }
-        } else {
+        } else if (in_cache) {
             const int e = i - npairs, kh = e / head_dim, dd = e - kh * head_dim;
             const float v = __ldcg(qkv + nq + nkv + e) + bias[nq + nkv + e];
             vc[((size_t)kh * head_dim + dd) * n_ctx + p] = __float2half_rn(v);

@@ -528,15 +528,8 @@ PFN_encodeTiled encode_fn() {
 }
 
 unsigned int* fa_err_ptr() {
-    static unsigned int* p = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_fattn_error) != cudaSuccess) {
-            cudaGetLastError();
-            p = nullptr;
-        }
-    });
-    return p;
+    static CfiSymbolPtr<unsigned int> p;
+    return p.get(g_fattn_error);
 }
 
 template <int D>
@@ -591,8 +584,8 @@ int launch_fa(const uint64_t* v, cudaStream_t stream) {
     a.nchunks = (ne11 + FA_BN - 1) / FA_BN;
     a.err = fa_err_ptr();
     constexpr size_t smem = fa_smem_bytes<D>();
-    static std::once_flag attr;
-    std::call_once(attr, [] { cudaFuncSetAttribute(cfi_fattn_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
+    static CfiPerDeviceOnce attr;
+    cfi_once_per_device(attr, [] { cudaFuncSetAttribute(cfi_fattn_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
     const char* ep = getenv("CFI_PDL");
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3((unsigned)((ne01 + FA_BM - 1) / FA_BM), (unsigned)ne02, (unsigned)ne03);

@@ -614,15 +614,8 @@ PFN_encodeTiled encode_fn() {
 }
 
 unsigned int* err_ptr() {
-    static unsigned int* p = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_gemm_error) != cudaSuccess) {
-            cudaGetLastError();
-            p = nullptr;
-        }
-    });
-    return p;
+    static CfiSymbolPtr<unsigned int> p;
+    return p.get(g_gemm_error);
 }
 
 int scalar_kind(int compute_type) {  // 0 f16, 1 f32, -1 unsupported (plan.rs:84-95)
@@ -776,8 +769,8 @@ int cfi_tc_gemm(const TcGemm& d, cudaStream_t stream) {
     // the previous kernel; the kernel waits for it before its first tensor load
     const char* ep = getenv("CFI_PDL");
     const bool pdl = !(ep && strcmp(ep, "0") == 0);
-    static std::once_flag attr;
-    std::call_once(attr, [] {
+    static CfiPerDeviceOnce attr;
+    cfi_once_per_device(attr, [] {
         cudaFuncSetAttribute(cfi_gemm_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
         cudaFuncSetAttribute(cfi_gemm_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
         cudaFuncSetAttribute(cfi_gemm_tc2<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);

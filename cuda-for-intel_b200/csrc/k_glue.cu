@@ -48,7 +48,7 @@ __global__ void qkv_store(float* __restrict__ q, float* __restrict__ k, float* _
     }
     const int p = pos[0];
     if (i < nq) q16[i] = __float2half_rn(q[i]);
-    if (i < nkv) {
+    if (i < nkv && p >= 0 && p < n_ctx) {  // a position outside the cache stores nothing
         const int h = i / head_dim, dd = i - h * head_dim;
         kc[((size_t)h * n_ctx + p) * head_dim + dd] = __float2half_rn(k[i]);
         vc[((size_t)h * head_dim + dd) * n_ctx + p] = __float2half_rn(v[i]);
@@ -334,6 +334,25 @@ __global__ void __launch_bounds__(256) swiglu_q81(const float* __restrict__ gu, 
     epi_swiglu_q81(gu, out, n, blockIdx.x * 8 + (threadIdx.x >> 5), gridDim.x * 8);
 }
 
+// Row-shard assembly after an all-gather of column-major slices: src holds `world` slices of
+// ncols columns x rows_padded values (rank r's rows first, padding after), dst ggml's column-major
+// ncols x nrows output; rank r owns rows [r*base + min(r, extra), +base + (r < extra)).
+__global__ void __launch_bounds__(256) gather_row_shards(const float* __restrict__ src, float* __restrict__ dst,
+                                                         uint32_t nrows, uint32_t ncols, uint32_t world) {
+    sm100::pdl_launch_dependents();
+    sm100::pdl_wait();
+    const uint32_t base = nrows / world, extra = nrows - base * world, rp = base + (extra ? 1u : 0u);
+    const uint64_t total = (uint64_t)nrows * ncols;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t c = (uint32_t)(i / nrows), row = (uint32_t)(i - (uint64_t)c * nrows);
+        // rank of `row`: the first `extra` ranks hold base + 1 rows
+        const uint32_t big = extra * (base + 1u);
+        const uint32_t r = row < big ? row / (base + 1u) : extra + (row - big) / base;
+        const uint32_t row0 = r * base + min(r, extra);
+        dst[i] = src[((uint64_t)r * ncols + c) * rp + (row - row0)];
+    }
+}
+
 inline dim3 g1(int n) { return dim3((unsigned)((n + 255) / 256)); }
 
 // Launch with programmatic dependent launch unless CFI_PDL=0 (each kernel waits for its predecessor
@@ -405,6 +424,16 @@ extern "C" int cfi_glue_swiglu(const float* g, const float* u, float* out, int n
 }
 extern "C" int cfi_glue_argmax_next(const float* logits, int n, int32_t* token, int32_t* pos, void* stream) {
     return launch(argmax_next, dim3(AMAX_CTAS), 512, stream, logits, n, token, pos);
+}
+
+extern "C" int cfi_glue_gather_row_shards(const float* src, float* dst, int nrows, int ncols, int world, void* stream) {
+    if (nrows <= 0 || ncols <= 0 || world <= 0 || world > nrows) return (int)cudaErrorInvalidValue;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint64_t total = (uint64_t)nrows * (uint64_t)ncols;
+    const unsigned grid = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 8));
+    return launch(gather_row_shards, dim3(grid), 256, stream, src, dst, (uint32_t)nrows, (uint32_t)ncols, (uint32_t)world);
 }
 
 extern "C" int cfi_fused_add_rmsnorm_q8_1(float* x, const float* y, const float* w, void* out, int n, float eps,

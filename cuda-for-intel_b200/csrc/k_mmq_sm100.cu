@@ -1027,15 +1027,8 @@ int scratch_for(size_t bytes, cudaStream_t stream, void** out) {
 }
 
 unsigned int* device_error_ptr() {
-    static unsigned int* p = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_cfi_device_error) != cudaSuccess) {
-            cudaGetLastError();
-            p = nullptr;
-        }
-    });
-    return p;
+    static CfiSymbolPtr<unsigned int> p;
+    return p.get(g_cfi_device_error);
 }
 
 // Tile width: the fewest tiles of at most 256 columns, balanced (631 columns -> 3 x 224).
@@ -1250,8 +1243,8 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     a.stride_channel_dst = scdst;
     a.stride_sample_dst = ssd;
     a.err = device_error_ptr();
-    static std::once_flag attr;
-    std::call_once(attr, [] {
+    static CfiPerDeviceOnce attr;
+    cfi_once_per_device(attr, [] {
         cudaFuncSetAttribute(cfi_qmm_tc<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
     });
     cudaLaunchConfig_t c = {};
@@ -1413,8 +1406,8 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     a.stride_channel_dst = scdst;
     a.stride_sample_dst = ssd;
     a.err = device_error_ptr();
-    static std::once_flag attr;
-    std::call_once(attr, [] {
+    static CfiPerDeviceOnce attr;
+    cfi_once_per_device(attr, [] {
         cudaFuncSetAttribute(cfi_mmq_tc<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     });
     dim3 grid((nrows + BM - 1) / BM, (ncols_dst + bn - 1) / bn, planes);
@@ -1521,11 +1514,19 @@ extern "C" int cfi_mmq_static_scratch(uint32_t ggml_type, void** kernel_params, 
         w = "ncols_x must be a non-zero multiple of 128 and ncols_dst, nchannels_y, nsamples_y non-zero";
         return fail((int)cudaErrorInvalidValue);
     }
+    if (planes > UINT32_MAX) {  // the launch counts channel x sample planes in 32 bits
+        w = "nchannels_y x nsamples_y exceeds 2^32 - 1";
+        return fail((int)cudaErrorInvalidValue);
+    }
+    // fp16 activation columns of Kt values: K, plus for Q4_K the correction columns (one per 32
+    // values, padded to the 64-value pipeline stage), i.e. Kt = K + ceil(K / 2048) * 64
     const uint64_t Kt = K + (ggml_type == T_Q4_K ? (K / 32 + BK - 1) / BK * BK : 0);
-    const uint64_t need = planes * ncols_dst * Kt * 2;
+    const unsigned __int128 need = (unsigned __int128)planes * ncols_dst * Kt * 2;  // cannot wrap
     if (need > CFI_MMQ_STATIC_SCRATCH_BYTES) {
-        w = "this GEMM needs " + std::to_string(need) + " bytes of scratch (ncols_dst x ncols_x x 2 per channel); the "
-            "static scratch holds " + std::to_string((unsigned long long)CFI_MMQ_STATIC_SCRATCH_BYTES);
+        const uint64_t shown = need > UINT64_MAX ? UINT64_MAX : (uint64_t)need;
+        w = "this GEMM needs " + std::to_string(shown) + " bytes of scratch (planes x ncols_dst x Kt x 2, Kt = ncols_x" +
+            (ggml_type == T_Q4_K ? std::string(" + ceil(ncols_x / 2048) x 64 for Q4_K") : std::string()) +
+            "); the static scratch holds " + std::to_string((unsigned long long)CFI_MMQ_STATIC_SCRATCH_BYTES);
         return fail((int)cudaErrorInvalidValue);
     }
     void* scratch = nullptr;

@@ -1197,10 +1197,10 @@ template <int EPI>
 int launch_epi(const void* w, const void* xq, float* y, int rows, int k, DecodeEpi e, size_t epi_smem, void* stream) {
     if (rows <= 0 || k <= 0 || k % 32 || (reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(xq) & 3))
         return (int)cudaErrorInvalidValue;
-    static unsigned int* counters = nullptr;
-    if (!counters && cudaGetSymbolAddress(reinterpret_cast<void**>(&counters), g_epi_count) != cudaSuccess)
-        return (int)cudaErrorInvalidSymbol;
-    e.counter = counters + EPI;
+    static CfiSymbolPtr<unsigned int[4]> counters;
+    unsigned int(*cp)[4] = counters.get(g_epi_count);
+    if (!cp) return (int)cudaErrorInvalidSymbol;
+    e.counter = *cp + EPI;
     int sms = 148, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1209,11 +1209,17 @@ int launch_epi(const void* w, const void* xq, float* y, int rows, int k, DecodeE
     size_t smem = 0;
     cfi_mmvq_stream_layout(T_Q8_0, 1, (uint32_t)k, (uint32_t)rows, grid, nb, 32, 48 * 1024, 3, &chunk, &nst, &smem);
     smem = std::max(smem, epi_smem);
-    static size_t attr_set[4] = {0, 0, 0, 0};
-    if (smem > 48 * 1024 && attr_set[EPI] < smem) {
-        if (cudaFuncSetAttribute(cfi_mmvq_epi<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return (int)cudaErrorInvalidValue;
-        attr_set[EPI] = smem;
+    // the largest dynamic shared memory set so far for this kernel, per device
+    static std::mutex attr_mu;
+    static size_t attr_set[CFI_MAX_DEVICES] = {};
+    if (smem > 48 * 1024) {
+        const int d = cfi_device_index();
+        std::lock_guard<std::mutex> lk(attr_mu);
+        if (d < 0 || attr_set[d] < smem) {
+            if (cudaFuncSetAttribute(cfi_mmvq_epi<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+                return (int)cudaErrorInvalidValue;
+            if (d >= 0) attr_set[d] = smem;
+        }
     }
     const uint3 none = make_uint3(0, 0, 0), fd1 = make_uint3(1, 0, 1);  // fastdiv triple of 1 (ggml's)
     const char* ep = getenv("CFI_PDL");

@@ -210,6 +210,7 @@ struct Dev {
     ~Dev() {
         for (void* p : bufs) cudaFree(p);
     }
+    // a failing call leaves its error for cudaGetLastError (read by CK)
     void* put(const void* src, size_t n) {
         void* p = nullptr;
         if (cudaMalloc(&p, n ? n : 16) != cudaSuccess) return nullptr;
@@ -219,6 +220,7 @@ struct Dev {
         return p;
     }
 };
+
 
 // Kernel parameter storage: one 16-byte-aligned slot per parameter.
 struct Args {
@@ -262,12 +264,14 @@ int run(const cfi_plan& plan, const uint32_t grid[3], const uint32_t block[3], A
     return rc;
 }
 
-#define CK(x)                                                    \
-    do {                                                         \
-        if (!(x)) {                                              \
-            *why = "probe allocation/copy failed";               \
-            return (int)cudaErrorMemoryAllocation;               \
-        }                                                        \
+// A failed allocation or copy is reported with the CUDA error of the call that failed.
+#define CK(x)                                                                                   \
+    do {                                                                                        \
+        if (!(x)) {                                                                             \
+            const cudaError_t e_ = cudaGetLastError();                                          \
+            *why = std::string("probe allocation/copy failed: ") + cudaGetErrorString(e_);      \
+            return (int)(e_ != cudaSuccess ? e_ : cudaErrorMemoryAllocation);                   \
+        }                                                                                       \
     } while (0)
 
 // probe.rs:353-368 (one channel, one sample, no ids)

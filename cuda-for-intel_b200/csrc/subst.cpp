@@ -13,7 +13,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cctype>
+#include <tuple>
 
 #include "cfi_kernels.h"
 #include "subst_host.hpp"
@@ -545,18 +547,20 @@ int decide(const std::string& name, const cfi_param* params, int nparams, const 
 // ---------------------------------------------------------------------------------------------
 // geometry (mod.rs:509-565), re-designed for the B200 kernels
 // ---------------------------------------------------------------------------------------------
-static int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0, v = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
-            n = v;
-        else {
-            cudaGetLastError();
-            n = 148;
-        }
+static int sm_count() {  // of the current device, cached per device (148 without one)
+    static std::atomic<int> n[64];
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
     }
-    return n;
+    if (dev >= 0 && dev < 64 && n[dev].load() > 0) return n[dev].load();
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+        cudaGetLastError();
+        v = 148;
+    }
+    if (dev >= 0 && dev < 64) n[dev].store(v);
+    return v;
 }
 
 static uint64_t rd_le(const void* p, size_t n) {
@@ -599,9 +603,14 @@ static int ensure_smem(const void* fn, size_t smem);
 // 8 without a device (host-only contexts), so the layout does not depend on one.
 static uint32_t resident_ctas(const void* fn, int threads, size_t smem) {
     static std::mutex mu;
-    static std::map<std::pair<const void*, size_t>, uint32_t> memo;
+    static std::map<std::tuple<int, const void*, size_t>, uint32_t> memo;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = -1;
+    }
     std::lock_guard<std::mutex> g(mu);
-    auto key = std::make_pair(fn, smem);
+    auto key = std::make_tuple(dev, fn, smem);
     auto it = memo.find(key);
     if (it != memo.end()) return it->second;
     int n = 0;
@@ -901,16 +910,23 @@ static PFN_launch driver_launch() {
     return fn;
 }
 
+// The dynamic shared memory attribute is per device: remembered per (device, kernel).
 static int ensure_smem(const void* fn, size_t smem) {
     static std::mutex mu;
-    static std::map<const void*, size_t> set;
+    static std::map<std::pair<int, const void*>, size_t> set;
     if (smem <= 48 * 1024) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = -1;
+    }
     std::lock_guard<std::mutex> g(mu);
-    auto it = set.find(fn);
+    const auto key = std::make_pair(dev, fn);
+    auto it = set.find(key);
     if (it != set.end() && it->second >= smem) return 0;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    set[fn] = smem;
+    set[key] = smem;
     return 0;
 }
 

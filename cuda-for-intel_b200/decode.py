@@ -131,10 +131,16 @@ class DecodeModel:
         self.token = tt.zeros(1, dtype=tt.int32, device=device)
         self.pos = tt.zeros(1, dtype=tt.int32, device=device)
         self.launches_per_step = 0
+        # the weights and state above were written on torch's current stream; steps may run on
+        # another one
+        tt.cuda.current_stream().synchronize()
 
     def reset(self, token, pos=None):
+        """Sets the token and position (on torch's current stream) and waits for them: the step
+        may be enqueued on another stream, whose kernels must not read them half-written."""
         self.token.fill_(int(token))
         self.pos.fill_(self.cfg.prompt if pos is None else int(pos))
+        self.t.cuda.current_stream().synchronize()
 
     def _chk(self, rc, what):
         if rc != 0:
@@ -387,5 +393,6 @@ def load_gguf(torch, ctx, device, path, fused=False, prompt=None, n_ctx=None, se
         if "output.weight" in names:
             m.head = torch.empty_like(m.embd)
             put(m.head, "output.weight", _Q8_0, (hidden, cfg.vocab))
+    torch.cuda.current_stream().synchronize()  # the copies above, before steps on any stream
     return m
 

@@ -25,7 +25,8 @@ CFI_API int cfi_glue_get_rows_q8_0(const void *table, const int32_t *ids, float 
 CFI_API int cfi_glue_qkv_bias(float *q, float *k, float *v, const float *bq, const float *bk, const float *bv, int nq,
                               int nkv, void *stream);
 /* K cache [kv head][pos][dim] and V cache [kv head][dim][pos] (f16, n_ctx positions) at pos[0];
- * q16 = f16(q) */
+ * q16 = f16(q).  A position outside [0, n_ctx) stores nothing in the caches (here and in the
+ * fused cache stores below). */
 CFI_API int cfi_glue_kv_store(const float *q, const float *k, const float *v, void *q16, void *kc, void *vc,
                               const int32_t *pos, int nq, int nkv, int head_dim, int n_ctx, void *stream);
 /* mask[j] = 0 for j <= pos[0], -inf after */
@@ -39,6 +40,13 @@ CFI_API int cfi_glue_swiglu(const float *g, const float *u, float *out, int n, v
 /* token[0] = first index of max(logits[0..n)); pos[0] += 1 (device-global partials: one call at a
  * time per device) */
 CFI_API int cfi_glue_argmax_next(const float *logits, int n, int32_t *token, int32_t *pos, void *stream);
+
+/* Row-shard assembly after an all-gather (the multi-GPU split of the weight rows): src holds
+ * `world` rank slices, slice r = ncols columns of rows_padded = ceil(nrows / world) fp32 values
+ * (rank r's rows first, padding after); dst gets ggml's column-major ncols x nrows output.  Rank
+ * r owns rows [r*base + min(r, extra), ... + base + (r < extra)) with base = nrows / world,
+ * extra = nrows % world (the split of shard.row_split). */
+CFI_API int cfi_glue_gather_row_shards(const float *src, float *dst, int nrows, int ncols, int world, void *stream);
 
 /*
  * Fused decode steps (one launch each where the ggml graph has two to five).  Results equal the

@@ -173,11 +173,12 @@ CFI_API void cfi_ctx_inject(cfi_ctx *ctx, int site, int nth, int code);
  * re-enter the driver's allocator and change the application's own memory accounting), a
  * serving process whose memory pool reserved all free HBM up front (cudaMalloc would fail at run
  * time), or a code path that cannot afford cudaMalloc's implicit device synchronisation.  The
- * GEMM's one piece of scratch -- an fp16 copy of the activations, ncols_dst x ncols_x x 2 bytes per
- * channel and sample -- then lives in a fixed array of CFI_MMQ_STATIC_SCRATCH_BYTES compiled into
- * the library; every GPU on which the library's kernels are loaded holds that array until the
- * process exits.  Larger problems are rejected with cudaErrorInvalidValue and a message in `why`
- * before anything is launched.
+ * GEMM's one piece of scratch -- an fp16 copy of the activations, planes x ncols_dst x Kt x 2
+ * bytes, where planes = nchannels_y x nsamples_y and Kt = ncols_x (Q8_0) or ncols_x +
+ * ceil(ncols_x / 2048) x 64 (Q4_K: the min-correction columns) -- then lives in a fixed array of
+ * CFI_MMQ_STATIC_SCRATCH_BYTES compiled into the library; every GPU on which the library's
+ * kernels are loaded holds that array until the process exits.  Larger problems are rejected
+ * with cudaErrorInvalidValue and a message in `why` before anything is launched.
  *
  * kernel_params are the 23 parameters of ggml-cuda's mul_mat_q<type, mmq_x, need_check> (x, y,
  * ids_dst, expert_bounds, dst, tmp_fixup, then 17 ints); inputs and outputs stay the caller's.

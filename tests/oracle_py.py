@@ -35,11 +35,23 @@ def build():
     subprocess.run(["make", "-s", "-C", ORACLE_DIR], check=True)
 
 
+def use_native_build():
+    """Rebuilds the oracle at -O3 -march=native for the host this runs on (`make native`, always
+    rebuilt so a copy made on another machine is never used) and makes lib() load that copy.
+    Only bench.py's CPU-baseline legs call this, before any other use of lib()."""
+    global LIB
+    if _o is not None:
+        raise RuntimeError("the oracle is already loaded")
+    subprocess.run(["make", "-s", "-B", "-C", ORACLE_DIR, "native"], check=True)
+    LIB = os.path.join(ORACLE_DIR, "_native", "liboracle.so")
+
+
 def lib():
     global _o
     if _o is None:
         srcs = [os.path.join(ORACLE_DIR, f) for f in ("cfi_oracle.c", "cfi_oracle.h", "cpu_baseline.c")]
-        if not os.path.exists(LIB) or any(os.path.getmtime(s) > os.path.getmtime(LIB) for s in srcs):
+        if os.path.dirname(LIB) == ORACLE_DIR and (
+                not os.path.exists(LIB) or any(os.path.getmtime(s) > os.path.getmtime(LIB) for s in srcs)):
             build()
         _o = C.CDLL(LIB)
         u8p, f32p = C.POINTER(C.c_uint8), C.POINTER(C.c_float)

@@ -5,8 +5,9 @@ scratch is a fixed array inside the library instead of a cudaMalloc'd buffer.
 
 Collected last on purpose.  Each call goes through the C ABI and is checked against the regular
 entry point (cfi_subst_launch of mul_mat_q) on the same inputs, for two calls in a row that leave
-different contents behind in the shared array; a problem too large for the array is refused
-before anything runs."""
+different contents behind in the shared array; the device's free memory is the same before and
+after a repeated call (the first call on a device may still load the library's kernels, which
+takes memory once); a problem too large for the array is refused before anything runs."""
 import ctypes as C
 
 import numpy as np
@@ -63,6 +64,16 @@ def test_static_scratch_gemm_matches_the_regular_entry_point_twice_in_a_row():
         assert np.all(np.isfinite(got))
         assert O.rel_l2(got, want) < REL_L2
         assert O.rel_l2(got, O.mmq_ref(ty, p, x, y, n)) < REL_L2
+        # the same call again: no device memory taken (a cudaMalloc'd scratch or workspace would
+        # lower the free bytes; nothing else allocates between the two readings)
+        d_static.fill_(float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        rc, why = static_call(ty, mmq_args(dx.data_ptr(), dy.data_ptr(), d_static.data_ptr(), words(p)))
+        assert rc == 0, why
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free_before
+        assert np.array_equal(d_static.cpu().numpy(), got)
     ctx.close()
 
 
