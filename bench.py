@@ -212,17 +212,19 @@ def prefill_gemm(cfi, g, stream, dev, peak_tf):
             "peak_tflops": peak_tf, "peak_kind": "measured bf16 dense (burst)", **out}
 
 
-def gemv_legs(cfi, g, stream, dev, peak):
+GEMV_SHAPES = ((12, ROWS, K, BATCHES, "q4k_8192x2048"), (12, 65536, 2048, (1, 8), "q4k_65536x2048"),
+               (8, 151936, 896, (1,), "q8_0_151936x896"))
+
+
+def gemv_legs(cfi, g, stream, dev, peak, shapes=GEMV_SHAPES):
     """Q4_K mul_mat_vec_q 8192x2048 at batch 1/2/4/8 on their own, and the large shapes (65536 x
-    2048 Q4_K, the 151936 x 896 Q8_0 lm_head) at batch 1: graphs of back-to-back launches over
-    rotated weight copies (> 3x L2), on a context that fetches weights before the dependent-launch
-    wait.  µs per launch and the fraction of HBM of the algorithmic bytes."""
+    2048 Q4_K at batch 1 and 8, the 151936 x 896 Q8_0 lm_head at batch 1): graphs of back-to-back
+    launches over rotated weight copies (> 3x L2), on a context that fetches weights before the
+    dependent-launch wait.  µs per launch and the fraction of HBM of the algorithmic bytes."""
     import torch
 
     out = {}
-    for ty, rows, k, batches, tag in ((cfi.Q4_K, ROWS, K, BATCHES, "q4k_8192x2048"),
-                                      (cfi.Q4_K, 65536, 2048, (1, 8), "q4k_65536x2048"),
-                                      (cfi.Q8_0, 151936, 896, (1,), "q8_0_151936x896")):
+    for ty, rows, k, batches, tag in shapes:
         w = cfi.synthetic_weights(ty, rows, k, seed=rows)
         wd = rotated(torch, dev, w, 3 * L2_BYTES)
         ncopy = wd.shape[0]
@@ -1023,6 +1025,26 @@ def run_gpu(args, rank, world):
             c.close()
 
 
+def only_gemv(spec):
+    """One GEMV shape alone (the gemv leg's timing loop), printed as one JSON line: the profiling
+    entry of the kernel summaries."""
+    import torch
+
+    import cfi_b200 as cfi
+
+    tname, rows, k, b = spec.split(":")
+    ty = {"q4k": cfi.Q4_K, "q8_0": cfi.Q8_0}[tname]
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = cfi.Ctx(0, const_weights=True)
+    g = cfi.GgmlCaller(ctx, "all")
+    stream = torch.cuda.Stream(device=dev)
+    res = gemv_legs(cfi, g, stream, dev, peaks()[0],
+                    shapes=((ty, int(rows), int(k), (int(b),), "%s_%sx%s" % (tname, rows, k)),))
+    print(json.dumps({"only_gemv": spec, **res}), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1037,9 +1059,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--separate-quantize", action="store_true",
                     help="launch quantize_q8_1 and mul_mat_vec_q separately (no CFI_CTX_DEFER_Q8_1)")
+    ap.add_argument("--only-gemv", default="",
+                    help="type:rows:k:batch (e.g. q4k:65536:2048:8): time only that mul_mat_vec_q (for profiling) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.only_gemv:
+        only_gemv(args.only_gemv)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

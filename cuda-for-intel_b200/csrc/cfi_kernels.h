@@ -47,6 +47,12 @@ struct CfiFuseQ {
 // the GEMV with the quantize in its prologue, on the direct-fill or the bulk-copy layout (the
 // same trailing words as that layout's kernel, then the CfiFuseQ); nullptr above 4 columns
 const void* cfi_native_mmvq_q81(uint32_t ty, uint32_t ncols, bool direct);
+// tensor-core Q4_K GEMV for 3..8 columns (exact int32 block dots, fp32 scales reassociated):
+// same parameters and trailing words as the streaming kernel; false when the layout does not fit
+const void* cfi_native_mmvq_mma(uint32_t ty, uint32_t ncols);
+bool cfi_mmvq_mma_layout(uint32_t ncols_x, uint32_t nrows, uint32_t grid_x, uint32_t ctas_per_sm, uint32_t chunk_target,
+                         uint32_t stage_budget, uint32_t max_stages, uint32_t* chunk_rows, uint32_t* nstages,
+                         size_t* smem);
 const void* cfi_native_mmvq_direct(uint32_t ty, uint32_t ncols);  // the direct-fill kernel (nstages 0)
 int cfi_mmvq_max_smem_bytes();
 unsigned int cfi_mmvq_error_take();

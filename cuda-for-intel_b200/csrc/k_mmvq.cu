@@ -783,6 +783,196 @@ CFI_DEV void q6k_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Tensor-core Q4_K GEMV for 3..8 columns (tolerance mode: the int32 block dots are exact, the fp32
+// scale arithmetic is reassociated; outputs agree with the reference's fp32 order to about 1e-7
+// relative).  The bit-exact decode-fast kernels above stay selectable (CFI_MMVQ_EXACT=1).
+//
+// y[r, c] = sum_sb d[r,sb] * sum_j d8[c,j] * sc[r,j] * sumi[r,c,j]  -  dmin[r,sb] * sum_j m[r,j] * dsum[c,j]
+// with j the 32-value sub-blocks of superblock sb, sumi the exact int8 block dot and dsum = d8 * sumq.
+//   * sumi: one mma.sync.m16n8k32 (u8 x s8 -> s32) per sub-block gives it for 16 weight rows and
+//     all 8 columns; the A fragments of a 32-byte nibble chunk (two sub-blocks) come from one
+//     ldmatrix.x4 of 16 rows, masked with 0x0F (low sub-block) or 0xF0 (high: 16 x sumi, the 1/16
+//     folded into that sub-block's staged d8);
+//   * the min term of a superblock is a 16 x 8 x 8 product (m over its 8 sub-blocks times dsum):
+//     two mma.sync.m16n8k8 tf32 with m exact and dsum split into tf32 hi + lo parts (~2^-21
+//     relative), accumulated in fp32;
+//   * the scale term stays on the CUDA cores: t += d8' * float(sumi * sc) per sub-block, then
+//     acc += d * t - dmin * m-term once per superblock.
+// Layouts in shared memory:
+//   * weights: the streaming kernel's stages, one row per pitch with pitch / 16 odd, so the eight
+//     16-byte rows of an ldmatrix phase hit eight different bank groups;
+//   * activations, per superblock: for each sub-block 8 columns x 32 qs bytes stored as words
+//     (0,4,1,5,2,6,3,7), so lane (n = lane / 4, t = lane % 4) loads its B fragment (words t and
+//     t + 4 of column n) with one 8-byte load, then the 8 columns' d8'; then dsum hi and lo as
+//     [sub-block][column] floats; columns >= NCOLS are zero;
+//   * work: (16-row tile, superblock) items of a chunk spread over the 8 warps, the partial tiles
+//     summed across warps through shared memory in warp order (deterministic).
+// ---------------------------------------------------------------------------------------------
+constexpr uint32_t MMA_SUB_BYTES = 288;                   // 8 columns x 32 qs bytes + 8 x d8'
+constexpr uint32_t MMA_SB_BYTES = 8 * MMA_SUB_BYTES + 512;  // + dsum hi / lo [8 sub-blocks][8 columns]
+constexpr uint32_t MMA_MAX_CHUNK = 32;                    // rows per chunk: at most two 16-row tiles
+constexpr uint32_t MMA_RED_BYTES = NW * 2 * 128 * 4;
+
+__host__ __device__ inline uint32_t mma_pitch(uint32_t row_bytes) {
+    const uint32_t p = (row_bytes + 15u) & ~15u;
+    return ((p >> 4) & 1u) ? p : p + 16u;
+}
+__host__ __device__ inline uint32_t mma_stage_bytes(uint32_t chunk_rows, uint32_t row_bytes) {
+    return (chunk_rows * mma_pitch(row_bytes) + 127u) & ~127u;
+}
+__host__ __device__ inline size_t mma_y_bytes(uint32_t nb32) { return ((size_t)(nb32 / 8) * MMA_SB_BYTES + 127) & ~(size_t)127; }
+
+CFI_DEV uint32_t tf32_bits(float x) {  // round to nearest (ties away), the tf32 operand format
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+template <int NCOLS>
+CFI_DEV YStage stage_y_mma(uint8_t* smem, const uint8_t* y0, size_t y_base, uint32_t stride_col_y, uint32_t nb32) {
+    for (uint32_t idx = threadIdx.x; idx < 8u * nb32; idx += blockDim.x) {
+        const uint32_t c = idx / nb32, b = idx - c * nb32, sb = b >> 3, j = b & 7;
+        uint8_t* sbp = smem + (size_t)sb * MMA_SB_BYTES;
+        uint8_t* g = sbp + j * MMA_SUB_BYTES;
+        uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+        float d8 = 0.0f, ds = 0.0f;
+        if (c < (uint32_t)NCOLS) {
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(y0 + (y_base + (size_t)c * stride_col_y + b) * Q8_1_BYTES);
+            uint32_t q[9];
+#pragma unroll
+            for (int i = 0; i < 9; i++) q[i] = __ldg(w + i);
+            int sum = 0;
+#pragma unroll
+            for (int i = 1; i < 9; i++) sum = dp4a(0x01010101, (int)q[i], sum);
+            lo = make_uint4(q[1], q[5], q[2], q[6]);
+            hi = make_uint4(q[3], q[7], q[4], q[8]);
+            d8 = h2f_bits((uint16_t)(q[0] & 0xffffu));
+            ds = d8 * (float)sum;
+        }
+        *reinterpret_cast<uint4*>(g + c * 32) = lo;
+        *reinterpret_cast<uint4*>(g + c * 32 + 16) = hi;
+        // odd sub-blocks are the high nibbles, whose MMA sums carry a factor 16
+        reinterpret_cast<float*>(g + 256)[c] = (j & 1) ? d8 * 0.0625f : d8;
+        const uint32_t dh = tf32_bits(ds);
+        const uint32_t dl = tf32_bits(ds - __uint_as_float(dh));
+        reinterpret_cast<uint32_t*>(sbp + 8 * MMA_SUB_BYTES)[j * 8 + c] = dh;
+        reinterpret_cast<uint32_t*>(sbp + 8 * MMA_SUB_BYTES + 256)[j * 8 + c] = dl;
+    }
+    return YStage{smem_u32(smem), 0, 0, nb32};
+}
+
+CFI_DEV void ldsm_x4(uint32_t a, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+CFI_DEV void mma_u8s8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int (&d)[4]) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%10, %10, %10, %10};"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+CFI_DEV void mma_tf32(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, float (&d)[4]) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Rows [r0, r1) of one chunk (at most MMA_MAX_CHUNK), staged at sbase with row pitch rstride.
+template <int NCOLS>
+CFI_DEV void q4k_chunk_mma(uint32_t sbase, uint32_t rstride, uint32_t r0, uint32_t r1, const YStage& y, uint32_t red,
+                           uint32_t tid, float* dplane, uint32_t stride_col_dst) {
+    const uint32_t lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const uint32_t nrows = r1 - r0, ntile = (nrows + 15) / 16, nsb = y.nb32 / 8;
+    float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    // this lane's ldmatrix row within a tile (matrices: rows 0-7 / 8-15 x bytes 0-15 / 16-31)
+    const uint32_t lrow = (lane & 7) + 8 * ((lane >> 3) & 1), lbyte = 16 * (lane >> 4);
+    const uint32_t mshift = 8 * t;
+    for (uint32_t item = warp; item < ntile * nsb; item += NW) {
+        const uint32_t tile = item >= nsb ? 1u : 0u, sb = item - tile * nsb;
+        const uint32_t arow = min(tile * 16 + lrow, nrows - 1);
+        const uint32_t aaddr = sbase + arow * rstride + sb * Q4_K_BYTES + 16 + lbyte;
+        float dx[2], dmin[2];
+        uint32_t scw[2][2], am[4];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t row = min(tile * 16 + g + 8 * h, nrows - 1);
+            const uint4 hd = lds128(sbase + row * rstride + sb * Q4_K_BYTES);
+            dx[h] = h2f_bits((uint16_t)(hd.x & 0xffffu));
+            dmin[h] = h2f_bits((uint16_t)(hd.x >> 16));
+            // get_scale_min_k4 for all 8 sub-blocks, four bytes at a time
+            scw[h][0] = hd.y & 0x3F3F3F3Fu;
+            scw[h][1] = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+            const uint32_t m_lo = hd.z & 0x3F3F3F3Fu;
+            const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+            // tf32 A fragment of the min term: (row g + 8h, sub-block t) and (.., t + 4)
+            am[h] = __float_as_uint((float)((m_lo >> mshift) & 0xffu));
+            am[h + 2] = __float_as_uint((float)((m_hi >> mshift) & 0xffu));
+        }
+        const uint32_t ysb = y.ya + sb * MMA_SB_BYTES;
+        float tm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        {
+            const uint32_t dsh = ysb + 8 * MMA_SUB_BYTES + (t * 8 + g) * 4;
+            mma_tf32(am, lds32(dsh), lds32(dsh + 128), tm);
+            mma_tf32(am, lds32(dsh + 256), lds32(dsh + 384), tm);
+        }
+        float tsc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            uint32_t raw[4];
+            ldsm_x4(aaddr + 32 * c, raw);
+#pragma unroll
+            for (int hn = 0; hn < 2; hn++) {
+                const int j = 2 * c + hn;  // sub-block of the superblock
+                const uint32_t msk = hn ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                const uint32_t a[4] = {raw[0] & msk, raw[1] & msk, raw[2] & msk, raw[3] & msk};
+                const uint32_t gb = ysb + j * MMA_SUB_BYTES;
+                const uint2 bw = lds64(gb + g * 32 + t * 8);
+                int s4[4];
+                mma_u8s8(a, bw.x, bw.y, s4);
+                const uint2 dd = lds64(gb + 256 + t * 8);  // d8' of columns 2t, 2t + 1
+                const float d80 = __uint_as_float(dd.x), d81 = __uint_as_float(dd.y);
+                const uint32_t sh = 8u * (uint32_t)(j & 3);
+                const int sc0 = (int)((scw[0][j >> 2] >> sh) & 0xffu), sc1 = (int)((scw[1][j >> 2] >> sh) & 0xffu);
+                tsc[0] = __fmaf_rn(d80, (float)(s4[0] * sc0), tsc[0]);
+                tsc[1] = __fmaf_rn(d81, (float)(s4[1] * sc0), tsc[1]);
+                tsc[2] = __fmaf_rn(d80, (float)(s4[2] * sc1), tsc[2]);
+                tsc[3] = __fmaf_rn(d81, (float)(s4[3] * sc1), tsc[3]);
+            }
+        }
+        // the two tiles of a chunk are unrolled so acc stays in registers
+#pragma unroll
+        for (int T = 0; T < 2; T++)
+            if (tile == (uint32_t)T)
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    acc[T][i] = __fmaf_rn(dx[i >> 1], tsc[i], __fmaf_rn(-dmin[i >> 1], tm[i], acc[T][i]));
+    }
+    // partial tiles of every warp, then the sum over warps in warp order
+#pragma unroll
+    for (int T = 0; T < 2; T++)
+        if ((uint32_t)T < ntile)
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(red + (((warp * 2 + T) * 4 + i) * 32 + lane) * 4), "f"(acc[T][i]));
+    __syncthreads();
+    for (uint32_t e = tid; e < ntile * 128; e += NW * 32) {
+        const uint32_t T = e >> 7, rr = (e >> 3) & 15, cc = e & 7;
+        if (cc >= (uint32_t)NCOLS || T * 16 + rr >= nrows) continue;
+        const uint32_t i = ((rr >> 3) << 1) | (cc & 1), ln = 4 * (rr & 7) + (cc >> 1);
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            float p;
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(p) : "r"(red + (((w * 2 + T) * 4 + i) * 32 + ln) * 4));
+            v += p;
+        }
+        dplane[(size_t)cc * stride_col_dst + r0 + T * 16 + rr] = v;
+    }
+}
+
 #define MMVQ_STREAM_PARAMS                                                                                           \
     const void *__restrict__ vx, const void *__restrict__ vy, const int32_t *__restrict__ ids, float *__restrict__ dst,     \
         uint32_t ncols_x, uint3 nchannels_y, uint32_t stride_row_x, uint32_t stride_col_y, uint32_t stride_col_dst,        \
@@ -794,7 +984,7 @@ CFI_DEV void q6k_chunk(uint32_t sbase, uint32_t rstride, bool dense, uint32_t r0
         stride_channel_y, stride_channel_dst, sample_ratio, stride_sample_x, stride_sample_y, stride_sample_dst, nrows,  \
         chunk_rows, nst
 
-template <uint32_t TY, int NCOLS, bool FQ = false, bool DIRECT = false>
+template <uint32_t TY, int NCOLS, bool FQ = false, bool DIRECT = false, bool MMA = false>
 CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) {
     // nst bit 8 (CFI_CTX_CONST_WEIGHTS): the weights are not written by any kernel, so their
     // first stages are fetched before waiting on the previous kernel (programmatic dependent
@@ -808,9 +998,10 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
     const uint32_t nb = ncols_x / block_values<TY>();
     const uint32_t nb32 = ncols_x / 32;
     const uint32_t row_bytes = nb * BB;
-    const bool dense = stride_row_x == nb;
-    const uint32_t rstride = st_row_stride(row_bytes, dense);
-    const uint32_t stage_bytes = st_stage_bytes(chunk_rows, row_bytes, dense);
+    // the tensor-core kernel copies row by row at its bank-conflict-free pitch
+    const bool dense = stride_row_x == nb && !MMA;
+    const uint32_t rstride = MMA ? mma_pitch(row_bytes) : st_row_stride(row_bytes, dense);
+    const uint32_t stage_bytes = MMA ? mma_stage_bytes(chunk_rows, row_bytes) : st_stage_bytes(chunk_rows, row_bytes, dense);
     const uint32_t channel_dst = blockIdx.y, sample_dst = blockIdx.z;
     const bool use_ids = NCOLS == 1 && ids != nullptr;
     const uint32_t sample_x = fastdiv(sample_dst, sample_ratio);
@@ -891,13 +1082,19 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
         }
     };
     auto stage_act = [&](uint8_t* at) -> YStage {
-        if constexpr (FQ)
+        if constexpr (MMA)
+            return stage_y_mma<NCOLS>(at, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
+        else if constexpr (FQ)
             return stage_y_q81<TY>(at, NCOLS, *fq, nb32);
         else
             return stage_y<TY>(at, NCOLS, static_cast<const uint8_t*>(vy), y_base, stride_col_y, nb32);
     };
+    // the tensor-core kernel's cross-warp partials follow its activation stage
+    const uint32_t red = MMA ? smem_u32(smem + nst * stage_bytes + mma_y_bytes(nb32)) : 0u;
     auto compute = [&](uint32_t sb, uint32_t r0, uint32_t r1, const YStage& y) {
-        if constexpr (TY == T_Q4_K)
+        if constexpr (MMA)
+            q4k_chunk_mma<NCOLS>(sb, rstride, r0, r1, y, red, tid, dplane, stride_col_dst);
+        else if constexpr (TY == T_Q4_K)
             q4k_chunk<NCOLS>(sb, rstride, r0, r1, y, tid, dplane, stride_col_dst);
         else if constexpr (TY == T_Q6_K)
             q6k_chunk<NCOLS>(sb, rstride, dense, r0, r1, y, lane, warp, plane, stride_row_x, dplane, stride_col_dst);
@@ -1007,6 +1204,12 @@ __global__ void __launch_bounds__(NW * 32) cfi_mmvq_stream(MMVQ_STREAM_PARAMS) {
     mmvq_stream_body<TY, NCOLS>(MMVQ_STREAM_ARGS);
 }
 
+// The tensor-core Q4_K GEMV (3..8 columns).
+template <int NCOLS>
+__global__ void __launch_bounds__(NW * 32) cfi_mmvq_mma(MMVQ_STREAM_PARAMS) {
+    mmvq_stream_body<T_Q4_K, NCOLS, false, false, true>(MMVQ_STREAM_ARGS);
+}
+
 // The direct-fill GEMV (nst == 0 from the host): 4 CTAs per SM for one or two columns.
 template <int NCOLS> constexpr int direct_min_ctas() { return NCOLS <= 2 ? 4 : 2; }
 template <uint32_t TY, int NCOLS>
@@ -1109,6 +1312,42 @@ const void* pick_q81(uint32_t ncols, bool direct) {
 
 }  // namespace
 
+const void* cfi_native_mmvq_mma(uint32_t ty, uint32_t ncols) {
+    if (ty != T_Q4_K) return nullptr;
+    switch (ncols) {
+    case 3: return reinterpret_cast<const void*>(&cfi_mmvq_mma<3>);
+    case 4: return reinterpret_cast<const void*>(&cfi_mmvq_mma<4>);
+    case 5: return reinterpret_cast<const void*>(&cfi_mmvq_mma<5>);
+    case 6: return reinterpret_cast<const void*>(&cfi_mmvq_mma<6>);
+    case 7: return reinterpret_cast<const void*>(&cfi_mmvq_mma<7>);
+    case 8: return reinterpret_cast<const void*>(&cfi_mmvq_mma<8>);
+    default: return nullptr;
+    }
+}
+
+bool cfi_mmvq_mma_layout(uint32_t ncols_x, uint32_t nrows, uint32_t grid_x, uint32_t ctas_per_sm, uint32_t chunk_target,
+                         uint32_t stage_budget, uint32_t max_stages, uint32_t* chunk_rows, uint32_t* nstages,
+                         size_t* smem) {
+    if (ncols_x == 0 || ncols_x % QK_K) return false;
+    const uint32_t row_bytes = ncols_x / QK_K * Q4_K_BYTES;
+    const uint32_t per_cta = (nrows + grid_x - 1) / grid_x;
+    uint32_t c = std::min(std::min(std::max(1u, chunk_target), MMA_MAX_CHUNK), std::max(1u, per_cta));
+    while (c > 1 && mma_stage_bytes(c, row_bytes) > stage_budget) c--;
+    const uint32_t chunks = (per_cta + c - 1) / c;
+    uint32_t nst = std::max(1u, std::min(std::min(max_stages, ST_MAX_STAGES), chunks));
+    // the grid's CTAs per SM must fit side by side (228 KB of shared memory per SM, 1 KB of it
+    // reserved per CTA)
+    const size_t fixed = mma_y_bytes(ncols_x / 32) + MMA_RED_BYTES;
+    const size_t cap = std::min((size_t)cfi_mmvq_max_smem_bytes(), (size_t)233472 / std::max(1u, ctas_per_sm) - 1024 - 128);
+    // long rows: fewer stages, then shorter chunks, until the CTA fits
+    while (nst > 1 && (size_t)nst * mma_stage_bytes(c, row_bytes) + fixed > cap) nst--;
+    while (c > 1 && (size_t)nst * mma_stage_bytes(c, row_bytes) + fixed > cap) c--;
+    *chunk_rows = c;
+    *nstages = nst;
+    *smem = (size_t)nst * mma_stage_bytes(c, row_bytes) + fixed;
+    return *smem <= cap;
+}
+
 const void* cfi_native_mmvq_direct(uint32_t ty, uint32_t ncols) {
     if (ty == T_Q8_0) return pick_direct<T_Q8_0>(ncols);
     if (ty == T_Q4_K) return pick_direct<T_Q4_K>(ncols);
@@ -1148,10 +1387,13 @@ void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint3
     uint32_t c = std::min(std::max(1u, chunk_target), std::max(1u, per_cta));
     while (c > 1 && st_stage_bytes(c, row_bytes, dense) > stage_budget) c--;
     const uint32_t chunks = (per_cta + c - 1) / c;
-    const uint32_t nst = std::max(1u, std::min(std::min(max_stages, ST_MAX_STAGES), chunks));
+    uint32_t nst = std::max(1u, std::min(std::min(max_stages, ST_MAX_STAGES), chunks));
+    const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127, cap = (size_t)cfi_mmvq_max_smem_bytes();
+    // long rows: fewer stages, then shorter chunks, until the CTA fits
+    while (nst > 1 && (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys > cap) nst--;
+    while (c > 1 && (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys > cap) c--;
     *chunk_rows = c;
     *nstages = nst;
-    const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127;
     *smem = (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys;
 }
 

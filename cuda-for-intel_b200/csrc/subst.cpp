@@ -668,7 +668,27 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
                 }
             }
         }
-        if (stream && !direct) {
+        // Q4_K with 3..8 columns: the tensor-core kernel (exact int32 block dots, fp32 scales
+        // reassociated: within ~1e-7 of the reference's order); CFI_MMVQ_EXACT=1 keeps the
+        // kernels that reproduce the decode-fast fp32 order bit for bit
+        bool mma = false;
+        if (stream && !direct && plan.ty == 12 && plan.ncols >= 3 && env_u32("CFI_MMVQ_EXACT", 0, 0, 1) == 0) {
+            const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", 2, 1, 8);
+            const uint32_t g1 = std::max(1u, std::min(nrows, std::max(1u, (uint32_t)(sm_count() * per_sm) / planes)));
+            uint32_t c1 = 0, n1 = 0;
+            size_t s1 = 0;
+            if (cfi_mmvq_mma_layout(ncols_x, nrows, g1, per_sm, env_u32("CFI_MMVQ_CHUNK", 32, 1, 256),
+                                    1024 * env_u32("CFI_MMVQ_STAGE_KB", 48, 4, 112), env_u32("CFI_MMVQ_STAGES", 3, 1, 4),
+                                    &c1, &n1, &s1)) {
+                mma = true;
+                nl.fn = cfi_native_mmvq_mma(plan.ty, plan.ncols);
+                nl.grid[0] = g1;
+                chunk = c1;
+                nstages = n1;
+                nl.smem = s1;
+            }
+        }
+        if (stream && !direct && !mma) {
             // CFI_MMVQ_STREAM_CTAS CTAs per SM shared by the channel/sample planes; chunks of
             // CFI_MMVQ_CHUNK rows within CFI_MMVQ_STAGE_KB per stage, CFI_MMVQ_STAGES stages
             const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", 2, 1, 8);

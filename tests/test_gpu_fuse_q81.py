@@ -87,6 +87,9 @@ def case(ty, ncols, nrows, ncols_x, pad, seed):
 def test_fused_quantize_gemv_equals_separate_launches(ctxs, monkeypatch, ty, ncols, direct):
     monkeypatch.setenv("CFI_DEFER_MAX_VALUES", "1048576")  # absorb every case here
     monkeypatch.setenv("CFI_MMVQ_DIRECT", direct)
+    # absorption is built on the decode-fast kernels (Q4_K with 3+ columns otherwise takes the
+    # tensor-core GEMV, which does not absorb)
+    monkeypatch.setenv("CFI_MMVQ_EXACT", "1")
     gp, gf, fctx = ctxs
     for nrows, ncols_x, pad in [(8192, 2048, 0), (300, 4096, 0), (37, 512, 512)]:
         w, x, ne00, ne0, s01 = case(ty, ncols, nrows, ncols_x, pad, 11 + ty + ncols + nrows)
