@@ -29,7 +29,8 @@
 //     buffers and O += P V (M 128, N = D, K 128; V is the MN-major B operand) into the TMEM output.
 // TMEM: scores at columns 0 and 128, output at 256.  Every wait is bounded (error word + abort).
 // Arithmetic: fp16 Q and P (as ggml's tensor-core kernel rounds them), fp32 scores, softmax and
-// accumulation; results agree with the exact softmax attention to ~1e-3 relative.
+// accumulation; results agree with the exact softmax attention to about 2e-4 relative L2 (nmse
+// about 4e-8 on the reference's probe cases), the error of the two fp16 roundings.
 #include <cuda.h>
 
 #include <string.h>

@@ -782,7 +782,7 @@ int probe_soft_max(const cfi_plan& plan, void* stream, std::string* why) {
 
 // probe.rs:379-390: one FlashAttention tile (16 + 3 queries), 4 heads over 2 KV heads, 70 keys
 // (a partial chunk), causal mask with a padded third, seed 0xfa77 (probe.rs:421-446); exact f64
-// attention on the host.  fp16 Q and P on the tensor cores: nmse < 1e-5 (~3e-3 relative).
+// attention on the host.  fp16 Q and P on the tensor cores (nmse about 4e-8): accepted below 1e-6.
 int probe_fattn(const cfi_plan& plan, void* stream, std::string* why) {
     const uint32_t d = plan.aux, nq = 19, nh = 4, nhk = 2, nkv = 70, ns = 1, nq_pad = 32;
     if (d != 64 && d != 128) {
@@ -862,7 +862,7 @@ int probe_fattn(const cfi_plan& plan, void* stream, std::string* why) {
     if (rc) return rc;
     CK(cudaMemcpy(got.data(), dd, got.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess);
     const double e = nmse(got, want);
-    if (!(e < 1e-5)) {
+    if (!(e < 1e-6)) {
         *why = "fattn probe nmse " + std::to_string(e);
         return (int)cudaErrorInvalidValue;
     }

@@ -1,7 +1,8 @@
 """GPU tests of the native FlashAttention (flash_attn_ext_f16 on tcgen05) through the substitution
 C ABI, against the exact f64 softmax attention of the reference's probe (src/subst/probe.rs:405-489)
 on its case generator (probe.rs:421-446).  Q and P are rounded to fp16 for the tensor cores, as
-ggml's own tensor-core kernel does, so the bound is 3e-3 relative L2."""
+ggml's own tensor-core kernel does; that rounding alone gives about 2e-4 relative L2 (nmse about
+4e-8, the same as a float64 model of the rounding), inside the 1e-3 relative L2 bound."""
 import numpy as np
 import pytest
 
@@ -11,7 +12,8 @@ import oracle_py as O
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-REL = 3e-3
+REL = 1e-3
+NMSE = 1e-6
 
 
 @pytest.fixture(scope="module")
@@ -51,6 +53,7 @@ def test_fattn_matches_exact_attention(dev, d, nq, nh, nh_kv, nkv, ns, causal):
     got, want = run_case(g, d, nq, nh, nh_kv, nkv, ns, causal, 0xfa77 + nq + d)
     assert np.isfinite(got).all()
     assert O.rel_l2(got, want) < REL, O.rel_l2(got, want)
+    assert O.nmse(got, want) < NMSE, O.nmse(got, want)
 
 
 def test_fattn_probe_and_fixup_skip(dev):
