@@ -247,7 +247,7 @@ def gemv_legs(cfi, g, stream, dev, peak, shapes=GEMV_SHAPES):
     return out
 
 
-def rowops_bench(cfi, g, stream, dev, peak):
+def rowops_bench(cfi, g, stream, dev, peak, big_only=False):
     """The row kernels at the decode shapes of configs 4/5 (µs per launch: one row or one token, the
     reference's profiled launches) and at a batched shape that streams from HBM (GB/s of
     read + write bytes, inputs rotated over > 2x L2): rms_norm_f32 with the weight multiply (rows of
@@ -266,7 +266,7 @@ def rowops_bench(cfi, g, stream, dev, peak):
 
     for ncols in (896, 1536):
         wv = torch.randn(ncols, device=dev)
-        for nrows, tag in ((1, "dec"), (16384, "big")):
+        for nrows, tag in ((1, "dec"), (16384, "big"))[1 if big_only else 0:]:
             nbuf = 1 if nrows == 1 else max(2, int(np.ceil(2 * L2_BYTES / (nrows * ncols * 8))))
             xs = torch.randn(nbuf, nrows * ncols, device=dev)
             ys = torch.zeros_like(xs)
@@ -278,7 +278,7 @@ def rowops_bench(cfi, g, stream, dev, peak):
                 out["rms_norm_%d_big_gbs" % ncols] = round(byts / us / 1e3, 1)
                 out["rms_norm_%d_big_frac" % ncols] = round(byts / us / 1e3 / peak, 4)
     for nh, hd in ((14, 64), (12, 128)):
-        for ntok, tag in ((1, "dec"), (4096, "big")):
+        for ntok, tag in ((1, "dec"), (4096, "big"))[1 if big_only else 0:]:
             n = nh * hd * ntok
             nbuf = 1 if ntok == 1 else max(2, int(np.ceil(2 * L2_BYTES / (n * 8))))
             xs = torch.randn(nbuf, n, device=dev)
@@ -292,7 +292,7 @@ def rowops_bench(cfi, g, stream, dev, peak):
                 out["rope_%dx%d_big_gbs" % (nh, hd)] = round(byts / us / 1e3, 1)
                 out["rope_%dx%d_big_frac" % (nh, hd)] = round(byts / us / 1e3 / peak, 4)
     ncols, nh = 632, 14
-    for ne01, tag in ((1, "dec"), (631 * 8, "big")):
+    for ne01, tag in ((1, "dec"), (631 * 8, "big"))[1 if big_only else 0:]:
         nbuf = 1 if ne01 == 1 else max(2, int(np.ceil(2 * L2_BYTES / (ne01 * nh * ncols * 8))))
         xs = torch.randn(nbuf, ne01 * nh * ncols, device=dev)
         ys = torch.zeros_like(xs)
@@ -305,7 +305,7 @@ def rowops_bench(cfi, g, stream, dev, peak):
             out["soft_max_big_gbs"] = round(byts / us / 1e3, 1)
             out["soft_max_big_frac"] = round(byts / us / 1e3 / peak, 4)
     for k in (896, 1536):
-        for ncol, tag in ((1, "dec"), (16384, "big")):
+        for ncol, tag in ((1, "dec"), (16384, "big"))[1 if big_only else 0:]:
             nbuf = 1 if ncol == 1 else max(2, int(np.ceil(2 * L2_BYTES / (ncol * k * 5))))
             xs = torch.randn(nbuf, ncol * k, device=dev)
             qs = torch.zeros(nbuf, ncol * k // 32 * 36, dtype=torch.uint8, device=dev)
@@ -1045,6 +1045,22 @@ def only_gemv(spec):
     ctx.close()
 
 
+def only_rowops():
+    """The row kernels at their batched shapes alone (the rowops leg without the decode shapes),
+    printed as one JSON line: the profiling entry of the row-kernel summaries."""
+    import torch
+
+    import cfi_b200 as cfi
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    stream = torch.cuda.Stream(device=dev)
+    print(json.dumps({"only_rowops": rowops_bench(cfi, g, stream, dev, peaks()[0], big_only=True)}), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1059,6 +1075,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--separate-quantize", action="store_true",
                     help="launch quantize_q8_1 and mul_mat_vec_q separately (no CFI_CTX_DEFER_Q8_1)")
+    ap.add_argument("--only-rowops", action="store_true",
+                    help="time only the row kernels at their batched shapes (for profiling) and exit")
     ap.add_argument("--only-gemv", default="",
                     help="type:rows:k:batch (e.g. q4k:65536:2048:8): time only that mul_mat_vec_q (for profiling) and exit")
     args = ap.parse_args()
@@ -1066,6 +1084,9 @@ def main():
         args.warmup = 3
     if args.only_gemv:
         only_gemv(args.only_gemv)
+        return
+    if args.only_rowops:
+        only_rowops()
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
