@@ -61,9 +61,16 @@ constexpr int CFI_MMVQ_WARPS = CFI_MMVQ_THREADS / 32;
 
 // k_rowops.cu
 const void* cfi_native_rms_norm(int do_multiply, int do_add);  // ggml rms_norm_f32<*, mul, add>
+const void* cfi_native_rms_norm_block(int do_multiply, int do_add);  // the same, one CTA per row (small launches)
 const void* cfi_native_rms_norm_plain();                        // rms_norm_f32<32> (iiilllf ABI)
 const void* cfi_native_rope_neox(int forward, int has_ff);     // rope_neox<fwd, ff, float>
 const void* cfi_native_soft_max(int mask_f16);                  // soft_max_f32<*, *, *, T>
+// warp-per-row soft_max (ncols % 4 == 0, <= cfi_soft_max_rows_max_cols(), aligned rows); trailing u32 ne01
+const void* cfi_native_soft_max_rows(int mask_f16);
+int cfi_soft_max_rows_max_cols();
+int cfi_rope_rows_per_warp(uint32_t nrows);  // rope_neox rows per warp for a launch of nrows rows (1: small)
+const void* cfi_native_rope_neox_pairs(int forward, int has_ff);  // thread per pair, for small launches
+int cfi_rope_max_ne0();       // longest row rope_neox takes (pairs per lane kept in registers)
 constexpr int CFI_ROWOP_THREADS = 256;
 
 // k_gemm_sm100.cu: tcgen05 GEMM on K-major fp16/bf16 operands, fp32 accumulation:

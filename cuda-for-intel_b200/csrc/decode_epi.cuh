@@ -22,9 +22,19 @@ CFI_DEV void q8_1_store_lane(float v, uint8_t* blk, int lane) {
     if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = (uint32_t)f2h_bits(d) | ((uint32_t)f2h_bits(sm) << 16);
 }
 
+// The sum-of-squares order of the warp-per-row rms_norm (vector path): lane l adds the squares of
+// its 16-byte pieces l, l + 32, ... in order, four fma each, then the xor butterfly 16..1.
+CFI_DEV float rms_fma4(float4 v, float ss) {
+    ss = __fmaf_rn(v.x, v.x, ss);
+    ss = __fmaf_rn(v.y, v.y, ss);
+    ss = __fmaf_rn(v.z, v.z, ss);
+    return __fmaf_rn(v.w, v.w, ss);
+}
+
 // x += y (y may be null), then q8_1 blocks of rms_norm(x) * w, by the whole block (>= 256
-// threads, a multiple of 32).  The sum of squares is formed as the native rms_norm forms it (256
-// thread-strided fma chains, then the two-level butterfly); hbuf: n floats of shared memory.
+// threads, a multiple of 32).  The sum of squares is formed as the native rms_norm forms it for a
+// decode step (cfi_rms_norm_block: 256 thread-strided fma chains, then the two-level butterfly),
+// so the two agree bit for bit; hbuf: n floats of shared memory.
 // y is read through L2 (it may have been written by other CTAs of this grid).
 CFI_DEV void epi_add_rmsnorm_q81(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ w,
                                  uint8_t* __restrict__ out, int n, float eps, float* hbuf) {

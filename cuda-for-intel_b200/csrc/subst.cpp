@@ -753,6 +753,15 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         if (block[1] != 1 || block[2] != 1 || !pow2(block[0]) || block[0] < 32 || block[0] > 1024) return false;
         nl.fn = plan.kernel == CFI_K_RMS_NORM ? cfi_native_rms_norm(plan.aux & 1, (plan.aux >> 1) & 1) : cfi_native_rms_norm_plain();
         memcpy(nl.grid, grid, sizeof nl.grid);
+        // batched launches (>= 1024 rows): one warp per row, 8 rows per CTA, the row count appended;
+        // fewer rows (a decode step): one CTA per row, the order the fused decode step reproduces
+        if (plan.kernel == CFI_K_RMS_NORM && (uint64_t)grid[0] * grid[1] * grid[2] >= 1024) {
+            const uint32_t wpb = CFI_ROWOP_THREADS / 32;
+            nl.grid[0] = (grid[0] + wpb - 1) / wpb;
+            nl.extra.push_back(grid[0]);
+        } else if (plan.kernel == CFI_K_RMS_NORM) {
+            nl.fn = cfi_native_rms_norm_block(plan.aux & 1, (plan.aux >> 1) & 1);
+        }
         nl.block[0] = CFI_ROWOP_THREADS;
         nl.pdl = pdl_enabled();
         break;
@@ -760,25 +769,59 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         if (!block_is(block, 1, 256, 1) || nvals < 7 || grid[2] != 1) return false;
         const uint64_t ne0 = (uint32_t)vals[2], n_dims = (uint32_t)vals[6];
         if (ne0 == 0 || (ne0 & 1) || (n_dims & 1) || n_dims > ne0) return false;
+        if (ne0 > (uint64_t)cfi_rope_max_ne0()) return false;
         const uint64_t nr = grid[0];
-        const uint64_t pairs = nr * (ne0 / 2);
-        nl.fn = cfi_native_rope_neox(plan.aux & 1, (plan.aux >> 1) & 1);
-        nl.grid[0] = (uint32_t)((pairs + CFI_ROWOP_THREADS - 1) / CFI_ROWOP_THREADS);
+        const uint32_t rpw = (uint32_t)cfi_rope_rows_per_warp((uint32_t)nr);
         nl.block[0] = CFI_ROWOP_THREADS;
         nl.extra.push_back((uint32_t)nr);
+        if (rpw > 1) {  // large launches: a warp per rpw rows, the frequencies kept per lane
+            const uint64_t rpc = (uint64_t)rpw * (CFI_ROWOP_THREADS / 32);
+            nl.fn = cfi_native_rope_neox(plan.aux & 1, (plan.aux >> 1) & 1);
+            nl.grid[0] = (uint32_t)((nr + rpc - 1) / rpc);
+            nl.extra.push_back(rpw);
+        } else {  // a thread per rotation pair
+            const uint64_t pairs = nr * (ne0 / 2);
+            nl.fn = cfi_native_rope_neox_pairs(plan.aux & 1, (plan.aux >> 1) & 1);
+            nl.grid[0] = (uint32_t)((pairs + CFI_ROWOP_THREADS - 1) / CFI_ROWOP_THREADS);
+        }
         nl.pdl = pdl_enabled();
         break;
     }
     case CFI_K_SOFT_MAX: {
         if (block[1] != 1 || block[2] != 1 || block[0] == 0 || block[0] > 1024) return false;
-        int64_t ncols = 0;
-        if (args && args[4]) memcpy(&ncols, static_cast<const uint8_t*>(args[4]) + 16, 8);
+        int64_t ncols = 0, nb[3] = {0, 0, 0};
+        if (args && args[4]) {
+            memcpy(&ncols, static_cast<const uint8_t*>(args[4]) + 16, 8);
+            memcpy(nb, static_cast<const uint8_t*>(args[4]) + 72, 24);  // nb11, nb12, nb13
+        }
         if (args && (ncols <= 0 || ncols * 4 > 200 * 1024)) return false;
-        nl.fn = cfi_native_soft_max(plan.aux & 1);
         memcpy(nl.grid, grid, sizeof nl.grid);
         nl.block[0] = CFI_ROWOP_THREADS;
-        nl.smem = (size_t)ncols * 4;
         nl.pdl = pdl_enabled();
+        // rows of at most 1024 columns in 16-byte pieces: one warp per row, the row in registers
+        // (launches of a few rows, as a decode step's heads, keep the CTA-per-row kernel: more
+        // threads per row give the shorter chain)
+        bool rows = false;
+        const uint64_t total_rows = (uint64_t)grid[0] * grid[1] * grid[2];
+        if (args && args[0] && args[1] && args[3] && ncols % 4 == 0 && ncols <= cfi_soft_max_rows_max_cols() &&
+            total_rows >= 1024) {
+            uint64_t xp = 0, mp = 0, dp = 0;
+            memcpy(&xp, args[0], 8);
+            memcpy(&mp, args[1], 8);
+            memcpy(&dp, args[3], 8);
+            const uint64_t malign = (plan.aux & 1) ? 8 : 16;
+            rows = ((xp | dp) & 15) == 0 && (mp % malign) == 0 &&
+                   (mp == 0 || ((uint64_t)nb[0] % malign == 0 && (uint64_t)nb[1] % malign == 0 && (uint64_t)nb[2] % malign == 0));
+        }
+        if (rows) {
+            const uint32_t wpb = CFI_ROWOP_THREADS / 32;
+            nl.fn = cfi_native_soft_max_rows(plan.aux & 1);
+            nl.grid[0] = (grid[0] + wpb - 1) / wpb;
+            nl.extra.push_back(grid[0]);
+        } else {
+            nl.fn = cfi_native_soft_max(plan.aux & 1);
+            nl.smem = (size_t)ncols * 4;
+        }
         break;
     }
     case CFI_K_FATTN: {

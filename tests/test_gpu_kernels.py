@@ -274,7 +274,10 @@ def test_decode_configs_full_size(dev, monkeypatch, ty, rows, k, ncols, exact):
 def test_rms_norm_matches_the_oracle(dev):
     ctx, g = dev
     rng = np.random.default_rng(12)
-    for rows, ncols, mul in [(4, 896, True), (631, 1536, True), (3, 896, False)]:
+    # under 1024 rows: one CTA per row; from 1024 rows: one warp per row (16-byte pieces, up to 16
+    # of them kept per lane: 3000 columns reload the rest; 1538 columns take the scalar path)
+    for rows, ncols, mul in [(4, 896, True), (631, 1536, True), (3, 896, False), (2048, 896, True),
+                             (1100, 1538, True), (1024, 3000, False), (1030, 1536, True)]:
         x = rng.normal(size=(rows, ncols)).astype(np.float32)
         w = rng.normal(size=ncols).astype(np.float32)
         dx, dw = to_dev(x), to_dev(w)
@@ -307,8 +310,13 @@ def test_rms_norm_reference_test_case(dev):
 def test_rope_neox_matches_the_oracle(dev, head_dim, heads, ff):
     ctx, g = dev
     rng = np.random.default_rng(head_dim + heads)
-    ntok = 7
+    for ntok in (7, 400):  # 400 tokens x 14-16 heads: four rows per warp
+        rope_case(g, rng, head_dim, heads, ff, ntok)
+
+
+def rope_case(g, rng, head_dim, heads, ff, ntok):
     pos = np.array([0, 1, 5, 100, 630, 631, 2047], dtype=np.int32)
+    pos = np.resize(pos, ntok) + np.arange(ntok, dtype=np.int32) // 7
     x = rng.normal(size=(ntok, heads, head_dim)).astype(np.float32)
     ffv = (1.0 + rng.random(head_dim // 2)).astype(np.float32) if ff else None
     dx, dp = to_dev(x), to_dev(pos)
@@ -322,7 +330,9 @@ def test_rope_neox_matches_the_oracle(dev, head_dim, heads, ff):
 
 
 @pytest.mark.parametrize("ncols,ne01,nheads,f16,max_bias", [(12, 1, 2, False, 0.0), (631, 1, 14, False, 0.0),
-                                                          (631, 5, 12, True, 0.0), (700, 3, 12, False, 8.0)])
+                                                          (631, 5, 12, True, 0.0), (700, 3, 12, False, 8.0),
+                                                          (632, 80, 14, False, 0.0), (640, 90, 12, True, 0.0),
+                                                          (1024, 100, 12, False, 8.0), (1100, 100, 12, False, 0.0)])
 def test_soft_max_matches_the_oracle(dev, ncols, ne01, nheads, f16, max_bias):
     ctx, g = dev
     rng = np.random.default_rng(ncols + nheads)
