@@ -104,3 +104,21 @@ float* cfi_splitk_workspace(size_t bytes, cudaStream_t stream);
 int cfi_splitk_reduce_f32(const float* ws, uint32_t ld_ws, uint32_t m, uint32_t n, uint32_t planes, uint32_t splits,
                           float* c, long long ldc, long long c_zstride, long long c_wstride, uint32_t nch,
                           cudaStream_t stream, bool pdl);
+
+// ---- per-(device, stream) scratch (stream_state.cpp) ----
+constexpr int CFI_AMAX_CTAS = 148;                                  // argmax_next CTAs
+constexpr int CFI_ATT_MAX_HEADS = 64, CFI_ATT_MAX_SPLIT = 64;        // split attention partials
+struct CfiGlueSlot {
+    unsigned int* amax_count;  // 1
+    unsigned int* att_count;   // CFI_ATT_MAX_HEADS
+    unsigned int* epi_count;   // 4 (GEMVs with a fused decode step, one per step kind)
+    float* amax_val;           // CFI_AMAX_CTAS
+    int* amax_idx;             // CFI_AMAX_CTAS
+    float* att_part;           // CFI_ATT_MAX_HEADS x CFI_ATT_MAX_SPLIT x (2 + 128)
+};
+// The glue slot of the current device and `stream` (0 or a CUDA error code).
+int cfi_glue_slot(cudaStream_t stream, CfiGlueSlot* out);
+// A buffer of at least `bytes` for (current device, stream, kind), grown outside stream capture
+// only (*err = cudaErrorStreamCaptureUnsupported when it would have to grow under capture).
+enum { CFI_BUF_SPLITK = 1, CFI_BUF_MMQ_SCRATCH = 2 };
+void* cfi_stream_buffer(int kind, size_t bytes, cudaStream_t stream, int* err);

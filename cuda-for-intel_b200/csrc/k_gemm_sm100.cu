@@ -630,30 +630,11 @@ bool dtype_ok(int t) { return t == CFI_R_32F || t == CFI_R_16F || t == CFI_R_16B
 
 }  // namespace
 
-// Per-device split-K workspace (fp32 partial tiles), grown outside stream capture only.  A
-// replaced buffer is kept, not freed: graphs captured earlier still name it.
-static std::mutex g_ws_mu;
-static std::map<int, std::pair<void*, size_t>> g_ws;
-static std::vector<void*> g_ws_retired;
+// Split-K workspace (fp32 partial tiles): the calling stream's own buffer (stream_state.cpp),
+// grown outside stream capture only; nullptr (no split) when it would have to grow under capture.
 static float* splitk_workspace(size_t bytes, cudaStream_t stream) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-    std::lock_guard<std::mutex> g(g_ws_mu);
-    auto& w = g_ws[dev];
-    if (w.second < bytes) {
-        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(stream, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone) return nullptr;
-        if (w.first) g_ws_retired.push_back(w.first);
-        w.first = nullptr;
-        w.second = 0;
-        const size_t want = bytes + bytes / 4;
-        if (cudaMalloc(&w.first, want) != cudaSuccess) {
-            cudaGetLastError();
-            return nullptr;
-        }
-        w.second = want;
-    }
-    return static_cast<float*>(w.first);
+    int err = 0;
+    return static_cast<float*>(cfi_stream_buffer(CFI_BUF_SPLITK, bytes, stream, &err));
 }
 
 // Shared tensor-core launcher (the cuBLAS-compatible GEMM and the prefill mul_mat_q use it).

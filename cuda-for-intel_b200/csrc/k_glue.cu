@@ -8,6 +8,7 @@
 
 #include "../../include/cfi_glue.h"
 #include "cfi_common.cuh"
+#include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
 #include "decode_epi.cuh"
 
@@ -88,12 +89,9 @@ __global__ void swiglu(const float* __restrict__ g, const float* __restrict__ u,
 }
 
 // token[0] = argmax(logits) (first index of the maximum), pos[0] += 1.  AMAX_CTAS CTAs reduce
-// contiguous ranges; the last CTA to finish (device counter) reduces their results in CTA order
-// and resets the counter.  The partials live in device globals: one call at a time per device.
-constexpr int AMAX_CTAS = 148;
-static __device__ float g_amax_val[AMAX_CTAS];
-static __device__ int g_amax_idx[AMAX_CTAS];
-static __device__ unsigned int g_amax_count;
+// contiguous ranges; the last CTA to finish (the slot's counter) reduces their results in CTA
+// order and resets the counter.  The partials live in the calling stream's glue slot.
+constexpr int AMAX_CTAS = CFI_AMAX_CTAS;
 
 CFI_DEV void amax_pair_reduce(float& best, int& idx) {
     for (int o = 16; o > 0; o >>= 1) {
@@ -107,7 +105,8 @@ CFI_DEV void amax_pair_reduce(float& best, int& idx) {
 }
 
 __global__ void __launch_bounds__(512) argmax_next(const float* __restrict__ logits, int n, int32_t* __restrict__ token,
-                                                   int32_t* __restrict__ pos) {
+                                                   int32_t* __restrict__ pos, float* __restrict__ amax_val,
+                                                   int* __restrict__ amax_idx, unsigned int* __restrict__ amax_count) {
     sm100::pdl_launch_dependents();
     sm100::pdl_wait();
     __shared__ float bv[16];
@@ -136,10 +135,10 @@ __global__ void __launch_bounds__(512) argmax_next(const float* __restrict__ log
         idx = lane < (int)(blockDim.x >> 5) ? bi[lane] : 0x7fffffff;
         amax_pair_reduce(best, idx);
         if (lane == 0) {
-            g_amax_val[blockIdx.x] = best;
-            g_amax_idx[blockIdx.x] = idx;
+            amax_val[blockIdx.x] = best;
+            amax_idx[blockIdx.x] = idx;
             __threadfence();
-            last = atomicAdd(&g_amax_count, 1u) == gridDim.x - 1;
+            last = atomicAdd(amax_count, 1u) == gridDim.x - 1;
         }
     }
     __syncthreads();
@@ -148,8 +147,8 @@ __global__ void __launch_bounds__(512) argmax_next(const float* __restrict__ log
     best = -INFINITY;
     idx = 0x7fffffff;
     for (int b = lane; b < (int)gridDim.x; b += 32) {
-        const float v = __ldcg(&g_amax_val[b]);
-        const int i = __ldcg(&g_amax_idx[b]);
+        const float v = __ldcg(&amax_val[b]);
+        const int i = __ldcg(&amax_idx[b]);
         if (v > best || (v == best && i < idx)) {
             best = v;
             idx = i;
@@ -159,7 +158,7 @@ __global__ void __launch_bounds__(512) argmax_next(const float* __restrict__ log
     if (lane == 0) {
         token[0] = idx;
         pos[0] += 1;
-        g_amax_count = 0;
+        *amax_count = 0;
     }
 }
 
@@ -200,17 +199,17 @@ __global__ void __launch_bounds__(256) qkv_rope_store(const float* __restrict__ 
 // [s chunk, (s + 1) chunk) that are <= pos[0] for query head h: scores (thread t: position t of the
 // range, the K row read whole with 16-byte loads), the range's max m_s, e_j = exp(score_j - m_s),
 // l_s = sum e_j and o_s[d] = sum e_j V[d][j] (256 / head_dim threads per dim over 8-position runs
-// of the V^T row).  The partials go to device globals; the last CTA of the head (device counter)
+// of the V^T row).  The partials go to the slot; the last CTA of the head (the slot's counter)
 // combines them in split order, out[d] = sum_s o_s[d] e^(m_s - M) / sum_s l_s e^(m_s - M), writes
-// the head_dim / 32 q8_1 blocks and resets the counter.  One call at a time per device.
-constexpr int ATT_MAX_CTX = 8192, ATT_MAX_HEADS = 64, ATT_MAX_SPLIT = 64, ATT_CHUNK = 128;
-static __device__ float g_att_part[ATT_MAX_HEADS * ATT_MAX_SPLIT * (2 + 128)];
-static __device__ unsigned int g_att_count[ATT_MAX_HEADS];
+// the head_dim / 32 q8_1 blocks and resets the counter.  The partials and counters live in the
+// calling stream's glue slot.
+constexpr int ATT_MAX_CTX = 8192, ATT_MAX_HEADS = CFI_ATT_MAX_HEADS, ATT_MAX_SPLIT = CFI_ATT_MAX_SPLIT, ATT_CHUNK = 128;
 
 __global__ void __launch_bounds__(256) attention_q81(const float* __restrict__ q, const __half* __restrict__ kc,
                                                     const __half* __restrict__ vc, const int32_t* __restrict__ pos,
                                                     uint8_t* __restrict__ out, int n_head, int n_kv_head, int head_dim,
-                                                    int n_ctx, float scale, int chunk) {
+                                                    int n_ctx, float scale, int chunk, float* __restrict__ att_part,
+                                                    unsigned int* __restrict__ att_count) {
     sm100::pdl_launch_dependents();
     sm100::pdl_wait();
     __shared__ float sc[ATT_CHUNK * 2];
@@ -293,7 +292,7 @@ __global__ void __launch_bounds__(256) attention_q81(const float* __restrict__ q
         }
     }
     for (int off = tpd / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    float* pp = g_att_part + ((size_t)h * ATT_MAX_SPLIT + split) * (2 + 128);
+    float* pp = att_part + ((size_t)h * ATT_MAX_SPLIT + split) * (2 + 128);
     if (part == 0) pp[2 + d] = acc;
     if (tid == 0) {
         pp[0] = mx;
@@ -301,12 +300,12 @@ __global__ void __launch_bounds__(256) attention_q81(const float* __restrict__ q
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = atomicAdd(&g_att_count[h], 1u) == (unsigned)nsplit - 1;
+    if (tid == 0) last = atomicAdd(&att_count[h], 1u) == (unsigned)nsplit - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
     // ---- combine the splits in order ----
-    const float* hp0 = g_att_part + (size_t)h * ATT_MAX_SPLIT * (2 + 128);
+    const float* hp0 = att_part + (size_t)h * ATT_MAX_SPLIT * (2 + 128);
     float M = -INFINITY;
     for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(hp0 + sp * (2 + 128)));
     if (tid < head_dim) {
@@ -324,7 +323,7 @@ __global__ void __launch_bounds__(256) attention_q81(const float* __restrict__ q
     __syncthreads();
     for (int b = warp; b < head_dim / 32; b += 8)
         q8_1_store_lane(o[32 * b + lane], out + ((size_t)h * (head_dim / 32) + b) * Q8_1_BYTES, lane);
-    if (tid == 0) g_att_count[h] = 0;
+    if (tid == 0) att_count[h] = 0;
 }
 
 // One warp per q8_1 block.
@@ -423,7 +422,10 @@ extern "C" int cfi_glue_swiglu(const float* g, const float* u, float* out, int n
     return launch(swiglu, g1(n), 256, stream, g, u, out, n);
 }
 extern "C" int cfi_glue_argmax_next(const float* logits, int n, int32_t* token, int32_t* pos, void* stream) {
-    return launch(argmax_next, dim3(AMAX_CTAS), 512, stream, logits, n, token, pos);
+    CfiGlueSlot sl;
+    const int rc = cfi_glue_slot(static_cast<cudaStream_t>(stream), &sl);
+    if (rc) return rc;
+    return launch(argmax_next, dim3(AMAX_CTAS), 512, stream, logits, n, token, pos, sl.amax_val, sl.amax_idx, sl.amax_count);
 }
 
 extern "C" int cfi_glue_gather_row_shards(const float* src, float* dst, int nrows, int ncols, int world, void* stream) {
@@ -462,8 +464,11 @@ extern "C" int cfi_fused_attention_q8_1(const float* q, const void* kc, const vo
     // position ranges of at most ATT_CHUNK (a multiple of 8, so V^T runs stay 16-byte aligned)
     const int nsplit = (n_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
     const int chunk = ((n_ctx + nsplit - 1) / nsplit + 7) / 8 * 8;
+    CfiGlueSlot sl;
+    const int rc = cfi_glue_slot(static_cast<cudaStream_t>(stream), &sl);
+    if (rc) return rc;
     return launch(attention_q81, dim3(n_head, nsplit), 256, stream, q, (const __half*)kc, (const __half*)vc, pos,
-                  (uint8_t*)out, n_head, n_kv_head, head_dim, n_ctx, scale, chunk);
+                  (uint8_t*)out, n_head, n_kv_head, head_dim, n_ctx, scale, chunk, sl.att_part, sl.att_count);
 }
 extern "C" int cfi_fused_swiglu_q8_1(const float* gu, void* out, int n, void* stream) {
     if (n <= 0 || n % 32) return (int)cudaErrorInvalidValue;

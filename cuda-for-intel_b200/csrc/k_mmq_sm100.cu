@@ -996,34 +996,12 @@ PFN_encodeTiled encode_fn() {
     return fn;
 }
 
-// Per-device activation scratch (fp16 copy of X), grown outside stream capture only.  A replaced
-// buffer is kept, not freed: graphs captured earlier still name it.
-struct Scratch {
-    void* p = nullptr;
-    size_t cap = 0;
-};
-std::mutex g_scratch_mu;
-std::map<int, Scratch> g_scratch;
-std::vector<void*> g_scratch_retired;
-
+// Activation scratch (fp16 copy of X, and the fp16 weights of the pre-pass path): the calling
+// stream's own buffer (stream_state.cpp), grown outside stream capture only.
 int scratch_for(size_t bytes, cudaStream_t stream, void** out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return (int)cudaErrorNoDevice;
-    std::lock_guard<std::mutex> g(g_scratch_mu);
-    Scratch& s = g_scratch[dev];
-    if (s.cap < bytes) {
-        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(stream, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone)
-            return (int)cudaErrorStreamCaptureUnsupported;
-        if (s.p) g_scratch_retired.push_back(s.p);
-        s.p = nullptr;
-        s.cap = 0;
-        size_t want = bytes + bytes / 4;
-        if (cudaMalloc(&s.p, want) != cudaSuccess) return (int)cudaErrorMemoryAllocation;
-        s.cap = want;
-    }
-    *out = s.p;
-    return 0;
+    int err = 0;
+    *out = cfi_stream_buffer(CFI_BUF_MMQ_SCRATCH, bytes, stream, &err);
+    return *out ? 0 : (err ? err : (int)cudaErrorMemoryAllocation);
 }
 
 unsigned int* device_error_ptr() {

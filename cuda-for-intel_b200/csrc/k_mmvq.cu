@@ -1432,17 +1432,16 @@ unsigned int cfi_mmvq_error_take() {
 }
 
 // ---- GEMV + fused decode step (include/cfi_glue.h) ----
-static __device__ unsigned int g_epi_count[4];
 
 namespace {
 template <int EPI>
 int launch_epi(const void* w, const void* xq, float* y, int rows, int k, DecodeEpi e, size_t epi_smem, void* stream) {
     if (rows <= 0 || k <= 0 || k % 32 || (reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(xq) & 3))
         return (int)cudaErrorInvalidValue;
-    static CfiSymbolPtr<unsigned int[4]> counters;
-    unsigned int(*cp)[4] = counters.get(g_epi_count);
-    if (!cp) return (int)cudaErrorInvalidSymbol;
-    e.counter = *cp + EPI;
+    CfiGlueSlot sl;  // the calling stream's counters
+    const int rc = cfi_glue_slot(static_cast<cudaStream_t>(stream), &sl);
+    if (rc) return rc;
+    e.counter = sl.epi_count + EPI;
     int sms = 148, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -37,8 +37,8 @@ CFI_API int cfi_glue_to_f16(const float *x, void *y, int n, void *stream);
 CFI_API int cfi_glue_add(float *x, const float *y, int n, void *stream);
 /* out = silu(g) * u */
 CFI_API int cfi_glue_swiglu(const float *g, const float *u, float *out, int n, void *stream);
-/* token[0] = first index of max(logits[0..n)); pos[0] += 1 (device-global partials: one call at a
- * time per device) */
+/* token[0] = first index of max(logits[0..n)); pos[0] += 1 (partials in the calling stream's own
+ * scratch: calls on different streams may overlap) */
 CFI_API int cfi_glue_argmax_next(const float *logits, int n, int32_t *token, int32_t *pos, void *stream);
 
 /* Row-shard assembly after an all-gather (the multi-GPU split of the weight rows): src holds
@@ -65,7 +65,7 @@ CFI_API int cfi_fused_qkv_rope_store(const float *qkv, const float *bias, float 
 /* Single-token attention over cache positions 0..pos[0]: per query head h (kv head h / (n_head /
  * n_kv_head)) softmax(scale K q) V in fp32 from the f16 caches, written as q8_1 blocks (head_dim
  * 64 or 128; n_head <= 64; n_ctx a multiple of 8, at most 8192; caches 16-byte aligned).  Split
- * over position ranges with device-global partials: one call at a time per device. */
+ * over position ranges, the partials in the calling stream's own scratch. */
 CFI_API int cfi_fused_attention_q8_1(const float *q, const void *kc, const void *vc, const int32_t *pos,
                                      void *out_q8_1, int n_head, int n_kv_head, int head_dim, int n_ctx, float scale,
                                      void *stream);
@@ -75,8 +75,8 @@ CFI_API int cfi_fused_swiglu_q8_1(const float *gu, void *out_q8_1, int n, void *
 /*
  * GEMV + fused step in one launch: y = W xq (W: rows x k Q8_0, row-major; xq: q8_1 blocks of one
  * column) through the streaming GEMV, whose last CTA to finish then runs the step on y.  Results
- * equal the GEMV followed by the standalone step, bit for bit.  A device counter per step kind
- * is shared: one call of a kind at a time per device.
+ * equal the GEMV followed by the standalone step, bit for bit.  The last-CTA counters are the
+ * calling stream's own.
  */
 /* ... then cfi_fused_add_rmsnorm_q8_1(x, y, norm_w, out, rows, eps); rows <= 8192 */
 CFI_API int cfi_fused_mmvq_add_rmsnorm_q8_1(const void *w, const void *xq, float *y, int rows, int k, float *x,

@@ -80,8 +80,13 @@ def finish(torch):
 
 
 @pytest.mark.gpu
-def test_kernels_match_the_fixtures(dev):
+@pytest.mark.parametrize("exact", ["0", "1"])
+def test_kernels_match_the_fixtures(dev, monkeypatch, exact):
+    """Bitwise against the frozen outputs, except the tensor-core Q4_K GEMV of 3-8 columns (the
+    default; exact int32 block dots, fp32 scales reassociated): nmse < 1e-10 there, bitwise again
+    with CFI_MMVQ_EXACT=1."""
     torch, ctx, g = dev
+    monkeypatch.setenv("CFI_MMVQ_EXACT", exact)
     s = torch.cuda.current_stream().cuda_stream
     n0, ne0, rows = (int(v) for v in G["q81_shape"])
     y = torch.zeros(G["q81_y"].size, dtype=torch.uint8, device="cuda")
@@ -96,7 +101,10 @@ def test_kernels_match_the_fixtures(dev):
         g.mmvq(p.ty, p.ncols_dst, dx.data_ptr(), dy.data_ptr(), out.data_ptr(), p.ncols_x, p.nrows_x,
                stride_row_x=p.stride_row_x, stride_col_y=p.stride_col_y, stride_col_dst=p.stride_col_dst, stream=s)
         finish(torch)
-        assert np.array_equal(bits(out.cpu().numpy()), bits(want)), "mmvq fixture %d" % i
+        if exact == "0" and p.ty == cfi.Q4_K and p.ncols_dst >= 3:
+            assert O.nmse(out.cpu().numpy(), want) < 1e-10, "mmvq fixture %d" % i
+        else:
+            assert np.array_equal(bits(out.cpu().numpy()), bits(want)), "mmvq fixture %d" % i
     for lay, key in ((0, "qmmq_d4"), (1, "qmmq_ds4")):
         q = torch.zeros(G[key].size, dtype=torch.uint8, device="cuda")
         g.quantize_mmq(lay, d(torch, G["qmmq_x"]).data_ptr(), q.data_ptr(), 512, 512, 7, stream=s)
