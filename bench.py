@@ -420,9 +420,9 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     """BASELINE config 5 decode: one batch-64 step (64 independent sequences) over the 28 Q4_K
     layers and the Q8_0 head, the rows of every matrix split over the `world` ranks
     (shard.row_split, weak in memory, strong in work).  Per product: quantize_q8_1_mmq of its input
-    (once per group), the native mul_mat_q on the rank's rows, and with N > 1 an NCCL all-gather of
-    the 64-column outputs on a comm stream followed by cfi_glue_gather_row_shards into ggml's
-    column-major dst.  A group's quantize waits for the previous group's gathers (its input is
+    (once per group), the native mul_mat_q on the rank's rows, and with N > 1 one NCCL all-gather
+    per group of products that share an input (their 64-column outputs back to back) on a comm
+    stream, followed by cfi_glue_gather_row_shards of each product into ggml's column-major dst.  A group's quantize waits for the previous group's gathers (its input is
     computed from them in a real model), so collective latency is exposed as it would be.
     Reported: the step time, the same step without collectives (kernels only), the collectives
     alone, and a check of rank 0's gathered logits against the unsharded head product on rank 0."""
@@ -458,22 +458,33 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     hq = torch.zeros(H // 128 * n * 144, dtype=torch.uint8, device=dev)
     names = list(C5_SHAPES) + ["head"]
     nrows = {**{nm: r for nm, (r, c) in C5_SHAPES.items()}, "head": V}
-    out = {nm: torch.zeros(n * sh[nm].rows_padded, dtype=torch.float32, device=dev) for nm in names}
-    gath = {nm: torch.zeros(world * n * sh[nm].rows_padded, dtype=torch.float32, device=dev) for nm in names} \
+    # the outputs of the products that share an input are back to back in one buffer per group, so
+    # one all-gather per group carries them (each rank's slices of a group contiguous)
+    groups = [inputs for inputs, _ in C5_GROUPS] + [("head",)]
+    gsize, goff = {}, {}
+    for grp in groups:
+        o = 0
+        for nm in grp:
+            goff[nm] = o
+            o += n * sh[nm].rows_padded
+        gsize[grp] = o
+    gbuf = {grp: torch.zeros(gsize[grp], dtype=torch.float32, device=dev) for grp in groups}
+    out = {nm: gbuf[grp][goff[nm]:goff[nm] + n * sh[nm].rows_padded] for grp in groups for nm in grp}
+    gath = {grp: torch.zeros(world * gsize[grp], dtype=torch.float32, device=dev) for grp in groups} \
         if world > 1 else None
     full = {nm: torch.zeros(n * nrows[nm], dtype=torch.float32, device=dev) for nm in names} if world > 1 else None
 
-    def gathers(cur, nms):
-        """all-gather + assembly of the named outputs on the comm stream after `cur`'s work so far;
-        returns the event that marks their completion."""
+    def gathers(cur, grp):
+        """all-gather of one group's outputs + assembly of each product into ggml's layout, on the
+        comm stream after `cur`'s work so far; returns the event that marks their completion."""
         ev = torch.cuda.Event()
         ev.record(cur)
         comm.wait_event(ev)
         with torch.cuda.stream(comm):
-            for nm in nms:
-                dist.all_gather_into_tensor(gath[nm], out[nm])
-                rc = L_.cfi_glue_gather_row_shards(gath[nm].data_ptr(), full[nm].data_ptr(), nrows[nm], n, world,
-                                                   comm.cuda_stream)
+            dist.all_gather_into_tensor(gath[grp], gbuf[grp])
+            for nm in grp:
+                rc = L_.cfi_glue_gather_row_shards(gath[grp].data_ptr() + 4 * goff[nm], full[nm].data_ptr(), nrows[nm],
+                                                   n, world, gsize[grp], comm.cuda_stream)
                 assert rc == 0, rc
         done = torch.cuda.Event()
         done.record(comm)
@@ -498,7 +509,7 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
                         g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, sh[nm].rows, n,
                               stream=st, stride_col_dst=sh[nm].rows_padded)
                 if coll:
-                    prev = gathers(cur, inputs)
+                    prev = gathers(cur, tuple(inputs))
         if kernels:
             if prev is not None:
                 cur.wait_event(prev)
@@ -506,7 +517,7 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
             g.mmq(cfi.Q8_0, head.data_ptr(), hq.data_ptr(), out["head"].data_ptr(), H, sh["head"].rows, n, stream=st,
                   stride_col_dst=sh["head"].rows_padded)
         if coll:
-            prev = gathers(cur, ["head"])
+            prev = gathers(cur, ("head",))
             cur.wait_event(prev)
 
     def timed(**kw):
@@ -561,16 +572,16 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
                  "logits_nonfinite": int((~torch.isfinite(got)).sum()), "ref_nonfinite": int((~torch.isfinite(ref)).sum())}
     if dist:
         dist.barrier()
-    launches = L * (4 + 7) + 2 + (L * 7 + 1 if world > 1 else 0)
+    launches = L * (4 + 7) + 2 + (L * 7 + 1 if world > 1 else 0)  # + one assembly per product
     res = {"ms": round(ms_step, 4), "tok_per_s": round(64 / (ms_step * 1e-3), 1),
            "weights_gbs": round(wbytes / ms_step / 1e6, 1),
            "frac": round(wbytes / ms_step / 1e6 / (peak_gbs * world), 4),
            "kernels_only_ms": round(ms_kern, 4), "collectives_only_ms": round(ms_coll, 4),
-           "all_gathers_per_step": (L * 7 + 1) if world > 1 else 0,
+           "all_gathers_per_step": (L * len(C5_GROUPS) + 1) if world > 1 else 0,
            "gathered_bytes_per_gpu": (world - 1) * n * 4 * (L * sum(sh[nm].rows_padded for nm in C5_SHAPES) +
                                                             sh["head"].rows_padded),
            "launches": launches, "gpus": world, **check}
-    del layers, head, head_full, out, gath, full
+    del layers, head, head_full, out, gbuf, gath, full
     return res
 
 

@@ -120,7 +120,7 @@ def lib():
     L.cfi_glue_add.argtypes = [vp, vp, i, vp]
     L.cfi_glue_swiglu.argtypes = [vp, vp, vp, i, vp]
     L.cfi_glue_argmax_next.argtypes = [vp, i, vp, vp, vp]
-    L.cfi_glue_gather_row_shards.argtypes = [vp, vp, i, i, i, vp]
+    L.cfi_glue_gather_row_shards.argtypes = [vp, vp, i, i, i, ll, vp]
     L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]

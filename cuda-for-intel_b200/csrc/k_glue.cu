@@ -333,11 +333,13 @@ __global__ void __launch_bounds__(256) swiglu_q81(const float* __restrict__ gu, 
     epi_swiglu_q81(gu, out, n, blockIdx.x * 8 + (threadIdx.x >> 5), gridDim.x * 8);
 }
 
-// Row-shard assembly after an all-gather of column-major slices: src holds `world` slices of
-// ncols columns x rows_padded values (rank r's rows first, padding after), dst ggml's column-major
-// ncols x nrows output; rank r owns rows [r*base + min(r, extra), +base + (r < extra)).
+// Row-shard assembly after an all-gather of column-major slices: src holds `world` slices (slice r
+// at src + r * rank_stride) of ncols columns x rows_padded values (rank r's rows first, padding
+// after), dst ggml's column-major ncols x nrows output; rank r owns rows
+// [r*base + min(r, extra), +base + (r < extra)).
 __global__ void __launch_bounds__(256) gather_row_shards(const float* __restrict__ src, float* __restrict__ dst,
-                                                         uint32_t nrows, uint32_t ncols, uint32_t world) {
+                                                         uint32_t nrows, uint32_t ncols, uint32_t world,
+                                                         uint64_t rank_stride) {
     sm100::pdl_launch_dependents();
     sm100::pdl_wait();
     const uint32_t base = nrows / world, extra = nrows - base * world, rp = base + (extra ? 1u : 0u);
@@ -348,7 +350,7 @@ __global__ void __launch_bounds__(256) gather_row_shards(const float* __restrict
         const uint32_t big = extra * (base + 1u);
         const uint32_t r = row < big ? row / (base + 1u) : extra + (row - big) / base;
         const uint32_t row0 = r * base + min(r, extra);
-        dst[i] = src[((uint64_t)r * ncols + c) * rp + (row - row0)];
+        dst[i] = src[(uint64_t)r * rank_stride + (uint64_t)c * rp + (row - row0)];
     }
 }
 
@@ -428,14 +430,18 @@ extern "C" int cfi_glue_argmax_next(const float* logits, int n, int32_t* token, 
     return launch(argmax_next, dim3(AMAX_CTAS), 512, stream, logits, n, token, pos, sl.amax_val, sl.amax_idx, sl.amax_count);
 }
 
-extern "C" int cfi_glue_gather_row_shards(const float* src, float* dst, int nrows, int ncols, int world, void* stream) {
-    if (nrows <= 0 || ncols <= 0 || world <= 0 || world > nrows) return (int)cudaErrorInvalidValue;
+extern "C" int cfi_glue_gather_row_shards(const float* src, float* dst, int nrows, int ncols, int world,
+                                          long long src_rank_stride, void* stream) {
+    if (nrows <= 0 || ncols <= 0 || world <= 0 || world > nrows || src_rank_stride < 0) return (int)cudaErrorInvalidValue;
+    const uint64_t rp = (uint64_t)(nrows / world + (nrows % world ? 1 : 0));
+    const uint64_t rs = src_rank_stride ? (uint64_t)src_rank_stride : rp * (uint64_t)ncols;
+    if (rs < rp * (uint64_t)ncols) return (int)cudaErrorInvalidValue;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint64_t total = (uint64_t)nrows * (uint64_t)ncols;
     const unsigned grid = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 8));
-    return launch(gather_row_shards, dim3(grid), 256, stream, src, dst, (uint32_t)nrows, (uint32_t)ncols, (uint32_t)world);
+    return launch(gather_row_shards, dim3(grid), 256, stream, src, dst, (uint32_t)nrows, (uint32_t)ncols, (uint32_t)world, rs);
 }
 
 extern "C" int cfi_fused_add_rmsnorm_q8_1(float* x, const float* y, const float* w, void* out, int n, float eps,

@@ -42,11 +42,14 @@ CFI_API int cfi_glue_swiglu(const float *g, const float *u, float *out, int n, v
 CFI_API int cfi_glue_argmax_next(const float *logits, int n, int32_t *token, int32_t *pos, void *stream);
 
 /* Row-shard assembly after an all-gather (the multi-GPU split of the weight rows): src holds
- * `world` rank slices, slice r = ncols columns of rows_padded = ceil(nrows / world) fp32 values
+ * `world` rank slices, slice r at src + r * src_rank_stride floats (0: ncols * rows_padded, the
+ * slices back to back), each ncols columns of rows_padded = ceil(nrows / world) fp32 values
  * (rank r's rows first, padding after); dst gets ggml's column-major ncols x nrows output.  Rank
  * r owns rows [r*base + min(r, extra), ... + base + (r < extra)) with base = nrows / world,
- * extra = nrows % world (the split of shard.row_split). */
-CFI_API int cfi_glue_gather_row_shards(const float *src, float *dst, int nrows, int ncols, int world, void *stream);
+ * extra = nrows % world (the split of shard.row_split).  A non-zero stride lets one all-gather
+ * carry several products' slices (each rank's slices of a group back to back). */
+CFI_API int cfi_glue_gather_row_shards(const float *src, float *dst, int nrows, int ncols, int world,
+                                       long long src_rank_stride, void *stream);
 
 /*
  * Fused decode steps (one launch each where the ggml graph has two to five).  Results equal the
