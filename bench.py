@@ -425,7 +425,8 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     stream, followed by cfi_glue_gather_row_shards of each product into ggml's column-major dst.  A group's quantize waits for the previous group's gathers (its input is
     computed from them in a real model), so collective latency is exposed as it would be.
     Reported: the step time, the same step without collectives (kernels only), the collectives
-    alone, and a check of rank 0's gathered logits against the unsharded head product on rank 0."""
+    alone, the step with the products of a group as parallel graph branches (side streams), and a
+    check of rank 0's gathered logits against the unsharded head product on rank 0."""
     import torch
 
     import shard
@@ -490,7 +491,12 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
         done.record(comm)
         return done
 
-    def step(kernels=True, collectives=True):
+    side = [torch.cuda.Stream(device=dev) for _ in range(2)]
+
+    def step(kernels=True, collectives=True, parallel=False):
+        """parallel: the products of a group after the first run on side streams, as parallel
+        branches (each product depends only on the group's quantized input); every stream has
+        its own split-K workspace and scratch."""
         cur = torch.cuda.current_stream()
         st = cur.cuda_stream
         coll = collectives and world > 1
@@ -505,9 +511,22 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
                     if prev is not None:
                         cur.wait_event(prev)
                     g.quantize_mmq(1, xf[k].data_ptr(), xq[k].data_ptr(), k, k, n, stream=st)
-                    for nm in inputs:
+                    branches = []
+                    if parallel and len(inputs) > 1:
+                        ev = torch.cuda.Event()
+                        ev.record(cur)
+                        for sd in side[:len(inputs) - 1]:
+                            sd.wait_event(ev)
+                    for i, nm in enumerate(inputs):
+                        on = side[i - 1] if parallel and i > 0 else cur
                         g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, sh[nm].rows, n,
-                              stream=st, stride_col_dst=sh[nm].rows_padded)
+                              stream=on.cuda_stream, stride_col_dst=sh[nm].rows_padded)
+                        if on is not cur:
+                            done = torch.cuda.Event()
+                            done.record(on)
+                            branches.append(done)
+                    for done in branches:
+                        cur.wait_event(done)
                 if coll:
                     prev = gathers(cur, tuple(inputs))
         if kernels:
@@ -553,6 +572,7 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     ms_step = timed()
     ms_kern = timed(collectives=False) if world > 1 else ms_step
     ms_coll = timed(kernels=False) if world > 1 else 0.0
+    ms_par = timed(parallel=True)
     # check: rank 0's gathered logits against the unsharded head product on rank 0
     check = {}
     with torch.cuda.stream(stream):
@@ -576,6 +596,8 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     res = {"ms": round(ms_step, 4), "tok_per_s": round(64 / (ms_step * 1e-3), 1),
            "weights_gbs": round(wbytes / ms_step / 1e6, 1),
            "frac": round(wbytes / ms_step / 1e6 / (peak_gbs * world), 4),
+           "parallel_products_ms": round(ms_par, 4),
+           "parallel_products_frac": round(wbytes / ms_par / 1e6 / (peak_gbs * world), 4),
            "kernels_only_ms": round(ms_kern, 4), "collectives_only_ms": round(ms_coll, 4),
            "all_gathers_per_step": (L * len(C5_GROUPS) + 1) if world > 1 else 0,
            "gathered_bytes_per_gpu": (world - 1) * n * 4 * (L * sum(sh[nm].rows_padded for nm in C5_SHAPES) +
@@ -848,6 +870,38 @@ def run_gpu(args, rank, world):
         legs[leg] = {"value": round(STEP_BYTES / us_l / 1e3, 2), "ms_per_step": round(us_l * 1e-3, 5),
                      "launches_per_step": 2 * len(BATCHES), "router": note}
 
+    # ---- the same step with its four independent (quantize, GEMV) pairs on four streams as
+    # parallel graph branches (1 GPU): the throughput of independent decode batches served together;
+    # the headline value above keeps ggml's one-stream order ----
+    if g_sep is not None:
+        pair_streams = [torch.cuda.Stream(device=dev) for _ in BATCHES]
+
+        def step_concurrent(phase, st):
+            cur = torch.cuda.current_stream()
+            fork = torch.cuda.Event()
+            fork.record(cur)
+            joins = []
+            for j, b in enumerate(BATCHES):
+                ps = pair_streams[j]
+                ps.wait_event(fork)
+                g_sep.quantize_q8_1(xs[b].data_ptr(), qs[b].data_ptr(), K, K, b, stream=ps.cuda_stream)
+                g_sep.mmvq(cfi.Q4_K, b, wd[(phase * len(BATCHES) + j) % ncopy].data_ptr(), qs[b].data_ptr(),
+                           y_views[b].data_ptr(), K, ROWS, stream=ps.cuda_stream)
+                done = torch.cuda.Event()
+                done.record(ps)
+                joins.append(done)
+            for done in joins:
+                cur.wait_event(done)
+        with torch.cuda.stream(stream):
+            step_concurrent(0, stream.cuda_stream)  # first use on each stream outside the capture
+        torch.cuda.synchronize()
+        us_c = graph_time_us(stream, lambda i, st: step_concurrent(i % nphase, st), reps=max(3, args.steps // 10),
+                             calls=nphase)
+        legs["concurrent_streams"] = {"value": round(STEP_BYTES / us_c / 1e3, 2), "ms_per_step": round(us_c * 1e-3, 5),
+                                      "launches_per_step": 2 * len(BATCHES),
+                                      "router": "the four (quantize_q8_1, mul_mat_vec_q) pairs on four streams (parallel "
+                                                "graph branches), CFI_CTX_CONST_WEIGHTS"}
+
     # ---- dominant kernel: mmvq Q4_K batch 1, back to back (one graph of ncopy launches over the
     # rotated weight copies), CUDA events on the launching stream around the replays ----
     def roof_body(i, st):
@@ -1014,6 +1068,7 @@ def run_gpu(args, rank, world):
         c5["decode_b64"] = config5_b64(cfi, g, stream, dev, peak, world, rank, dist, comm)
         summary["config5_b64_ms"] = c5["decode_b64"]["ms"]
         summary["config5_b64_kernels_ms"] = c5["decode_b64"]["kernels_only_ms"]
+        summary["config5_b64_parallel_ms"] = c5["decode_b64"]["parallel_products_ms"]
         line["config5"] = c5
     if world == 1 and "cpu" in legs_on:
         gbs, used, n, el = cpu_baseline(args.cpu_seconds)
