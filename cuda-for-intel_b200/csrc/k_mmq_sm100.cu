@@ -1271,6 +1271,14 @@ int launch_tc(const uint64_t* v, cudaStream_t stream, void* fixed_xh = nullptr, 
     const size_t xh_pad = (xh_bytes + 255) & ~(size_t)255;
     const size_t wh_bytes = (size_t)planes_x * nrows * Kt * 2;
     int rc = 0;
+    // at most 64 columns (a decode batch): the skinny kernel streams the weights once on the
+    // warp-level int8 MMAs, in one launch (not for the allocation-free entry point: its K split
+    // takes the stream's buffers)
+    if (!fixed_xh && cfi_mmq_skinny_applies(TY, x, y, K, ncols_dst, srx, planes)) {
+        const char* ep = getenv("CFI_PDL");
+        return cfi_mmq_skinny_launch(TY, x, y, dst, K, nrows, ncols_dst, ncols_y, srx, scd, device_error_ptr(), stream,
+                                     !(ep && strcmp(ep, "0") == 0));
+    }
     const bool fused = qmm_applicable<TY>(x, K, srx, scx, ssx, nch_x, ns / smr);
     if (fixed_xh) {
         if (xh_bytes > fixed_cap) return (int)cudaErrorInvalidValue;

@@ -32,6 +32,7 @@
 #include "sm100_ptx.cuh"
 #include "decode_epi.cuh"
 #include "q81_block.cuh"
+#include "mma_sync.cuh"
 #include "../../include/cfi_glue.h"
 
 #include <algorithm>
@@ -55,26 +56,6 @@ template <uint32_t TY, int NCOLS> __host__ __device__ constexpr int rows_per_war
     return TY == T_Q4_K ? (NCOLS == 1 ? 2 : 1) : (NCOLS <= 2 ? 2 : 1);
 }
 
-CFI_DEV uint4 lds128(uint32_t a) {
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-    return v;
-}
-CFI_DEV uint2 lds64(uint32_t a) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-    return v;
-}
-CFI_DEV uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-CFI_DEV uint32_t lds16(uint32_t a) {
-    unsigned short v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
 CFI_DEV void l2_prefetch(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -823,11 +804,6 @@ __host__ __device__ inline uint32_t mma_stage_bytes(uint32_t chunk_rows, uint32_
 }
 __host__ __device__ inline size_t mma_y_bytes(uint32_t nb32) { return ((size_t)(nb32 / 8) * MMA_SB_BYTES + 127) & ~(size_t)127; }
 
-CFI_DEV uint32_t tf32_bits(float x) {  // round to nearest (ties away), the tf32 operand format
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
 
 template <int NCOLS>
 CFI_DEV YStage stage_y_mma(uint8_t* smem, const uint8_t* y0, size_t y_base, uint32_t stride_col_y, uint32_t nb32) {
@@ -862,23 +838,6 @@ CFI_DEV YStage stage_y_mma(uint8_t* smem, const uint8_t* y0, size_t y_base, uint
     return YStage{smem_u32(smem), 0, 0, nb32};
 }
 
-CFI_DEV void ldsm_x4(uint32_t a, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(a));
-}
-CFI_DEV void mma_u8s8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int (&d)[4]) {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-                 "{%10, %10, %10, %10};"
-                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
-}
-CFI_DEV void mma_tf32(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, float (&d)[4]) {
-    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-                 "{%0, %1, %2, %3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 // Rows [r0, r1) of one chunk (at most MMA_MAX_CHUNK), staged at sbase with row pitch rstride.
 template <int NCOLS>

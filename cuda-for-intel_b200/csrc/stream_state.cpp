@@ -143,6 +143,13 @@ void* cfi_stream_buffer(int kind, size_t bytes, cudaStream_t stream, int* err) {
             *err = (int)cudaErrorMemoryAllocation;
             return nullptr;
         }
+        if (kind == CFI_BUF_COUNTERS && cudaMemset(b.p, 0, want) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(b.p);
+            b.p = nullptr;
+            *err = (int)cudaErrorMemoryAllocation;
+            return nullptr;
+        }
         b.cap = want;
     }
     return b.p;

@@ -184,3 +184,46 @@ def test_mmq_forced_tile_width_keeps_two_raw_slots(monkeypatch, bn):
         assert st["native_failures"] == 0 and st["stock_launches"] == 0
     finally:
         ctx.close()
+
+
+# the skinny mul_mat_q (<= 64 columns, Q4_K / Q8_0, one plane, K % 256 == 0): exact int32 block
+# dots on the warp-level MMAs, fp32 scales in ggml's mmq roundings -- within about 1e-6 of the
+# oracle's order (the tcgen05 path's fp16 operands give ~1e-4)
+SKINNY_REL = 1e-5
+
+
+@pytest.mark.parametrize("ty,case", [
+    (cfi.Q4_K, (1536, 1000, 64, 1, 1, 1)),   # 63 tiles, the last ragged
+    (cfi.Q4_K, (8960, 300, 33, 1, 1, 1)),    # 35 chunks: K split by shared-memory room; 5 n-tiles, the last partial
+    (cfi.Q4_K, (256, 1, 1, 1, 1, 1)),        # one row, one column, one chunk
+    (cfi.Q4_K, (2048, 129, 17, 1, 1, 1)),
+    (cfi.Q8_0, (1536, 4000, 64, 1, 1, 1)),   # the batch-64 head's width
+    (cfi.Q8_0, (2048, 130, 8, 1, 1, 1)),
+    (cfi.Q8_0, (256, 70, 3, 1, 1, 1)),
+    (cfi.Q8_0, (256, 20000, 64, 1, 1, 1)),   # more tiles than warps: several rounds per warp
+    (cfi.Q4_K, (512, 20000, 40, 1, 1, 1)),
+])
+def test_mmq_skinny_matches_the_oracle(dev, monkeypatch, ty, case):
+    ctx, g = dev
+    ncols_x, nrows, ncols, nch, ratio, nsamples = case
+    p, x, y, n = O.mmq_case(ty, ncols_x, nrows, ncols, nch, ratio, nsamples, 77 + ncols + ty)
+    want = O.mmq_ref(ty, p, x, y, n)
+    got = run(g, ty, p, x, y, n)
+    assert np.isfinite(got).all()
+    assert O.rel_l2(got, want) < SKINNY_REL, O.rel_l2(got, want)
+    # every row-group shape (KP warps per tile), alone and with K split over three CTAs (the
+    # tile partials and their counters); the planner picks one of these for each product
+    for kp in ("1", "2", "4", "8"):
+        for splits in (None, "3"):
+            monkeypatch.setenv("CFI_MMQ_SKINNY_KP", kp)
+            if splits:
+                monkeypatch.setenv("CFI_MMQ_SKINNY_SPLITS", splits)
+            again = run(g, ty, p, x, y, n)
+            assert O.rel_l2(again, want) < SKINNY_REL, (kp, splits, O.rel_l2(again, want))
+            monkeypatch.delenv("CFI_MMQ_SKINNY_SPLITS", raising=False)
+    monkeypatch.delenv("CFI_MMQ_SKINNY_KP")
+    if n >= 256:  # the tcgen05 path on the same case (its fp16 operands: the 1e-3 bound needs a few hundred outputs)
+        monkeypatch.setenv("CFI_MMQ_SKINNY", "0")
+        tc = run(g, ty, p, x, y, n)
+        assert O.rel_l2(tc, want) < REL_L2
+    assert ctx.stats()["stock_launches"] == 0
