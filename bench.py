@@ -493,10 +493,11 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
 
     side = [torch.cuda.Stream(device=dev) for _ in range(2)]
 
-    def step(kernels=True, collectives=True, parallel=False):
+    def step(kernels=True, collectives=True, parallel=False, grouped=False):
         """parallel: the products of a group after the first run on side streams, as parallel
         branches (each product depends only on the group's quantized input); every stream has
-        its own split-K workspace and scratch."""
+        its own split-K workspace and scratch.  grouped: the products of a group in one launch
+        (cfi_mmq_skinny_group) instead of one mul_mat_q each."""
         cur = torch.cuda.current_stream()
         st = cur.cuda_stream
         coll = collectives and world > 1
@@ -517,7 +518,13 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
                         ev.record(cur)
                         for sd in side[:len(inputs) - 1]:
                             sd.wait_event(ev)
+                    if grouped and len(inputs) > 1:
+                        cfi.mmq_skinny_group(cfi.Q4_K, [lay[nm].data_ptr() for nm in inputs], xq[k].data_ptr(),
+                                             [out[nm].data_ptr() for nm in inputs], [sh[nm].rows for nm in inputs], k, n,
+                                             stride_col_dst=[sh[nm].rows_padded for nm in inputs], stream=st)
                     for i, nm in enumerate(inputs):
+                        if grouped and len(inputs) > 1:
+                            break
                         on = side[i - 1] if parallel and i > 0 else cur
                         g.mmq(cfi.Q4_K, lay[nm].data_ptr(), xq[k].data_ptr(), out[nm].data_ptr(), k, sh[nm].rows, n,
                               stream=on.cuda_stream, stride_col_dst=sh[nm].rows_padded)
@@ -573,6 +580,7 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     ms_kern = timed(collectives=False) if world > 1 else ms_step
     ms_coll = timed(kernels=False) if world > 1 else 0.0
     ms_par = timed(parallel=True)
+    ms_grp = timed(grouped=True)
     # check: rank 0's gathered logits against the unsharded head product on rank 0
     check = {}
     with torch.cuda.stream(stream):
@@ -598,6 +606,9 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
            "frac": round(wbytes / ms_step / 1e6 / (peak_gbs * world), 4),
            "parallel_products_ms": round(ms_par, 4),
            "parallel_products_frac": round(wbytes / ms_par / 1e6 / (peak_gbs * world), 4),
+           "grouped_products_ms": round(ms_grp, 4),
+           "grouped_products_frac": round(wbytes / ms_grp / 1e6 / (peak_gbs * world), 4),
+           "grouped_launches": launches - L * sum(len(i) - 1 for i, _ in C5_GROUPS),
            "kernels_only_ms": round(ms_kern, 4), "collectives_only_ms": round(ms_coll, 4),
            "all_gathers_per_step": (L * len(C5_GROUPS) + 1) if world > 1 else 0,
            "gathered_bytes_per_gpu": (world - 1) * n * 4 * (L * sum(sh[nm].rows_padded for nm in C5_SHAPES) +

@@ -121,6 +121,7 @@ def lib():
     L.cfi_glue_swiglu.argtypes = [vp, vp, vp, i, vp]
     L.cfi_glue_argmax_next.argtypes = [vp, i, vp, vp, vp]
     L.cfi_glue_gather_row_shards.argtypes = [vp, vp, i, i, i, ll, vp]
+    L.cfi_mmq_skinny_group.argtypes = [C.c_uint32, i, vp, vp, vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp]
     L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]
@@ -556,6 +557,22 @@ class GgmlCaller:
 # ---------------------------------------------------------------------------------------------
 # host-side weight quantizers (synthetic weights for tests and the benchmark)
 # ---------------------------------------------------------------------------------------------
+def mmq_skinny_group(ty, xs, y, dsts, nrows, k, ncols, ncols_y=None, stride_row_x=None, stride_col_dst=None,
+                     stream=0):
+    """cfi_mmq_skinny_group: products i (device pointers xs[i] -> dsts[i], nrows[i] rows each) over one
+    q8_1_mmq activation buffer y in one launch; row strides default to k / block values, output
+    column strides to nrows[i]."""
+    n = len(xs)
+    qk = 256 if ty == Q4_K else 32
+    srx = stride_row_x or [k // qk] * n
+    scd = stride_col_dst or list(nrows)
+    P = C.c_void_p * n
+    U = C.c_uint32 * n
+    rc = lib().cfi_mmq_skinny_group(ty, n, P(*xs), C.c_void_p(y), P(*dsts), U(*nrows), U(*srx), U(*scd), k, ncols,
+                                    ncols_y or ncols, C.c_void_p(stream))
+    check(rc, "cfi_mmq_skinny_group")
+
+
 def quantize_q8_0(w):
     """ggml quantize_row_q8_0 over rows of `w` (float32, K % 32 == 0): d = amax/127 (fp16),
     q = round(x / d).  Returns uint8 [rows, K/32*34]."""

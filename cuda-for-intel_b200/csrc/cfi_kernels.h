@@ -127,6 +127,11 @@ void* cfi_stream_buffer(int kind, size_t bytes, cudaStream_t stream, int* err);
 // ---- k_mmq_skinny.cu: mul_mat_q for at most 64 columns (Q4_K / Q8_0, one plane, K % 256 == 0) ----
 bool cfi_mmq_skinny_applies(uint32_t ty, const void* x, const void* y, uint32_t K, uint32_t ncols_dst,
                             uint32_t stride_row_x, uint32_t planes);
+// n <= 4 products over the same activations in one launch (their tiles back to back)
+int cfi_mmq_skinny_group_launch(uint32_t ty, int n, const void* const* x, const void* y, float* const* dst,
+                                const uint32_t* nrows, const uint32_t* stride_row_x, const uint32_t* stride_col_dst,
+                                uint32_t K, uint32_t ncols_dst, uint32_t ncols_y, unsigned int* err, cudaStream_t stream,
+                                bool pdl);
 int cfi_mmq_skinny_launch(uint32_t ty, const void* x, const void* y, float* dst, uint32_t K, uint32_t nrows,
                           uint32_t ncols_dst, uint32_t ncols_y, uint32_t stride_row_x, uint32_t stride_col_dst,
                           unsigned int* err, cudaStream_t stream, bool pdl);

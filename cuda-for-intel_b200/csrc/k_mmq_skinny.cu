@@ -46,9 +46,10 @@ namespace {
 
 using namespace sm100;
 
-constexpr int SK_THREADS = 256, SK_WARPS = 8, SK_TR = 16;  // threads, warps, rows per tile
+constexpr int SK_TR = 16;  // rows per tile
 constexpr int SK_MAX_NT = 8;                                // 8-column n-tiles (64 columns)
 constexpr int SK_MAX_STAGES = 8;
+constexpr int SK_DEFAULT_WARPS = 8;  // CTA size: 8 or 16 warps (CFI_MMQ_SKINNY_WARPS)
 constexpr int SK_PART_FLOATS = SK_MAX_NT * 4 * 32;          // one tile's partial, lane-major
 constexpr uint32_t SK_MAGIC = 0x4B400000u;                  // 1.5 * 2^23 as a float
 
@@ -61,36 +62,64 @@ __host__ __device__ constexpr uint32_t sk_xdt(uint32_t nt) { return (2 * nt + 3)
 //   act  [kr][2 blocks][NC8 columns][144]     raw q8_1_mmq blocks
 //   xd   [kr][8 sub-blocks][4 t][XDT]         float d of column n * 8 + 2t + e at n * 2 + e
 //   xs   [kr][8][NC8 + 8]                     Q4_K: float s (padded rows: conflict-free tf32 B loads)
-//   ring [8 warps][stages][16 x chunk bytes]  weights
-//   red  [8 warps][NT x 4][32]                KP > 1: the parts of a tile
-//   bars act[kr], scales[kr], ring[8][stages]
+//   ring [W warps][stages][16 x chunk bytes]  weights
+//   red  [slots][NT x 4][32]                  KP > 1: the parts of a tile (W - W / KP slots, or
+//                                             one per row group when they are added in turn)
+//   bars act[kr], scales[kr], ring[W][stages]
 struct SkLayout {
     uint32_t act, xd, xs, ring, red, bars, total;
 };
-__host__ __device__ inline SkLayout sk_layout(uint32_t ty, uint32_t nt, uint32_t kr, uint32_t stages, uint32_t kp) {
+__host__ __device__ inline uint32_t sk_red_slots(uint32_t w, uint32_t kp, bool par) {
+    return kp > 1 ? (par ? w - w / kp : w / kp) : 0;
+}
+__host__ __device__ inline SkLayout sk_layout(uint32_t ty, uint32_t nt, uint32_t kr, uint32_t stages, uint32_t kp,
+                                              uint32_t w, bool par) {
     SkLayout l;
     const uint32_t nc8 = nt * 8, cb = ty == T_Q4_K ? 144u : 272u;
     l.act = 0;
     l.xd = l.act + kr * 2 * nc8 * 144;
     l.xs = l.xd + kr * 8 * 4 * sk_xdt(nt) * 4;
     l.ring = l.xs + (ty == T_Q4_K ? kr * 8 * (nc8 + 8) * 4 : 0);
-    l.red = l.ring + SK_WARPS * stages * SK_TR * cb;
-    l.bars = l.red + (kp > 1 ? SK_WARPS * nt * 4 * 32 * 4 : 0);
-    l.total = l.bars + (2 * kr + SK_WARPS * stages) * 8;
+    l.red = l.ring + w * stages * SK_TR * cb;
+    l.bars = l.red + sk_red_slots(w, kp, par) * nt * 4 * 32 * 4;
+    l.total = l.bars + (2 * kr + w * stages) * 8;
     return l;
 }
 
+constexpr int SK_MAX_GROUP = 4;  // products of one launch (they read the same activations)
+
 struct SkArgs {
-    const uint8_t* x;  // weights
+    // product i: weights x[i] (nrows[i] rows, stride_row_x[i] blocks apart), output dst[i]
+    // (column c at c * stride_col_dst[i]); its 16-row tiles are tiles tile_begin[i] .. of the launch
+    const uint8_t* x[SK_MAX_GROUP];
+    float* dst[SK_MAX_GROUP];
+    uint32_t nrows[SK_MAX_GROUP], stride_row_x[SK_MAX_GROUP], stride_col_dst[SK_MAX_GROUP];
+    uint32_t tile_begin[SK_MAX_GROUP];
+    uint32_t ngroup;
     const uint8_t* y;  // q8_1_mmq activations
-    float* dst;
-    uint32_t nrows, ncols, ncols_y, stride_row_x, stride_col_dst;
+    uint32_t ncols, ncols_y;
     uint32_t nchunks, kr, ksplits;  // 256-value chunks of K, chunks per K split, splits
     uint32_t kp, ntiles, stages;    // warps per row group, 16-row tiles, ring stages per warp
+    uint32_t red_par;               // KP > 1: a slot per part (one barrier) or per row group (parts in turn)
     float* ws;                      // K splits: partials [tile][split][SK_PART_FLOATS]
     unsigned int* counters;         // K splits: per tile
     unsigned int* err;
 };
+
+// The product a launch tile belongs to (constant indices only: no local copy of the arguments).
+struct SkProd {
+    const uint8_t* x;
+    float* dst;
+    uint32_t nrows, srx, scd, tile;  // tile: the tile's index within its product
+};
+CFI_DEV SkProd sk_prod(const SkArgs& a, uint32_t tile) {
+    SkProd p = {a.x[0], a.dst[0], a.nrows[0], a.stride_row_x[0], a.stride_col_dst[0], tile};
+#pragma unroll
+    for (int i = 1; i < SK_MAX_GROUP; i++)
+        if ((uint32_t)i < a.ngroup && tile >= a.tile_begin[i])
+            p = {a.x[i], a.dst[i], a.nrows[i], a.stride_row_x[i], a.stride_col_dst[i], tile - a.tile_begin[i]};
+    return p;
+}
 
 // 16-byte global -> shared copy on the LSU path (L2 only), and an arrival on `bar` once every
 // copy this thread issued before it has landed (the arrival does not count toward the barrier's
@@ -197,16 +226,18 @@ CFI_DEV void sk_subblock(const uint32_t (&af)[4], uint64_t w0, uint64_t w1, uint
     }
 }
 
-template <uint32_t TY, int NT>
-__global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) {
+template <uint32_t TY, int NT, int W>
+__global__ void __launch_bounds__(W * 32, 1) cfi_mmq_skinny(const SkArgs a) {
     constexpr uint32_t CB = sk_chunk_bytes<TY>(), WB = SK_TR * CB, NC8 = NT * 8;
     constexpr uint32_t XSP = NC8 + 8, XDT = sk_xdt(NT);
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_abort;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-    const uint32_t KP = a.kp, RW = SK_WARPS / KP, rw = warp / KP, kp = warp % KP;
+    const uint32_t KP = a.kp, RW = W / KP, rw = warp / KP, kp = warp % KP;
+    // 16 warps: the sub-block loops stay rolled so a thread fits the 128 registers of a full SM
+    constexpr int UNR = W >= 16 ? 1 : 4;
     const uint32_t S = a.stages, kr = a.kr;
-    const SkLayout L = sk_layout(TY, NT, kr, S, KP);
+    const SkLayout L = sk_layout(TY, NT, kr, S, KP, W, a.red_par != 0);
     uint8_t* act = smem + L.act;
     float* xd = reinterpret_cast<float*>(smem + L.xd);
     float* xs = reinterpret_cast<float*>(smem + L.xs);
@@ -231,7 +262,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
             mbar_init(abar + i, 1);
             mbar_init(sbar + i, 32);
         }
-        for (uint32_t i = 0; i < SK_WARPS * S; i++) mbar_init(sbar + kr + i, 32);
+        for (uint32_t i = 0; i < W * S; i++) mbar_init(sbar + kr + i, 32);
         fence_mbar_init();
     }
     __syncthreads();
@@ -244,14 +275,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
     // when its own copies have landed
     auto issue = [&](uint32_t s) {
         const uint32_t tile = tile0 + (s / nq) * tstride, chunk = c0 + kp + (s % nq) * KP;
+        const SkProd pr = sk_prod(a, tile);
         uint8_t* st = ring + (s % S) * WB;
 #pragma unroll
         for (uint32_t k = 0; k < (WB / 16 + 31) / 32; k++) {
             const uint32_t seg = lane + 32 * k;
             if (seg < WB / 16) {
                 const uint32_t r = seg / (CB / 16), off = (seg % (CB / 16)) * 16;
-                const uint32_t row = min(tile * SK_TR + r, a.nrows - 1);  // rows past the end: a copy of the last
-                const uint8_t* src = a.x + (size_t)row * a.stride_row_x * xbytes + (size_t)chunk * CB + off;
+                const uint32_t row = min(pr.tile * SK_TR + r, pr.nrows - 1);  // rows past the end: a copy of the last
+                const uint8_t* src = pr.x + (size_t)row * pr.srx * xbytes + (size_t)chunk * CB + off;
                 cp_async16(st + r * CB + off, src);
             }
         }
@@ -281,7 +313,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
             s_abort = 1;
         }
     };
-    for (uint32_t ci = warp; ci < nck; ci += SK_WARPS) {
+    for (uint32_t ci = warp; ci < nck; ci += W) {
         if (!failed && !__all_sync(0xffffffffu, mbar_wait(abar + ci, 0, abort_flag))) fail(0x5c0000u);
         if (!failed) {
             for (uint32_t hb = lane; hb < 2 * NC8; hb += 32) {  // (block half, column)
@@ -339,26 +371,23 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
             if (TY == T_Q4_K) {
                 const uint4 h0 = *reinterpret_cast<const uint4*>(st + g * CB);
                 const uint4 h1 = *reinterpret_cast<const uint4*>(st + (g + 8) * CB);
-                float wsc[2][8];
+                float dd[2];
+                uint32_t scw[2][2];  // [row][sub-blocks 0-3, 4-7]: 6-bit scales, one per byte
                 uint32_t am[4];
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
                     const uint4 hd = h ? h1 : h0;
-                    const float d = h2f_bits((uint16_t)(hd.x & 0xffffu)), dmin = h2f_bits((uint16_t)(hd.x >> 16));
-                    const uint32_t scl = hd.y & 0x3F3F3F3Fu, mlo = hd.z & 0x3F3F3F3Fu;
-                    const uint32_t sch = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+                    dd[h] = h2f_bits((uint16_t)(hd.x & 0xffffu));
+                    const float dmin = h2f_bits((uint16_t)(hd.x >> 16));
+                    scw[h][0] = hd.y & 0x3F3F3F3Fu;
+                    scw[h][1] = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+                    const uint32_t mlo = hd.z & 0x3F3F3F3Fu;
                     const uint32_t mhi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {  // half(d * sc), ggml's rounding; odd sub-blocks / 16
-                        const uint32_t sc = ((j < 4 ? scl : sch) >> (8 * (j & 3))) & 0xffu;
-                        const float v = __half2float(__float2half_rn(d * (float)sc));
-                        wsc[h][j] = (j & 1) ? v * 0.0625f : v;
-                    }
                     // tf32 A of the min term: -half(dmin * m) at (row, sub-block t) and (row, t + 4)
                     am[h] = __float_as_uint(-__half2float(__float2half_rn(dmin * (float)((mlo >> (8 * t)) & 0xffu))));
                     am[h + 2] = __float_as_uint(-__half2float(__float2half_rn(dmin * (float)((mhi >> (8 * t)) & 0xffu))));
                 }
-#pragma unroll
+#pragma unroll UNR
                 for (int c4 = 0; c4 < 4; c4++) {  // nibble group c4: sub-blocks 2 c4 (low) and 2 c4 + 1 (high)
                     uint32_t raw[4];
                     ldsm_x4v(sw + lrow * CB + 16 + 32 * c4 + lbyte, raw);
@@ -367,7 +396,14 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
                         const int j = 2 * c4 + hi;
                         const uint32_t msk = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
                         const uint32_t af[4] = {raw[0] & msk, raw[1] & msk, raw[2] & msk, raw[3] & msk};
-                        sk_subblock<true, NT>(af, pk2f(wsc[0][j], wsc[0][j]), pk2f(wsc[1][j], wsc[1][j]),
+                        float w2[2];
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {  // half(d * sc), ggml's rounding; odd sub-blocks / 16
+                            const uint32_t sc = ((c4 < 2 ? scw[h][0] : scw[h][1]) >> (8 * (j & 3))) & 0xffu;
+                            const float v = __half2float(__float2half_rn(dd[h] * (float)sc));
+                            w2[h] = hi ? v * 0.0625f : v;
+                        }
+                        sk_subblock<true, NT>(af, pk2f(w2[0], w2[0]), pk2f(w2[1], w2[1]),
                                               yb + (j / 4) * NC8 * MMQ_BLOCK_BYTES + 32 * (j % 4), xdc + j * 4 * XDT, acc);
                     }
                 }
@@ -378,27 +414,31 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
                                acc[n][0], acc[n][1]);
             } else {
                 // Q8_0: block j of a row at j * 34 (d) and j * 34 + 2 (quants); rows g and g + 8
+#pragma unroll UNR
+                for (int j2 = 0; j2 < 4; j2++) {
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    uint32_t af[4];
-                    float wd[2];
+                    for (int odd = 0; odd < 2; odd++) {
+                        const int j = 2 * j2 + odd;
+                        uint32_t af[4];
+                        float wd[2];
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const uint8_t* rb = st + (g + 8 * h) * CB + 34 * j;
-                        wd[h] = h2f_bits(*reinterpret_cast<const uint16_t*>(rb));
-                        const uint8_t* o = rb + 2 + 4 * t;  // quants 4t .. 4t + 3, and 16 + 4t ..
-                        if ((j & 1) == 0) {                 // 2-byte aligned: shift two words together
-                            const uint32_t* wp = reinterpret_cast<const uint32_t*>(o - 2);
-                            af[h] = __funnelshift_r(wp[0], wp[1], 16);
-                            af[h + 2] = __funnelshift_r(wp[4], wp[5], 16);
-                        } else {
-                            const uint32_t* wp = reinterpret_cast<const uint32_t*>(o);
-                            af[h] = wp[0];
-                            af[h + 2] = wp[4];
+                        for (int h = 0; h < 2; h++) {
+                            const uint8_t* rb = st + (g + 8 * h) * CB + 34 * j;
+                            wd[h] = h2f_bits(*reinterpret_cast<const uint16_t*>(rb));
+                            const uint8_t* o = rb + 2 + 4 * t;  // quants 4t .. 4t + 3, and 16 + 4t ..
+                            if (!odd) {                         // 2-byte aligned: shift two words together
+                                const uint32_t* wp = reinterpret_cast<const uint32_t*>(o - 2);
+                                af[h] = __funnelshift_r(wp[0], wp[1], 16);
+                                af[h + 2] = __funnelshift_r(wp[4], wp[5], 16);
+                            } else {
+                                const uint32_t* wp = reinterpret_cast<const uint32_t*>(o);
+                                af[h] = wp[0];
+                                af[h + 2] = wp[4];
+                            }
                         }
+                        sk_subblock<false, NT>(af, pk2f(wd[0], wd[0]), pk2f(wd[1], wd[1]),
+                                               yb + (j / 4) * NC8 * MMQ_BLOCK_BYTES + 32 * (j % 4), xdc + j * 4 * XDT, acc);
                     }
-                    sk_subblock<false, NT>(af, pk2f(wd[0], wd[0]), pk2f(wd[1], wd[1]),
-                                           yb + (j / 4) * NC8 * MMQ_BLOCK_BYTES + 32 * (j % 4), xdc + j * 4 * XDT, acc);
                 }
             }
             __syncwarp();  // every lane is done with the slot before it is refilled
@@ -413,9 +453,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
             upk2(acc[n][0], out[n][0], out[n][1]);
             upk2(acc[n][1], out[n][2], out[n][3]);
         }
-        // ---- the parts of the tile (KP > 1), in part order ----
-        if (KP > 1) {
-            float* mine = red + warp * (NT * 4 * 32);
+        // ---- the parts of the tile (KP > 1) ----
+        if (KP > 1 && a.red_par) {  // a slot per part, added in part order after one barrier
+            float* mine = red + (rw * (KP - 1) + kp - 1) * (NT * 4 * 32);
             if (has && kp > 0) {
 #pragma unroll
                 for (int n = 0; n < NT; n++)
@@ -425,22 +465,43 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
             __syncthreads();
             if (has && kp == 0) {
                 for (uint32_t k2 = 1; k2 < KP; k2++) {
-                    const float* o = red + (warp + k2) * (NT * 4 * 32);
+                    const float* o = red + (rw * (KP - 1) + k2 - 1) * (NT * 4 * 32);
 #pragma unroll
                     for (int n = 0; n < NT; n++)
 #pragma unroll
                         for (int e = 0; e < 4; e++) out[n][e] += o[(n * 4 + e) * 32 + lane];
                 }
             }
+        } else if (KP > 1) {  // one slot per row group: parts KP - 1, ..., 1 add into it in turn
+            float* slot = red + rw * (NT * 4 * 32);
+            for (uint32_t k2 = KP - 1; k2 >= 1; k2--) {
+                if (has && kp == k2) {
+#pragma unroll
+                    for (int n = 0; n < NT; n++)
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            float* q = slot + (n * 4 + e) * 32 + lane;
+                            *q = k2 == KP - 1 ? out[n][e] : *q + out[n][e];
+                        }
+                }
+                __syncthreads();
+            }
+            if (has && kp == 0) {
+#pragma unroll
+                for (int n = 0; n < NT; n++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) out[n][e] += slot[(n * 4 + e) * 32 + lane];
+            }
         }
         if (has && kp == 0 && !failed) {
+            const SkProd pr = sk_prod(a, tile);
             if (a.ksplits == 1) {
 #pragma unroll
                 for (int n = 0; n < NT; n++)
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const uint32_t row = tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
-                        if (row < a.nrows && col < a.ncols) a.dst[(size_t)col * a.stride_col_dst + row] = out[n][e];
+                        const uint32_t row = pr.tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
+                        if (row < pr.nrows && col < a.ncols) pr.dst[(size_t)col * pr.scd + row] = out[n][e];
                     }
             } else {
                 // K splits: this split's partial, then the last warp of the tile adds them in order
@@ -477,8 +538,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
                     for (int n = 0; n < NT; n++)
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
-                            const uint32_t row = tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
-                            if (row < a.nrows && col < a.ncols) a.dst[(size_t)col * a.stride_col_dst + row] = out[n][e];
+                            const uint32_t row = pr.tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
+                            if (row < pr.nrows && col < a.ncols) pr.dst[(size_t)col * pr.scd + row] = out[n][e];
                         }
                     if (lane == 0) a.counters[tile] = 0u;
                 }
@@ -500,34 +561,40 @@ __global__ void __launch_bounds__(SK_THREADS, 1) cfi_mmq_skinny(const SkArgs a) 
     }
 }
 
-template <uint32_t TY>
-const void* sk_kernel(int nt) {
+template <uint32_t TY, int W>
+const void* sk_kernel_w(int nt) {
     switch (nt) {
-    case 1: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 1>);
-    case 2: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 2>);
-    case 3: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 3>);
-    case 4: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 4>);
-    case 5: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 5>);
-    case 6: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 6>);
-    case 7: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 7>);
-    case 8: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 8>);
+    case 1: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 1, W>);
+    case 2: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 2, W>);
+    case 3: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 3, W>);
+    case 4: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 4, W>);
+    case 5: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 5, W>);
+    case 6: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 6, W>);
+    case 7: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 7, W>);
+    case 8: return reinterpret_cast<const void*>(&cfi_mmq_skinny<TY, 8, W>);
     default: return nullptr;
     }
+}
+const void* sk_kernel(uint32_t ty, int nt, int w) {
+    if (ty == T_Q4_K) return w == 16 ? sk_kernel_w<T_Q4_K, 16>(nt) : sk_kernel_w<T_Q4_K, 8>(nt);
+    return w == 16 ? sk_kernel_w<T_Q8_0, 16>(nt) : sk_kernel_w<T_Q8_0, 8>(nt);
 }
 
 struct SkPlan {
     uint32_t kr, ksplits, kp, nx, stages;
+    bool par;
     size_t smem;
 };
 
-// Work split of one product: K splits only where the K range's activations do not fit in shared
-// memory; then the row-group shape KP (warps per tile) and the CTA count that give the fewest
-// chunks per warp (ties: smaller KP, fewer parts to combine); then as many ring stages as fit.
-bool sk_plan(uint32_t ty, uint32_t nt, uint32_t nchunks, uint32_t ntiles, int sms, size_t smem_max, SkPlan& p) {
-    const uint32_t cb = ty == T_Q4_K ? 144u : 272u;
+// Work split of one product over CTAs of w warps: K splits only where the K range's activations
+// do not fit in shared memory; then the row-group shape KP (warps per tile) and the CTA count that
+// give the fewest chunks per warp (ties: smaller KP, fewer parts to combine); then as many ring
+// stages as fit, and a slot per part for the tile's parts when those fit too.
+bool sk_plan(uint32_t ty, uint32_t nt, uint32_t nchunks, uint32_t ntiles, int sms, size_t smem_max, uint32_t w,
+             SkPlan& p) {
     uint32_t kr_max = 0;
     for (uint32_t kr = 1; kr <= std::min(nchunks, 32u); kr++) {  // <= 32: a warp's mask of released chunks
-        if (sk_layout(ty, nt, kr, 2, 8).total > smem_max) break;
+        if (sk_layout(ty, nt, kr, 2, 1, w, false).total > smem_max) break;
         kr_max = kr;
     }
     if (kr_max == 0) return false;
@@ -539,13 +606,16 @@ bool sk_plan(uint32_t ty, uint32_t nt, uint32_t nchunks, uint32_t ntiles, int sm
     p.kr = (nchunks + ks - 1) / ks;
     p.ksplits = (nchunks + p.kr - 1) / p.kr;
     const uint32_t per_split = std::max(1u, (uint32_t)sms / p.ksplits);
-    // CFI_MMQ_SKINNY_KP (1, 2, 4 or 8) fixes the row-group shape instead (tests of each form)
+    // CFI_MMQ_SKINNY_KP (1, 2, 4, 8, 16 up to the warp count) fixes the row-group shape instead
+    // (tests of each form)
     const char* ekp = getenv("CFI_MMQ_SKINNY_KP");
     const uint32_t kp_only = ekp ? (uint32_t)atoi(ekp) : 0u;
     double best = 1e30;
-    for (uint32_t kp = 1; kp <= 8; kp *= 2) {
+    bool any = false;
+    for (uint32_t kp = 1; kp <= w; kp *= 2) {
         if (kp_only && kp != kp_only) continue;
-        const uint32_t rw = 8 / kp;
+        if (sk_layout(ty, nt, p.kr, 1, kp, w, false).total > smem_max) continue;
+        const uint32_t rw = w / kp;
         const uint32_t nx = std::min(per_split, (ntiles + rw - 1) / rw);
         const uint32_t rounds = (ntiles + nx * rw - 1) / (nx * rw);
         const double cost = (double)rounds * ((p.kr + kp - 1) / kp) + (kp > 1 ? 0.25 * rounds : 0.0);
@@ -553,16 +623,18 @@ bool sk_plan(uint32_t ty, uint32_t nt, uint32_t nchunks, uint32_t ntiles, int sm
             best = cost;
             p.kp = kp;
             p.nx = nx;
+            any = true;
         }
     }
-    const uint32_t rw = 8 / p.kp;
+    if (!any) return false;
+    const uint32_t rw = w / p.kp;
     const uint32_t rounds = (ntiles + p.nx * rw - 1) / (p.nx * rw);
     const uint32_t steps = rounds * ((p.kr + p.kp - 1) / p.kp);  // most steps of one warp
     p.stages = 1;
     for (uint32_t st = 1; st <= (uint32_t)SK_MAX_STAGES && st <= std::max(1u, steps); st++)
-        if (sk_layout(ty, nt, p.kr, st, p.kp).total <= smem_max) p.stages = st;
-    p.smem = sk_layout(ty, nt, p.kr, p.stages, p.kp).total;
-    (void)cb;
+        if (sk_layout(ty, nt, p.kr, st, p.kp, w, false).total <= smem_max) p.stages = st;
+    p.par = sk_layout(ty, nt, p.kr, p.stages, p.kp, w, true).total <= smem_max;
+    p.smem = sk_layout(ty, nt, p.kr, p.stages, p.kp, w, p.par).total;
     return p.smem <= smem_max;
 }
 
@@ -599,27 +671,40 @@ bool cfi_mmq_skinny_applies(uint32_t ty, const void* x, const void* y, uint32_t 
     return true;
 }
 
-int cfi_mmq_skinny_launch(uint32_t ty, const void* x, const void* y, float* dst, uint32_t K, uint32_t nrows,
-                          uint32_t ncols_dst, uint32_t ncols_y, uint32_t stride_row_x, uint32_t stride_col_dst,
-                          unsigned int* err, cudaStream_t stream, bool pdl) {
+int cfi_mmq_skinny_group_launch(uint32_t ty, int n, const void* const* x, const void* y, float* const* dst,
+                                const uint32_t* nrows, const uint32_t* stride_row_x, const uint32_t* stride_col_dst,
+                                uint32_t K, uint32_t ncols_dst, uint32_t ncols_y, unsigned int* err, cudaStream_t stream,
+                                bool pdl) {
     const int nt = (int)((ncols_dst + 7) / 8);
-    const void* fn = ty == T_Q4_K ? sk_kernel<T_Q4_K>(nt) : sk_kernel<T_Q8_0>(nt);
-    if (!fn || nrows == 0) return (int)cudaErrorInvalidValue;
+    const char* ew = getenv("CFI_MMQ_SKINNY_WARPS");
+    const int w = ew && atoi(ew) == 16 ? 16 : (ew && atoi(ew) == 8 ? 8 : SK_DEFAULT_WARPS);
+    const void* fn = sk_kernel(ty, nt, w);
+    if (!fn || n < 1 || n > SK_MAX_GROUP || ncols_dst > ncols_y || K == 0 || K % 256 || (reinterpret_cast<uintptr_t>(y) & 15))
+        return (int)cudaErrorInvalidValue;
     const SkDev dv = sk_dev();
     SkArgs a = {};
-    a.x = static_cast<const uint8_t*>(x);
+    uint32_t tiles = 0;
+    for (int i = 0; i < n; i++) {
+        if (nrows[i] == 0 || (reinterpret_cast<uintptr_t>(x[i]) & 15) || (ty == T_Q8_0 && stride_row_x[i] % 8))
+            return (int)cudaErrorInvalidValue;
+        a.x[i] = static_cast<const uint8_t*>(x[i]);
+        a.dst[i] = dst[i];
+        a.nrows[i] = nrows[i];
+        a.stride_row_x[i] = stride_row_x[i];
+        a.stride_col_dst[i] = stride_col_dst[i];
+        a.tile_begin[i] = tiles;
+        tiles += (nrows[i] + SK_TR - 1) / SK_TR;
+    }
+    a.ngroup = (uint32_t)n;
     a.y = static_cast<const uint8_t*>(y);
-    a.dst = dst;
-    a.nrows = nrows;
     a.ncols = ncols_dst;
     a.ncols_y = ncols_y;
-    a.stride_row_x = stride_row_x;
-    a.stride_col_dst = stride_col_dst;
     a.nchunks = K / 256;
-    a.ntiles = (nrows + SK_TR - 1) / SK_TR;
+    a.ntiles = tiles;
     a.err = err;
     SkPlan p;
-    if (!sk_plan(ty, (uint32_t)nt, a.nchunks, a.ntiles, dv.sms, dv.smem_max, p)) return (int)cudaErrorInvalidValue;
+    if (!sk_plan(ty, (uint32_t)nt, a.nchunks, a.ntiles, dv.sms, dv.smem_max, (uint32_t)w, p))
+        return (int)cudaErrorInvalidValue;
     if (p.ksplits > 1) {
         int e1 = 0, e2 = 0;
         a.ws = static_cast<float*>(
@@ -631,13 +716,14 @@ int cfi_mmq_skinny_launch(uint32_t ty, const void* x, const void* y, float* dst,
     a.ksplits = p.ksplits;
     a.kp = p.kp;
     a.stages = p.stages;
-    static CfiPerDeviceOnce attr[2][SK_MAX_NT + 1];
-    cfi_once_per_device(attr[ty == T_Q4_K][nt], [&] {
+    a.red_par = p.par ? 1u : 0u;
+    static CfiPerDeviceOnce attr[2][2][SK_MAX_NT + 1];
+    cfi_once_per_device(attr[ty == T_Q4_K][w == 16][nt], [&] {
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dv.smem_max);
     });
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3(p.nx, p.ksplits, 1);
-    c.blockDim = dim3(SK_THREADS, 1, 1);
+    c.blockDim = dim3(w * 32, 1, 1);
     c.dynamicSmemBytes = p.smem;
     c.stream = stream;
     cudaLaunchAttribute at[1];
@@ -647,4 +733,11 @@ int cfi_mmq_skinny_launch(uint32_t ty, const void* x, const void* y, float* dst,
     c.numAttrs = pdl ? 1 : 0;
     void* args[] = {&a};
     return (int)cudaLaunchKernelExC(&c, fn, args);
+}
+
+int cfi_mmq_skinny_launch(uint32_t ty, const void* x, const void* y, float* dst, uint32_t K, uint32_t nrows,
+                          uint32_t ncols_dst, uint32_t ncols_y, uint32_t stride_row_x, uint32_t stride_col_dst,
+                          unsigned int* err, cudaStream_t stream, bool pdl) {
+    return cfi_mmq_skinny_group_launch(ty, 1, &x, y, &dst, &nrows, &stride_row_x, &stride_col_dst, K, ncols_dst, ncols_y,
+                                       err, stream, pdl);
 }

@@ -31,6 +31,7 @@
 #include <string>
 #include <vector>
 
+#include "../../include/cfi_glue.h"
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
@@ -1528,6 +1529,17 @@ extern "C" int cfi_mmq_static_scratch(uint32_t ggml_type, void** kernel_params, 
 unsigned int cfi_gemm_error_take();  // k_gemm_sm100.cu
 namespace cfi {
 unsigned int fattn_error_take();     // k_fattn_sm100.cu
+}
+
+extern "C" int cfi_mmq_skinny_group(uint32_t type, int n, const void* const* x, const void* y, float* const* dst,
+                                    const uint32_t* nrows, const uint32_t* stride_row_x, const uint32_t* stride_col_dst,
+                                    uint32_t K, uint32_t ncols, uint32_t ncols_y, void* stream) {
+    if ((type != T_Q4_K && type != T_Q8_0) || !x || !dst || !nrows || !stride_row_x || !stride_col_dst || ncols == 0 ||
+        ncols > 64)
+        return (int)cudaErrorInvalidValue;
+    const char* ep = getenv("CFI_PDL");
+    return cfi_mmq_skinny_group_launch(type, n, x, y, dst, nrows, stride_row_x, stride_col_dst, K, ncols, ncols_y,
+                                       device_error_ptr(), static_cast<cudaStream_t>(stream), !(ep && strcmp(ep, "0") == 0));
 }
 
 extern "C" unsigned int cfi_device_error(void) {

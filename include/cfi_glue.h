@@ -51,6 +51,18 @@ CFI_API int cfi_glue_argmax_next(const float *logits, int n, int32_t *token, int
 CFI_API int cfi_glue_gather_row_shards(const float *src, float *dst, int nrows, int ncols, int world,
                                        long long src_rank_stride, void *stream);
 
+/* Up to 4 mul_mat_q products that read the same q8_1_mmq activations y (K values, K % 256 == 0,
+ * ncols <= 64 columns, y's block rows ncols_y >= ncols columns wide) in one launch of the skinny
+ * kernel that the native mul_mat_q uses at <= 64 columns: product i writes dst[i][c *
+ * stride_col_dst[i] + r] = sum_k W_i[r][k] y[c][k] for its nrows[i] rows, W_i in `type` blocks
+ * (Q4_K = 12 or Q8_0 = 8; 16-byte aligned; stride_row_x[i] blocks per row, a multiple of 8 for
+ * Q8_0).  The int32 block dots are exact; the fp32 sums agree with the separate products to
+ * reassociation (the launch's shape is planned for all tiles together).  Batched decode: the q, k
+ * and v products, or gate and up, in one launch instead of three or two. */
+CFI_API int cfi_mmq_skinny_group(uint32_t type, int n, const void *const *x, const void *y, float *const *dst,
+                                 const uint32_t *nrows, const uint32_t *stride_row_x, const uint32_t *stride_col_dst,
+                                 uint32_t K, uint32_t ncols, uint32_t ncols_y, void *stream);
+
 /*
  * Fused decode steps (one launch each where the ggml graph has two to five).  Results equal the
  * unfused chain where stated; n, nq, nkv multiples of 32.

@@ -3,6 +3,8 @@
 The tensor-core path dequantises both operands to fp16, so it is held to the stated 1e-3 relative
 L2 bound against the oracle's mmq reference (refs.rs:771-834), on the reference's own test shapes
 (src/subst/tests.rs:312, 480) and on BASELINE config 3 at full size."""
+import ctypes as C
+
 import numpy as np
 import pytest
 
@@ -211,19 +213,67 @@ def test_mmq_skinny_matches_the_oracle(dev, monkeypatch, ty, case):
     got = run(g, ty, p, x, y, n)
     assert np.isfinite(got).all()
     assert O.rel_l2(got, want) < SKINNY_REL, O.rel_l2(got, want)
-    # every row-group shape (KP warps per tile), alone and with K split over three CTAs (the
-    # tile partials and their counters); the planner picks one of these for each product
-    for kp in ("1", "2", "4", "8"):
-        for splits in (None, "3"):
-            monkeypatch.setenv("CFI_MMQ_SKINNY_KP", kp)
-            if splits:
-                monkeypatch.setenv("CFI_MMQ_SKINNY_SPLITS", splits)
-            again = run(g, ty, p, x, y, n)
-            assert O.rel_l2(again, want) < SKINNY_REL, (kp, splits, O.rel_l2(again, want))
-            monkeypatch.delenv("CFI_MMQ_SKINNY_SPLITS", raising=False)
+    # both CTA sizes, every row-group shape (KP warps per tile), alone and with K split over
+    # three CTAs (the tile partials and their counters); the planner picks one of these
+    for warps in ("8", "16"):
+        monkeypatch.setenv("CFI_MMQ_SKINNY_WARPS", warps)
+        for kp in ("1", "2", "4", "8", "16")[:4 if warps == "8" else 5]:
+            for splits in (None, "3"):
+                monkeypatch.setenv("CFI_MMQ_SKINNY_KP", kp)
+                if splits:
+                    monkeypatch.setenv("CFI_MMQ_SKINNY_SPLITS", splits)
+                again = run(g, ty, p, x, y, n)
+                assert O.rel_l2(again, want) < SKINNY_REL, (warps, kp, splits, O.rel_l2(again, want))
+                monkeypatch.delenv("CFI_MMQ_SKINNY_SPLITS", raising=False)
     monkeypatch.delenv("CFI_MMQ_SKINNY_KP")
+    monkeypatch.delenv("CFI_MMQ_SKINNY_WARPS")
     if n >= 256:  # the tcgen05 path on the same case (its fp16 operands: the 1e-3 bound needs a few hundred outputs)
         monkeypatch.setenv("CFI_MMQ_SKINNY", "0")
         tc = run(g, ty, p, x, y, n)
         assert O.rel_l2(tc, want) < REL_L2
     assert ctx.stats()["stock_launches"] == 0
+
+
+# cfi_mmq_skinny_group: products that read one activation buffer in one launch (batched decode's
+# q, k, v or gate, up); each product against the oracle and against its own mul_mat_q call
+@pytest.mark.parametrize("ty,k,rows,ncols", [
+    (cfi.Q4_K, 1536, (1536, 256, 256), 64),   # q, k, v of the batch-64 step (shapes of config 5)
+    (cfi.Q4_K, 2048, (300, 129, 17, 1000), 40),  # four products, ragged tiles, 5 n-tiles
+    (cfi.Q8_0, 1536, (4000, 70), 64),
+    (cfi.Q8_0, 256, (33,), 3),
+])
+def test_mmq_skinny_group_matches_the_oracle(dev, ty, k, rows, ncols):
+    ctx, g = dev
+    cases = [O.mmq_case(ty, k, r, ncols, 1, 1, 1, 500 + i + ty) for i, r in enumerate(rows)]
+    y = cases[0][2]  # every product reads the first case's activations
+    dy = torch.from_numpy(y).cuda()
+    dxs = [torch.from_numpy(c[1]).cuda() for c in cases]
+    dds = [torch.full((c[3],), float("nan"), dtype=torch.float32, device="cuda") for c in cases]
+    cfi.mmq_skinny_group(ty, [d.data_ptr() for d in dxs], dy.data_ptr(), [d.data_ptr() for d in dds], list(rows), k,
+                         ncols, stream=stream())
+    torch.cuda.synchronize()
+    assert cfi.lib().cfi_device_error() == 0
+    for (p, x, _, n), dd in zip(cases, dds):
+        got = dd.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert O.rel_l2(got, O.mmq_ref(ty, p, x, y, n)) < SKINNY_REL
+        alone = run(g, ty, p, x, y, n)  # the same product through the native mul_mat_q
+        assert O.rel_l2(got, alone) < 1e-6
+
+
+def test_mmq_skinny_group_refuses_bad_arguments(dev):
+    L = cfi.lib()
+    buf = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    P, U = C.c_void_p * 5, C.c_uint32 * 5
+    base = buf.data_ptr()
+    xs, ds = P(*[base] * 5), P(*[base] * 5)
+    nr, sr, sc = U(*[16] * 5), U(*[8] * 5), U(*[16] * 5)
+    s = C.c_void_p(stream())
+    assert L.cfi_mmq_skinny_group(cfi.Q4_K, 0, xs, C.c_void_p(base), ds, nr, sr, sc, 256, 8, 8, s) != 0  # no product
+    assert L.cfi_mmq_skinny_group(cfi.Q4_K, 5, xs, C.c_void_p(base), ds, nr, sr, sc, 256, 8, 8, s) != 0  # more than 4
+    assert L.cfi_mmq_skinny_group(cfi.Q4_0, 1, xs, C.c_void_p(base), ds, nr, sr, sc, 256, 8, 8, s) != 0  # type
+    assert L.cfi_mmq_skinny_group(cfi.Q4_K, 1, xs, C.c_void_p(base), ds, nr, sr, sc, 255, 8, 8, s) != 0  # K % 256
+    assert L.cfi_mmq_skinny_group(cfi.Q4_K, 1, xs, C.c_void_p(base), ds, nr, sr, sc, 256, 65, 65, s) != 0  # > 64 columns
+    assert L.cfi_mmq_skinny_group(cfi.Q4_K, 1, xs, C.c_void_p(base + 8), ds, nr, sr, sc, 256, 8, 8, s) != 0  # y alignment
+    torch.cuda.synchronize()
+    assert L.cfi_device_error() == 0
