@@ -1122,6 +1122,43 @@ def only_gemv(spec):
     ctx.close()
 
 
+def only_mmq(spec):
+    """One mul_mat_q shape alone (type:rows:k:cols, e.g. q8_0:151936:1536:64 for the batch-64
+    head), timed like the prefill leg (graph of back-to-back calls over rotated weight copies) and
+    printed as one JSON line: the profiling entry of the mul_mat_q summaries."""
+    import torch
+
+    import cfi_b200 as cfi
+
+    tname, rows, k, n = spec.split(":")
+    ty = {"q4k": cfi.Q4_K, "q8_0": cfi.Q8_0}[tname]
+    rows, k, n = int(rows), int(k), int(n)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = cfi.Ctx(0)
+    g = cfi.GgmlCaller(ctx, "all")
+    stream = torch.cuda.Stream(device=dev)
+    w = cfi.synthetic_weights(ty, rows, k, seed=rows)
+    wd = rotated(torch, dev, w, 3 * L2_BYTES)
+    ncopy = wd.shape[0]
+    xf = torch.from_numpy(np.random.default_rng(k).normal(size=(n, k)).astype(np.float32)).to(dev)
+    q = torch.zeros(k // 128 * n * 144, dtype=torch.uint8, device=dev)
+    d = torch.zeros(n * rows, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        g.quantize_mmq(1 if ty == cfi.Q4_K else 0, xf.data_ptr(), q.data_ptr(), k, k, n, stream=stream.cuda_stream)
+        g.mmq(ty, wd[0].data_ptr(), q.data_ptr(), d.data_ptr(), k, rows, n, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    us = graph_time_us(stream, lambda i, st: g.mmq(ty, wd[i % ncopy].data_ptr(), q.data_ptr(), d.data_ptr(), k, rows, n,
+                                                    stream=st), reps=5, calls=max(ncopy, 8))
+    wbytes = w.size
+    print(json.dumps({"only_mmq": spec, "us": round(us, 3), "weights_gbs": round(wbytes / us / 1e3, 1),
+                      "weights_frac": round(wbytes / us / 1e3 / peaks()[0], 4),
+                      "tflops": round(2.0 * rows * k * n / us / 1e6, 1), "weight_copies": ncopy,
+                      "device_error": int(cfi.lib().cfi_device_error())}), flush=True)
+    ctx.close()
+
+
 def only_rowops():
     """The row kernels at their batched shapes alone (the rowops leg without the decode shapes),
     printed as one JSON line: the profiling entry of the row-kernel summaries."""
@@ -1152,6 +1189,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--separate-quantize", action="store_true",
                     help="launch quantize_q8_1 and mul_mat_vec_q separately (no CFI_CTX_DEFER_Q8_1)")
+    ap.add_argument("--only-mmq", default="",
+                    help="time one mul_mat_q shape type:rows:k:cols (q4k or q8_0) and exit (profiling entry)")
     ap.add_argument("--only-rowops", action="store_true",
                     help="time only the row kernels at their batched shapes (for profiling) and exit")
     ap.add_argument("--only-gemv", default="",
@@ -1161,6 +1200,9 @@ def main():
         args.warmup = 3
     if args.only_gemv:
         only_gemv(args.only_gemv)
+        return
+    if args.only_mmq:
+        only_mmq(args.only_mmq)
         return
     if args.only_rowops:
         only_rowops()
