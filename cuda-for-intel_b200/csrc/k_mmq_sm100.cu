@@ -426,14 +426,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 // superblock headers from global memory.  K may be split over blockIdx.z (plane * splits +
 // split) in whole chunks; split partials go to a workspace through the C tensor map and an
 // ordered reduction kernel sums them.
-constexpr int QMM_THREADS = 352;
-constexpr int QMM_MMA_WARP = 8, QMM_B_WARP = 9, QMM_RAW_WARP = 10;
-constexpr int QMM_MAX_NS = 4, QMM_MAX_RAW = 4;
+// G groups of 8 dequantising warps (G = 2: the groups take alternate K stages, so two stages'
+// hand-off chains overlap), then the MMA, B-load and raw-load warps
+template <int G> constexpr int qmm_threads() { return (8 * G + 3) * 32; }
+constexpr int QMM_THREADS = qmm_threads<1>();
+constexpr int QMM_MAX_NS = 6, QMM_MAX_RAW = 4;
 
 struct QmmArgs {
     const uint8_t* x;  // weights (for the Q4_K correction stages)
     uint32_t K, Kt, nrows, ncols_dst, bn;
     uint32_t ns, nraw, b_stage;  // A/B ring depth, raw ring depth, bytes of a B stage
+    uint32_t pre;                // bytes before the B ring: the A ring, or (A in TMEM) what the
+                                 // epilogue's staging needs beyond the B ring it reuses
     uint32_t splits, kchunk;     // stages per split (a multiple of 4)
     uint32_t stride_row_x, stride_channel_x, stride_sample_x;  // blocks
     uint32_t nchannels_y, channel_ratio, sample_ratio;
@@ -446,10 +450,29 @@ struct QmmArgs {
 template <uint32_t TY>
 constexpr uint32_t qmm_raw_row() { return TY == T_Q4_K ? 144u : 272u; }
 
+// Where a dequantising thread puts the 8 fp16 values (4 words) of 16-byte chunk `chunk` of its
+// row's 64-value stage (`rel`: the chunk's index among the thread's four): the SW128 shared-memory
+// atom of the A ring, or registers bound for the TMEM A ring (word 4 rel + i = TMEM column 4 rel + i
+// of the thread's 16: the fp16 pairs of K elements in order).
+struct ASinkSmem {
+    uint8_t* atom;
+    int r;
+    CFI_DEV void put(int chunk, int, uint32_t a, uint32_t b, uint32_t c, uint32_t d) const { st_chunk(atom, r, chunk, a, b, c, d); }
+};
+struct ASinkRegs {
+    uint32_t* w;
+    CFI_DEV void put(int, int rel, uint32_t a, uint32_t b, uint32_t c, uint32_t d) const {
+        w[4 * rel] = a;
+        w[4 * rel + 1] = b;
+        w[4 * rel + 2] = c;
+        w[4 * rel + 3] = d;
+    }
+};
+
 // Q8_0 stage s4 of a chunk, block 2 s4 + hh of row r: the block starts 4 s4 + 2 hh bytes into the
 // 16-byte aligned 48-byte window at row + 64 s4 + 32 hh.
-template <int S4>
-CFI_DEV void qmm_dequant_q80(const uint8_t* rowp, int hh, uint8_t* atom, int r) {
+template <int S4, class Sink>
+CFI_DEV void qmm_dequant_q80(const uint8_t* rowp, int hh, const Sink& sink) {
     const uint4* win = reinterpret_cast<const uint4*>(rowp + 64 * S4 + 32 * hh);
     const uint4 c0 = win[0], c1 = win[1], c2 = win[2];
     const uint32_t w[12] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x, c2.y, c2.z, c2.w};
@@ -462,7 +485,7 @@ CFI_DEV void qmm_dequant_q80(const uint8_t* rowp, int hh, uint8_t* atom, int r) 
             uint32_t v0, v1, v2, v3;
             dequant4(q0, d2, v0, v1);
             dequant4(q1, d2, v2, v3);
-            st_chunk(atom, r, c, v0, v1, v2, v3);
+            sink.put(c, c, v0, v1, v2, v3);
         }
     } else {  // d in the high half of word S4, quants word-aligned from word S4 + 1
         const __half2 d2 = __half2half2(__ushort_as_half((uint16_t)(w[S4] >> 16)));
@@ -471,13 +494,16 @@ CFI_DEV void qmm_dequant_q80(const uint8_t* rowp, int hh, uint8_t* atom, int r) 
             uint32_t v0, v1, v2, v3;
             dequant4(w[S4 + 1 + 2 * c], d2, v0, v1);
             dequant4(w[S4 + 2 + 2 * c], d2, v2, v3);
-            st_chunk(atom, r, 4 + c, v0, v1, v2, v3);
+            sink.put(4 + c, c, v0, v1, v2, v3);
         }
     }
 }
 
-template <uint32_t TY>
-__global__ void __launch_bounds__(QMM_THREADS, 1)
+// TA: the dequantised A tiles go to a ring in tensor memory (tcgen05.st from the dequantising
+// warps, each into its own 32-lane quadrant) and the MMAs read A from there, so shared memory
+// carries only B, the raw weights and the epilogue; else to the SW128 A ring in shared memory.
+template <uint32_t TY, bool TA, int G>
+__global__ void __launch_bounds__(qmm_threads<G>(), 1)
     cfi_qmm_tc(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_b,
                const __grid_constant__ CUtensorMap tmap_c, const QmmArgs a) {
     constexpr uint32_t RAW_ROW = qmm_raw_row<TY>();
@@ -485,8 +511,8 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t NS = a.ns, NR = a.nraw;
-    uint8_t* sA = smem;
-    uint8_t* sB = sA + NS * A_STAGE;
+    uint8_t* sA = smem;  // the A ring (TA: no A ring; the epilogue's staging from here on)
+    uint8_t* sB = sA + a.pre;
     uint8_t* sRaw = sB + NS * a.b_stage;
     uint64_t* full = reinterpret_cast<uint64_t*>(sRaw + NR * RAW_BYTES);
     uint64_t* empty = full + QMM_MAX_NS;
@@ -498,8 +524,13 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
     volatile int* epi_ok = abort_flag + 1;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int QMM_MMA_WARP = 8 * G, QMM_B_WARP = 8 * G + 1;
     const uint32_t bn = a.bn;
-    const uint32_t tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+    // TMEM: the accumulator in columns [0, bn); with TA the A ring (NS x 32 columns: 64 fp16 per
+    // lane and stage) from column acol, the allocation the next power of two
+    const uint32_t acol = (bn + 31) / 32 * 32;
+    const uint32_t tneed = TA ? acol + NS * (BK / 2) : bn;
+    const uint32_t tmem_cols = tneed <= 32 ? 32 : tneed <= 64 ? 64 : tneed <= 128 ? 128 : tneed <= 256 ? 256 : 512;
     const int kmain = (int)(a.K / BK), ktotal = (int)(a.Kt / BK);
     const uint32_t split = blockIdx.z % a.splits, plane = blockIdx.z / a.splits;
     const int k0 = (int)(split * a.kchunk);
@@ -517,7 +548,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
         }
         for (uint32_t i = 0; i < NR; i++) {
             mbar_init(&raw_full[i], 1);  // the raw load's expect_tx
-            mbar_init(&raw_empty[i], 8);
+            mbar_init(&raw_empty[i], 8 * G);  // every dequantising warp, after its last stage of the chunk
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -534,15 +565,17 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
     pdl_launch_dependents();
     pdl_wait();  // weights and activations may come from the previous kernel
 
-    if (warp < 8) {
-        // ================= dequantization (256 threads), then the epilogue =================
-        const int r = tid & (BM - 1), hh = tid >> 7;
-        for (int i = 0; i < nsteps; i++) {
+    if (warp < 8 * G) {
+        // ================= dequantization (256 threads per group), then the epilogue =================
+        // group grp takes stages grp, grp + G, ...; row r, K half hh of each
+        const int r = tid & (BM - 1), hh = (tid >> 7) & 1, grp = warp >> 3;
+        for (int i = grp; i < nsteps; i += G) {
             const int s = k0 + i;
             const uint32_t slot = (uint32_t)i % NS;
             const int j = i >> 2;  // chunk of the CTA (k0 is a multiple of 4)
             bool ok = true;
-            if (s < kmain && (i & 3) == 0) ok = mbar_wait(&raw_full[j % NR], (uint32_t)(j / NR) & 1, abort_flag);
+            // the group's first stage of a raw chunk waits for the chunk
+            if (s < kmain && (i & 3) < G) ok = mbar_wait(&raw_full[j % NR], (uint32_t)(j / NR) & 1, abort_flag);
             if (ok) ok = mbar_wait(&empty[slot], ((uint32_t)(i / NS) & 1) ^ 1, abort_flag);
             if (!ok) {
                 if (lane == 0) {
@@ -551,15 +584,28 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
                 }
                 break;
             }
+            if (TA) tc_fence_after();  // the MMAs that read this TMEM stage have completed
             uint8_t* atom = sA + slot * A_STAGE;
+            uint32_t tw[16];
+            const ASinkSmem ss{atom, r};
+            const ASinkRegs sr{tw};
             if (s < kmain) {
                 const uint8_t* rowp = sRaw + (j % NR) * RAW_BYTES + r * RAW_ROW;
                 if (TY == T_Q8_0) {
-                    switch (s & 3) {
-                    case 0: qmm_dequant_q80<0>(rowp, hh, atom, r); break;
-                    case 1: qmm_dequant_q80<1>(rowp, hh, atom, r); break;
-                    case 2: qmm_dequant_q80<2>(rowp, hh, atom, r); break;
-                    default: qmm_dequant_q80<3>(rowp, hh, atom, r); break;
+                    if (TA) {
+                        switch (s & 3) {
+                        case 0: qmm_dequant_q80<0>(rowp, hh, sr); break;
+                        case 1: qmm_dequant_q80<1>(rowp, hh, sr); break;
+                        case 2: qmm_dequant_q80<2>(rowp, hh, sr); break;
+                        default: qmm_dequant_q80<3>(rowp, hh, sr); break;
+                        }
+                    } else {
+                        switch (s & 3) {
+                        case 0: qmm_dequant_q80<0>(rowp, hh, ss); break;
+                        case 1: qmm_dequant_q80<1>(rowp, hh, ss); break;
+                        case 2: qmm_dequant_q80<2>(rowp, hh, ss); break;
+                        default: qmm_dequant_q80<3>(rowp, hh, ss); break;
+                        }
                     }
                 } else {  // Q4_K: sub-block g = 2 (s % 4) + hh of the chunk's superblock
                     const uint4 h = *reinterpret_cast<const uint4*>(rowp);
@@ -578,7 +624,10 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
                         uint32_t v0, v1, v2, v3;
                         dequant4_u4(q[2 * c], 4 * hh, d2, v0, v1);
                         dequant4_u4(q[2 * c + 1], 4 * hh, d2, v2, v3);
-                        st_chunk(atom, r, 4 * hh + c, v0, v1, v2, v3);
+                        if (TA)
+                            sr.put(4 * hh + c, c, v0, v1, v2, v3);
+                        else
+                            ss.put(4 * hh + c, c, v0, v1, v2, v3);
                     }
                 }
             } else if constexpr (TY == T_Q4_K) {  // Q4_K correction stage: A[r][K + g] = half(-dmin * m_g) (refs.rs:712)
@@ -615,16 +664,30 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
                         }
                         v[p] = hv[0] | (hv[1] << 16);
                     }
-                    st_chunk(atom, r, sbl, v[0], v[1], v[2], v[3]);
+                    if (TA)
+                        sr.put(sbl, t, v[0], v[1], v[2], v[3]);
+                    else
+                        ss.put(sbl, t, v[0], v[1], v[2], v[3]);
                 }
             }
-            fence_proxy_async_smem();  // this thread's A-tile writes, visible to the tensor core
+
+            if (TA) {
+                // lanes 32 (warp % 4) .. + 31 = rows; columns acol + 32 slot + 16 hh .. + 15
+                tmem_st16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + acol + slot * (BK / 2) + 16 * hh, tw);
+                tmem_st_wait();
+                tc_fence_before();
+            } else {
+                fence_proxy_async_smem();  // this thread's A-tile writes, visible to the tensor core
+            }
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&full[slot]);
-                if (s < kmain && ((i & 3) == 3 || s == kmain - 1 || i == nsteps - 1)) mbar_arrive(&raw_empty[j % NR]);
+                // the group's last stage of the chunk releases it
+                const int last = min(4 * j + 3, min(nsteps - 1, kmain - 1 - k0));
+                if (s < kmain && i + G > last) mbar_arrive(&raw_empty[j % NR]);
             }
         }
+        if (warp >= 8) goto exit_roles;  // the second group has no epilogue part
         // ================= epilogue: TMEM -> shared -> TMA stores =================
         if (tid == 0) {
             bool got = false;
@@ -679,9 +742,14 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
                 tc_fence_after();
                 const uint32_t abase = smem_u32(sA + slot * A_STAGE), bbase = smem_u32(sB + slot * a.b_stage);
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++)
-                    mma_f16(tmem, sw128_kmajor_desc(abase + 32 * k), sw128_kmajor_desc(bbase + 32 * k), idesc,
-                            (i > 0 || k > 0) ? 1u : 0u);
+                for (int k = 0; k < BK / 16; k++) {
+                    if (TA)  // A: 8 TMEM columns (16 fp16 per lane) per K step
+                        mma_f16_ts(tmem, tmem + acol + slot * (BK / 2) + 8 * k, sw128_kmajor_desc(bbase + 32 * k), idesc,
+                                   (i > 0 || k > 0) ? 1u : 0u);
+                    else
+                        mma_f16(tmem, sw128_kmajor_desc(abase + 32 * k), sw128_kmajor_desc(bbase + 32 * k), idesc,
+                                (i > 0 || k > 0) ? 1u : 0u);
+                }
                 mma_commit(&empty[slot]);
             }
             mma_commit(done);  // also after a failure: `done` then tracks the MMAs already issued
@@ -703,7 +771,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp == 8 * G + 2) {
         // ================= raw weight chunks =================
         if (lane == 0) {
             prefetch_tmap(&tmap_w);
@@ -721,6 +789,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1)
         }
         __syncwarp();
     }
+exit_roles:
     tc_fence_before();
     __syncthreads();
     if (warp == QMM_MMA_WARP) {
@@ -1100,6 +1169,10 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
         return (v >= (int)lo && v <= (int)hi && (v % 16 == 0 || hi <= 16)) ? (uint32_t)v : dflt;
     };
     const uint32_t rtiles = (nrows + BM - 1) / BM;
+    // CFI_QMM_TMEM_A=0: the dequantised A tiles through shared memory instead of tensor memory
+    // (in TMEM the A ring costs no shared memory)
+    const char* eta = getenv("CFI_QMM_TMEM_A");
+    const bool ta = !(eta && strcmp(eta, "0") == 0);
     uint32_t bn = tile_n(ncols_dst), ns_dflt = bn <= 128 ? 4 : 3, raw_dflt = QMM_MAX_RAW;
     if ((uint64_t)rtiles * ((ncols_dst + bn - 1) / bn) * planes > (uint64_t)sms) {
         for (uint32_t ct = (ncols_dst + 159) / 160; ct <= (ncols_dst + 63) / 64; ct++) {
@@ -1186,14 +1259,20 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
         tma_c = enc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dst, dc, scs, boxc, esc, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
-    // 4. ring depths within the shared-memory limit
+    // 4. ring depths within the shared-memory limit (with A in TMEM the epilogue stages its chunks
+    // in the B ring, plus what that ring lacks)
     const uint32_t b_stage = bn * BK * 2;
-    uint32_t ns_ring = env_in("CFI_QMM_STAGES", ns_dflt, 2, QMM_MAX_NS);
+    const uint32_t stage_need = tma_c ? 8 * 2048 * 4 : 8 * 1024 * 4;  // epilogue staging, 8 warps
+    uint32_t ns_ring = env_in("CFI_QMM_STAGES", ns_dflt, 2, ta ? QMM_MAX_NS : 4);
+    auto pre_bytes = [&](uint32_t ns_) -> size_t {
+        return ta ? (size_t)(stage_need > ns_ * b_stage ? (stage_need - ns_ * b_stage + 1023) / 1024 * 1024 : 0)
+                  : (size_t)ns_ * A_STAGE;
+    };
     // a CFI_QMM_BN wider than the automatic tile may leave no room for two raw slots at the
     // default depth: give up A/B stages first
-    while (ns_ring > 2 && 1024 + (size_t)ns_ring * (A_STAGE + b_stage) + 256 + 2 * (size_t)RAW_BYTES > QMM_SMEM_LIMIT)
+    while (ns_ring > 2 && 1024 + pre_bytes(ns_ring) + (size_t)ns_ring * b_stage + 256 + 2 * (size_t)RAW_BYTES > QMM_SMEM_LIMIT)
         ns_ring--;
-    const size_t fixed = 1024 + (size_t)ns_ring * (A_STAGE + b_stage) + 256;
+    const size_t fixed = 1024 + pre_bytes(ns_ring) + (size_t)ns_ring * b_stage + 256;
     const uint32_t nraw = std::min<uint32_t>(env_in("CFI_QMM_RAW", raw_dflt, 2, QMM_MAX_RAW),
                                              (uint32_t)std::min<size_t>(QMM_MAX_RAW, (QMM_SMEM_LIMIT - fixed) / RAW_BYTES));
     if (nraw < 2) return (int)cudaErrorInvalidValue;
@@ -1208,6 +1287,7 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     a.ns = ns_ring;
     a.nraw = nraw;
     a.b_stage = b_stage;
+    a.pre = (uint32_t)pre_bytes(ns_ring);
     a.splits = splits;
     a.kchunk = kchunk;
     a.stride_row_x = srx;
@@ -1224,16 +1304,26 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     a.err = device_error_ptr();
     static CfiPerDeviceOnce attr;
     cfi_once_per_device(attr, [] {
-        cudaFuncSetAttribute(cfi_qmm_tc<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
+        cudaFuncSetAttribute(cfi_qmm_tc<TY, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
+        cudaFuncSetAttribute(cfi_qmm_tc<TY, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
+        cudaFuncSetAttribute(cfi_qmm_tc<TY, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
+        cudaFuncSetAttribute(cfi_qmm_tc<TY, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);
     });
+    // two dequantising groups where a CTA has the SM to itself (more than half the shared
+    // memory); CFI_QMM_GROUPS=1 keeps one
+    const char* eg = getenv("CFI_QMM_GROUPS");
+    const int groups = (eg && atoi(eg) == 1) ? 1 : (eg && atoi(eg) == 2) ? 2 : (smem > QMM_SMEM_LIMIT / 2 ? 2 : 1);
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3((nrows + BM - 1) / BM, (ncols_dst + bn - 1) / bn, planes * splits);
-    c.blockDim = dim3(QMM_THREADS, 1, 1);
+    c.blockDim = dim3(groups == 2 ? qmm_threads<2>() : qmm_threads<1>(), 1, 1);
     c.dynamicSmemBytes = smem;
     c.stream = stream;
     c.attrs = at;
     c.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&c, cfi_qmm_tc<TY>, tw, tb, tc, a);
+    cudaError_t e = groups == 2 ? (ta ? cudaLaunchKernelEx(&c, cfi_qmm_tc<TY, true, 2>, tw, tb, tc, a)
+                                      : cudaLaunchKernelEx(&c, cfi_qmm_tc<TY, false, 2>, tw, tb, tc, a))
+                                : (ta ? cudaLaunchKernelEx(&c, cfi_qmm_tc<TY, true, 1>, tw, tb, tc, a)
+                                      : cudaLaunchKernelEx(&c, cfi_qmm_tc<TY, false, 1>, tw, tb, tc, a));
     if (e != cudaSuccess) return (int)e;
     if (splits > 1)
         return cfi_splitk_reduce_f32(ws, ld_ws, nrows, ncols_dst, planes, splits, dst, (long long)scd, (long long)scdst,
