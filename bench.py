@@ -655,7 +655,8 @@ def fattn_bench(cfi, g, stream, dev, peak_tf):
 def decode_bench(stream, dev, ntok=48, warm=3, fused=False, defer=False, const_weights=False):
     """Qwen2.5-0.5B-architecture decode (24 layers, Q8_0 random weights, 631-token
     seeded KV cache), one CUDA graph per token step replayed for `ntok` greedy tokens.  fused: the
-    stacked-weight step with the fused glue kernels (9 launches per layer instead of 25).  defer:
+    stacked-weight step with the fused glue kernels (9 launches per layer instead of 25); fused=3: that
+    step as one persistent cooperative launch (cfi_decode_step_q8_0).  defer:
     ggml's sequence on a context that holds each quantize_q8_1 back for the GEMV reading it (every
     GEMV on the streaming kernel, which is the one that absorbs it).  const_weights: the GEMVs copy
     their weights before waiting on the previous kernel (CFI_CTX_CONST_WEIGHTS)."""
@@ -1064,6 +1065,7 @@ def run_gpu(args, rank, world):
             dec["ggml_const_weights"] = decode_bench(stream, dev, const_weights=True)
             dec["ggml_deferred_quantize"] = decode_bench(stream, dev, defer=True, const_weights=True)
             dec["fused"] = decode_bench(stream, dev, fused=1, const_weights=True)
+            dec["persistent"] = decode_bench(stream, dev, fused=3)
             line["decode"] = dec
             summary["config4_tok_s"] = dec["fused"]["tok_per_s"]
         if "config1" in legs_on:

@@ -121,6 +121,8 @@ def lib():
     L.cfi_glue_swiglu.argtypes = [vp, vp, vp, i, vp]
     L.cfi_glue_argmax_next.argtypes = [vp, i, vp, vp, vp]
     L.cfi_glue_gather_row_shards.argtypes = [vp, vp, i, i, i, ll, vp]
+    L.cfi_decode_step_q8_0.argtypes = [vp, vp, vp]
+    L.cfi_decode_step_error.restype = C.c_uint
     L.cfi_mmq_skinny_group.argtypes = [C.c_uint32, i, vp, vp, vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp]
     L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
@@ -287,6 +289,19 @@ class KernelArgs:
             raw = C.string_at(C.addressof(o), min(8, C.sizeof(o)))
             out.append(int.from_bytes(raw.ljust(8, b"\0"), "little"))
         return out
+
+
+class DecodeLayer(C.Structure):
+    """CfiDecodeLayer (include/cfi_glue.h)."""
+    _fields_ = [(n, C.c_void_p) for n in ("wqkv", "bqkv", "wo", "wgu", "wd", "attn_norm", "ffn_norm", "kc", "vc")]
+
+
+class DecodeStep(C.Structure):
+    """CfiDecodeStep (include/cfi_glue.h)."""
+    _fields_ = ([(n, C.c_int) for n in ("hidden", "n_head", "n_kv_head", "head_dim", "ffn", "vocab", "n_ctx", "n_layers")] +
+                [("eps", C.c_float), ("theta", C.c_float)] +
+                [(n, C.c_void_p) for n in ("embd", "head", "out_norm", "x", "qkv", "qr", "o", "gu", "dn", "logits", "hq", "aq",
+                                           "gq", "token", "pos")])
 
 
 class Ctx:

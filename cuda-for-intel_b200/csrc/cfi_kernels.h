@@ -121,7 +121,7 @@ int cfi_glue_slot(cudaStream_t stream, CfiGlueSlot* out);
 // A buffer of at least `bytes` for (current device, stream, kind), grown outside stream capture
 // only (*err = cudaErrorStreamCaptureUnsupported when it would have to grow under capture).
 // (CFI_BUF_COUNTERS buffers are zeroed when allocated; their kernels leave them at zero)
-enum { CFI_BUF_SPLITK = 1, CFI_BUF_MMQ_SCRATCH = 2, CFI_BUF_SKINNY_WS = 3, CFI_BUF_COUNTERS = 4 };
+enum { CFI_BUF_SPLITK = 1, CFI_BUF_MMQ_SCRATCH = 2, CFI_BUF_SKINNY_WS = 3, CFI_BUF_COUNTERS = 4, CFI_BUF_DECODE_SYNC = 5 };
 void* cfi_stream_buffer(int kind, size_t bytes, cudaStream_t stream, int* err);
 
 // ---- k_mmq_skinny.cu: mul_mat_q for at most 64 columns (Q4_K / Q8_0, one plane, K % 256 == 0) ----

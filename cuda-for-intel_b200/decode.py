@@ -167,6 +167,8 @@ class DecodeModel:
                 del os.environ[key]
 
     def _step(self, stream):
+        if self.fused == 3:
+            return self.step_persistent(stream)
         if self.fused:
             return self.step_fused(stream)
         c, g, L, s = self.cfg, self.g, self.L, stream
@@ -274,6 +276,28 @@ class DecodeModel:
                   "add_rmsnorm")
         gemv(self.head, self.hq, self.logits, c.vocab, c.hidden)
         self._chk(L.cfi_glue_argmax_next(P(self.logits), c.vocab, P(self.token), P(self.pos), sv), "argmax")
+
+    def step_persistent(self, stream):
+        """fused == 3: the whole step of fused == 1 as one persistent launch (cfi_decode_step_q8_0,
+        grid-wide barriers between the phases), its results equal to that chain's bit for bit."""
+        c, L = self.cfg, self.L
+        if getattr(self, "_ds", None) is None:
+            a = lambda t: t.data_ptr()
+            lays = (cfi.DecodeLayer * c.layers)()
+            for i, lay in enumerate(self.layers):
+                lays[i] = cfi.DecodeLayer(a(lay["wqkv"]), a(lay["bqkv"]), a(lay["wo"]), a(lay["wgu"]), a(lay["wd"]),
+                                          a(lay["attn_norm"]), a(lay["ffn_norm"]), a(lay["kc"]), a(lay["vc"]))
+            raw = bytes(lays)
+            self._ds_layers = self.t.frombuffer(bytearray(raw), dtype=self.t.uint8).to(self.dev)
+            self.t.cuda.current_stream().synchronize()
+            self._ds = cfi.DecodeStep(c.hidden, c.n_head, c.n_kv_head, c.head_dim, c.ffn, c.vocab, c.n_ctx, c.layers,
+                                      c.eps, c.theta, a(self.embd), a(self.head), a(self.out_norm), a(self.x), a(self.qkv),
+                                      a(self.qr), a(self.o), a(self.gu2), a(self.dn), a(self.logits), a(self.hq), a(self.aq),
+                                      a(self.gq), a(self.token), a(self.pos))
+        self.launches_per_step = 1
+        rc = L.cfi_decode_step_q8_0(C.byref(self._ds), C.c_void_p(self._ds_layers.data_ptr()), C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError("cfi_decode_step_q8_0 failed: %d" % rc)
 
     def step_fused_epi(self, stream):
         c, L = self.cfg, self.L

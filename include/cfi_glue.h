@@ -104,6 +104,41 @@ CFI_API int cfi_fused_mmvq_qkv_rope_store(const void *w, const void *xq, float *
                                           float *q_out, void *kc, void *vc, const int32_t *pos, int nq, int nkv,
                                           int head_dim, int n_ctx, float theta, void *stream);
 
+/*
+ * One whole decode token step of a Q8_0 Qwen2-architecture model in a single persistent launch
+ * (one CTA per SM, cooperative, grid-wide barriers between the phases): the op sequence of the
+ * fused glue chain -- get_rows of token[0], per layer add_rmsnorm_q8_1 (x += dn), the stacked QKV
+ * GEMV, qkv_rope_store, the split attention, the O GEMV, add_rmsnorm_q8_1 (x += o), the stacked
+ * gate/up GEMV, swiglu_q8_1, the down GEMV; then add_rmsnorm_q8_1 with out_norm, the head GEMV and
+ * argmax_next -- with the same results bit for bit (logits, token, pos, the caches, and x, hq,
+ * qkv, qr, aq, o, gu, gq, dn as the chain leaves them).  hidden <= 1536 and a multiple of 64; ffn
+ * a multiple of 64, ffn / 32 <= 384; head_dim 64 or 128; n_ctx a multiple of 8, at most 8192.
+ * layers_dev: n_layers CfiDecodeLayer in device memory.  Returns a CUDA error code; a barrier
+ * that times out (2 s) aborts the launch and records a code for cfi_decode_step_error().
+ */
+typedef struct {
+    const void *wqkv;  /* (n_head + 2 n_kv_head) head_dim x hidden Q8_0: q, k, v rows stacked */
+    const float *bqkv; /* the stacked biases */
+    const void *wo;    /* hidden x n_head head_dim */
+    const void *wgu;   /* 2 ffn x hidden: the gate rows, then the up rows */
+    const void *wd;    /* hidden x ffn */
+    const float *attn_norm, *ffn_norm;
+    void *kc, *vc;     /* f16 K cache [kv head][pos][dim], V cache [kv head][dim][pos] */
+} CfiDecodeLayer;
+typedef struct {
+    int hidden, n_head, n_kv_head, head_dim, ffn, vocab, n_ctx, n_layers;
+    float eps, theta;
+    const void *embd;     /* vocab x hidden Q8_0 token embedding */
+    const void *head;     /* vocab x hidden Q8_0 output matrix */
+    const float *out_norm;
+    float *x, *qkv, *qr, *o, *gu, *dn, *logits;
+    void *hq, *aq, *gq;   /* q8_1 buffers: hidden, n_head head_dim and ffn values */
+    int32_t *token, *pos;
+} CfiDecodeStep;
+CFI_API int cfi_decode_step_q8_0(const CfiDecodeStep *s, const CfiDecodeLayer *layers_dev, void *stream);
+/* Reads and clears the persistent decode step's error word (0: no barrier gave up). */
+CFI_API unsigned int cfi_decode_step_error(void);
+
 #ifdef __cplusplus
 }
 #endif
