@@ -426,7 +426,11 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     computed from them in a real model), so collective latency is exposed as it would be.
     Reported: the step time, the same step without collectives (kernels only), the collectives
     alone, the step with the products of a group as parallel graph branches (side streams), and a
-    check of rank 0's gathered logits against the unsharded head product on rank 0."""
+    check of rank 0's gathered logits against the unsharded head product on rank 0.  With N > 1
+    also `peer_ms`: the all-gather fused into the products over NVLink peer memory (each group in
+    one cfi_mmq_skinny_group_peers launch that stores every rank's rows into every rank's
+    gathered dst and ends once the peers' rows are in; cfi_peer.h), its logits checked against
+    the NCCL path's."""
     import torch
 
     import shard
@@ -492,8 +496,42 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
         return done
 
     side = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    # the all-gather over NVLink peer memory: every product's gathered ggml dst (n x nrows) in
+    # one peer buffer per rank, mapped into every rank (cfi_peer.h)
+    pg, poff = None, {}
+    if world > 1:
+        o = 0
+        for nm in names:
+            poff[nm] = o
+            o += (n * nrows[nm] * 4 + 255) // 256 * 256
 
-    def step(kernels=True, collectives=True, parallel=False, grouped=False):
+        def exchange(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+
+        pg = cfi.PeerGroup(rank, world, o, exchange)
+
+    def peer_step():
+        """Each group of products in one skinny launch that stores every rank's rows into every
+        rank's gathered output (peer stores over NVLink) and ends once the peers' rows have
+        arrived (its last CTA's bounded wait for their signals): no collective, no assembly
+        kernel, no extra launch."""
+        st = torch.cuda.current_stream().cuda_stream
+        for lay in layers:
+            for inputs, k in C5_GROUPS:
+                g.quantize_mmq(1, xf[k].data_ptr(), xq[k].data_ptr(), k, k, n, stream=st)
+                cfi.mmq_skinny_group_peers(cfi.Q4_K, [lay[nm].data_ptr() for nm in inputs], xq[k].data_ptr(),
+                                           [pg.data + poff[nm] + 4 * sh[nm].row0 for nm in inputs],
+                                           [sh[nm].rows for nm in inputs], k, n, pg,
+                                           stride_col_dst=[nrows[nm] for nm in inputs], stream=st)
+        g.quantize_mmq(0, xf[H].data_ptr(), hq.data_ptr(), H, H, n, stream=st)
+        cfi.mmq_skinny_group_peers(cfi.Q8_0, [head.data_ptr()], hq.data_ptr(), [pg.data + poff["head"] + 4 * sh["head"].row0],
+                                   [sh["head"].rows], H, n, pg, stride_col_dst=[V], stream=st)
+
+    def step(kernels=True, collectives=True, parallel=False, grouped=False, peer=False):
+        if peer:
+            return peer_step()
         """parallel: the products of a group after the first run on side streams, as parallel
         branches (each product depends only on the group's quantized input); every stream has
         its own split-K workspace and scratch.  grouped: the products of a group in one launch
@@ -581,11 +619,24 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
     ms_coll = timed(kernels=False) if world > 1 else 0.0
     ms_par = timed(parallel=True)
     ms_grp = timed(grouped=True)
-    # check: rank 0's gathered logits against the unsharded head product on rank 0
+    ms_peer = timed(peer=True) if world > 1 else None
+    # check: rank 0's gathered logits (the NCCL path's, and the peer path's) against the
+    # unsharded head product on rank 0
     check = {}
     with torch.cuda.stream(stream):
         step()
     torch.cuda.synchronize()
+    peer_head = None
+    if world > 1:
+        with torch.cuda.stream(stream):
+            step(peer=True)
+        torch.cuda.synchronize()
+        if rank == 0:
+            peer_head = torch.empty(n * V, dtype=torch.float32, device=dev)
+            rc = L_.cfi_glue_gather_row_shards(pg.data + poff["head"], peer_head.data_ptr(), V, n, 1, 0,
+                                               torch.cuda.current_stream().cuda_stream)  # one rank's "gather": a copy
+            assert rc == 0, rc
+            torch.cuda.synchronize()
     if rank == 0:
         got = (full["head"] if world > 1 else out["head"]).view(n, V)
         ref = torch.zeros(n * V, dtype=torch.float32, device=dev)
@@ -598,8 +649,16 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
         diff = (got.double() - ref.double()).norm() / ref.double().norm()
         check = {"logits_bitwise_equal": bool(torch.equal(got, ref)), "logits_rel_l2": float(diff),
                  "logits_nonfinite": int((~torch.isfinite(got)).sum()), "ref_nonfinite": int((~torch.isfinite(ref)).sum())}
+        if peer_head is not None:
+            ph = peer_head.view(n, V)
+            check["peer_logits_equal_nccl_path"] = bool(torch.equal(ph, got))
+            check["peer_logits_rel_l2"] = float((ph.double() - ref.double()).norm() / ref.double().norm())
+            check["peer_logits_nonfinite"] = int((~torch.isfinite(ph)).sum())
+    err = int(L_.cfi_device_error())
     if dist:
         dist.barrier()
+    if pg is not None:
+        pg.close()
     launches = L * (4 + 7) + 2 + (L * 7 + 1 if world > 1 else 0)  # + one assembly per product
     res = {"ms": round(ms_step, 4), "tok_per_s": round(64 / (ms_step * 1e-3), 1),
            "weights_gbs": round(wbytes / ms_step / 1e6, 1),
@@ -613,7 +672,11 @@ def config5_b64(cfi, g, stream, dev, peak_gbs, world, rank, dist, comm):
            "all_gathers_per_step": (L * len(C5_GROUPS) + 1) if world > 1 else 0,
            "gathered_bytes_per_gpu": (world - 1) * n * 4 * (L * sum(sh[nm].rows_padded for nm in C5_SHAPES) +
                                                             sh["head"].rows_padded),
-           "launches": launches, "gpus": world, **check}
+           "launches": launches, "gpus": world, "device_error": err, **check}
+    if ms_peer is not None:
+        res.update({"peer_ms": round(ms_peer, 4), "peer_tok_per_s": round(64 / (ms_peer * 1e-3), 1),
+                    "peer_frac": round(wbytes / ms_peer / 1e6 / (peak_gbs * world), 4),
+                    "peer_launches": 2 * (L * len(C5_GROUPS) + 1)})
     del layers, head, head_full, out, gbuf, gath, full
     return res
 
@@ -1082,6 +1145,8 @@ def run_gpu(args, rank, world):
         summary["config5_b64_ms"] = c5["decode_b64"]["ms"]
         summary["config5_b64_kernels_ms"] = c5["decode_b64"]["kernels_only_ms"]
         summary["config5_b64_parallel_ms"] = c5["decode_b64"]["parallel_products_ms"]
+        if "peer_ms" in c5["decode_b64"]:
+            summary["config5_b64_peer_ms"] = c5["decode_b64"]["peer_ms"]
         line["config5"] = c5
     if world == 1 and "cpu" in legs_on:
         gbs, used, n, el = cpu_baseline(args.cpu_seconds)

@@ -124,6 +124,13 @@ def lib():
     L.cfi_decode_step_q8_0.argtypes = [vp, vp, vp]
     L.cfi_decode_step_error.restype = C.c_uint
     L.cfi_mmq_skinny_group.argtypes = [C.c_uint32, i, vp, vp, vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp]
+    L.cfi_mmq_skinny_group_peers.argtypes = [C.c_uint32, i, vp, vp, vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32,
+                                             C.POINTER(PeerSet), vp]
+    L.cfi_peer_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p), vp]
+    L.cfi_peer_open.argtypes = [vp, C.POINTER(C.c_void_p)]
+    L.cfi_peer_close.argtypes = [vp]
+    L.cfi_peer_free.argtypes = [vp]
+    L.cfi_peer_barrier.argtypes = [C.POINTER(PeerSet), vp]
     L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]
@@ -586,6 +593,93 @@ def mmq_skinny_group(ty, xs, y, dsts, nrows, k, ncols, ncols_y=None, stride_row_
     rc = lib().cfi_mmq_skinny_group(ty, n, P(*xs), C.c_void_p(y), P(*dsts), U(*nrows), U(*srx), U(*scd), k, ncols,
                                     ncols_y or ncols, C.c_void_p(stream))
     check(rc, "cfi_mmq_skinny_group")
+
+
+PEER_HANDLE_BYTES = 64
+PEER_MAX_RANKS = 8
+
+
+class PeerSet(C.Structure):
+    """cfi_peer.h's CfiPeerSet: a rank's view of its group."""
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("delta", C.c_longlong * PEER_MAX_RANKS),
+                ("sig_remote", C.c_void_p * PEER_MAX_RANKS), ("sig_local", C.c_void_p), ("expect", C.c_void_p)]
+
+
+class PeerGroup:
+    """One peer buffer per rank of one node, each mapped into every rank's process (CUDA IPC over
+    NVLink; cfi_peer.h): `nbytes` bytes of outputs at offset 0, then the ranks' signal slots and
+    this rank's wait counts.  `exchange(obj)` returns every rank's obj in rank
+    order (torch.distributed.all_gather_object, or any channel between the ranks).  A product
+    launched with `peers` stores its outputs into every rank's copy at the same offset and ends
+    once every rank's rows are here; barrier() is the group's signal and wait alone."""
+
+    def __init__(self, rank, world, nbytes, exchange):
+        if not 1 <= world <= PEER_MAX_RANKS or not 0 <= rank < world:
+            raise ValueError("bad rank %d of %d" % (rank, world))
+        self.rank, self.world = rank, world
+        self.data_bytes = (nbytes + 255) // 256 * 256
+        sig_off = self.data_bytes
+        expect_off = sig_off + 4 * world
+        L = lib()
+        self.base = C.c_void_p()
+        handle = C.create_string_buffer(PEER_HANDLE_BYTES)
+        check(L.cfi_peer_alloc(expect_off + 4 * world + 256, C.byref(self.base), C.cast(handle, C.c_void_p)),
+              "cfi_peer_alloc")
+        self.ptrs, self._opened = [], []
+        try:
+            handles = exchange(handle.raw)
+            for r, h in enumerate(handles):
+                if r == rank:
+                    self.ptrs.append(self.base.value)
+                    continue
+                p = C.c_void_p()
+                check(L.cfi_peer_open(h, C.byref(p)), "cfi_peer_open")
+                self._opened.append(p.value)
+                self.ptrs.append(p.value)
+        except Exception:
+            self.close()
+            raise
+        ps = PeerSet()
+        ps.rank, ps.world = rank, world
+        for r in range(world):
+            ps.delta[r] = self.ptrs[r] - self.base.value
+            ps.sig_remote[r] = self.ptrs[r] + sig_off + 4 * rank
+        ps.sig_local = self.base.value + sig_off
+        ps.expect = self.base.value + expect_off
+        self.peers = ps
+
+    @property
+    def data(self):
+        """Device address of this rank's outputs."""
+        return self.base.value
+
+    def barrier(self, stream=0):
+        check(lib().cfi_peer_barrier(C.byref(self.peers), C.c_void_p(stream)), "cfi_peer_barrier")
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (every rank synchronised first)."""
+        L = lib()
+        for p in self._opened:
+            L.cfi_peer_close(C.c_void_p(p))
+        self._opened = []
+        if self.base.value:
+            L.cfi_peer_free(self.base)
+            self.base = C.c_void_p()
+
+
+def mmq_skinny_group_peers(ty, xs, y, dsts, nrows, k, ncols, group, ncols_y=None, stride_row_x=None,
+                           stride_col_dst=None, stream=0):
+    """cfi_mmq_skinny_group_peers: mmq_skinny_group whose outputs (inside `group`'s data) are also
+    stored into every other rank's copy; it ends once every rank's rows are here."""
+    n = len(xs)
+    qk = 256 if ty == Q4_K else 32
+    srx = stride_row_x or [k // qk] * n
+    scd = stride_col_dst or list(nrows)
+    P = C.c_void_p * n
+    U = C.c_uint32 * n
+    rc = lib().cfi_mmq_skinny_group_peers(ty, n, P(*xs), C.c_void_p(y), P(*dsts), U(*nrows), U(*srx), U(*scd), k, ncols,
+                                          ncols_y or ncols, C.byref(group.peers), C.c_void_p(stream))
+    check(rc, "cfi_mmq_skinny_group_peers")
 
 
 def quantize_q8_0(w):

@@ -124,14 +124,31 @@ int cfi_glue_slot(cudaStream_t stream, CfiGlueSlot* out);
 enum { CFI_BUF_SPLITK = 1, CFI_BUF_MMQ_SCRATCH = 2, CFI_BUF_SKINNY_WS = 3, CFI_BUF_COUNTERS = 4, CFI_BUF_DECODE_SYNC = 5 };
 void* cfi_stream_buffer(int kind, size_t bytes, cudaStream_t stream, int* err);
 
+// The library's device error word (k_mmq_sm100.cu; read and cleared by cfi_device_error).
+unsigned int* cfi_device_error_word();
+
 // ---- k_mmq_skinny.cu: mul_mat_q for at most 64 columns (Q4_K / Q8_0, one plane, K % 256 == 0) ----
 bool cfi_mmq_skinny_applies(uint32_t ty, const void* x, const void* y, uint32_t K, uint32_t ncols_dst,
                             uint32_t stride_row_x, uint32_t planes);
+// A rank's group for the all-gather over peer memory, as the kernels take it (cfi_peer.h's
+// CfiPeerSet, checked, plus the wait bound): with world == 1 a launch stores only locally.
+constexpr int CFI_MAX_RANKS = 8;
+struct CfiPeerDev {
+    int rank, world;
+    long long delta[CFI_MAX_RANKS];            // byte offset to rank r's copy (0 for this rank)
+    unsigned int* sig_remote[CFI_MAX_RANKS];  // rank r's slot for this rank
+    unsigned int* sig_local;                  // this rank's slots, one per rank
+    unsigned int* expect;                     // this rank's wait counts, one per rank
+    unsigned long long limit_ns;              // bound of each wait for a peer
+};
+struct CfiPeerSet;
+// Checks a CfiPeerSet and fills `out` (k_peer.cu); 0 or cudaErrorInvalidValue.
+int cfi_peer_dev(const CfiPeerSet* in, CfiPeerDev* out);
 // n <= 4 products over the same activations in one launch (their tiles back to back)
 int cfi_mmq_skinny_group_launch(uint32_t ty, int n, const void* const* x, const void* y, float* const* dst,
                                 const uint32_t* nrows, const uint32_t* stride_row_x, const uint32_t* stride_col_dst,
                                 uint32_t K, uint32_t ncols_dst, uint32_t ncols_y, unsigned int* err, cudaStream_t stream,
-                                bool pdl);
+                                bool pdl, const CfiPeerDev* peers = nullptr);
 int cfi_mmq_skinny_launch(uint32_t ty, const void* x, const void* y, float* dst, uint32_t K, uint32_t nrows,
                           uint32_t ncols_dst, uint32_t ncols_y, uint32_t stride_row_x, uint32_t stride_col_dst,
                           unsigned int* err, cudaStream_t stream, bool pdl);

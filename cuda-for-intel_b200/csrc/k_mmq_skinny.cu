@@ -36,6 +36,7 @@
 // skips its remaining work and lets its copies in flight land).
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
+#include "peer_sync.cuh"
 #include "sm100_ptx.cuh"
 
 #include <algorithm>
@@ -104,6 +105,10 @@ struct SkArgs {
     float* ws;                      // K splits: partials [tile][split][SK_PART_FLOATS]
     unsigned int* counters;         // K splits: per tile
     unsigned int* err;
+    // all-gather over peer memory (world > 1): every output also at its address + delta[r] on
+    // every other rank r; after the launch's last store its last CTA signals the peers and waits
+    // for theirs (world == 1: local stores only)
+    CfiPeerDev pr;
 };
 
 // The product a launch tile belongs to (constant indices only: no local copy of the arguments).
@@ -119,6 +124,28 @@ CFI_DEV SkProd sk_prod(const SkArgs& a, uint32_t tile) {
         if ((uint32_t)i < a.ngroup && tile >= a.tile_begin[i])
             p = {a.x[i], a.dst[i], a.nrows[i], a.stride_row_x[i], a.stride_col_dst[i], tile - a.tile_begin[i]};
     return p;
+}
+
+// A warp's outputs of one tile (m16n8 accumulator layout: lane (g, t) holds rows g, g + 8 of
+// columns 2t, 2t + 1 of each 8-column tile n) into dst and, for an all-gather over peer memory,
+// into every peer's copy (plain stores over NVLink).
+// Ranks in turn from this one, so the ranks' first stores go to different GPUs.  (`a` is the
+// kernel's __grid_constant__ parameter: the offsets are read from the parameter space with a
+// run-time index, without a local copy of the arguments.)
+template <int NT>
+CFI_DEV void sk_store(const SkArgs& a, const SkProd& pr, const float (&out)[NT][4], int g, int t) {
+#pragma unroll 1
+    for (int i = 0; i < a.pr.world; i++) {
+        const int r = a.pr.rank + i < a.pr.world ? a.pr.rank + i : a.pr.rank + i - a.pr.world;
+        float* d = reinterpret_cast<float*>(reinterpret_cast<char*>(pr.dst) + a.pr.delta[r]);
+#pragma unroll
+        for (int n = 0; n < NT; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const uint32_t row = pr.tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
+                if (row < pr.nrows && col < a.ncols) d[(size_t)col * pr.scd + row] = out[n][e];
+            }
+    }
 }
 
 // 16-byte global -> shared copy on the LSU path (L2 only), and an arrival on `bar` once every
@@ -227,7 +254,7 @@ CFI_DEV void sk_subblock(const uint32_t (&af)[4], uint64_t w0, uint64_t w1, uint
 }
 
 template <uint32_t TY, int NT, int W>
-__global__ void __launch_bounds__(W * 32, 1) cfi_mmq_skinny(const SkArgs a) {
+__global__ void __launch_bounds__(W * 32, 1) cfi_mmq_skinny(const __grid_constant__ SkArgs a) {
     constexpr uint32_t CB = sk_chunk_bytes<TY>(), WB = SK_TR * CB, NC8 = NT * 8;
     constexpr uint32_t XSP = NC8 + 8, XDT = sk_xdt(NT);
     extern __shared__ __align__(128) uint8_t smem[];
@@ -496,13 +523,7 @@ __global__ void __launch_bounds__(W * 32, 1) cfi_mmq_skinny(const SkArgs a) {
         if (has && kp == 0 && !failed) {
             const SkProd pr = sk_prod(a, tile);
             if (a.ksplits == 1) {
-#pragma unroll
-                for (int n = 0; n < NT; n++)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const uint32_t row = pr.tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
-                        if (row < pr.nrows && col < a.ncols) pr.dst[(size_t)col * pr.scd + row] = out[n][e];
-                    }
+                sk_store<NT>(a, pr, out, g, t);
             } else {
                 // K splits: this split's partial, then the last warp of the tile adds them in order
                 float* part = a.ws + ((size_t)tile * a.ksplits + blockIdx.y) * SK_PART_FLOATS;
@@ -534,13 +555,7 @@ __global__ void __launch_bounds__(W * 32, 1) cfi_mmq_skinny(const SkArgs a) {
 #pragma unroll
                             for (int e = 0; e < 4; e++) out[n][e] += v[n][e];
                     }
-#pragma unroll
-                    for (int n = 0; n < NT; n++)
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const uint32_t row = pr.tile * SK_TR + g + 8 * (e >> 1), col = n * 8 + 2 * t + (e & 1);
-                            if (row < pr.nrows && col < a.ncols) pr.dst[(size_t)col * pr.scd + row] = out[n][e];
-                        }
+                    sk_store<NT>(a, pr, out, g, t);
                     if (lane == 0) a.counters[tile] = 0u;
                 }
             }
@@ -558,6 +573,19 @@ __global__ void __launch_bounds__(W * 32, 1) cfi_mmq_skinny(const SkArgs a) {
             for (uint32_t ci = 0; ci < nck; ci++)
                 while (!mbar_try_wait(abar + ci, 0) && globaltimer() < deadline) {
                 }
+    }
+    if (a.pr.world > 1) {
+        // this CTA's stores (the peers' copies included; ordered before thread 0 by the CTA
+        // barrier) made visible to the system, then its share of the launch's signal to every
+        // peer; CTA 0 then waits for every peer's whole signal, so the launch completes once
+        // every rank's rows are here (a CTA that gave up signals too: its error is in the error
+        // word, and the peers do not wait out their limit)
+        __syncthreads();
+        if (tid == 0) {
+            const bool first = blockIdx.x == 0 && blockIdx.y == 0;
+            peer_signal_cta(a.pr, gridDim.x * gridDim.y, first);
+            if (first) peer_wait_all(a.pr, a.err);
+        }
     }
 }
 
@@ -674,7 +702,7 @@ bool cfi_mmq_skinny_applies(uint32_t ty, const void* x, const void* y, uint32_t 
 int cfi_mmq_skinny_group_launch(uint32_t ty, int n, const void* const* x, const void* y, float* const* dst,
                                 const uint32_t* nrows, const uint32_t* stride_row_x, const uint32_t* stride_col_dst,
                                 uint32_t K, uint32_t ncols_dst, uint32_t ncols_y, unsigned int* err, cudaStream_t stream,
-                                bool pdl) {
+                                bool pdl, const CfiPeerDev* peers) {
     const int nt = (int)((ncols_dst + 7) / 8);
     const char* ew = getenv("CFI_MMQ_SKINNY_WARPS");
     const int w = ew && atoi(ew) == 16 ? 16 : (ew && atoi(ew) == 8 ? 8 : SK_DEFAULT_WARPS);
@@ -702,9 +730,15 @@ int cfi_mmq_skinny_group_launch(uint32_t ty, int n, const void* const* x, const 
     a.nchunks = K / 256;
     a.ntiles = tiles;
     a.err = err;
+    if (peers) {
+        a.pr = *peers;
+    } else {
+        a.pr.world = 1;  // rank 0, delta[0] = 0: local stores
+    }
     SkPlan p;
     if (!sk_plan(ty, (uint32_t)nt, a.nchunks, a.ntiles, dv.sms, dv.smem_max, (uint32_t)w, p))
         return (int)cudaErrorInvalidValue;
+    if (a.pr.world > 1 && (size_t)p.nx * p.ksplits >= CFI_PEER_UNIT) return (int)cudaErrorInvalidValue;  // signal units
     if (p.ksplits > 1) {
         int e1 = 0, e2 = 0;
         a.ws = static_cast<float*>(

@@ -32,6 +32,7 @@
 #include <vector>
 
 #include "../../include/cfi_glue.h"
+#include "../../include/cfi_peer.h"
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
 #include "sm100_ptx.cuh"
@@ -1631,6 +1632,25 @@ extern "C" int cfi_mmq_skinny_group(uint32_t type, int n, const void* const* x, 
     return cfi_mmq_skinny_group_launch(type, n, x, y, dst, nrows, stride_row_x, stride_col_dst, K, ncols, ncols_y,
                                        device_error_ptr(), static_cast<cudaStream_t>(stream), !(ep && strcmp(ep, "0") == 0));
 }
+
+extern "C" int cfi_mmq_skinny_group_peers(uint32_t type, int n, const void* const* x, const void* y, float* const* dst,
+                                          const uint32_t* nrows, const uint32_t* stride_row_x,
+                                          const uint32_t* stride_col_dst, uint32_t K, uint32_t ncols, uint32_t ncols_y,
+                                          const CfiPeerSet* peers, void* stream) {
+    if ((type != T_Q4_K && type != T_Q8_0) || !x || !dst || !nrows || !stride_row_x || !stride_col_dst || ncols == 0 ||
+        ncols > 64)
+        return (int)cudaErrorInvalidValue;
+    CfiPeerDev pd;
+    const int rc = cfi_peer_dev(peers, &pd);
+    if (rc) return rc;
+    const char* ep = getenv("CFI_PDL");
+    return cfi_mmq_skinny_group_launch(type, n, x, y, dst, nrows, stride_row_x, stride_col_dst, K, ncols, ncols_y,
+                                       device_error_ptr(), static_cast<cudaStream_t>(stream), !(ep && strcmp(ep, "0") == 0),
+                                       &pd);
+}
+
+// The library's device error word (the bounded waits of the kernels in other files record there).
+unsigned int* cfi_device_error_word() { return device_error_ptr(); }
 
 extern "C" unsigned int cfi_device_error(void) {
     unsigned int v = 0, z = 0;
