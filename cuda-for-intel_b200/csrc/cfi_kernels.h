@@ -18,10 +18,11 @@ const void* cfi_native_quantize_mmq(int ds4);
 const void* cfi_native_mmvq(uint32_t ty, uint32_t ncols, bool stream);
 bool cfi_mmvq_streams(uint32_t ncols);
 bool cfi_mmvq_stream_only(uint32_t ty);  // types without the row kernel (Q6_K, Q4_0)
-// streaming kernel: rows per shared-memory stage and dynamic shared memory of a launch
+// streaming kernel: rows per shared-memory stage and dynamic shared memory of a launch whose grid
+// holds ctas_per_sm CTAs per SM
 void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
                             uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,
-                            uint32_t* chunk_rows, uint32_t* nstages, size_t* smem);
+                            uint32_t ctas_per_sm, uint32_t* chunk_rows, uint32_t* nstages, size_t* smem);
 // direct-fill kernel (cfi_native_mmvq_direct, `nstages` 0): plain global loads into two
 // register-fed stages of at most 16 KB.  False when the rows are strided or one row is larger than a stage.
 bool cfi_mmvq_direct_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,

@@ -949,6 +949,9 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
     // first stages are fetched before waiting on the previous kernel (programmatic dependent
     // launch), overlapping its tail; only the activations (and an ids table) wait
     const bool early = (nst & 0x100u) != 0 && !(NCOLS == 1 && ids != nullptr);
+    // nst bit 9: the L2 hint for the CTA's whole row range is given in the early form too, so HBM
+    // streams the rows ahead of the shared-memory stages (which then copy from L2)
+    const bool hint_early = (nst & 0x200u) != 0;
     nst &= 0xffu;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[ST_MAX_STAGES];
@@ -973,7 +976,7 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
         for (uint32_t s = 0; s < nst; s++) mbar_init(&full[s], 1);
         fence_mbar_init();
         // L2 hint for this CTA's rows (the ids table may come from the previous kernel: skip)
-        if (!use_ids && !early && rend > rbeg) {
+        if (!use_ids && (!early || hint_early) && rend > rbeg) {
             const uint32_t channel_x = fastdiv(channel_dst, channel_ratio);
             const uint8_t* pl = static_cast<const uint8_t*>(vx) +
                                 ((size_t)sample_x * stride_sample_x + (size_t)channel_x * stride_channel_x) * BB;
@@ -1338,7 +1341,7 @@ bool cfi_mmvq_streams(uint32_t ncols) { return ncols >= 1 && ncols <= 8; }
 
 void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint32_t nrows, uint32_t grid_x,
                             uint32_t stride_row_x, uint32_t chunk_target, uint32_t stage_budget, uint32_t max_stages,
-                            uint32_t* chunk_rows, uint32_t* nstages, size_t* smem) {
+                            uint32_t ctas_per_sm, uint32_t* chunk_rows, uint32_t* nstages, size_t* smem) {
     const uint32_t nb = ncols_x / block_values_of(ty);
     const uint32_t row_bytes = nb * block_bytes_of(ty);
     const bool dense = stride_row_x == nb;
@@ -1347,7 +1350,10 @@ void cfi_mmvq_stream_layout(uint32_t ty, uint32_t ncols, uint32_t ncols_x, uint3
     while (c > 1 && st_stage_bytes(c, row_bytes, dense) > stage_budget) c--;
     const uint32_t chunks = (per_cta + c - 1) / c;
     uint32_t nst = std::max(1u, std::min(std::min(max_stages, ST_MAX_STAGES), chunks));
-    const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127, cap = (size_t)cfi_mmvq_max_smem_bytes();
+    // the grid holds ctas_per_sm CTAs per SM: each fits its share of the SM's 228 KB (1 KB of it
+    // reserved per CTA, and the kernel's static words), so the grid runs in one wave
+    const size_t ys = ((size_t)ncols * (ncols_x / 32) * 40 + 127) & ~(size_t)127;
+    const size_t cap = std::min((size_t)cfi_mmvq_max_smem_bytes(), (size_t)233472 / std::max(1u, ctas_per_sm) - 1024 - 128);
     // long rows: fewer stages, then shorter chunks, until the CTA fits
     while (nst > 1 && (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys > cap) nst--;
     while (c > 1 && (size_t)nst * st_stage_bytes(c, row_bytes, dense) + ys > cap) c--;
@@ -1407,7 +1413,7 @@ int launch_epi(const void* w, const void* xq, float* y, int rows, int k, DecodeE
     const uint32_t nb = (uint32_t)k / 32, grid = std::max(1u, std::min((uint32_t)rows, 2u * (uint32_t)sms));
     uint32_t chunk = 0, nst = 0;
     size_t smem = 0;
-    cfi_mmvq_stream_layout(T_Q8_0, 1, (uint32_t)k, (uint32_t)rows, grid, nb, 32, 48 * 1024, 3, &chunk, &nst, &smem);
+    cfi_mmvq_stream_layout(T_Q8_0, 1, (uint32_t)k, (uint32_t)rows, grid, nb, 32, 48 * 1024, 3, 2, &chunk, &nst, &smem);
     smem = std::max(smem, epi_smem);
     // the largest dynamic shared memory set so far for this kernel, per device
     static std::mutex attr_mu;

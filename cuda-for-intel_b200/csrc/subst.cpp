@@ -691,13 +691,17 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         }
         if (stream && !direct && !mma) {
             // CFI_MMVQ_STREAM_CTAS CTAs per SM shared by the channel/sample planes; chunks of
-            // CFI_MMVQ_CHUNK rows within CFI_MMVQ_STAGE_KB per stage, CFI_MMVQ_STAGES stages
-            const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", 2, 1, 8);
+            // CFI_MMVQ_CHUNK rows within CFI_MMVQ_STAGE_KB per stage, CFI_MMVQ_STAGES stages (as
+            // many as fit the CTAs' shares of the SM).  Default: 3 CTAs per SM (two 32-row stages
+            // each) for 32 MB of weights and more, measured 0.77 / 0.73 of HBM on the 151936 x 896
+            // Q8_0 lm_head and a 65536 x 2048 Q4_K matrix against 0.61 / 0.66 with 2 (three stages);
+            // 2 below, where the launch is latency-bound (8192 x 2048 Q4_K: 3.4 against 4.5 us)
+            const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", wkb * planes >= 32u * 1024u ? 3 : 2, 1, 8);
             const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
             nl.grid[0] = std::max(1u, std::min(nrows, cap));
             cfi_mmvq_stream_layout(plan.ty, plan.ncols, ncols_x, nrows, nl.grid[0], (uint32_t)vals[6],
                                    env_u32("CFI_MMVQ_CHUNK", 32, 1, 256), 1024 * env_u32("CFI_MMVQ_STAGE_KB", 48, 4, 112),
-                                   env_u32("CFI_MMVQ_STAGES", 3, 1, 4), &chunk, &nstages, &nl.smem);
+                                   env_u32("CFI_MMVQ_STAGES", 3, 1, 4), per_sm, &chunk, &nstages, &nl.smem);
         } else if (!stream) {
             const uint32_t per_sm = env_u32("CFI_MMVQ_CTAS", 4, 1, 8);
             const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
@@ -1205,7 +1209,7 @@ int launch_to(cfi_ctx* ctx, const cfi_plan* plan, void* stock_fn, const uint32_t
             NativeLaunch nl;
             if (map_launch(*plan, grid, block, vals.data(), (int)vals.size(), args, &nl) && native_ready(ctx, *plan, stream)) {
                 if ((ctx->flags & CFI_CTX_CONST_WEIGHTS) && plan->kernel == CFI_K_MMVQ && nl.extra.size() == 3 && vals[2] == 0)
-                    nl.extra[2] |= 0x100u;  // fetch the weights before waiting on the previous kernel
+                    nl.extra[2] |= 0x100u | (env_u32("CFI_MMVQ_HINT_EARLY", 0, 0, 1) ? 0x200u : 0u);  // fetch the weights before waiting on the previous kernel (and hint L2 with all of them)
                 int code = 0;
                 int rc = 0;
                 if (injected(ctx, CFI_SITE_NATIVE_LAUNCH, &code))
