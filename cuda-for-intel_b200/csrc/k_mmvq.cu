@@ -401,9 +401,11 @@ __global__ void __launch_bounds__(NW * 32)
 // asks L2 for its weight rows (a hint, never a read) and lets its own dependents launch, so a
 // chain of GEMVs (with the quantizer between them, which also triggers first) keeps several
 // grids resident and the HBM stream of later launches overlaps the work of earlier ones.  After
-// the wait the CTA copies its rows L2 -> shared memory in chunks (cp.async.bulk, two stages,
-// 16-byte-aligned interior of every row; Q8_0's ragged 2-byte ends by plain loads) while it
-// stages the q8_1 activations, and computes chunk k while chunk k+1 lands.
+// the wait the CTA copies its rows L2 -> shared memory in chunks (cp.async.bulk, up to four
+// stages, 16-byte-aligned interior of every row; Q8_0's ragged 2-byte ends by plain loads) while
+// it stages the q8_1 activations, and computes chunk k while later chunks land.  Where a CTA
+// refills its stages, each warp takes its rows of a chunk as soon as the chunk has landed and
+// counts itself out of the stage; the last warp out refills it (no CTA-wide barrier per chunk).
 //
 // Arithmetic (per output column, bit-exact to the one-warp decode-fast model of the reference,
 // src/subst/refs.rs:435-497): model lane l accumulates the 32-value groups l, l+32, l+64, ... of
@@ -952,6 +954,7 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
     // nst bit 9: the L2 hint for the CTA's whole row range is given in the early form too, so HBM
     // streams the rows ahead of the shared-memory stages (which then copy from L2)
     const bool hint_early = (nst & 0x200u) != 0;
+    const uint32_t nst_word = nst;
     nst &= 0xffu;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[ST_MAX_STAGES];
@@ -970,10 +973,20 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
     const uint32_t rbeg = (uint32_t)((uint64_t)blockIdx.x * nrows / gridDim.x);
     const uint32_t rend = (uint32_t)((uint64_t)(blockIdx.x + 1) * nrows / gridDim.x);
     const uint32_t nchunks = (rend - rbeg + chunk_rows - 1) / chunk_rows;
+    // a CTA that refills its stages runs the per-warp pipeline below, unless nst bit 10 asks for
+    // the CTA-wide chunk loop (as a CTA whose chunks all fit its stages does)
+    const bool warp_pipe = !MMA && (nst_word & 0x400u) == 0 && nchunks > nst;
     if constexpr (FQ) cluster_arrive_relaxed();  // completed in stage_y_q81
 
+    // per-warp pipeline (every kernel but the tensor-core one, whose chunk ends in a cross-warp
+    // sum): a stage's barrier completes on the filling warp's two arrivals (bulk bytes announced;
+    // its ragged-end stores done) and the bulk bytes; done[s] counts the warps through the stage
+    __shared__ uint32_t done[ST_MAX_STAGES];
     if (tid == 0) {
-        for (uint32_t s = 0; s < nst; s++) mbar_init(&full[s], 1);
+        for (uint32_t s = 0; s < nst; s++) {
+            mbar_init(&full[s], warp_pipe ? 2 : 1);
+            done[s] = 0;
+        }
         fence_mbar_init();
         // L2 hint for this CTA's rows (the ids table may come from the previous kernel: skip)
         if (!use_ids && (!early || hint_early) && rend > rbeg) {
@@ -1042,6 +1055,34 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
                 range_copy(st + k * rstride, rs, rs + row_bytes, &full[s], (idx & 15) == 0, idx & 15);
             }
         }
+    };
+    // the same fill by one whole warp (the per-warp pipeline): lane 0 announces the bytes and
+    // issues the bulk copies, lanes store the ragged ends, then lane 0 arrives for them
+    auto fill_w = [&](uint32_t ch, uint32_t s) {
+        const uint32_t r0 = rbeg + ch * chunk_rows, r1 = min(r0 + chunk_rows, rend);
+        uint8_t* st = smem + s * stage_bytes;
+        if (dense) {
+            const uintptr_t b0 = plane + (uintptr_t)r0 * nb * BB, b1 = plane + (uintptr_t)r1 * nb * BB;
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], range_bytes(b0, b1));
+            range_copy(st, b0, b1, &full[s], lane == 0, lane);
+        } else {
+            if (lane == 0) {
+                uint32_t tx = 0;
+                for (uint32_t r = r0; r < r1; r++) {
+                    const uintptr_t rs = plane + (uintptr_t)r * stride_row_x * BB;
+                    tx += range_bytes(rs, rs + row_bytes);
+                }
+                mbar_arrive_expect_tx(&full[s], tx);
+            }
+            __syncwarp();
+            for (uint32_t idx = lane; idx < (r1 - r0) * 16; idx += 32) {
+                const uint32_t k = idx / 16;
+                const uintptr_t rs = plane + (uintptr_t)(r0 + k) * stride_row_x * BB;
+                range_copy(st + k * rstride, rs, rs + row_bytes, &full[s], (idx & 15) == 0, idx & 15);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
     };
     auto stage_act = [&](uint8_t* at) -> YStage {
         if constexpr (MMA)
@@ -1131,20 +1172,52 @@ CFI_DEV void mmvq_stream_body(MMVQ_STREAM_PARAMS, const CfiFuseQ* fq = nullptr) 
         }
         return;
     } else {
+    auto first_fills = [&]() {
+        if (!warp_pipe) {
+            for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
+        } else if (warp == 0) {
+            for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill_w(ch, ch);
+        }
+    };
     if (early) {
         __syncthreads();  // the barrier inits precede the fills' waits in other threads
         resolve();
-        for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
+        first_fills();
     }
     pdl_launch_dependents();
     pdl_wait();
     __syncthreads();
     if (!early) {
         resolve();
-        for (uint32_t ch = 0; ch < nst && ch < nchunks; ch++) fill(ch, ch);
+        first_fills();
     }
     const YStage y = stage_act(smem + nst * stage_bytes);
     __syncthreads();
+
+    if (warp_pipe) {
+        // each warp takes its rows of every chunk as soon as the chunk has landed; the last warp
+        // through a stage refills it (no CTA-wide barrier between chunks)
+        for (uint32_t ch = 0; ch < nchunks; ch++) {
+            const uint32_t s = ch % nst;
+            if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (ch / nst) & 1, &g_mmvq_abort))) {
+                if (lane == 0) cfi_set_error(&g_mmvq_error, 0x4d560000u | ch);
+                return;
+            }
+            const uint32_t r0 = rbeg + ch * chunk_rows, r1 = min(r0 + chunk_rows, rend);
+            compute(smem_u32(smem + s * stage_bytes), r0, r1, y);
+            __syncwarp();
+            uint32_t prev = 0;
+            if (lane == 0) prev = atomicAdd(&done[s], 1u);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == NW - 1) {
+                // every warp has read the stage: reset its count (ordered before the next
+                // chunk's readers by the fill's arrivals) and refill it
+                if (lane == 0) done[s] = 0u;
+                if (ch + nst < nchunks) fill_w(ch + nst, s);
+            }
+        }
+        return;
+    }
 
     for (uint32_t ch = 0; ch < nchunks; ch++) {
         const uint32_t s = ch % nst;

@@ -696,12 +696,26 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
             // each) for 32 MB of weights and more, measured 0.77 / 0.73 of HBM on the 151936 x 896
             // Q8_0 lm_head and a 65536 x 2048 Q4_K matrix against 0.61 / 0.66 with 2 (three stages);
             // 2 below, where the launch is latency-bound (8192 x 2048 Q4_K: 3.4 against 4.5 us)
-            const uint32_t per_sm = env_u32("CFI_MMVQ_STREAM_CTAS", wkb * planes >= 32u * 1024u ? 3 : 2, 1, 8);
-            const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
-            nl.grid[0] = std::max(1u, std::min(nrows, cap));
-            cfi_mmvq_stream_layout(plan.ty, plan.ncols, ncols_x, nrows, nl.grid[0], (uint32_t)vals[6],
-                                   env_u32("CFI_MMVQ_CHUNK", 32, 1, 256), 1024 * env_u32("CFI_MMVQ_STAGE_KB", 48, 4, 112),
-                                   env_u32("CFI_MMVQ_STAGES", 3, 1, 4), per_sm, &chunk, &nstages, &nl.smem);
+            const uint32_t ctarget = env_u32("CFI_MMVQ_CHUNK", 32, 1, 256);
+            auto layout = [&](uint32_t per_sm) {
+                const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
+                nl.grid[0] = std::max(1u, std::min(nrows, cap));
+                cfi_mmvq_stream_layout(plan.ty, plan.ncols, ncols_x, nrows, nl.grid[0], (uint32_t)vals[6], ctarget,
+                                       1024 * env_u32("CFI_MMVQ_STAGE_KB", 48, 4, 112), env_u32("CFI_MMVQ_STAGES", 3, 1, 4),
+                                       per_sm, &chunk, &nstages, &nl.smem);
+            };
+            if (getenv("CFI_MMVQ_STREAM_CTAS")) {
+                layout(env_u32("CFI_MMVQ_STREAM_CTAS", 2, 1, 8));
+            } else {
+                // 3 per SM only where each still holds two whole chunks (65536 x 2048 Q4_K with two
+                // columns: 32.2 us with one stage of 3 CTAs, 19.5 us with 2 CTAs of three stages)
+                const bool big = wkb * planes >= 32u * 1024u;
+                layout(big ? 3u : 2u);
+                if (big) {
+                    const uint32_t per_cta = (nrows + nl.grid[0] - 1) / nl.grid[0];
+                    if (nstages < 2 || chunk < std::min(ctarget, per_cta)) layout(2u);
+                }
+            }
         } else if (!stream) {
             const uint32_t per_sm = env_u32("CFI_MMVQ_CTAS", 4, 1, 8);
             const uint32_t cap = std::max(1u, (uint32_t)(sm_count() * per_sm) / planes);
@@ -714,7 +728,8 @@ bool map_launch(const cfi_plan& plan, const uint32_t grid[3], const uint32_t blo
         nl.block[0] = CFI_MMVQ_THREADS;
         nl.extra.push_back(nrows);
         nl.extra.push_back(chunk);
-        nl.extra.push_back(nstages);
+        // CFI_MMVQ_WARP_PIPE=0: the streaming kernels' CTA-wide chunk loop (bit 10 of the stage word)
+        nl.extra.push_back(nstages | (nstages && env_u32("CFI_MMVQ_WARP_PIPE", 1, 0, 1) == 0 ? 0x400u : 0u));
         nl.pdl = pdl_enabled();
         nl.grid[1] = grid[1];
         nl.grid[2] = grid[2];
