@@ -446,6 +446,9 @@ struct QmmArgs {
     float* dst;
     uint32_t stride_col_dst, stride_channel_dst, stride_sample_dst;
     unsigned int* err;
+    // Q8_0 rows whose stride is not a multiple of 16 bytes (no tensor map can address them): the
+    // raw-load warp copies the chunks with cp.async instead; row_bytes = K / 32 * 34
+    uint32_t raw_direct, row_bytes;
 };
 
 template <uint32_t TY>
@@ -548,7 +551,7 @@ __global__ void __launch_bounds__(qmm_threads<G>(), 1)
             mbar_init(&empty[i], 1);     // tcgen05.commit
         }
         for (uint32_t i = 0; i < NR; i++) {
-            mbar_init(&raw_full[i], 1);  // the raw load's expect_tx
+            mbar_init(&raw_full[i], a.raw_direct ? 32 : 1);  // the raw load's expect_tx, or each lane's copies
             mbar_init(&raw_empty[i], 8 * G);  // every dequantising warp, after its last stage of the chunk
         }
         mbar_init(done, 1);
@@ -774,7 +777,36 @@ __global__ void __launch_bounds__(qmm_threads<G>(), 1)
         __syncwarp();
     } else if (warp == 8 * G + 2) {
         // ================= raw weight chunks =================
-        if (lane == 0) {
+        if (TY == T_Q8_0 && a.raw_direct) {
+            // each lane copies rows lane, lane + 32, ... of a chunk with cp.async: 16-byte pieces
+            // where the row's chunk starts 16-byte aligned, else 8-byte pieces (rows are 8-byte
+            // aligned); a chunk past K (K not a multiple of 256) stops at the row's end, a
+            // multiple of 8 bytes (K % 128 == 0); rows past the matrix copy its last row
+            const uint8_t* base = a.x + ((size_t)sx * a.stride_sample_x + (size_t)cx * a.stride_channel_x) * Q8_0_BYTES;
+            const size_t rstride = (size_t)a.stride_row_x * Q8_0_BYTES;
+            for (int j = 0; j < nchunks; j++) {
+                const uint32_t rs = (uint32_t)j % NR;
+                if (!__all_sync(0xffffffffu, mbar_wait(&raw_empty[rs], ((uint32_t)(j / NR) & 1) ^ 1, abort_flag))) {
+                    if (lane == 0) {
+                        cfi_set_error(a.err, 0xc00 + rs);
+                        *abort_flag = 1;
+                    }
+                    break;
+                }
+                const uint32_t cbyte = (uint32_t)(k0 / 4 + j) * RAW_ROW;
+                const uint32_t cb = min(RAW_ROW, a.row_bytes - cbyte);
+                for (uint32_t r = lane; r < BM; r += 32) {
+                    const uint8_t* src = base + (size_t)min(row0 + r, a.nrows - 1) * rstride + cbyte;
+                    const uint32_t d = smem_u32(sRaw + rs * RAW_BYTES + r * RAW_ROW);
+                    uint32_t o = 0;
+                    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0)
+                        for (; o + 16 <= cb; o += 16) cp_async16_cg(d + o, src + o);
+                    for (; o < cb; o += 8) cp_async8_ca(d + o, src + o);
+                }
+                cp_async_mbar_arrive_noinc(&raw_full[rs]);
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight when the CTA ends
+        } else if (lane == 0) {
             prefetch_tmap(&tmap_w);
             constexpr int XU = TY == T_Q4_K ? 144 : 136;  // chunk width in tensor-map elements (u8 / u16)
             for (int j = 0; j < nchunks; j++) {
@@ -1088,9 +1120,24 @@ uint32_t tile_n(uint32_t ncols_dst) {
     return tiles > 1 ? (per + 31) / 32 * 32 : (per + 15) / 16 * 16;
 }
 
-// The fused quantized GEMM applies when TMA can address the raw weight chunks: every row, channel
-// and sample start 16-byte aligned.  Q4_K (144-byte superblocks) always; Q8_0 (34-byte blocks)
-// when K and the block strides are multiples of 256 values / 8 blocks.  CFI_MMQ_FUSED=0 off.
+// Q8_0 whose raw chunks no tensor map can address (a row stride of 4 mod 8 blocks, or K not a
+// multiple of 256) but whose rows, channels and samples start 8-byte aligned and whose K is a
+// multiple of 128 (the last chunk a multiple of 8 bytes): the raw-load warp copies with cp.async.
+// K = 896 (28-block rows of the Qwen2.5-0.5B projections) is the case.  Only with
+// CFI_MMQ_RAW_DIRECT=1: on config 3's 4864 x 896 x 631 it measured 19.5 us against 14.5 us for the
+// fp16 weight pre-pass and the plain tensor-core GEMM (the fused kernel's dequantising chain, not
+// the pre-pass, limits a CTA that runs 14 K stages).
+inline bool qmm_raw_direct(uint32_t K, uint32_t srx, uint32_t scx, uint32_t ssx, uint32_t nch_x, uint32_t ns_x) {
+    const char* e = getenv("CFI_MMQ_RAW_DIRECT");
+    if (!(e && strcmp(e, "1") == 0)) return false;
+    if (K % 256 == 0 && srx % 8 == 0 && (nch_x == 1 || scx % 8 == 0) && (ns_x == 1 || ssx % 8 == 0)) return false;
+    return K % 128 == 0 && srx % 4 == 0 && (nch_x == 1 || scx % 4 == 0) && (ns_x == 1 || ssx % 4 == 0);
+}
+
+// The fused quantized GEMM applies when the raw weight chunks can be staged: TMA when every row,
+// channel and sample starts 16-byte aligned -- Q4_K (144-byte superblocks) always, Q8_0 (34-byte
+// blocks) when K and the block strides are multiples of 256 values / 8 blocks -- else, on request,
+// Q8_0 by cp.async (qmm_raw_direct).  CFI_MMQ_FUSED=0 off.
 template <uint32_t TY>
 bool qmm_applicable(const uint8_t* x, uint32_t K, uint32_t srx, uint32_t scx, uint32_t ssx, uint32_t nch_x,
                     uint32_t ns_x) {
@@ -1099,7 +1146,8 @@ bool qmm_applicable(const uint8_t* x, uint32_t K, uint32_t srx, uint32_t scx, ui
     if (e && strcmp(e, "0") == 0) return false;
     if (reinterpret_cast<uintptr_t>(x) & 15) return false;
     if (TY == T_Q4_K) return K % 256 == 0;
-    return K % 256 == 0 && srx % 8 == 0 && (nch_x == 1 || scx % 8 == 0) && (ns_x == 1 || ssx % 8 == 0);
+    if (K % 256 == 0 && srx % 8 == 0 && (nch_x == 1 || scx % 8 == 0) && (ns_x == 1 || ssx % 8 == 0)) return true;
+    return qmm_raw_direct(K, srx, scx, ssx, nch_x, ns_x);
 }
 
 constexpr uint32_t QMM_SMEM_LIMIT = 232448;  // 227 KB of dynamic shared memory per CTA
@@ -1138,7 +1186,10 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     constexpr uint32_t RAW_ROW = qmm_raw_row<TY>();
     constexpr uint32_t BB = TY == T_Q4_K ? Q4_K_BYTES : Q8_0_BYTES;
     CUtensorMap tw, tb, tc;
-    {
+    const bool raw_direct = TY == T_Q8_0 && qmm_raw_direct(K, srx, scx, ssx, nch_x, ns_x);
+    if (raw_direct) {
+        memset(&tw, 0, sizeof tw);  // not read: the raw chunks are copied with cp.async
+    } else {
         const uint32_t es = TY == T_Q4_K ? 1 : 2;
         const cuuint64_t rowb = (cuuint64_t)srx * BB;
         const cuuint64_t chb = nch_x > 1 ? (cuuint64_t)scx * BB : rowb * nrows;
@@ -1303,6 +1354,8 @@ int launch_qmm(const uint8_t* x, const uint8_t* y, float* dst, void* xh, uint32_
     a.stride_channel_dst = scdst;
     a.stride_sample_dst = ssd;
     a.err = device_error_ptr();
+    a.raw_direct = raw_direct ? 1u : 0u;
+    a.row_bytes = K / 32 * Q8_0_BYTES;
     static CfiPerDeviceOnce attr;
     cfi_once_per_device(attr, [] {
         cudaFuncSetAttribute(cfi_qmm_tc<TY, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QMM_SMEM_LIMIT);

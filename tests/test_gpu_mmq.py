@@ -71,12 +71,17 @@ def test_mmq_matches_the_oracle(dev, ty, shapes):
     (cfi.Q4_K, (1536, 260, 631, 1, 1, 1)),     # three column tiles
     (cfi.Q8_0, (1024, 300, 100, 1, 1, 1)),
     (cfi.Q8_0, (2048, 129, 40, 2, 1, 2)),      # channels x samples
+    (cfi.Q8_0, (896, 300, 100, 1, 1, 1)),      # 28-block rows (952 bytes): raw chunks by cp.async, the last one half
+    (cfi.Q8_0, (640, 129, 40, 2, 1, 2)),       # 20-block rows, channels x samples, cp.async
 ])
 def test_mmq_fused_and_prepass_paths_agree(dev, monkeypatch, ty, case):
-    """The fused kernel (TMA-staged raw weights dequantised in shared memory, split K) and the
-    pre-pass path (weights to fp16 in HBM, then the shared GEMM) against the oracle and each other."""
+    """The fused kernel (raw weights staged by TMA, or by cp.async where the rows are not 16-byte
+    aligned, dequantised on chip, split K) and the pre-pass path (weights to fp16 in HBM, then the
+    shared GEMM) against the oracle and each other."""
     ctx, g = dev
     ncols_x, nrows, ncols, nch, ratio, nsamples = case
+    if ty == cfi.Q8_0 and ncols_x % 256:
+        monkeypatch.setenv("CFI_MMQ_RAW_DIRECT", "1")  # the cp.async raw path is opt-in
     p, x, y, n = O.mmq_case(ty, ncols_x, nrows, ncols, nch, ratio, nsamples, 11 + ncols + ty)
     want = O.mmq_ref(ty, p, x, y, n)
     outs = []
