@@ -8,8 +8,10 @@ that every GEMV reads from HBM (inputs larger than L2).  Kernels are launched th
 substitution C ABI (cfi_subst_launch with ggml kernelParams); the timed region replays one CUDA
 graph of exactly --steps steps, replayed once before timing.  With --gpus N (torchrun) every rank
 owns an 8192-row shard of an (8192 N) x 2048 matrix (weak scaling) and the outputs are
-all-gathered over NCCL each step (step i gathers step i-1's outputs on a second stream while its
-own kernels run, all inside the graph).  Every N also runs config 5's batch-64 decode step with
+all-gathered each step (step i gathers step i-1's outputs on a second stream while its own
+kernels run, all inside the graph) by cfi_peer_all_gather (a few CTAs storing each rank's slice
+into every rank's IPC-mapped buffer over NVLink, bounded signal and wait), or over NCCL with
+--exchange nccl.  Every N also runs config 5's batch-64 decode step with
 the rows of every matrix split over the ranks and an all-gather of every product's outputs.
 
 Further legs (1 GPU): per-batch GEMV kernel times, large GEMV shapes (65536 x 2048 Q4_K, the
@@ -855,8 +857,27 @@ def run_gpu(args, rank, world):
         o += b * ROWS
     y_views_p = [{b: ya[offs[b]:offs[b] + b * ROWS] for b in BATCHES} for ya in y_sets]
     y_views = y_views_p[0]
-    gathered = torch.zeros(world * y_all.numel(), dtype=torch.float32, device=dev) if world > 1 else None
+    gathered_sets = [torch.zeros(world * y_all.numel(), dtype=torch.float32, device=dev) for _ in range(2)] \
+        if world > 1 and args.exchange == "nccl" else None
     comm = torch.cuda.Stream(device=dev) if world > 1 else None
+    # the peer exchange: one gathered range per output set (world slices of y_all each) in a
+    # buffer every rank maps (cfi_peer.h)
+    ybytes = y_all.numel() * 4
+    pgx = None
+    if world > 1 and args.exchange == "peer":
+        def exchange_obj(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+        pgx = cfi.PeerGroup(rank, world, 2 * world * ybytes, exchange_obj)
+
+    def all_gather(ysrc, parity, st):
+        """step outputs ysrc (output set `parity`) gathered over the ranks on stream st"""
+        if pgx is not None:
+            pgx.all_gather(ysrc.data_ptr(), ybytes, parity * world * ybytes, stream=st.cuda_stream)
+        else:
+            with torch.cuda.stream(st):
+                dist.all_gather_into_tensor(gathered_sets[parity], ysrc)
     torch.cuda.synchronize()  # everything above was written on torch's stream; the steps run on `stream`
 
     def step(phase, s, parity=0, gg=None, xsrc=None):
@@ -876,8 +897,7 @@ def run_gpu(args, rank, world):
             fork = torch.cuda.Event()
             fork.record(cur)
             comm.wait_event(fork)
-            with torch.cuda.stream(comm):
-                dist.all_gather_into_tensor(gathered, y_sets[1 - parity])
+            all_gather(y_sets[1 - parity], 1 - parity, comm)
         step(phase, cur.cuda_stream, parity)
         if dist:
             join = torch.cuda.Event()
@@ -890,7 +910,7 @@ def run_gpu(args, rank, world):
         for i in range(max(1, args.warmup)):
             step(i % nphase, stream.cuda_stream)
             if dist:
-                dist.all_gather_into_tensor(gathered, y_all)
+                all_gather(y_all, 0, stream)
     torch.cuda.synchronize()
     # One CUDA graph holds exactly the K timed steps (step i: weight phase i % nphase, output set
     # i % 2; programmatic dependent launch overlaps consecutive steps inside it).  It is replayed
@@ -1023,7 +1043,6 @@ def run_gpu(args, rank, world):
     # with N > 1 GPUs: step i's outputs are all-gathered on the comm stream after its kernels;
     # step i+2 waits for that collective before it rewrites the same output buffer
     ev_ag = [torch.cuda.Event() for _ in range(2)]
-    gathered2 = [gathered, torch.zeros_like(gathered)] if dist else None
 
     ge = torch.cuda.CUDAGraph()
     with torch.cuda.graph(ge, stream=stream):
@@ -1050,8 +1069,7 @@ def run_gpu(args, rank, world):
             ev_comp[p].record(cur)
             if dist:
                 comm.wait_event(ev_comp[p])
-                with torch.cuda.stream(comm):
-                    dist.all_gather_into_tensor(gathered2[p], y_sets[p])
+                all_gather(y_sets[p], p, comm)
                 ev_ag[p].record(comm)
             with torch.cuda.stream(copy_o):
                 copy_o.wait_event(ev_comp[p])
@@ -1075,7 +1093,8 @@ def run_gpu(args, rank, world):
     e2e_note = ("host fp32 activations in (one pinned buffer) and fp32 outputs out (two pinned buffers) every "
                 "step, weights resident; copies on one stream per direction overlap the neighbouring steps' kernels%s; "
                 "one CUDA graph of the K steps, replayed once before timing; wall clock until the last output is on "
-                "the host" % (", outputs all-gathered over NCCL on a third stream" if dist else ""))
+                "the host" % ((", outputs all-gathered on a third stream (%s)" % ("NCCL" if pgx is None else "cfi_peer_all_gather"))
+                              if dist else ""))
     del ge
     if dist:
         t = torch.tensor([e2e_s], device=dev)
@@ -1094,7 +1113,8 @@ def run_gpu(args, rank, world):
                 "config": {"workload": "config2: Q4_K 8192x2048 GEMV + quantize_q8_1, batch 1/2/4/8",
                            "rows_per_gpu": ROWS, "k": K, "batches": "1,2,4,8", "weight_copies": ncopy,
                            "l2": "inputs larger than L2: %d weight copies (%.0f MB) rotated" % (ncopy, ncopy * W_BYTES / 1e6),
-                           "parallelism": "row-sharded x%d + NCCL all-gather" % world if world > 1 else "single GPU",
+                           "parallelism": ("row-sharded x%d + %s all-gather" % (world, "NCCL" if pgx is None else "peer-memory (NVLink)"))
+                           if world > 1 else "single GPU",
                            "bytes_per_step_per_gpu": STEP_BYTES,
                            "cuda_graph": "one graph of exactly the K timed steps, replayed once before timing",
                            "router": "CFI_CTX_CONST_WEIGHTS" + (" + CFI_CTX_DEFER_Q8_1" if defer else "")},
@@ -1161,7 +1181,10 @@ def run_gpu(args, rank, world):
         line["summary"] = summary
         print(json.dumps(line), flush=True)
     if dist:
-        dist.barrier()
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still stores into another's exchange buffer
+        if pgx is not None:
+            pgx.close()
         dist.destroy_process_group()
     ctx.close()
     for c in (ctx_sep, ctx_plain):
@@ -1249,6 +1272,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--legs", default="all", help="comma list of %s (default all)" % ",".join(ALL_LEGS))
+    ap.add_argument("--exchange", default="peer", choices=("peer", "nccl"),
+                    help="N > 1: the headline step's all-gather over peer memory (default) or NCCL")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-decode", action="store_true")

@@ -131,6 +131,7 @@ def lib():
     L.cfi_peer_close.argtypes = [vp]
     L.cfi_peer_free.argtypes = [vp]
     L.cfi_peer_barrier.argtypes = [C.POINTER(PeerSet), vp]
+    L.cfi_peer_all_gather.argtypes = [vp, C.c_size_t, vp, C.POINTER(PeerSet), vp]
     L.cfi_fused_add_rmsnorm_q8_1.argtypes = [vp, vp, vp, vp, i, f, vp]
     L.cfi_fused_qkv_rope_store.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, vp]
     L.cfi_fused_attention_q8_1.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, f, vp]
@@ -655,6 +656,12 @@ class PeerGroup:
 
     def barrier(self, stream=0):
         check(lib().cfi_peer_barrier(C.byref(self.peers), C.c_void_p(stream)), "cfi_peer_barrier")
+
+    def all_gather(self, src, nbytes, dst_off, stream=0):
+        """Every rank's nbytes at device address src into [dst_off + r * nbytes) of every rank's
+        data, ranks in order; returns once (on the stream) this rank's data holds them all."""
+        check(lib().cfi_peer_all_gather(C.c_void_p(src), nbytes, C.c_void_p(self.data + dst_off), C.byref(self.peers),
+                                        C.c_void_p(stream)), "cfi_peer_all_gather")
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (every rank synchronised first)."""

@@ -11,6 +11,8 @@
 // GPU).
 #include <string.h>
 
+#include <algorithm>
+
 #include "../../include/cfi_peer.h"
 #include "cfi_common.cuh"
 #include "cfi_kernels.h"
@@ -36,6 +38,31 @@ __global__ void __launch_bounds__(32, 1) cfi_peer_barrier_kernel(const __grid_co
     if (threadIdx.x == 0) {
         peer_signal_cta(p, 1, true);
         peer_wait_all(p, err);
+    }
+}
+
+// All-gather of one slice per rank: grid-stride 16-byte copies of this rank's slice into its
+// place in every rank's buffer (ranks in turn from this one), then the per-CTA signal and CTA 0's
+// wait (peer_sync.cuh).  dst: this rank's buffer at the gathered range; delta[r] maps it to rank r's.
+__global__ void __launch_bounds__(256) cfi_peer_all_gather_kernel(const uint4* __restrict__ src, uint4* dst, uint32_t n16,
+                                                                   const __grid_constant__ CfiPeerDev p, unsigned int* err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    uint4* mine = dst + (size_t)p.rank * n16;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x) {
+        const uint4 v = src[i];
+        for (int k = 0; k < p.world; k++) {
+            const int r = p.rank + k < p.world ? p.rank + k : p.rank + k - p.world;
+            reinterpret_cast<uint4*>(reinterpret_cast<char*>(mine + i) + p.delta[r])[0] = v;
+        }
+    }
+    if (p.world > 1) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const bool first = blockIdx.x == 0;
+            peer_signal_cta(p, gridDim.x, first);
+            if (first) peer_wait_all(p, err);
+        }
     }
 }
 
@@ -108,4 +135,28 @@ extern "C" int cfi_peer_barrier(const CfiPeerSet* peers, void* stream) {
     c.numAttrs = ep && strcmp(ep, "0") == 0 ? 0 : 1;
     unsigned int* err = cfi_device_error_word();
     return (int)cudaLaunchKernelEx(&c, cfi_peer_barrier_kernel, p, err);
+}
+
+extern "C" int cfi_peer_all_gather(const void* src, size_t bytes, void* dst, const CfiPeerSet* peers, void* stream) {
+    CfiPeerDev p;
+    const int rc = cfi_peer_dev(peers, &p);
+    if (rc) return rc;
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15) || bytes % 16 ||
+        bytes / 16 > 0xffffffffull)
+        return (int)cudaErrorInvalidValue;
+    if (bytes == 0) return 0;
+    const uint32_t n16 = (uint32_t)(bytes / 16);
+    const char* ep = getenv("CFI_PDL");
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3(std::min<uint32_t>(16u, std::max<uint32_t>(1u, (n16 + 4095) / 4096)), 1, 1);
+    c.blockDim = dim3(256, 1, 1);
+    c.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    c.attrs = at;
+    c.numAttrs = ep && strcmp(ep, "0") == 0 ? 0 : 1;
+    unsigned int* err = cfi_device_error_word();
+    return (int)cudaLaunchKernelEx(&c, cfi_peer_all_gather_kernel, static_cast<const uint4*>(src), static_cast<uint4*>(dst),
+                                   n16, p, err);
 }

@@ -65,6 +65,16 @@ typedef struct CfiPeerSet {
  * set (until cfi_device_error reads it), later waits of the group give up at once. */
 CFI_API int cfi_peer_barrier(const CfiPeerSet *peers, void *stream);
 
+/* All-gather over the group: dst is the gathered range inside this rank's peer buffer (world *
+ * bytes; rank r's copy of it at dst + delta[r]); every rank stores its `bytes` at src (device
+ * memory) at dst + rank * bytes of every rank's copy (its own included), then signals and waits
+ * as cfi_peer_barrier does, so when it completes this rank's range holds every rank's slice, rank
+ * by rank (the layout of an all_gather_into_tensor).  src, dst and bytes multiples of 16; every
+ * rank passes the same bytes and the same offset of dst in its buffer.  A few CTAs do the copy
+ * (plain 16-byte loads and stores over NVLink), so the kernels running beside it keep the rest of
+ * the GPU. */
+CFI_API int cfi_peer_all_gather(const void *src, size_t bytes, void *dst, const CfiPeerSet *peers, void *stream);
+
 /* cfi_mmq_skinny_group (cfi_glue.h) as one step of an all-gather over the group: every output
  * value written at address a of dst[i] (inside this rank's peer buffer) is also written at
  * a + delta[r] on every other rank r; after its last store the launch signals every peer and

@@ -30,6 +30,11 @@ UNIT = 65536  # what one launch adds to its slot on each peer, over all its CTAs
 # shards, and one Q8_0 product with an odd column count
 GROUPS = [(cfi.Q4_K, 1536, (1536, 256, 257), 64), (cfi.Q8_0, 1536, (5001,), 37)]
 ITERS = 3
+GATHER_BYTES = 200000  # one rank's slice of the cfi_peer_all_gather test (a multiple of 16)
+
+
+def gather_slice(rank, it):
+    return np.arange(GATHER_BYTES // 4, dtype=np.float32) + np.float32(1000.0 * rank + 0.5 * it)
 
 
 def free_port():
@@ -111,12 +116,21 @@ def rank_main(rank, world, port, outdir):
                                      [h.rows for h in sh], k, ncols, stream=s)
                 for i in range(len(rows)):
                     shards[it, gi, i] = loc[i]
+        # cfi_peer_all_gather: a new slice per iteration, the gathered range read after each
+        pg2 = cfi.PeerGroup(rank, world, world * GATHER_BYTES, exchange)
+        gat = {}
+        for it in range(ITERS):
+            src = torch.from_numpy(gather_slice(rank, it)).cuda()
+            pg2.all_gather(src.data_ptr(), GATHER_BYTES, 0, stream=s)
+            gat[it] = device_floats(pg2.data, world * GATHER_BYTES // 4).clone()
         torch.cuda.synchronize()
         err = cfi.lib().cfi_device_error()
         np.savez(os.path.join(outdir, "rank%d.npz" % rank), err=np.uint32(err),
                  **{"g_%d_%d_%d" % key: t.cpu().numpy() for key, t in snaps.items()},
-                 **{"s_%d_%d_%d" % key: t.cpu().numpy() for key, t in shards.items()})
+                 **{"s_%d_%d_%d" % key: t.cpu().numpy() for key, t in shards.items()},
+                 **{"a_%d" % it: t.cpu().numpy() for it, t in gat.items()})
         dist.barrier()  # every rank done with the others' buffers before any is unmapped
+        pg2.close()
     finally:
         if pg is not None:
             pg.close()
@@ -152,6 +166,11 @@ def test_peer_all_gather_matches_the_shards_and_the_oracle():
                     p, x = ws[i]
                     ref = O.mmq_ref(ty, p, x, ys[it], ncols * r)
                     assert O.rel_l2(want.ravel(), ref) < SKINNY_REL, (it, gi, i)
+        # cfi_peer_all_gather: every rank's slice in rank order on every rank, each iteration's own
+        for it in range(ITERS):
+            want = np.concatenate([gather_slice(rk, it) for rk in range(world)])
+            for rk in range(world):
+                assert np.array_equal(res[rk]["a_%d" % it], want), (it, rk)
 
 
 def one_gpu_group(ctr, scratch):
@@ -222,6 +241,21 @@ def test_peer_product_whose_peer_never_signals_ends_with_the_error_word(monkeypa
     assert int(scratch[0]) == UNIT  # one launch's whole signal, over all its CTAs
 
 
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_peer_all_gather_of_a_group_of_one_copies():
+    """world 1: the slice lands at dst (no signal, no wait)."""
+    L = cfi.lib()
+    ps = cfi.PeerSet()
+    ps.rank, ps.world = 0, 1
+    src = torch.arange(4096, dtype=torch.float32, device="cuda")
+    dst = torch.full((4096 + 16,), float("nan"), device="cuda")
+    assert L.cfi_peer_all_gather(C.c_void_p(src.data_ptr()), 16384, C.c_void_p(dst.data_ptr() + 64), C.byref(ps),
+                                 C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    assert L.cfi_device_error() == 0
+    assert torch.equal(dst[16:], src) and torch.isnan(dst[:16]).all()
+
+
 def test_peer_calls_refuse_bad_arguments():
     L = cfi.lib()
     buf = C.c_void_p(1 << 20)
@@ -241,3 +275,9 @@ def test_peer_calls_refuse_bad_arguments():
     args = (P(buf), buf, P(buf), U(16), U(8), U(16), 256, 8, 8)
     assert L.cfi_mmq_skinny_group_peers(cfi.Q4_K, 1, *args, C.byref(ps), None) != 0
     assert L.cfi_mmq_skinny_group_peers(cfi.Q4_K, 1, *args, None, None) != 0
+    one = cfi.PeerSet()
+    one.rank, one.world = 0, 1
+    assert L.cfi_peer_all_gather(buf, 24, buf, C.byref(one), None) != 0               # not 16-byte sized
+    assert L.cfi_peer_all_gather(C.c_void_p(buf.value + 8), 32, buf, C.byref(one), None) != 0  # source alignment
+    assert L.cfi_peer_all_gather(buf, 32, C.c_void_p(buf.value + 4), C.byref(one), None) != 0  # destination alignment
+    assert L.cfi_peer_all_gather(buf, 32, buf, None, None) != 0
